@@ -1,0 +1,209 @@
+/*
+ * lt_kv.h -- C ABI of the B200 paged KV-cache path.
+ *
+ * Drop-in replacement for the reference engine's KV cache API
+ * (engine/crates/native/src/kv.rs, struct KvCache) and the attention closure
+ * of Model::forward (engine/crates/native/src/model.rs:431-476), exposed as
+ * plain `extern "C"` functions over pointers and sizes so that the Rust host
+ * (NativeBackend, engine/crates/native/src/lib.rs:45-198) can bind it through
+ * a thin FFI module.  No torch or C++ types cross this boundary.
+ *
+ * Model.  One handle owns one paged cache on one CUDA device: the K/V block
+ * pool in HBM, the device copy of every sequence's block table, and the host
+ * bookkeeping (refcounts, LIFO free list, per-sequence block lists) that the
+ * reference keeps in KvCache.  The bookkeeping runs on the host thread and
+ * is bit-identical to the reference's; the data work (copy-on-write block
+ * copies, K/V append, attention, compaction) runs as sm_100a kernels on the
+ * stream the caller passes.
+ *
+ * Threading.  A handle is not thread-safe (KvCache is owned by the single
+ * engine thread, engine/crates/engine/src/scheduler.rs:103-119).  Issue all
+ * kernel-launching calls of one handle on one stream, or synchronise when
+ * switching streams.  Bookkeeping-only calls (truncate, share) take no
+ * stream; their device-side effect is applied, in call order, right before
+ * the next kernel-launching call.
+ *
+ * Pointers.  Arguments named *_host are host memory; `k`, `v`, `q`, `out`
+ * and the pointers of lt_kv_rows are device memory.  seq / pos / block /
+ * slot arrays are host memory (they are the reference's Vec arguments).
+ *
+ * Errors.  Every fallible call returns an lt_status; the message of the last
+ * error is kept per handle (lt_kv_last_error).
+ */
+#ifndef LT_KV_H
+#define LT_KV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Tokens per block: kv.rs:13 (BLOCK = 16). */
+#define LT_KV_BLOCK 16
+
+typedef enum lt_status {
+    LT_OK = 0,
+    LT_E_FULL = 1,        /* "KV cache full" (kv.rs:71)                         */
+    LT_E_NONCONTIG = 2,   /* "position not contiguous" (kv.rs:87-92)            */
+    LT_E_ARG = 3,         /* invalid argument (id out of range, bad size, ...)  */
+    LT_E_CUDA = 4,        /* a CUDA runtime call failed                         */
+    LT_E_NCCL = 5,        /* an NCCL call failed                                */
+    LT_E_TIMEOUT = 6,     /* a bounded device wait gave up (kernel error flag)  */
+    LT_E_UNSUPPORTED = 7  /* shape outside what the kernels implement           */
+} lt_status;
+
+typedef enum lt_dtype {
+    LT_F32 = 0,
+    LT_F16 = 1
+} lt_dtype;
+
+typedef struct lt_kv lt_kv;
+
+/* Creation parameters.  KvCache::new(n_layers, kv_dim, n_tokens) (kv.rs:35-48)
+ * with kv_dim = n_kv_heads * head_dim, plus the sizes the device buffers are
+ * planned for, so no call after lt_kv_create allocates device memory. */
+typedef struct lt_kv_config {
+    uint32_t n_layers;
+    uint32_t n_kv_heads;        /* KV heads held by this handle                  */
+    uint32_t head_dim;          /* 64 or 128                                     */
+    uint32_t n_heads;           /* query heads for those KV heads; n_heads /
+                                   n_kv_heads = GQA group (model.rs:401), <= 8   */
+    uint32_t n_tokens;          /* pool capacity in tokens (rounded up to blocks) */
+    uint32_t max_seqs;          /* sequence ids are in [0, max_seqs): seq == slot
+                                   (engine/crates/engine/src/backend.rs:19-20)   */
+    uint32_t max_batch;         /* most tokens per append / write / attend call  */
+    uint32_t max_blocks_per_seq;/* 0: n_blocks (never limits)                    */
+    int32_t device;             /* CUDA ordinal; -1 = bookkeeping only (no GPU)  */
+} lt_kv_config;
+
+/* KvCache::new (kv.rs:35-48): zero-filled pool, free list (0..n_blocks).rev()
+ * so the first allocation returns block 0. */
+lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out);
+/* Drop (frees device and host memory; synchronises the device first). */
+void lt_kv_destroy(lt_kv* kv);
+/* Message of the last failed call on this handle ("" if none). */
+const char* lt_kv_last_error(const lt_kv* kv);
+
+/* KvCache::capacity (kv.rs:50-52): n_blocks * 16 tokens. Backend::n_ctx. */
+uint32_t lt_kv_capacity(const lt_kv* kv);
+/* KvCache::bytes (kv.rs:54-56): K + V pool bytes. */
+uint64_t lt_kv_bytes(const lt_kv* kv);
+/* KvCache::len (kv.rs:58-60): 0 for an unknown sequence. */
+uint32_t lt_kv_len(const lt_kv* kv, uint32_t seq);
+/* KvCache::free_blocks (kv.rs:185-187). */
+uint32_t lt_kv_free_blocks(const lt_kv* kv);
+
+/* KvCache::append (kv.rs:85-121) for a batch, as Model::forward claims every
+ * batch token before any layer runs (model.rs:380-383).  For token i:
+ * pos[i] must equal the sequence's length (else LT_E_NONCONTIG); a new block
+ * is taken at slot 0 (else LT_E_FULL); a write into a shared last block
+ * copies it first (copy-on-write, all layers, K and V).  Returns the (block,
+ * slot) cell of each token.  Stops at the first error: *n_done tokens were
+ * claimed and stay claimed, the failing sequence is unchanged -- exactly the
+ * reference's `collect::<Result<Vec<_>>>()`.  The copy-on-write copies are
+ * enqueued on `stream`. */
+lt_status lt_kv_append(lt_kv* kv, const uint32_t* seq_host, const uint32_t* pos_host, uint32_t n,
+                       int32_t* block_host, int32_t* slot_host, uint32_t* n_done, void* stream);
+
+/* KvCache::write (kv.rs:123-131) for n cells of one layer, as the per-layer
+ * loop of Model::forward does (model.rs:414-429).  k and v are device arrays
+ * [n][n_kv_heads * head_dim] of `dtype`; f32 is rounded to f16 with
+ * round-to-nearest-even (bit-identical to half::f16::from_f32), f16 is
+ * stored unchanged. */
+lt_status lt_kv_write(lt_kv* kv, uint32_t layer, const int32_t* block_host, const int32_t* slot_host,
+                      uint32_t n, const void* k, const void* v, lt_dtype dtype, void* stream);
+
+/* Attention closure of Model::forward (model.rs:431-476) for n tokens of one
+ * layer: token i attends over positions [0, pos[i]] of sequence seq[i]
+ * through its block table, GQA with group n_heads / n_kv_heads.
+ * q and out are device arrays [n][n_heads * head_dim] (q: f32 or f16; out:
+ * f32 or f16), head h*group+g reads KV head h.  scale is the reference's
+ * 1/sqrt(head_dim) (model.rs:402).  Softmax and accumulation are f32. */
+lt_status lt_kv_attend(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype,
+                       const uint32_t* seq_host, const uint32_t* pos_host, uint32_t n, void* out,
+                       lt_dtype out_dtype, float scale, void* stream);
+
+/* write + attend in one kernel launch (the K/V rows of each token are
+ * written by the attention work item that covers them, then attended to).
+ * Same results as lt_kv_write followed by lt_kv_attend with the same
+ * arguments.  k/v dtype: `kv_dtype`. */
+lt_status lt_kv_write_attend(lt_kv* kv, uint32_t layer, const int32_t* block_host,
+                             const int32_t* slot_host, const void* k, const void* v, lt_dtype kv_dtype,
+                             const void* q, lt_dtype q_dtype, const uint32_t* seq_host,
+                             const uint32_t* pos_host, uint32_t n, void* out, lt_dtype out_dtype,
+                             float scale, void* stream);
+
+/* KvCache::truncate (kv.rs:153-169): drop positions [from, len) of seq,
+ * releasing whole blocks past ceil(from/16) in ascending order; no-op for an
+ * unknown seq or from >= len.  Backend::kv_remove (native/src/lib.rs:192). */
+void lt_kv_truncate(lt_kv* kv, uint32_t seq, uint32_t from);
+
+/* KvCache::share (kv.rs:172-183): truncate(dst, 0), then let dst start with
+ * the first min(len, len(src)) tokens of src by sharing its blocks (refcount
+ * + 1 each).  Backend::kv_copy (native/src/lib.rs:196). */
+void lt_kv_share(lt_kv* kv, uint32_t src, uint32_t dst, uint32_t len);
+
+/* Compaction (no counterpart in the reference, which never moves blocks):
+ * free ids ascending are paired with live ids descending while free < live;
+ * each such live block is moved (all layers, K and V) onto the free id, its
+ * refcount moves with it and every block-table entry is remapped, on host
+ * and device alike; the free list is rebuilt descending so the next
+ * allocation returns the lowest free id.  Every sequence's rows() are
+ * byte-identical before and after.  *n_moved (optional) = blocks moved. */
+lt_status lt_kv_compact(lt_kv* kv, uint32_t* n_moved, void* stream);
+
+/* Apply every pending bookkeeping change to the device (block tables,
+ * pending copies) on `stream` now. */
+lt_status lt_kv_flush(lt_kv* kv, void* stream);
+
+/* KvCache::rows (kv.rs:135-150): gather rows [0, n) of seq in `layer` into
+ * device arrays k_out / v_out [n][n_kv_heads * head_dim] (f16, reference
+ * row layout). */
+lt_status lt_kv_rows(lt_kv* kv, uint32_t layer, uint32_t seq, uint32_t n, void* k_out, void* v_out,
+                     void* stream);
+
+/* Reads (and clears) the device error flag set by bounded waits in the
+ * kernels; synchronises `stream`.  LT_OK or LT_E_TIMEOUT / LT_E_CUDA. */
+lt_status lt_kv_check(lt_kv* kv, void* stream);
+
+/* ---- introspection (parity checks, debugging) ---------------------------- */
+
+/* Block ids of seq's table; returns the count, copies min(count, cap). */
+uint32_t lt_kv_seq_blocks(const lt_kv* kv, uint32_t seq, int32_t* out_host, uint32_t cap);
+/* Refcount of every block (n_blocks entries). */
+uint32_t lt_kv_refs(const lt_kv* kv, uint32_t* out_host, uint32_t cap);
+/* Free list, bottom of the stack first; returns its length. */
+uint32_t lt_kv_free_list(const lt_kv* kv, int32_t* out_host, uint32_t cap);
+uint32_t lt_kv_n_blocks(const lt_kv* kv);
+
+/* Device pool layout, for tools that read it directly:
+ * f16 [layer][block][kv_head][2 (K, V)][16 slots][head_dim], where the 16-byte
+ * chunk c of row `slot` is stored at chunk position (c ^ (slot & 7)) within
+ * its 128-byte group (a bank-conflict-free shared-memory image once a block
+ * is bulk-copied).  Returns the device base address. */
+void* lt_kv_device_pool(const lt_kv* kv);
+/* Device block tables: int32 [max_seqs][max_blocks_per_seq]. */
+const int32_t* lt_kv_device_tables(const lt_kv* kv, uint32_t* max_blocks_per_seq);
+
+/* Copy the raw device pool bytes of `layer`, blocks [block0, block0+count),
+ * into host memory (layout of lt_kv_device_pool); synchronous.  For parity
+ * checks of whole pools against the reference layout. */
+lt_status lt_kv_read_pool(lt_kv* kv, uint32_t layer, uint32_t block0, uint32_t count, void* out_host);
+
+/* Attention-kernel timing.  While enabled, CUDA events bracket every
+ * attention launch (lt_kv_attend, lt_kv_write_attend) on its own stream;
+ * enabling resets the totals. */
+lt_status lt_kv_profile(lt_kv* kv, int enable);
+/* Total duration (ms) and count of the bracketed attention launches since
+ * profiling was enabled; waits for the recorded events. */
+lt_status lt_kv_profile_read(lt_kv* kv, double* total_ms, uint64_t* launches);
+
+/* Kernel launches made by this handle since creation (all kinds). */
+uint64_t lt_kv_launch_count(const lt_kv* kv);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LT_KV_H */

@@ -1,0 +1,97 @@
+"""ctypes binding of the C ABI in include/lt_kv.h (liblt_kv.so).
+
+This is the same binding a Python host of the reference would write; the
+Rust host binds the same symbols through `extern "C"`.
+There is no fallback: if the library cannot be loaded or built, import fails.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+
+from . import build as _build
+
+LT_OK, LT_E_FULL, LT_E_NONCONTIG, LT_E_ARG, LT_E_CUDA, LT_E_NCCL, LT_E_TIMEOUT, LT_E_UNSUPPORTED = range(8)
+LT_F32, LT_F16 = 0, 1
+BLOCK = 16
+
+# Every function include/lt_kv.h declares (tests check the export table).
+EXPORTS = (
+    "lt_kv_create", "lt_kv_destroy", "lt_kv_last_error", "lt_kv_capacity", "lt_kv_bytes", "lt_kv_len",
+    "lt_kv_free_blocks", "lt_kv_append", "lt_kv_write", "lt_kv_attend", "lt_kv_write_attend",
+    "lt_kv_truncate", "lt_kv_share", "lt_kv_compact", "lt_kv_flush", "lt_kv_rows", "lt_kv_check",
+    "lt_kv_seq_blocks", "lt_kv_refs", "lt_kv_free_list", "lt_kv_n_blocks", "lt_kv_device_pool",
+    "lt_kv_device_tables", "lt_kv_read_pool", "lt_kv_launch_count", "lt_kv_profile", "lt_kv_profile_read",
+)
+
+
+class lt_kv_config(C.Structure):
+    _fields_ = [
+        ("n_layers", C.c_uint32),
+        ("n_kv_heads", C.c_uint32),
+        ("head_dim", C.c_uint32),
+        ("n_heads", C.c_uint32),
+        ("n_tokens", C.c_uint32),
+        ("max_seqs", C.c_uint32),
+        ("max_batch", C.c_uint32),
+        ("max_blocks_per_seq", C.c_uint32),
+        ("device", C.c_int32),
+    ]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def _declare(L):
+    u32, i32, u64, p, st = C.c_uint32, C.c_int32, C.c_uint64, C.c_void_p, C.c_int
+    sig = {
+        "lt_kv_create": (st, [C.POINTER(lt_kv_config), C.POINTER(p)]),
+        "lt_kv_destroy": (None, [p]),
+        "lt_kv_last_error": (C.c_char_p, [p]),
+        "lt_kv_capacity": (u32, [p]),
+        "lt_kv_bytes": (u64, [p]),
+        "lt_kv_len": (u32, [p, u32]),
+        "lt_kv_free_blocks": (u32, [p]),
+        "lt_kv_n_blocks": (u32, [p]),
+        "lt_kv_append": (st, [p, p, p, u32, p, p, C.POINTER(u32), p]),
+        "lt_kv_write": (st, [p, u32, p, p, u32, p, p, C.c_int, p]),
+        "lt_kv_attend": (st, [p, u32, p, C.c_int, p, p, u32, p, C.c_int, C.c_float, p]),
+        "lt_kv_write_attend": (st, [p, u32, p, p, p, p, C.c_int, p, C.c_int, p, p, u32, p, C.c_int,
+                                    C.c_float, p]),
+        "lt_kv_truncate": (None, [p, u32, u32]),
+        "lt_kv_share": (None, [p, u32, u32, u32]),
+        "lt_kv_compact": (st, [p, C.POINTER(u32), p]),
+        "lt_kv_flush": (st, [p, p]),
+        "lt_kv_rows": (st, [p, u32, u32, u32, p, p, p]),
+        "lt_kv_check": (st, [p, p]),
+        "lt_kv_seq_blocks": (u32, [p, u32, p, u32]),
+        "lt_kv_refs": (u32, [p, p, u32]),
+        "lt_kv_free_list": (u32, [p, p, u32]),
+        "lt_kv_device_pool": (p, [p]),
+        "lt_kv_device_tables": (p, [p, C.POINTER(u32)]),
+        "lt_kv_read_pool": (st, [p, u32, u32, u32, p]),
+        "lt_kv_launch_count": (u64, [p]),
+        "lt_kv_profile": (st, [p, C.c_int]),
+        "lt_kv_profile_read": (st, [p, C.POINTER(C.c_double), C.POINTER(u64)]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+
+
+def lib():
+    """Load liblt_kv.so (building it with nvcc first if it is missing or stale)."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            path = _build.build()
+            L = C.CDLL(str(path))
+            _declare(L)
+            _lib = L
+    return _lib
+
+
+def library_path() -> str:
+    return str(_build.LIB)

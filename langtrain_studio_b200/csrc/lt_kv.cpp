@@ -1,0 +1,822 @@
+// Host side of the B200 paged KV cache: the reference's KvCache bookkeeping
+// (engine/crates/native/src/kv.rs) kept bit-identical on the host, the
+// device mirror of the block tables, and the C ABI of include/lt_kv.h.
+//
+// Host/device split.  Allocation, refcounts, the LIFO free list and every
+// sequence's block list live here (they are O(tokens/16) integer work and
+// their order must match the reference exactly).  Their device-side effects
+// -- copy-on-write block copies, compaction moves and block-table entries --
+// are queued and applied by one kv_apply_plan launch right before the next
+// kernel that reads them, on that kernel's stream.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "lt_kv.h"
+#include "lt_kv_internal.h"
+
+using ltkv::kBlock;
+
+namespace {
+
+constexpr int kSlots = 8;  // staging ring depth (pinned host + device pairs)
+constexpr uint32_t kClean = 0xFFFFFFFFu;
+
+struct Slot {
+    void* host = nullptr;
+    void* dev = nullptr;
+    cudaEvent_t ev = nullptr;
+    uint64_t gen = 0;
+    bool used = false;
+};
+
+// Device copy of a small host array, reused while the contents are unchanged
+// (e.g. the same batch cells for every layer of a forward pass).
+struct UploadCache {
+    std::vector<char> key;
+    int slot = -1;
+    uint64_t gen = 0;
+};
+
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    // dev < 0 (bookkeeping-only handle): touch no CUDA state at all.
+    explicit DeviceGuard(int dev) {
+        if (dev < 0) return;
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+struct lt_kv {
+    lt_kv_config cfg{};
+    uint32_t n_blocks = 0, kv_dim = 0, group = 0, max_blocks = 0;
+    size_t block_elems = 0;   // f16 elements of one block in one layer (all heads, K and V)
+    size_t layer_elems = 0;   // f16 elements of one layer of the pool
+
+    // ---- reference bookkeeping (kv.rs:15-26) ----
+    std::vector<std::vector<int32_t>> blocks;  // per sequence
+    std::vector<uint32_t> lens;
+    std::vector<uint32_t> refs;
+    std::vector<int32_t> free_list;  // stack: back() is popped first
+
+    std::string err;
+    bool dev = false;
+
+    // ---- device state ----
+    uint16_t* d_pool = nullptr;
+    int32_t* d_tables = nullptr;
+    float* d_part_o = nullptr;
+    float* d_part_ml = nullptr;
+    int32_t* d_counters = nullptr;
+    int32_t* d_err = nullptr;
+    size_t ws_slots = 0;
+    size_t slot_bytes = 0;
+    Slot slots[kSlots];
+    int next_slot = 0;
+
+    // ---- queued device work ----
+    std::vector<int2> pend_copies;
+    std::vector<uint32_t> mark_src, mark_dst;
+    uint32_t epoch = 1;
+    std::vector<uint32_t> dirty_from;  // per seq, first table index to re-upload
+    std::vector<uint32_t> dirty_list;
+    std::vector<int2> tw_tmp;
+
+    std::vector<int32_t> dev_shadow;  // what the device tables hold (host copy)
+
+    // attention-kernel timing (lt_kv_profile)
+    bool profiling = false;
+    std::vector<cudaEvent_t> prof_ev;  // pairs (start, end), ring
+    size_t prof_head = 0, prof_pending = 0;
+    double prof_ms = 0.0;
+    uint64_t prof_count = 0;
+
+    UploadCache cells_cache, items_cache;
+    std::vector<ltkv::WorkItem> items_tmp;
+    std::vector<int2> cells_tmp;
+    int cb_override = 0;
+    uint64_t launches = 0;
+};
+
+namespace {
+
+lt_status fail(lt_kv* kv, lt_status s, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (kv) kv->err = buf;
+    return s;
+}
+
+#define LT_CUDA(kv, call)                                                                              \
+    do {                                                                                               \
+        cudaError_t e_ = (call);                                                                       \
+        if (e_ != cudaSuccess) return fail((kv), LT_E_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+void free_device(lt_kv* kv) {
+    cudaFree(kv->d_pool);
+    cudaFree(kv->d_tables);
+    cudaFree(kv->d_part_o);
+    cudaFree(kv->d_part_ml);
+    cudaFree(kv->d_counters);
+    cudaFree(kv->d_err);
+    for (auto& s : kv->slots) {
+        if (s.host) cudaFreeHost(s.host);
+        if (s.dev) cudaFree(s.dev);
+        if (s.ev) cudaEventDestroy(s.ev);
+        s = Slot{};
+    }
+    for (cudaEvent_t e : kv->prof_ev) cudaEventDestroy(e);
+    kv->prof_ev.clear();
+    kv->d_pool = nullptr;
+    kv->d_tables = nullptr;
+    kv->d_part_o = kv->d_part_ml = nullptr;
+    kv->d_counters = kv->d_err = nullptr;
+}
+
+// Next staging slot; waits until every kernel that read its previous
+// contents has finished (the slot's event).
+int acquire_slot(lt_kv* kv) {
+    const int s = kv->next_slot;
+    kv->next_slot = (s + 1) % kSlots;
+    Slot& sl = kv->slots[s];
+    if (sl.used) cudaEventSynchronize(sl.ev);
+    sl.gen++;
+    sl.used = true;
+    return s;
+}
+
+lt_status mark_slot_use(lt_kv* kv, int s, cudaStream_t st) {
+    LT_CUDA(kv, cudaEventRecord(kv->slots[s].ev, st));
+    return LT_OK;
+}
+
+// Upload `bytes` of `src` through the staging ring, reusing the previous
+// upload of the same contents while its slot has not been recycled.
+lt_status upload(lt_kv* kv, UploadCache& cache, const void* src, size_t bytes, cudaStream_t st, const void** dptr,
+                 int* slot_out) {
+    if (bytes > kv->slot_bytes) return fail(kv, LT_E_ARG, "upload of %zu bytes exceeds staging slot", bytes);
+    if (cache.slot >= 0 && kv->slots[cache.slot].gen == cache.gen && cache.key.size() == bytes &&
+        std::memcmp(cache.key.data(), src, bytes) == 0) {
+        *dptr = kv->slots[cache.slot].dev;
+        *slot_out = cache.slot;
+        return LT_OK;
+    }
+    const int s = acquire_slot(kv);
+    std::memcpy(kv->slots[s].host, src, bytes);
+    LT_CUDA(kv, cudaMemcpyAsync(kv->slots[s].dev, kv->slots[s].host, bytes, cudaMemcpyHostToDevice, st));
+    cache.key.assign(static_cast<const char*>(src), static_cast<const char*>(src) + bytes);
+    cache.slot = s;
+    cache.gen = kv->slots[s].gen;
+    *dptr = kv->slots[s].dev;
+    *slot_out = s;
+    return LT_OK;
+}
+
+// Launch kv_apply_plan for `copies` and table writes `tw`, split to fit the
+// staging slots.  All copies in one call are independent of each other.
+lt_status run_plan(lt_kv* kv, const std::vector<int2>& copies, const std::vector<int2>& tw, cudaStream_t st) {
+    const size_t cap = kv->slot_bytes / sizeof(int2);
+    size_t ci = 0, ti = 0;
+    while (ci < copies.size() || ti < tw.size()) {
+        const size_t nc = std::min(copies.size() - ci, cap);
+        const size_t nt = std::min(tw.size() - ti, cap - nc);
+        const int s = acquire_slot(kv);
+        int2* h = static_cast<int2*>(kv->slots[s].host);
+        if (nc) std::memcpy(h, copies.data() + ci, nc * sizeof(int2));
+        if (nt) std::memcpy(h + nc, tw.data() + ti, nt * sizeof(int2));
+        LT_CUDA(kv, cudaMemcpyAsync(kv->slots[s].dev, h, (nc + nt) * sizeof(int2), cudaMemcpyHostToDevice, st));
+        const int2* d = static_cast<const int2*>(kv->slots[s].dev);
+        LT_CUDA(kv, ltkv::launch_apply_plan(kv->d_pool, kv->layer_elems, kv->block_elems, (int)kv->cfg.n_layers, d,
+                                            (int)nc, kv->d_tables, d + nc, (int)nt, st));
+        kv->launches++;
+        lt_status rc = mark_slot_use(kv, s, st);
+        if (rc) return rc;
+        ci += nc;
+        ti += nt;
+    }
+    return LT_OK;
+}
+
+lt_status flush(lt_kv* kv, cudaStream_t st) {
+    if (!kv->dev) {
+        kv->pend_copies.clear();
+        for (uint32_t s : kv->dirty_list) kv->dirty_from[s] = kClean;
+        kv->dirty_list.clear();
+        return LT_OK;
+    }
+    if (kv->pend_copies.empty() && kv->dirty_list.empty()) return LT_OK;
+    kv->tw_tmp.clear();
+    for (uint32_t s : kv->dirty_list) {
+        const auto& bl = kv->blocks[s];
+        const size_t row = (size_t)s * kv->max_blocks;
+        for (size_t i = kv->dirty_from[s]; i < bl.size(); ++i) {
+            if (kv->dev_shadow[row + i] == bl[i]) continue;  // device already holds it
+            kv->dev_shadow[row + i] = bl[i];
+            kv->tw_tmp.push_back(make_int2((int)(row + i), bl[i]));
+        }
+        kv->dirty_from[s] = kClean;
+    }
+    kv->dirty_list.clear();
+    lt_status rc = run_plan(kv, kv->pend_copies, kv->tw_tmp, st);
+    kv->pend_copies.clear();
+    kv->epoch++;
+    return rc;
+}
+
+void mark_dirty(lt_kv* kv, uint32_t seq, uint32_t idx) {
+    if (!kv->dev) return;
+    if (kv->dirty_from[seq] == kClean) {
+        kv->dirty_list.push_back(seq);
+        kv->dirty_from[seq] = idx;
+    } else if (idx < kv->dirty_from[seq]) {
+        kv->dirty_from[seq] = idx;
+    }
+}
+
+void release_block(lt_kv* kv, int32_t b) {  // kv.rs:76-82
+    kv->refs[b] -= 1;
+    if (kv->refs[b] == 0) kv->free_list.push_back(b);
+}
+
+// KvCache::append for one token (kv.rs:85-121).
+lt_status append_one(lt_kv* kv, uint32_t seq, uint32_t pos, int32_t* block_out, int32_t* slot_out,
+                     cudaStream_t st) {
+    if (seq >= kv->cfg.max_seqs) return fail(kv, LT_E_ARG, "seq %u out of range (max_seqs %u)", seq, kv->cfg.max_seqs);
+    auto& bl = kv->blocks[seq];
+    const uint32_t len = kv->lens[seq];
+    if (pos != len) return fail(kv, LT_E_NONCONTIG, "seq %u: position %u is not contiguous (length %u)", seq, pos, len);
+    const uint32_t slot = pos % kBlock;
+    if (slot == 0) {
+        if (bl.size() >= kv->max_blocks)
+            return fail(kv, LT_E_ARG, "seq %u exceeds max_blocks_per_seq (%u)", seq, kv->max_blocks);
+        if (kv->free_list.empty()) return fail(kv, LT_E_FULL, "KV cache full");
+        const int32_t b = kv->free_list.back();  // kv.rs:67-74
+        kv->free_list.pop_back();
+        kv->refs[b] = 1;
+        bl.push_back(b);
+        mark_dirty(kv, seq, (uint32_t)bl.size() - 1);
+    } else {
+        const int32_t last = bl.back();
+        if (kv->refs[last] > 1) {  // copy-on-write, kv.rs:99-110
+            if (kv->free_list.empty()) return fail(kv, LT_E_FULL, "KV cache full");
+            const int32_t nb = kv->free_list.back();
+            if (kv->dev) {
+                // A queued copy that reads `nb` or writes `last`/`nb` must land first.
+                if (kv->mark_dst[last] == kv->epoch || kv->mark_dst[nb] == kv->epoch || kv->mark_src[nb] == kv->epoch) {
+                    lt_status rc = flush(kv, st);
+                    if (rc) return rc;
+                }
+                kv->pend_copies.push_back(make_int2(last, nb));
+                kv->mark_src[last] = kv->epoch;
+                kv->mark_dst[nb] = kv->epoch;
+            }
+            kv->free_list.pop_back();
+            kv->refs[nb] = 1;
+            release_block(kv, last);
+            bl.back() = nb;
+            mark_dirty(kv, seq, (uint32_t)bl.size() - 1);
+        }
+    }
+    kv->lens[seq] = pos + 1;
+    *block_out = bl.back();
+    *slot_out = (int32_t)slot;
+    return LT_OK;
+}
+
+void truncate_impl(lt_kv* kv, uint32_t seq, uint32_t from) {  // kv.rs:153-169
+    if (seq >= kv->cfg.max_seqs) return;
+    auto& bl = kv->blocks[seq];
+    if (from >= kv->lens[seq]) return;
+    const size_t keep = (from + kBlock - 1) / kBlock;
+    for (size_t i = keep; i < bl.size(); ++i) release_block(kv, bl[i]);  // ascending order
+    bl.resize(keep);
+    kv->lens[seq] = from;
+}
+
+lt_status require_device(lt_kv* kv) {
+    if (!kv->dev) return fail(kv, LT_E_ARG, "handle was created without a device (device = -1)");
+    return LT_OK;
+}
+
+int pick_cb(lt_kv* kv, uint64_t total_blocks) {
+    if (kv->cb_override > 0) return kv->cb_override;
+    (void)total_blocks;
+    return 32;
+}
+
+// Build attention work items for n tokens; returns the number of partial
+// slots used through *parts.
+lt_status build_items(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n, bool fused) {
+    uint64_t total_blocks = 0;
+    for (uint32_t i = 0; i < n; ++i) total_blocks += (pos[i] + kBlock) / kBlock;
+    int cb = pick_cb(kv, total_blocks);
+    for (;;) {
+        size_t parts = 0;
+        for (uint32_t i = 0; i < n; ++i) {
+            const uint32_t nb = (pos[i] + kBlock) / kBlock;
+            const uint32_t nc = (nb + cb - 1) / cb;
+            if (nc > 1) parts += nc;
+        }
+        if (parts <= kv->ws_slots) break;
+        cb *= 2;
+    }
+    kv->items_tmp.clear();
+    int32_t part_base = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t nb = (pos[i] + kBlock) / kBlock;
+        const int32_t nc = (int32_t)((nb + cb - 1) / cb);
+        for (int32_t c = 0; c < nc; ++c) {
+            ltkv::WorkItem w;
+            w.tok = (int32_t)i;
+            w.seq = (int32_t)seq[i];
+            w.pos = (int32_t)pos[i];
+            w.chunk = c;
+            w.nchunks = nc;
+            w.part_base = nc > 1 ? part_base : 0;
+            w.cb = cb;
+            w.write_row = (fused && c == nc - 1) ? 1 : 0;
+            kv->items_tmp.push_back(w);
+        }
+        if (nc > 1) part_base += nc;
+    }
+    return LT_OK;
+}
+
+lt_status check_tokens(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n) {
+    if (n > kv->cfg.max_batch) return fail(kv, LT_E_ARG, "batch of %u tokens exceeds max_batch %u", n, kv->cfg.max_batch);
+    for (uint32_t i = 0; i < n; ++i) {
+        if (seq[i] >= kv->cfg.max_seqs) return fail(kv, LT_E_ARG, "seq %u out of range", seq[i]);
+        if (pos[i] >= kv->lens[seq[i]])
+            return fail(kv, LT_E_ARG, "seq %u: position %u not in the cache (length %u)", seq[i], pos[i],
+                        kv->lens[seq[i]]);
+    }
+    return LT_OK;
+}
+
+lt_status check_cells(lt_kv* kv, const int32_t* block, const int32_t* slot, uint32_t n) {
+    if (n > kv->cfg.max_batch) return fail(kv, LT_E_ARG, "batch of %u tokens exceeds max_batch %u", n, kv->cfg.max_batch);
+    for (uint32_t i = 0; i < n; ++i) {
+        if (block[i] < 0 || (uint32_t)block[i] >= kv->n_blocks || slot[i] < 0 || slot[i] >= kBlock)
+            return fail(kv, LT_E_ARG, "cell %u (block %d, slot %d) out of range", i, block[i], slot[i]);
+    }
+    return LT_OK;
+}
+
+constexpr size_t kProfPairs = 512;
+
+// Fold the oldest `n` recorded (start, end) pairs into the totals.
+lt_status prof_drain(lt_kv* kv, size_t n) {
+    while (n-- && kv->prof_pending) {
+        const size_t tail = (kv->prof_head + kProfPairs - kv->prof_pending) % kProfPairs;
+        float ms = 0.f;
+        LT_CUDA(kv, cudaEventSynchronize(kv->prof_ev[2 * tail + 1]));
+        LT_CUDA(kv, cudaEventElapsedTime(&ms, kv->prof_ev[2 * tail], kv->prof_ev[2 * tail + 1]));
+        kv->prof_ms += ms;
+        kv->prof_count++;
+        kv->prof_pending--;
+    }
+    return LT_OK;
+}
+
+// Record the start event of the next attention launch; *end gets its end event.
+lt_status prof_begin(lt_kv* kv, cudaStream_t st, cudaEvent_t* end) {
+    if (kv->prof_pending == kProfPairs) {
+        lt_status rc = prof_drain(kv, 1);
+        if (rc) return rc;
+    }
+    const size_t i = kv->prof_head;
+    kv->prof_head = (kv->prof_head + 1) % kProfPairs;
+    kv->prof_pending++;
+    LT_CUDA(kv, cudaEventRecord(kv->prof_ev[2 * i], st));
+    *end = kv->prof_ev[2 * i + 1];
+    return LT_OK;
+}
+
+lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype, const uint32_t* seq,
+                      const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale, const void* k,
+                      const void* v, lt_dtype kv_dtype, bool fused, cudaStream_t st) {
+    lt_status rc = flush(kv, st);
+    if (rc) return rc;
+    if (n == 0) return LT_OK;
+    build_items(kv, seq, pos, n, fused);
+    const void* d_items = nullptr;
+    int s_items = -1;
+    rc = upload(kv, kv->items_cache, kv->items_tmp.data(), kv->items_tmp.size() * sizeof(ltkv::WorkItem), st,
+                &d_items, &s_items);
+    if (rc) return rc;
+    ltkv::AttnParams p{};
+    p.pool_layer = kv->d_pool + (size_t)layer * kv->layer_elems;
+    p.pool_layer_w = kv->d_pool + (size_t)layer * kv->layer_elems;
+    p.tables = kv->d_tables;
+    p.max_blocks = (int32_t)kv->max_blocks;
+    p.items = static_cast<const ltkv::WorkItem*>(d_items);
+    p.n_items = (int32_t)kv->items_tmp.size();
+    p.n_kv_heads = (int32_t)kv->cfg.n_kv_heads;
+    p.group = (int32_t)kv->group;
+    p.q = q;
+    p.q_f32 = q_dtype == LT_F32;
+    p.out = out;
+    p.out_f32 = out_dtype == LT_F32;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.part_o = kv->d_part_o;
+    p.part_ml = kv->d_part_ml;
+    p.counters = kv->d_counters;
+    p.err = kv->d_err;
+    p.k_new = k;
+    p.v_new = v;
+    p.kv_f32 = kv_dtype == LT_F32;
+    cudaEvent_t ev_end = nullptr;
+    if (kv->profiling) {
+        lt_status prc = prof_begin(kv, st, &ev_end);
+        if (prc) return prc;
+    }
+    LT_CUDA(kv, ltkv::launch_attend(p, (int)kv->cfg.head_dim, st));
+    kv->launches++;
+    if (ev_end) LT_CUDA(kv, cudaEventRecord(ev_end, st));
+    return mark_slot_use(kv, s_items, st);
+}
+
+}  // namespace
+
+// ============================================================== C ABI ====
+
+extern "C" {
+
+lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
+    if (!cfg || !out) return LT_E_ARG;
+    *out = nullptr;
+    const lt_kv_config c = *cfg;
+    if (c.n_layers == 0 || c.n_kv_heads == 0 || c.n_heads == 0 || c.max_seqs == 0 || c.max_batch == 0)
+        return LT_E_ARG;
+    if (c.n_heads % c.n_kv_heads != 0) return LT_E_ARG;
+    if (c.head_dim != 64 && c.head_dim != 128) return LT_E_UNSUPPORTED;
+    if (c.n_heads / c.n_kv_heads > (uint32_t)ltkv::kMaxGroup) return LT_E_UNSUPPORTED;
+    lt_kv* kv = new (std::nothrow) lt_kv();
+    if (!kv) return LT_E_ARG;
+    kv->cfg = c;
+    kv->n_blocks = (c.n_tokens + kBlock - 1) / kBlock;  // kv.rs:36
+    kv->kv_dim = c.n_kv_heads * c.head_dim;
+    kv->group = c.n_heads / c.n_kv_heads;
+    kv->max_blocks = c.max_blocks_per_seq ? std::min(c.max_blocks_per_seq, kv->n_blocks) : kv->n_blocks;
+    if (kv->max_blocks == 0) kv->max_blocks = 1;
+    if ((uint64_t)c.max_seqs * kv->max_blocks > 0x7FFFFFFFull) {
+        delete kv;
+        return LT_E_ARG;
+    }
+    kv->block_elems = (size_t)c.n_kv_heads * 2 * kBlock * c.head_dim;
+    kv->layer_elems = (size_t)kv->n_blocks * kv->block_elems;
+    kv->blocks.resize(c.max_seqs);
+    kv->lens.assign(c.max_seqs, 0);
+    kv->refs.assign(kv->n_blocks, 0);
+    kv->free_list.resize(kv->n_blocks);
+    for (uint32_t i = 0; i < kv->n_blocks; ++i) kv->free_list[i] = (int32_t)(kv->n_blocks - 1 - i);  // kv.rs:45
+    kv->dirty_from.assign(c.max_seqs, kClean);
+    if (const char* e = getenv("LT_KV_CHUNK_BLOCKS")) kv->cb_override = atoi(e);
+
+    if (c.device >= 0) {
+        kv->dev = true;
+        kv->mark_src.assign(kv->n_blocks, 0);
+        kv->mark_dst.assign(kv->n_blocks, 0);
+        kv->dev_shadow.assign((size_t)c.max_seqs * kv->max_blocks, 0);  // tables are zeroed below
+        DeviceGuard g(c.device);
+        lt_status rc = LT_OK;
+        auto ck = [&](cudaError_t e, const char* what) {
+            if (e != cudaSuccess && rc == LT_OK) rc = fail(kv, LT_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+        };
+        if (!g.ok) ck(cudaErrorInvalidDevice, "cudaSetDevice");
+        const size_t pool_bytes = (size_t)c.n_layers * kv->layer_elems * 2;
+        kv->ws_slots = std::max<size_t>(2048, 4 * (size_t)c.max_batch);
+        const size_t gd = (size_t)kv->group * c.head_dim;
+        if (rc == LT_OK) ck(cudaMalloc(&kv->d_pool, std::max<size_t>(pool_bytes, 16)), "cudaMalloc(pool)");
+        if (rc == LT_OK) ck(cudaMemset(kv->d_pool, 0, std::max<size_t>(pool_bytes, 16)), "cudaMemset(pool)");
+        const size_t tbytes = (size_t)c.max_seqs * kv->max_blocks * 4;
+        if (rc == LT_OK) ck(cudaMalloc(&kv->d_tables, tbytes), "cudaMalloc(tables)");
+        if (rc == LT_OK) ck(cudaMemset(kv->d_tables, 0, tbytes), "cudaMemset(tables)");
+        if (rc == LT_OK)
+            ck(cudaMalloc(&kv->d_part_o, kv->ws_slots * c.n_kv_heads * gd * sizeof(float)), "cudaMalloc(partials)");
+        if (rc == LT_OK)
+            ck(cudaMalloc(&kv->d_part_ml, kv->ws_slots * c.n_kv_heads * kv->group * 2 * sizeof(float)),
+               "cudaMalloc(partials)");
+        const size_t cbytes = (size_t)c.max_batch * c.n_kv_heads * 4;
+        if (rc == LT_OK) ck(cudaMalloc(&kv->d_counters, cbytes), "cudaMalloc(counters)");
+        if (rc == LT_OK) ck(cudaMemset(kv->d_counters, 0, cbytes), "cudaMemset(counters)");
+        if (rc == LT_OK) ck(cudaMalloc(&kv->d_err, sizeof(int32_t)), "cudaMalloc(err)");
+        if (rc == LT_OK) ck(cudaMemset(kv->d_err, 0, sizeof(int32_t)), "cudaMemset(err)");
+        kv->slot_bytes = std::max<size_t>(1u << 20, sizeof(ltkv::WorkItem) * ((size_t)c.max_batch + kv->ws_slots) + 64);
+        for (auto& s : kv->slots) {
+            if (rc != LT_OK) break;
+            ck(cudaHostAlloc(&s.host, kv->slot_bytes, cudaHostAllocDefault), "cudaHostAlloc(staging)");
+            if (rc == LT_OK) ck(cudaMalloc(&s.dev, kv->slot_bytes), "cudaMalloc(staging)");
+            if (rc == LT_OK) ck(cudaEventCreateWithFlags(&s.ev, cudaEventDisableTiming), "cudaEventCreate");
+        }
+        if (rc == LT_OK) ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        if (rc != LT_OK) {
+            free_device(kv);
+            delete kv;
+            return rc;
+        }
+    }
+    *out = kv;
+    return LT_OK;
+}
+
+void lt_kv_destroy(lt_kv* kv) {
+    if (!kv) return;
+    if (kv->dev) {
+        DeviceGuard g(kv->cfg.device);
+        cudaDeviceSynchronize();
+        free_device(kv);
+    }
+    delete kv;
+}
+
+const char* lt_kv_last_error(const lt_kv* kv) { return kv ? kv->err.c_str() : "null handle"; }
+
+uint32_t lt_kv_capacity(const lt_kv* kv) { return kv->n_blocks * kBlock; }
+
+uint64_t lt_kv_bytes(const lt_kv* kv) { return (uint64_t)kv->cfg.n_layers * kv->layer_elems * 2; }
+
+uint32_t lt_kv_len(const lt_kv* kv, uint32_t seq) { return seq < kv->cfg.max_seqs ? kv->lens[seq] : 0; }
+
+uint32_t lt_kv_free_blocks(const lt_kv* kv) { return (uint32_t)kv->free_list.size(); }
+
+uint32_t lt_kv_n_blocks(const lt_kv* kv) { return kv->n_blocks; }
+
+lt_status lt_kv_append(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n, int32_t* block_out,
+                       int32_t* slot_out, uint32_t* n_done, void* stream) {
+    if (!kv) return LT_E_ARG;
+    DeviceGuard g(kv->dev ? kv->cfg.device : -1);
+    uint32_t i = 0;
+    lt_status rc = LT_OK;
+    for (; i < n; ++i) {
+        rc = append_one(kv, seq[i], pos[i], &block_out[i], &slot_out[i], static_cast<cudaStream_t>(stream));
+        if (rc) break;
+    }
+    if (n_done) *n_done = i;
+    return rc;
+}
+
+lt_status lt_kv_write(lt_kv* kv, uint32_t layer, const int32_t* block, const int32_t* slot, uint32_t n,
+                      const void* k, const void* v, lt_dtype dtype, void* stream) {
+    if (!kv) return LT_E_ARG;
+    lt_status rc = require_device(kv);
+    if (rc) return rc;
+    if (layer >= kv->cfg.n_layers) return fail(kv, LT_E_ARG, "layer %u out of range", layer);
+    if ((rc = check_cells(kv, block, slot, n))) return rc;
+    DeviceGuard g(kv->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = flush(kv, st))) return rc;
+    if (n == 0) return LT_OK;
+    kv->cells_tmp.resize(n);
+    for (uint32_t i = 0; i < n; ++i) kv->cells_tmp[i] = make_int2(block[i], slot[i]);
+    const void* d_cells = nullptr;
+    int s = -1;
+    if ((rc = upload(kv, kv->cells_cache, kv->cells_tmp.data(), n * sizeof(int2), st, &d_cells, &s))) return rc;
+    LT_CUDA(kv, ltkv::launch_write(kv->d_pool + (size_t)layer * kv->layer_elems, static_cast<const int2*>(d_cells),
+                                   (int)n, (int)kv->cfg.n_kv_heads, (int)kv->cfg.head_dim, k, v, dtype == LT_F32, st));
+    kv->launches++;
+    return mark_slot_use(kv, s, st);
+}
+
+lt_status lt_kv_attend(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype, const uint32_t* seq,
+                       const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale, void* stream) {
+    if (!kv) return LT_E_ARG;
+    lt_status rc = require_device(kv);
+    if (rc) return rc;
+    if (layer >= kv->cfg.n_layers) return fail(kv, LT_E_ARG, "layer %u out of range", layer);
+    if ((rc = check_tokens(kv, seq, pos, n))) return rc;
+    DeviceGuard g(kv->cfg.device);
+    return attend_impl(kv, layer, q, q_dtype, seq, pos, n, out, out_dtype, scale, nullptr, nullptr, LT_F32, false,
+                       static_cast<cudaStream_t>(stream));
+}
+
+lt_status lt_kv_write_attend(lt_kv* kv, uint32_t layer, const int32_t* block, const int32_t* slot, const void* k,
+                             const void* v, lt_dtype kv_dtype, const void* q, lt_dtype q_dtype, const uint32_t* seq,
+                             const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale,
+                             void* stream) {
+    if (!kv) return LT_E_ARG;
+    lt_status rc = require_device(kv);
+    if (rc) return rc;
+    if (layer >= kv->cfg.n_layers) return fail(kv, LT_E_ARG, "layer %u out of range", layer);
+    if ((rc = check_tokens(kv, seq, pos, n))) return rc;
+    if ((rc = check_cells(kv, block, slot, n))) return rc;
+    // One kernel is only equivalent to write-then-attend when every token's
+    // new row is the only new row its attention reads: one token per
+    // sequence, written to its own sequence's last cell, in a block no other
+    // sequence references.
+    bool fusable = true;
+    for (uint32_t i = 0; i < n && fusable; ++i) {
+        const auto& bl = kv->blocks[seq[i]];
+        if (pos[i] + 1 != kv->lens[seq[i]] || bl[pos[i] / kBlock] != block[i] ||
+            (int32_t)(pos[i] % kBlock) != slot[i] || kv->refs[block[i]] != 1)
+            fusable = false;
+    }
+    if (fusable && n > 1) {
+        std::vector<uint32_t> sorted(seq, seq + n);
+        std::sort(sorted.begin(), sorted.end());
+        fusable = std::adjacent_find(sorted.begin(), sorted.end()) == sorted.end();
+    }
+    if (!fusable) {
+        if ((rc = lt_kv_write(kv, layer, block, slot, n, k, v, kv_dtype, stream))) return rc;
+        return lt_kv_attend(kv, layer, q, q_dtype, seq, pos, n, out, out_dtype, scale, stream);
+    }
+    DeviceGuard g(kv->cfg.device);
+    return attend_impl(kv, layer, q, q_dtype, seq, pos, n, out, out_dtype, scale, k, v, kv_dtype, true,
+                       static_cast<cudaStream_t>(stream));
+}
+
+void lt_kv_truncate(lt_kv* kv, uint32_t seq, uint32_t from) {
+    if (kv) truncate_impl(kv, seq, from);
+}
+
+void lt_kv_share(lt_kv* kv, uint32_t src, uint32_t dst, uint32_t len) {  // kv.rs:172-183
+    if (!kv) return;
+    truncate_impl(kv, dst, 0);
+    if (src >= kv->cfg.max_seqs || dst >= kv->cfg.max_seqs) return;
+    const uint32_t slen = kv->lens[src];
+    if (slen == 0) return;  // unknown source (share(x, x, _) lands here as well)
+    len = std::min(len, slen);
+    const size_t nb = (len + kBlock - 1) / kBlock;
+    for (size_t i = 0; i < nb; ++i) kv->refs[kv->blocks[src][i]] += 1;
+    if (len > 0) {
+        kv->blocks[dst].assign(kv->blocks[src].begin(), kv->blocks[src].begin() + nb);
+        kv->lens[dst] = len;
+        mark_dirty(kv, dst, 0);
+    }
+}
+
+lt_status lt_kv_compact(lt_kv* kv, uint32_t* n_moved, void* stream) {
+    if (!kv) return LT_E_ARG;
+    DeviceGuard g(kv->dev ? kv->cfg.device : -1);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    lt_status rc = flush(kv, st);
+    if (rc) return rc;
+    const uint32_t nb = kv->n_blocks;
+    std::vector<int32_t> fr, lv, remap(nb);
+    for (uint32_t b = 0; b < nb; ++b) {
+        remap[b] = (int32_t)b;
+        if (kv->refs[b] == 0) fr.push_back((int32_t)b);
+    }
+    for (uint32_t b = nb; b-- > 0;)
+        if (kv->refs[b] != 0) lv.push_back((int32_t)b);
+    std::vector<int2> moves;
+    for (size_t j = 0; j < fr.size() && j < lv.size() && fr[j] < lv[j]; ++j) {
+        const int32_t src = lv[j], dst = fr[j];
+        moves.push_back(make_int2(src, dst));
+        kv->refs[dst] = kv->refs[src];
+        kv->refs[src] = 0;
+        remap[src] = dst;
+    }
+    std::vector<int2> tw;
+    if (!moves.empty()) {
+        for (uint32_t s = 0; s < kv->cfg.max_seqs; ++s) {
+            auto& bl = kv->blocks[s];
+            for (size_t i = 0; i < bl.size(); ++i) {
+                const int32_t nbk = remap[bl[i]];
+                if (nbk != bl[i]) {
+                    bl[i] = nbk;
+                    const size_t idx = (size_t)s * kv->max_blocks + i;
+                    if (kv->dev && kv->dev_shadow[idx] != nbk) {
+                        kv->dev_shadow[idx] = nbk;
+                        tw.push_back(make_int2((int)idx, nbk));
+                    }
+                }
+            }
+        }
+    }
+    kv->free_list.clear();
+    for (uint32_t b = nb; b-- > 0;)
+        if (kv->refs[b] == 0) kv->free_list.push_back((int32_t)b);
+    if (n_moved) *n_moved = (uint32_t)moves.size();
+    if (kv->dev && (!moves.empty() || !tw.empty())) {
+        rc = run_plan(kv, moves, tw, st);
+        kv->epoch++;
+    }
+    return rc;
+}
+
+lt_status lt_kv_flush(lt_kv* kv, void* stream) {
+    if (!kv) return LT_E_ARG;
+    DeviceGuard g(kv->dev ? kv->cfg.device : -1);
+    return flush(kv, static_cast<cudaStream_t>(stream));
+}
+
+lt_status lt_kv_rows(lt_kv* kv, uint32_t layer, uint32_t seq, uint32_t n, void* k_out, void* v_out, void* stream) {
+    if (!kv) return LT_E_ARG;
+    lt_status rc = require_device(kv);
+    if (rc) return rc;
+    if (layer >= kv->cfg.n_layers || seq >= kv->cfg.max_seqs || n > kv->lens[seq])
+        return fail(kv, LT_E_ARG, "rows(layer %u, seq %u, n %u) out of range", layer, seq, n);
+    DeviceGuard g(kv->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = flush(kv, st))) return rc;
+    LT_CUDA(kv, ltkv::launch_rows(kv->d_pool + (size_t)layer * kv->layer_elems,
+                                  kv->d_tables + (size_t)seq * kv->max_blocks, (int)n, (int)kv->cfg.n_kv_heads,
+                                  (int)kv->cfg.head_dim, static_cast<uint16_t*>(k_out), static_cast<uint16_t*>(v_out),
+                                  st));
+    kv->launches++;
+    return LT_OK;
+}
+
+lt_status lt_kv_check(lt_kv* kv, void* stream) {
+    if (!kv) return LT_E_ARG;
+    if (!kv->dev) return LT_OK;
+    DeviceGuard g(kv->cfg.device);
+    LT_CUDA(kv, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    int32_t flag = 0;
+    LT_CUDA(kv, cudaMemcpy(&flag, kv->d_err, sizeof flag, cudaMemcpyDeviceToHost));
+    if (flag) {
+        // A timed-out work item leaves its (token, head) counter behind.
+        LT_CUDA(kv, cudaMemset(kv->d_err, 0, sizeof(int32_t)));
+        LT_CUDA(kv, cudaMemset(kv->d_counters, 0, (size_t)kv->cfg.max_batch * kv->cfg.n_kv_heads * 4));
+        LT_CUDA(kv, cudaDeviceSynchronize());
+        return fail(kv, LT_E_TIMEOUT, "a bounded device wait timed out; the affected outputs are invalid");
+    }
+    return LT_OK;
+}
+
+uint32_t lt_kv_seq_blocks(const lt_kv* kv, uint32_t seq, int32_t* out, uint32_t cap) {
+    if (!kv || seq >= kv->cfg.max_seqs) return 0;
+    const auto& bl = kv->blocks[seq];
+    for (size_t i = 0; i < bl.size() && i < cap; ++i) out[i] = bl[i];
+    return (uint32_t)bl.size();
+}
+
+uint32_t lt_kv_refs(const lt_kv* kv, uint32_t* out, uint32_t cap) {
+    for (uint32_t b = 0; b < kv->n_blocks && b < cap; ++b) out[b] = kv->refs[b];
+    return kv->n_blocks;
+}
+
+uint32_t lt_kv_free_list(const lt_kv* kv, int32_t* out, uint32_t cap) {
+    for (size_t i = 0; i < kv->free_list.size() && i < cap; ++i) out[i] = kv->free_list[i];
+    return (uint32_t)kv->free_list.size();
+}
+
+void* lt_kv_device_pool(const lt_kv* kv) { return kv ? kv->d_pool : nullptr; }
+
+const int32_t* lt_kv_device_tables(const lt_kv* kv, uint32_t* max_blocks_per_seq) {
+    if (!kv) return nullptr;
+    if (max_blocks_per_seq) *max_blocks_per_seq = kv->max_blocks;
+    return kv->d_tables;
+}
+
+lt_status lt_kv_read_pool(lt_kv* kv, uint32_t layer, uint32_t block0, uint32_t count, void* out) {
+    if (!kv) return LT_E_ARG;
+    lt_status rc = require_device(kv);
+    if (rc) return rc;
+    if (layer >= kv->cfg.n_layers || block0 > kv->n_blocks || count > kv->n_blocks - block0)
+        return fail(kv, LT_E_ARG, "read_pool(layer %u, blocks %u+%u) out of range", layer, block0, count);
+    DeviceGuard g(kv->cfg.device);
+    LT_CUDA(kv, cudaDeviceSynchronize());
+    LT_CUDA(kv, cudaMemcpy(out, kv->d_pool + (size_t)layer * kv->layer_elems + (size_t)block0 * kv->block_elems,
+                           (size_t)count * kv->block_elems * 2, cudaMemcpyDeviceToHost));
+    return LT_OK;
+}
+
+lt_status lt_kv_profile(lt_kv* kv, int enable) {
+    if (!kv) return LT_E_ARG;
+    lt_status rc = require_device(kv);
+    if (rc) return rc;
+    DeviceGuard g(kv->cfg.device);
+    if (kv->prof_ev.empty()) {
+        kv->prof_ev.resize(2 * kProfPairs);
+        for (auto& e : kv->prof_ev) LT_CUDA(kv, cudaEventCreate(&e));
+    }
+    if ((rc = prof_drain(kv, kProfPairs))) return rc;
+    kv->profiling = enable != 0;
+    kv->prof_ms = 0.0;
+    kv->prof_count = 0;
+    return LT_OK;
+}
+
+lt_status lt_kv_profile_read(lt_kv* kv, double* total_ms, uint64_t* launches) {
+    if (!kv) return LT_E_ARG;
+    DeviceGuard g(kv->dev ? kv->cfg.device : -1);
+    lt_status rc = prof_drain(kv, kProfPairs);
+    if (rc) return rc;
+    if (total_ms) *total_ms = kv->prof_ms;
+    if (launches) *launches = kv->prof_count;
+    return LT_OK;
+}
+
+uint64_t lt_kv_launch_count(const lt_kv* kv) { return kv ? kv->launches : 0; }
+
+}  // extern "C"

@@ -1,0 +1,285 @@
+"""Python host mirror of the reference's paged KV cache over the C ABI.
+
+`KvCache` keeps the method names, argument meaning and error behaviour of
+the reference's `KvCache` (engine/crates/native/src/kv.rs:15-188) and of the
+attention closure of `Model::forward` (engine/crates/native/src/model.rs:
+431-476), batched the way `Model::forward` drives them.  Every call goes
+through liblt_kv.so; device arrays are torch CUDA tensors, host arrays are
+numpy.  Nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import numpy as np
+
+from . import _native as N
+
+BLOCK = N.BLOCK
+
+
+class KvError(RuntimeError):
+    """A failed C-ABI call; `code` is the lt_status value."""
+
+    def __init__(self, code: int, message: str, n_done: int | None = None):
+        super().__init__(message)
+        self.code = code
+        self.n_done = n_done
+
+
+class KvCacheFull(KvError):
+    pass
+
+
+class KvNonContiguous(KvError):
+    pass
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def _dptr(t) -> C.c_void_p:
+    return C.c_void_p(t.data_ptr())
+
+
+def _stream(stream) -> C.c_void_p:
+    if stream is None:
+        import torch
+
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(getattr(stream, "cuda_stream", stream))
+
+
+def _dtype_code(t) -> int:
+    import torch
+
+    if t.dtype == torch.float32:
+        return N.LT_F32
+    if t.dtype == torch.float16:
+        return N.LT_F16
+    raise TypeError(f"unsupported dtype {t.dtype} (float32 or float16)")
+
+
+def _u32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int64).astype(np.uint32))
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+
+class KvCache:
+    """Paged f16 KV cache of 16-token blocks on one CUDA device.
+
+    ``KvCache(n_layers, n_kv_heads, head_dim, n_tokens)`` is the reference's
+    ``KvCache::new(n_layers, n_kv_heads * head_dim, n_tokens)``.  ``device=-1``
+    builds a bookkeeping-only handle (no GPU), for host-side tests.
+    """
+
+    def __init__(self, n_layers: int, n_kv_heads: int, head_dim: int, n_tokens: int, *, n_heads: int | None = None,
+                 max_seqs: int = 256, max_batch: int = 512, max_blocks_per_seq: int = 0, device: int = 0):
+        self._lib = N.lib()
+        cfg = N.lt_kv_config(
+            n_layers=n_layers, n_kv_heads=n_kv_heads, head_dim=head_dim,
+            n_heads=n_heads if n_heads is not None else n_kv_heads, n_tokens=n_tokens, max_seqs=max_seqs,
+            max_batch=max_batch, max_blocks_per_seq=max_blocks_per_seq, device=device)
+        h = C.c_void_p()
+        rc = self._lib.lt_kv_create(C.byref(cfg), C.byref(h))
+        if rc != N.LT_OK:
+            raise KvError(rc, f"lt_kv_create failed with status {rc}")
+        self._h = h
+        self.n_layers, self.n_kv_heads, self.head_dim = n_layers, n_kv_heads, head_dim
+        self.n_heads = cfg.n_heads
+        self.kv_dim = n_kv_heads * head_dim
+        self.max_seqs, self.max_batch, self.device = max_seqs, max_batch, device
+        self.n_blocks = self._lib.lt_kv_n_blocks(h)
+
+    def close(self):
+        h = getattr(self, "_h", None)
+        if h:
+            self._lib.lt_kv_destroy(h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---------------------------------------------------------------- errors
+    def _err(self, rc: int, n_done: int | None = None) -> KvError:
+        msg = self._lib.lt_kv_last_error(self._h).decode()
+        cls = {N.LT_E_FULL: KvCacheFull, N.LT_E_NONCONTIG: KvNonContiguous}.get(rc, KvError)
+        return cls(rc, msg, n_done)
+
+    def _check(self, rc: int):
+        if rc != N.LT_OK:
+            raise self._err(rc)
+
+    # ------------------------------------------------------------- accessors
+    def capacity(self) -> int:
+        """Tokens the pool holds (kv.rs:50; Backend::n_ctx)."""
+        return self._lib.lt_kv_capacity(self._h)
+
+    def bytes(self) -> int:
+        return self._lib.lt_kv_bytes(self._h)
+
+    def len(self, seq: int) -> int:
+        return self._lib.lt_kv_len(self._h, seq)
+
+    def free_blocks(self) -> int:
+        return self._lib.lt_kv_free_blocks(self._h)
+
+    # -------------------------------------------------------------- mutation
+    def append(self, seq: int, pos: int, stream=None):
+        """Claim the cell for `pos` of `seq` (kv.rs:85-121) -> (block, slot)."""
+        blocks, slots = self.append_batch([seq], [pos], stream=stream)
+        return int(blocks[0]), int(slots[0])
+
+    def append_batch(self, seqs, positions, stream=None):
+        """Claim cells for a batch in order (model.rs:380-383).  On error the
+        raised KvError carries `n_done`: the tokens claimed before it."""
+        seqs, positions = _u32(seqs), _u32(positions)
+        n = seqs.size
+        blocks = np.zeros(max(n, 1), np.int32)
+        slots = np.zeros(max(n, 1), np.int32)
+        done = C.c_uint32()
+        st = _stream(stream) if self.device >= 0 else C.c_void_p(0)
+        rc = self._lib.lt_kv_append(self._h, _ptr(seqs), _ptr(positions), n, _ptr(blocks), _ptr(slots),
+                                    C.byref(done), st)
+        if rc != N.LT_OK:
+            raise self._err(rc, done.value)
+        return blocks[:n], slots[:n]
+
+    def write(self, layer: int, blocks, slots, k, v, stream=None):
+        """KvCache::write for n cells (kv.rs:123-131): k, v CUDA [n, kv_dim]."""
+        blocks, slots = _i32(blocks), _i32(slots)
+        n = blocks.size
+        assert k.is_cuda and k.is_contiguous() and v.is_contiguous() and k.dtype == v.dtype
+        assert k.numel() == n * self.kv_dim and v.numel() == n * self.kv_dim
+        self._check(self._lib.lt_kv_write(self._h, layer, _ptr(blocks), _ptr(slots), n, _dptr(k), _dptr(v),
+                                          _dtype_code(k), _stream(stream)))
+
+    def attend(self, layer: int, q, seqs, positions, out=None, out_dtype=None, scale: float | None = None,
+               stream=None):
+        """Attention closure (model.rs:431-476): q CUDA [n, n_heads*head_dim]."""
+        import torch
+
+        seqs, positions = _u32(seqs), _u32(positions)
+        n = seqs.size
+        assert q.is_cuda and q.is_contiguous() and q.numel() == n * self.n_heads * self.head_dim
+        if out is None:
+            out = torch.empty((n, self.n_heads * self.head_dim), dtype=out_dtype or torch.float32, device=q.device)
+        if scale is None:
+            scale = float(np.float32(1.0) / np.float32(math.sqrt(self.head_dim)))
+        self._check(self._lib.lt_kv_attend(self._h, layer, _dptr(q), _dtype_code(q), _ptr(seqs), _ptr(positions), n,
+                                           _dptr(out), _dtype_code(out), scale, _stream(stream)))
+        return out
+
+    def write_attend(self, layer: int, blocks, slots, k, v, q, seqs, positions, out=None, out_dtype=None,
+                     scale: float | None = None, stream=None):
+        """write() then attend() for the same tokens, in one kernel when legal."""
+        import torch
+
+        blocks, slots = _i32(blocks), _i32(slots)
+        seqs, positions = _u32(seqs), _u32(positions)
+        n = seqs.size
+        if out is None:
+            out = torch.empty((n, self.n_heads * self.head_dim), dtype=out_dtype or torch.float32, device=q.device)
+        if scale is None:
+            scale = float(np.float32(1.0) / np.float32(math.sqrt(self.head_dim)))
+        self._check(self._lib.lt_kv_write_attend(
+            self._h, layer, _ptr(blocks), _ptr(slots), _dptr(k), _dptr(v), _dtype_code(k), _dptr(q), _dtype_code(q),
+            _ptr(seqs), _ptr(positions), n, _dptr(out), _dtype_code(out), scale, _stream(stream)))
+        return out
+
+    def truncate(self, seq: int, start: int):
+        """Drop positions start.. of seq (kv.rs:153-169; Backend::kv_remove)."""
+        self._lib.lt_kv_truncate(self._h, seq, start)
+
+    def share(self, src: int, dst: int, length: int):
+        """dst starts with the first `length` tokens of src (kv.rs:172-183)."""
+        self._lib.lt_kv_share(self._h, src, dst, length)
+
+    def compact(self, stream=None) -> int:
+        moved = C.c_uint32()
+        st = _stream(stream) if self.device >= 0 else C.c_void_p(0)
+        self._check(self._lib.lt_kv_compact(self._h, C.byref(moved), st))
+        return moved.value
+
+    def flush(self, stream=None):
+        st = _stream(stream) if self.device >= 0 else C.c_void_p(0)
+        self._check(self._lib.lt_kv_flush(self._h, st))
+
+    def check(self, stream=None):
+        st = _stream(stream) if self.device >= 0 else C.c_void_p(0)
+        self._check(self._lib.lt_kv_check(self._h, st))
+
+    def rows(self, layer: int, seq: int, n: int, stream=None):
+        """K and V rows 0..n of seq (kv.rs:135-150) as f16 CUDA [n, kv_dim]."""
+        import torch
+
+        k = torch.empty((n, self.kv_dim), dtype=torch.float16, device=f"cuda:{self.device}")
+        v = torch.empty_like(k)
+        self._check(self._lib.lt_kv_rows(self._h, layer, seq, n, _dptr(k), _dptr(v), _stream(stream)))
+        return k, v
+
+    # --------------------------------------------------------- introspection
+    def seq_blocks(self, seq: int) -> np.ndarray:
+        n = self._lib.lt_kv_seq_blocks(self._h, seq, None, 0)
+        out = np.zeros(max(n, 1), np.int32)
+        self._lib.lt_kv_seq_blocks(self._h, seq, _ptr(out), n)
+        return out[:n]
+
+    def refs(self) -> np.ndarray:
+        out = np.zeros(max(self.n_blocks, 1), np.uint32)
+        self._lib.lt_kv_refs(self._h, _ptr(out), self.n_blocks)
+        return out[: self.n_blocks]
+
+    def free_list(self) -> np.ndarray:
+        out = np.zeros(max(self.n_blocks, 1), np.int32)
+        n = self._lib.lt_kv_free_list(self._h, _ptr(out), self.n_blocks)
+        return out[:n]
+
+    def profile(self, enable: bool = True):
+        """Bracket every attention launch with CUDA events (resets totals)."""
+        self._check(self._lib.lt_kv_profile(self._h, int(enable)))
+
+    def profile_read(self):
+        """(total ms, launches) of the attention launches timed so far."""
+        ms, n = C.c_double(), C.c_uint64()
+        self._check(self._lib.lt_kv_profile_read(self._h, C.byref(ms), C.byref(n)))
+        return ms.value, n.value
+
+    def launch_count(self) -> int:
+        return self._lib.lt_kv_launch_count(self._h)
+
+    def read_pool(self, layer: int) -> np.ndarray:
+        """Raw device pool of one layer: uint16 [block][kv_head][2][16][head_dim]
+        with the chunk swizzle of include/lt_kv.h still applied."""
+        out = np.zeros((self.n_blocks, self.n_kv_heads, 2, BLOCK, self.head_dim), np.uint16)
+        self._check(self._lib.lt_kv_read_pool(self._h, layer, 0, self.n_blocks, _ptr(out)))
+        return out
+
+    def pool_reference_layout(self, layer: int):
+        """This layer's pool as the reference lays it out (kv.rs:20):
+        (K, V) uint16 [block][slot][kv_dim]."""
+        return unswizzle_pool(self.read_pool(layer))
+
+
+def unswizzle_pool(raw: np.ndarray):
+    """Invert the device pool layout: [block][head][2][16][D] with chunk c of
+    slot s stored at c ^ (s & 7) -> reference (K, V) [block][16][head*D]."""
+    nb, hkv, _, blk, d = raw.shape
+    ch = d // 8
+    chunks = raw.reshape(nb, hkv, 2, blk, ch, 8)
+    slot = np.arange(blk)[:, None]
+    c = np.arange(ch)[None, :]
+    phys = c ^ (slot & 7)  # logical chunk c lives at physical chunk phys
+    logical = chunks[:, :, :, np.arange(blk)[:, None], phys, :]  # [nb, hkv, 2, blk, ch, 8]
+    logical = logical.reshape(nb, hkv, 2, blk, d)
+    k = logical[:, :, 0].transpose(0, 2, 1, 3).reshape(nb, blk, hkv * d)
+    v = logical[:, :, 1].transpose(0, 2, 1, 3).reshape(nb, blk, hkv * d)
+    return np.ascontiguousarray(k), np.ascontiguousarray(v)
