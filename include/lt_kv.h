@@ -51,7 +51,9 @@ typedef enum lt_status {
     LT_E_CUDA = 4,        /* a CUDA runtime call failed                         */
     LT_E_NCCL = 5,        /* an NCCL call failed                                */
     LT_E_TIMEOUT = 6,     /* a bounded device wait gave up (kernel error flag)  */
-    LT_E_UNSUPPORTED = 7  /* shape outside what the kernels implement           */
+    LT_E_UNSUPPORTED = 7, /* shape outside what the kernels implement           */
+    LT_E_SCRATCH = 8      /* request too large for lt_paged_attend_noalloc's
+                             fixed scratch (see LT_NOALLOC_*)                   */
 } lt_status;
 
 typedef enum lt_dtype {
@@ -202,6 +204,36 @@ lt_status lt_kv_profile_read(lt_kv* kv, double* total_ms, uint64_t* launches);
 
 /* Kernel launches made by this handle since creation (all kinds). */
 uint64_t lt_kv_launch_count(const lt_kv* kv);
+
+/* ---- allocation-free attention ------------------------------------------- */
+
+/* No counterpart in the reference.  The same paged decode attention as
+ * lt_kv_attend, for callers that cannot call cudaMalloc: hosts whose device
+ * memory is wholly owned by their own allocator or fixed budget, and hosts
+ * that cannot pay for cudaMalloc's possible device-wide synchronisation on
+ * their step path.  The caller passes everything: the pool of one layer
+ * (lt_kv_device_pool layout, i.e. lt_kv_device_pool(kv) + layer *
+ * n_blocks * n_kv_heads * 2 * 16 * head_dim halves), the device block tables
+ * ([seq][max_blocks_per_seq] int32), host seq/pos arrays, device q and out.
+ * Nothing is allocated: the kernel's scratch (split-K partials, counters,
+ * work list) lives in one static device array of LT_NOALLOC_SCRATCH_BYTES
+ * that every GPU loading this library holds until the process exits.
+ *   - At most LT_NOALLOC_MAX_TOKENS tokens per call, and the partials must
+ *     fit the array; larger requests return LT_E_SCRATCH before any work.
+ *   - The first call on a device looks up the array's address with that
+ *     device current; make that first call before any stream capture.
+ *   - All calls share the array and it keeps the last call's contents; each
+ *     call clears its counters first.  Calls that overlap on the GPU race:
+ *     issue them in order on one stream.
+ *   - The call does not synchronise; a bounded device wait that gives up
+ *     leaves that call's outputs invalid without a status. */
+#define LT_NOALLOC_SCRATCH_BYTES (8u << 20)
+#define LT_NOALLOC_MAX_TOKENS 1024u
+lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_kv_heads, uint32_t head_dim,
+                                  uint32_t n_heads, const int32_t* tables, uint32_t max_blocks_per_seq,
+                                  const uint32_t* seq_host, const uint32_t* pos_host, uint32_t n,
+                                  const void* q, lt_dtype q_dtype, void* out, lt_dtype out_dtype,
+                                  float scale, void* stream);
 
 #ifdef __cplusplus
 }

@@ -11,7 +11,9 @@ import threading
 
 from . import build as _build
 
-LT_OK, LT_E_FULL, LT_E_NONCONTIG, LT_E_ARG, LT_E_CUDA, LT_E_NCCL, LT_E_TIMEOUT, LT_E_UNSUPPORTED = range(8)
+LT_OK, LT_E_FULL, LT_E_NONCONTIG, LT_E_ARG, LT_E_CUDA, LT_E_NCCL, LT_E_TIMEOUT, LT_E_UNSUPPORTED, LT_E_SCRATCH = range(9)
+LT_NOALLOC_SCRATCH_BYTES = 8 << 20
+LT_NOALLOC_MAX_TOKENS = 1024
 LT_F32, LT_F16 = 0, 1
 BLOCK = 16
 
@@ -22,6 +24,7 @@ EXPORTS = (
     "lt_kv_truncate", "lt_kv_share", "lt_kv_compact", "lt_kv_flush", "lt_kv_rows", "lt_kv_check",
     "lt_kv_seq_blocks", "lt_kv_refs", "lt_kv_free_list", "lt_kv_n_blocks", "lt_kv_device_pool",
     "lt_kv_device_tables", "lt_kv_read_pool", "lt_kv_launch_count", "lt_kv_profile", "lt_kv_profile_read",
+    "lt_paged_attend_noalloc",
 )
 
 
@@ -74,6 +77,8 @@ def _declare(L):
         "lt_kv_launch_count": (u64, [p]),
         "lt_kv_profile": (st, [p, C.c_int]),
         "lt_kv_profile_read": (st, [p, C.POINTER(C.c_double), C.POINTER(u64)]),
+        "lt_paged_attend_noalloc": (st, [p, u32, u32, u32, p, u32, p, p, u32, p, C.c_int, p, C.c_int,
+                                         C.c_float, p]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

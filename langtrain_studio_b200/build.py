@@ -18,7 +18,7 @@ INCLUDE = ROOT / "include"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "liblt_kv.so"
 
-SOURCES = [CSRC / "lt_kv_kernels.cu", CSRC / "lt_kv.cpp"]
+SOURCES = [CSRC / "lt_kv_kernels.cu", CSRC / "lt_kv.cpp", CSRC / "lt_kv_noalloc.cu"]
 HEADERS = [CSRC / "lt_kv_internal.h", INCLUDE / "lt_kv.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
