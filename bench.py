@@ -45,6 +45,41 @@ def rank_info():
             int(os.environ.get("LOCAL_RANK", 0)))
 
 
+def shard_seed(rank: int) -> int:
+    """Sequence sharding: every rank owns its own 64 sequences (own lengths,
+    own pool, own seed); nothing crosses ranks on the data path."""
+    return 1234 + rank
+
+
+def reduce_max(x: float, device, world: int) -> float:
+    """Max over ranks of a per-rank device time (whole-job time of a step)."""
+    if world <= 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def fill_plan(lens: np.ndarray, seed: int):
+    """(seqs, positions) of the cache fill: each sequence's context in
+    16-token pieces, pieces of all sequences randomly interleaved (seed+1) so
+    physical block ids are scattered across sequences."""
+    rng = np.random.default_rng(seed + 1)
+    pieces = np.repeat(np.arange(len(lens)), (lens + BLOCK - 1) // BLOCK)
+    rng.shuffle(pieces)
+    cur = np.zeros(len(lens), np.int64)
+    seqs, pos = [], []
+    for s in pieces:
+        n = min(BLOCK, int(lens[s] - cur[s]))
+        seqs.append(np.full(n, s))
+        pos.append(np.arange(cur[s], cur[s] + n))
+        cur[s] += n
+    return np.concatenate(seqs), np.concatenate(pos)
+
+
 def workload(seed: int):
     rng = np.random.default_rng(seed)
     lens = rng.integers(CTX_LO, CTX_HI + 1, BATCH)
@@ -150,18 +185,7 @@ def build_cache(kv_mod, torch, device: int, lens: np.ndarray, seed: int):
     n_blocks = int(((lens + headroom + BLOCK - 1) // BLOCK).sum()) + BATCH
     kv = kv_mod.KvCache(1, N_KV_HEADS, HEAD_DIM, n_blocks * BLOCK, n_heads=N_HEADS, max_seqs=BATCH,
                         max_batch=8192, device=device)
-    rng = np.random.default_rng(seed + 1)
-    pieces = np.repeat(np.arange(BATCH), (lens + BLOCK - 1) // BLOCK)
-    rng.shuffle(pieces)
-    cur = np.zeros(BATCH, np.int64)
-    seqs, pos = [], []
-    for s in pieces:
-        n = min(BLOCK, int(lens[s] - cur[s]))
-        seqs.append(np.full(n, s))
-        pos.append(np.arange(cur[s], cur[s] + n))
-        cur[s] += n
-    seqs = np.concatenate(seqs)
-    pos = np.concatenate(pos)
+    seqs, pos = fill_plan(lens, seed)
     gen = torch.Generator(device=f"cuda:{device}")
     gen.manual_seed(seed)
     chunk = 8192
@@ -180,7 +204,7 @@ class Stepper:
 
     def __init__(self, kv, lens, k, v, q, out):
         self.kv, self.lens = kv, lens
-        self.seqs = np.arange(BATCH, dtype=np.uint32)
+        self.seqs = np.arange(len(lens), dtype=np.uint32)
         self.k, self.v, self.q, self.out = k, v, q, out
         self.phase = 0
 
@@ -191,7 +215,7 @@ class Stepper:
         lens_now = self.lens + self.phase + 1
         self.phase += 1
         if self.phase == CYCLE:
-            for i in range(BATCH):
+            for i in range(len(self.lens)):
                 self.kv.truncate(i, int(self.lens[i]))  # Backend::kv_remove
             self.phase = 0
         return lens_now
@@ -209,7 +233,7 @@ def run_ours(args, rank, world, local):
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    seed = 1234 + rank
+    seed = shard_seed(rank)
     lens = workload(seed)
     kv = build_cache(kv_mod, torch, local, lens, seed)
     g = torch.Generator(device=dev)
@@ -258,11 +282,7 @@ def run_ours(args, rank, world, local):
     kv.profile(False)
     clk = clocks.stop()
     kv.check()
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+    ms_max = reduce_max(ms, dev, world)
     # ---------------- end-to-end through the public API ----------------
     hq = torch.empty_like(q, device="cpu").pin_memory()
     hk = torch.empty_like(k, device="cpu").pin_memory()
@@ -295,10 +315,7 @@ def run_ours(args, rank, world, local):
     f1.record()
     barrier()
     e2e_ms = f0.elapsed_time(f1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = reduce_max(e2e_ms, dev, world)
     h2d = (q.numel() + k.numel() + v.numel()) * 2
     d2h = out.numel() * 2
 
@@ -353,24 +370,230 @@ def run_ours(args, rank, world, local):
 
 
 # ---------------------------------------------------------------------------
+# further configurations; run with
+# --config c3 / c4-batch / c4-head.  The driver's default line is configs[1].
+
+
+def _json_common(args, world, metric_value, unit, ms_step, config):
+    return {"metric": METRIC, "value": metric_value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic: f16 K/V and q ~ N(0,1), seeded",
+            "config": config}
+
+
+def run_c3(args, rank, world, local):
+    """configs[2], prefix-sharing stress: one 2048-token source, 256 sequences
+    made with share(src, s, 2047) (the scheduler's cap = len-1 rule), whose
+    first append at position 2047 copies the shared partial block (256
+    copy-on-write copies in one plan launch), a distinct 256-token suffix
+    each, then decode steps of append + fused write/attention over all 256.
+    Shared blocks are counted once for the unique-byte roofline."""
+    import torch
+
+    from langtrain_studio_b200 import kv as kv_mod
+
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    n_seq, prefix, suffix = 256, 2048, 256
+    hq, hkv, d = 32, 8, 128
+    kvd = hkv * d
+    steps, warm = args.steps, args.warmup
+    total_dec = steps + warm
+    per_seq_blocks = 1 + (suffix + total_dec + 2 + BLOCK - 1) // BLOCK
+    n_blocks = prefix // BLOCK + n_seq * per_seq_blocks + 8
+    kv = kv_mod.KvCache(1, hkv, d, n_blocks * BLOCK, n_heads=hq, max_seqs=n_seq + 1, max_batch=8192, device=local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(shard_seed(rank))
+    rnd = lambda n: torch.randn((n, kvd), generator=g, device=dev, dtype=torch.float16)
+    b, s = kv.append_batch(np.zeros(prefix, np.uint32), np.arange(prefix))
+    kv.write(0, b, s, rnd(prefix), rnd(prefix))
+    seqs = np.arange(1, n_seq + 1, dtype=np.uint32)
+    for i in seqs:
+        kv.share(0, int(i), prefix - 1)
+    kv.flush()
+    torch.cuda.synchronize()
+    # divergence: 256 copy-on-write copies of the shared partial block
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = kv.launch_count()
+    c0.record()
+    b, s = kv.append_batch(seqs, np.full(n_seq, prefix - 1))
+    kv.flush()
+    c1.record()
+    torch.cuda.synchronize()
+    cow_ms = c0.elapsed_time(c1)
+    cow_launches = kv.launch_count() - launches0
+    cow_bytes = n_seq * kvd * 2 * BLOCK * 2 * 2  # K+V block, read + write
+    kv.write(0, b, s, rnd(n_seq), rnd(n_seq))
+    # distinct suffixes
+    pos = np.arange(prefix, prefix + suffix)
+    for i0 in range(0, n_seq, 32):
+        ss = np.repeat(seqs[i0:i0 + 32], suffix)
+        pp = np.tile(pos, len(seqs[i0:i0 + 32]))
+        b, s = kv.append_batch(ss, pp)
+        kv.write(0, b, s, rnd(ss.size), rnd(ss.size))
+    lens = np.full(n_seq, prefix + suffix, np.int64)
+    k, v = rnd(n_seq), rnd(n_seq)
+    q = torch.randn((n_seq, hq * d), generator=g, device=dev, dtype=torch.float16)
+    out = torch.empty_like(q)
+    shared_blocks = (prefix - 1) // BLOCK  # blocks 0..126 stay shared after the copy
+
+    def step():
+        pos = lens.astype(np.uint32)
+        b, s = kv.append_batch(seqs, pos)
+        kv.write_attend(0, b, s, k, v, q, seqs, pos, out=out)
+        lens[:] += 1
+
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    kv.profile(True)
+    l0 = kv.launch_count()
+    uniq = logical = 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        lens_now = lens + 1
+        row = kvd * 2 * 2  # K+V bytes of one position
+        logical += int(lens_now.sum()) * row
+        uniq += shared_blocks * BLOCK * row + int((lens_now - shared_blocks * BLOCK).sum()) * row
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    attn_ms, attn_n = kv.profile_read()
+    kv.check()
+    extra = n_seq * hq * d * 2 * 2 + n_seq * 2 * kvd * 2 * 2  # q, out, appended rows
+    peak, kind = measured_peak()
+    per_launch_u = uniq / steps + extra
+    achieved = per_launch_u / (attn_ms / attn_n * 1e-3) / 1e9
+    res = _json_common(args, world, n_seq * steps / (ms * 1e-3), "tokens/s", ms / steps, {
+        "workload": "configs[2]: prefix-sharing stress, 256 seqs sharing a 2048-token prefix (share(src, s, 2047)), "
+                    "256-token distinct suffixes, decode steps, Llama-3-8B attention shape, one layer",
+        "n_heads": hq, "n_kv_heads": hkv, "head_dim": d, "block_tokens": BLOCK,
+        "context_at_start": prefix + suffix})
+    res.update({
+        "hbm_gbs_unique": (uniq + extra * steps) / (ms * 1e-3) / 1e9,
+        "hbm_gbs_logical": (logical + extra * steps) / (ms * 1e-3) / 1e9,
+        "roofline": {"bound": "hbm", "kernel": "paged_attn_kernel<128> + kv_combine_kernel (unique bytes)",
+                     "achieved": achieved, "peak": peak, "peak_kind": kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "algorithmic_bytes_per_launch": int(per_launch_u),
+                     "logical_bytes_per_launch": int(logical / steps + extra), "avg_launch_ms": attn_ms / attn_n},
+        "cow": {"copies": n_seq, "bytes": cow_bytes, "ms": cow_ms, "gbs": cow_bytes / (cow_ms * 1e-3) / 1e9,
+                "launches": cow_launches},
+        "gpu_launches": kv.launch_count() - l0,
+    })
+    kv.close()
+    return res
+
+
+def run_c4(args, rank, world, local, mode):
+    """configs[3], long-context decode at the Llama-3-70B attention shape (64 q
+    heads, 8 KV heads, head_dim 128): 16 sequences of 32768 tokens.
+      batch: sequences sharded across ranks (16/N each), no collective;
+      head:  KV heads sharded across ranks (8/N each), bookkeeping replicated,
+             one NCCL all-gather of the per-head attention outputs per step."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from langtrain_studio_b200 import kv as kv_mod
+
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    B, L, hq, hkv, d = 16, 32768, 64, 8, 128
+    if mode == "batch":
+        assert B % world == 0
+        n_seq, my_hkv, my_hq = B // world, hkv, hq
+    else:
+        assert hkv % world == 0
+        n_seq, my_hkv, my_hq = B, hkv // world, hq // world
+    kvd = my_hkv * d
+    n_blocks = n_seq * ((L + CYCLE + 1 + BLOCK - 1) // BLOCK) + 8
+    kv = kv_mod.KvCache(1, my_hkv, d, n_blocks * BLOCK, n_heads=my_hq, max_seqs=n_seq, max_batch=8192, device=local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(shard_seed(rank))
+    chunk = 8192
+    for sq in range(n_seq):
+        for p0 in range(0, L, chunk):
+            b, s = kv.append_batch(np.full(chunk, sq), np.arange(p0, p0 + chunk))
+            kv.write(0, b, s, torch.randn((chunk, kvd), generator=g, device=dev, dtype=torch.float16),
+                     torch.randn((chunk, kvd), generator=g, device=dev, dtype=torch.float16))
+    lens = np.full(n_seq, L, np.int64)
+    seqs = np.arange(n_seq, dtype=np.uint32)
+    k = torch.randn((n_seq, kvd), generator=g, device=dev, dtype=torch.float16)
+    v = torch.randn((n_seq, kvd), generator=g, device=dev, dtype=torch.float16)
+    q = torch.randn((n_seq, my_hq * d), generator=g, device=dev, dtype=torch.float16)
+    out = torch.empty_like(q)
+    gathered = torch.empty((world, n_seq, my_hq * d), device=dev, dtype=torch.float16) if mode == "head" else None
+    st = Stepper(kv, lens, k, v, q, out)
+
+    def step():
+        lens_now = st.step()
+        if gathered is not None and world > 1:
+            dist.all_gather_into_tensor(gathered, out)  # rank r's heads r*G..: [world][seq][heads*D]
+        return lens_now
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    while st.phase != 0:
+        step()
+    kv.profile(True)
+    l0 = kv.launch_count()
+    byts = 0
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        lens_now = step()
+        byts += int(lens_now.sum()) * kvd * 2 * 2 + n_seq * (my_hq * d * 2 * 2 + 2 * kvd * 2 * 2)
+    e1.record()
+    barrier()
+    ms = reduce_max(e0.elapsed_time(e1), dev, world)
+    attn_ms, attn_n = kv.profile_read()
+    kv.check()
+    peak, kind = measured_peak()
+    achieved = byts / args.steps / (attn_ms / attn_n * 1e-3) / 1e9
+    res = None
+    if rank == 0:
+        res = _json_common(args, world, B * args.steps / (ms * 1e-3), "tokens/s", ms / args.steps, {
+            "workload": f"configs[3]: long-context decode, Llama-3-70B attention shape, 16 seqs x 32768 tokens, "
+                        f"{mode}-sharded x{world}, one layer",
+            "n_heads": hq, "n_kv_heads": hkv, "head_dim": d, "block_tokens": BLOCK,
+            "per_rank": {"seqs": n_seq, "kv_heads": my_hkv, "q_heads": my_hq},
+            "collective": "NCCL all_gather_into_tensor of [seqs, q_heads*D] f16 per step" if mode == "head" and world > 1
+            else "none"})
+        res["scaling"] = "strong" if mode == "head" else "weak"
+        res["hbm_gbs_per_gpu"] = byts / args.steps / (ms / args.steps * 1e-3) / 1e9
+        res["roofline"] = {"bound": "hbm", "kernel": "paged_attn_kernel<128> + kv_combine_kernel (rank 0)",
+                           "achieved": achieved, "peak": peak, "peak_kind": kind, "unit": "GB/s",
+                           "frac": achieved / peak, "traffic": None,
+                           "algorithmic_bytes_per_launch": int(byts / args.steps), "avg_launch_ms": attn_ms / attn_n}
+        res["gpu_launches"] = kv.launch_count() - l0
+    if world > 1:
+        dist.barrier()
+        kv.close()
+        dist.destroy_process_group()
+    else:
+        kv.close()
+    return res
+
+
+# ---------------------------------------------------------------------------
 # CPU arm (restated reference path)
 
 
 def cpu_fill(ok_mod, lens, seed):
     n_blocks = int(((lens + CYCLE + 1 + BLOCK - 1) // BLOCK).sum()) + BATCH
     ok = ok_mod.OracleKv(1, N_KV_HEADS * HEAD_DIM, n_blocks * BLOCK, max_seqs=BATCH)
-    rng = np.random.default_rng(seed + 1)
-    pieces = np.repeat(np.arange(BATCH), (lens + BLOCK - 1) // BLOCK)
-    rng.shuffle(pieces)
-    cur = np.zeros(BATCH, np.int64)
-    seqs, pos = [], []
-    for s in pieces:
-        n = min(BLOCK, int(lens[s] - cur[s]))
-        seqs.append(np.full(n, s))
-        pos.append(np.arange(cur[s], cur[s] + n))
-        cur[s] += n
-    seqs = np.concatenate(seqs)
-    pos = np.concatenate(pos)
+    seqs, pos = fill_plan(lens, seed)
     drng = np.random.default_rng(seed)
     chunk = 16384
     for i in range(0, seqs.size, chunk):
@@ -458,7 +681,10 @@ def main():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample budget (rank 0, N=1)")
+    ap.add_argument("--config", choices=["c2", "c3", "c4-batch", "c4-head"], default="c2",
+                    help="c2: configs[1] (default, the headline); c3: configs[2]; c4-*: configs[3]")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="CPU-baseline sample budget in seconds (rank 0, N=1); 0 skips it")
     args = ap.parse_args()
     rank, world, local = rank_info()
     if args.impl == "reference":
@@ -466,9 +692,19 @@ def main():
         if res is not None:
             print(json.dumps(res), flush=True)
         return
+    if args.config == "c3":
+        res = run_c3(args, rank, world, local)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
+    if args.config.startswith("c4"):
+        res = run_c4(args, rank, world, local, args.config.split("-")[1])
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
     res = run_ours(args, rank, world, local)
     if rank == 0 and res is not None:
-        if world == 1:
+        if world == 1 and args.cpu_seconds > 0:
             threads = os.cpu_count() or 1
             value, steps, dt = cpu_run(workload(1234), 1234, budget_s=args.cpu_seconds, max_steps=10 ** 6,
                                        threads=threads)

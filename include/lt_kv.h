@@ -215,16 +215,16 @@ uint64_t lt_kv_launch_count(const lt_kv* kv);
  * (lt_kv_device_pool layout, i.e. lt_kv_device_pool(kv) + layer *
  * n_blocks * n_kv_heads * 2 * 16 * head_dim halves), the device block tables
  * ([seq][max_blocks_per_seq] int32), host seq/pos arrays, device q and out.
- * Nothing is allocated: the kernel's scratch (split-K partials, counters,
- * work list) lives in one static device array of LT_NOALLOC_SCRATCH_BYTES
+ * Nothing is allocated: the kernel's scratch (split-K partials and the work
+ * plan) lives in one static device array of LT_NOALLOC_SCRATCH_BYTES
  * that every GPU loading this library holds until the process exits.
  *   - At most LT_NOALLOC_MAX_TOKENS tokens per call, and the partials must
  *     fit the array; larger requests return LT_E_SCRATCH before any work.
  *   - The first call on a device looks up the array's address with that
  *     device current; make that first call before any stream capture.
  *   - All calls share the array and it keeps the last call's contents; each
- *     call clears its counters first.  Calls that overlap on the GPU race:
- *     issue them in order on one stream.
+ *     call clears its error word and rewrites what it reads.  Calls that
+ *     overlap on the GPU race: issue them in order on one stream.
  *   - The call does not synchronise; a bounded device wait that gives up
  *     leaves that call's outputs invalid without a status. */
 #define LT_NOALLOC_SCRATCH_BYTES (8u << 20)

@@ -14,12 +14,14 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
 
 #include "lt_kv.h"
 #include "lt_kv_internal.h"
+#include "lt_kv_plan.h"
 
 using ltkv::kBlock;
 
@@ -81,9 +83,8 @@ struct lt_kv {
     int32_t* d_tables = nullptr;
     float* d_part_o = nullptr;
     float* d_part_ml = nullptr;
-    int32_t* d_counters = nullptr;
     int32_t* d_err = nullptr;
-    size_t ws_slots = 0;
+    size_t ws_slots = 0;  // split-K partial slots (one per split piece)
     size_t slot_bytes = 0;
     Slot slots[kSlots];
     int next_slot = 0;
@@ -106,9 +107,11 @@ struct lt_kv {
     uint64_t prof_count = 0;
 
     UploadCache cells_cache, items_cache;
-    std::vector<ltkv::WorkItem> items_tmp;
+    std::vector<ltkv::Piece> pieces_tmp;
+    std::vector<int32_t> warp_off_tmp, last_tmp;
+    std::vector<int4> combine_tmp;
+    std::vector<char> upload_tmp;
     std::vector<int2> cells_tmp;
-    int cb_override = 0;
     uint64_t launches = 0;
 };
 
@@ -135,7 +138,6 @@ void free_device(lt_kv* kv) {
     cudaFree(kv->d_tables);
     cudaFree(kv->d_part_o);
     cudaFree(kv->d_part_ml);
-    cudaFree(kv->d_counters);
     cudaFree(kv->d_err);
     for (auto& s : kv->slots) {
         if (s.host) cudaFreeHost(s.host);
@@ -148,7 +150,7 @@ void free_device(lt_kv* kv) {
     kv->d_pool = nullptr;
     kv->d_tables = nullptr;
     kv->d_part_o = kv->d_part_ml = nullptr;
-    kv->d_counters = kv->d_err = nullptr;
+    kv->d_err = nullptr;
 }
 
 // Next staging slot; waits until every kernel that read its previous
@@ -316,50 +318,6 @@ lt_status require_device(lt_kv* kv) {
     return LT_OK;
 }
 
-int pick_cb(lt_kv* kv, uint64_t total_blocks) {
-    if (kv->cb_override > 0) return kv->cb_override;
-    (void)total_blocks;
-    return 32;
-}
-
-// Build attention work items for n tokens; returns the number of partial
-// slots used through *parts.
-lt_status build_items(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n, bool fused) {
-    uint64_t total_blocks = 0;
-    for (uint32_t i = 0; i < n; ++i) total_blocks += (pos[i] + kBlock) / kBlock;
-    int cb = pick_cb(kv, total_blocks);
-    for (;;) {
-        size_t parts = 0;
-        for (uint32_t i = 0; i < n; ++i) {
-            const uint32_t nb = (pos[i] + kBlock) / kBlock;
-            const uint32_t nc = (nb + cb - 1) / cb;
-            if (nc > 1) parts += nc;
-        }
-        if (parts <= kv->ws_slots) break;
-        cb *= 2;
-    }
-    kv->items_tmp.clear();
-    int32_t part_base = 0;
-    for (uint32_t i = 0; i < n; ++i) {
-        const uint32_t nb = (pos[i] + kBlock) / kBlock;
-        const int32_t nc = (int32_t)((nb + cb - 1) / cb);
-        for (int32_t c = 0; c < nc; ++c) {
-            ltkv::WorkItem w;
-            w.tok = (int32_t)i;
-            w.seq = (int32_t)seq[i];
-            w.pos = (int32_t)pos[i];
-            w.chunk = c;
-            w.nchunks = nc;
-            w.part_base = nc > 1 ? part_base : 0;
-            w.cb = cb;
-            w.write_row = (fused && c == nc - 1) ? 1 : 0;
-            kv->items_tmp.push_back(w);
-        }
-        if (nc > 1) part_base += nc;
-    }
-    return LT_OK;
-}
-
 lt_status check_tokens(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n) {
     if (n > kv->cfg.max_batch) return fail(kv, LT_E_ARG, "batch of %u tokens exceeds max_batch %u", n, kv->cfg.max_batch);
     for (uint32_t i = 0; i < n; ++i) {
@@ -413,32 +371,63 @@ lt_status prof_begin(lt_kv* kv, cudaStream_t st, cudaEvent_t* end) {
 lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype, const uint32_t* seq,
                       const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale, const void* k,
                       const void* v, lt_dtype kv_dtype, bool fused, cudaStream_t st) {
+    if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
+        (k && (reinterpret_cast<uintptr_t>(k) & 15)) || (v && (reinterpret_cast<uintptr_t>(v) & 15)))
+        return fail(kv, LT_E_ARG, "q, out, k and v must be 16-byte aligned device pointers");
     lt_status rc = flush(kv, st);
     if (rc) return rc;
     if (n == 0) return LT_OK;
-    build_items(kv, seq, pos, n, fused);
-    const void* d_items = nullptr;
-    int s_items = -1;
-    rc = upload(kv, kv->items_cache, kv->items_tmp.data(), kv->items_tmp.size() * sizeof(ltkv::WorkItem), st,
-                &d_items, &s_items);
+    // stream-K partition: pieces grouped by warp, warp offsets, split list
+    const int q_f32 = q_dtype == LT_F32;
+    const int max_warps = ltkv::attend_warps(kv->cfg.device, (int)kv->group, (int)kv->cfg.head_dim, q_f32);
+    if (max_warps <= 0) return fail(kv, LT_E_CUDA, "could not size the attention launch on device %d", kv->cfg.device);
+    const size_t pairs = (size_t)n * kv->cfg.n_kv_heads;
+    kv->pieces_tmp.resize(pairs + max_warps);
+    kv->warp_off_tmp.resize((size_t)max_warps + 1);
+    kv->combine_tmp.resize(pairs);
+    const int32_t* last = nullptr;
+    if (fused) {
+        kv->last_tmp.resize(n);
+        for (uint32_t i = 0; i < n; ++i) kv->last_tmp[i] = kv->blocks[seq[i]][pos[i] / kBlock];
+        last = kv->last_tmp.data();
+    }
+    const ltkv::StreamPlan pl = ltkv::plan_stream_k(seq, pos, n, (int)kv->cfg.n_kv_heads, max_warps, last,
+                                                    kv->pieces_tmp.data(), kv->warp_off_tmp.data(),
+                                                    kv->combine_tmp.data());
+    if ((size_t)pl.n_slots > kv->ws_slots)
+        return fail(kv, LT_E_ARG, "attention needs %d partial slots, the handle has %zu", pl.n_slots, kv->ws_slots);
+    // one upload: [pieces][warp offsets, 16-byte padded][split list]
+    const size_t pb = (size_t)pl.n_pieces * sizeof(ltkv::Piece);
+    const size_t wb = (((size_t)pl.n_warps + 1) * sizeof(int32_t) + 15) & ~size_t(15);
+    const size_t cbytes = (size_t)pl.n_combine * sizeof(int4);
+    kv->upload_tmp.resize(pb + wb + cbytes);
+    std::memcpy(kv->upload_tmp.data(), kv->pieces_tmp.data(), pb);
+    std::memcpy(kv->upload_tmp.data() + pb, kv->warp_off_tmp.data(), ((size_t)pl.n_warps + 1) * sizeof(int32_t));
+    if (cbytes) std::memcpy(kv->upload_tmp.data() + pb + wb, kv->combine_tmp.data(), cbytes);
+    const void* d_plan = nullptr;
+    int s_plan = -1;
+    rc = upload(kv, kv->items_cache, kv->upload_tmp.data(), pb + wb + cbytes, st, &d_plan, &s_plan);
     if (rc) return rc;
+    const char* dp = static_cast<const char*>(d_plan);
     ltkv::AttnParams p{};
     p.pool_layer = kv->d_pool + (size_t)layer * kv->layer_elems;
     p.pool_layer_w = kv->d_pool + (size_t)layer * kv->layer_elems;
     p.tables = kv->d_tables;
     p.max_blocks = (int32_t)kv->max_blocks;
-    p.items = static_cast<const ltkv::WorkItem*>(d_items);
-    p.n_items = (int32_t)kv->items_tmp.size();
+    p.pieces = reinterpret_cast<const ltkv::Piece*>(dp);
+    p.warp_off = reinterpret_cast<const int32_t*>(dp + pb);
+    p.n_warps = pl.n_warps;
+    p.combine = reinterpret_cast<const int4*>(dp + pb + wb);
+    p.n_combine = pl.n_combine;
     p.n_kv_heads = (int32_t)kv->cfg.n_kv_heads;
     p.group = (int32_t)kv->group;
     p.q = q;
-    p.q_f32 = q_dtype == LT_F32;
+    p.q_f32 = q_f32;
     p.out = out;
     p.out_f32 = out_dtype == LT_F32;
     p.scale_log2 = scale * 1.4426950408889634f;
     p.part_o = kv->d_part_o;
     p.part_ml = kv->d_part_ml;
-    p.counters = kv->d_counters;
     p.err = kv->d_err;
     p.k_new = k;
     p.v_new = v;
@@ -449,9 +438,9 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
         if (prc) return prc;
     }
     LT_CUDA(kv, ltkv::launch_attend(p, (int)kv->cfg.head_dim, st));
-    kv->launches++;
+    kv->launches += ltkv::attend_launches(p);
     if (ev_end) LT_CUDA(kv, cudaEventRecord(ev_end, st));
-    return mark_slot_use(kv, s_items, st);
+    return mark_slot_use(kv, s_plan, st);
 }
 
 }  // namespace
@@ -489,7 +478,6 @@ lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
     kv->free_list.resize(kv->n_blocks);
     for (uint32_t i = 0; i < kv->n_blocks; ++i) kv->free_list[i] = (int32_t)(kv->n_blocks - 1 - i);  // kv.rs:45
     kv->dirty_from.assign(c.max_seqs, kClean);
-    if (const char* e = getenv("LT_KV_CHUNK_BLOCKS")) kv->cb_override = atoi(e);
 
     if (c.device >= 0) {
         kv->dev = true;
@@ -503,24 +491,25 @@ lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
         };
         if (!g.ok) ck(cudaErrorInvalidDevice, "cudaSetDevice");
         const size_t pool_bytes = (size_t)c.n_layers * kv->layer_elems * 2;
-        kv->ws_slots = std::max<size_t>(2048, 4 * (size_t)c.max_batch);
+        // Split pieces of one call: at most one per (token, head) plus one per warp.
+        const int max_warps = std::max(ltkv::attend_warps(c.device, (int)kv->group, (int)c.head_dim, 1),
+                                       ltkv::attend_warps(c.device, (int)kv->group, (int)c.head_dim, 0));
+        if (max_warps <= 0) ck(cudaErrorInvalidDevice, "attend_warps");
+        kv->ws_slots = (size_t)c.max_batch * c.n_kv_heads + (size_t)std::max(max_warps, 0);
         const size_t gd = (size_t)kv->group * c.head_dim;
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_pool, std::max<size_t>(pool_bytes, 16)), "cudaMalloc(pool)");
         if (rc == LT_OK) ck(cudaMemset(kv->d_pool, 0, std::max<size_t>(pool_bytes, 16)), "cudaMemset(pool)");
         const size_t tbytes = (size_t)c.max_seqs * kv->max_blocks * 4;
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_tables, tbytes), "cudaMalloc(tables)");
         if (rc == LT_OK) ck(cudaMemset(kv->d_tables, 0, tbytes), "cudaMemset(tables)");
+        if (rc == LT_OK) ck(cudaMalloc(&kv->d_part_o, kv->ws_slots * gd * sizeof(float)), "cudaMalloc(partials)");
         if (rc == LT_OK)
-            ck(cudaMalloc(&kv->d_part_o, kv->ws_slots * c.n_kv_heads * gd * sizeof(float)), "cudaMalloc(partials)");
-        if (rc == LT_OK)
-            ck(cudaMalloc(&kv->d_part_ml, kv->ws_slots * c.n_kv_heads * kv->group * 2 * sizeof(float)),
-               "cudaMalloc(partials)");
-        const size_t cbytes = (size_t)c.max_batch * c.n_kv_heads * 4;
-        if (rc == LT_OK) ck(cudaMalloc(&kv->d_counters, cbytes), "cudaMalloc(counters)");
-        if (rc == LT_OK) ck(cudaMemset(kv->d_counters, 0, cbytes), "cudaMemset(counters)");
+            ck(cudaMalloc(&kv->d_part_ml, kv->ws_slots * kv->group * 2 * sizeof(float)), "cudaMalloc(partials)");
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_err, sizeof(int32_t)), "cudaMalloc(err)");
         if (rc == LT_OK) ck(cudaMemset(kv->d_err, 0, sizeof(int32_t)), "cudaMemset(err)");
-        kv->slot_bytes = std::max<size_t>(1u << 20, sizeof(ltkv::WorkItem) * ((size_t)c.max_batch + kv->ws_slots) + 64);
+        kv->slot_bytes = std::max<size_t>(
+            1u << 20, sizeof(ltkv::Piece) * kv->ws_slots + sizeof(int32_t) * ((size_t)max_warps + 1) +
+                          sizeof(int4) * (size_t)c.max_batch * c.n_kv_heads + 64);
         for (auto& s : kv->slots) {
             if (rc != LT_OK) break;
             ck(cudaHostAlloc(&s.host, kv->slot_bytes, cudaHostAllocDefault), "cudaHostAlloc(staging)");
@@ -746,7 +735,6 @@ lt_status lt_kv_check(lt_kv* kv, void* stream) {
     if (flag) {
         // A timed-out work item leaves its (token, head) counter behind.
         LT_CUDA(kv, cudaMemset(kv->d_err, 0, sizeof(int32_t)));
-        LT_CUDA(kv, cudaMemset(kv->d_counters, 0, (size_t)kv->cfg.max_batch * kv->cfg.n_kv_heads * 4));
         LT_CUDA(kv, cudaDeviceSynchronize());
         return fail(kv, LT_E_TIMEOUT, "a bounded device wait timed out; the affected outputs are invalid");
     }

@@ -9,27 +9,29 @@ namespace ltkv {
 constexpr int kBlock = 16;           // tokens per block (kv.rs:13)
 constexpr int kMaxGroup = 8;         // q heads per KV head the attention kernel handles
 
-// One attention work item: token `tok` (index into q/out), sequence `seq`
-// with length pos+1, blocks [chunk*cb, min((chunk+1)*cb, nb)) of its table.
-// nchunks > 1 means the item writes a partial to slot part_base + chunk and
-// the last item of (tok, head) to finish combines them.
-struct WorkItem {
-    int32_t tok;
-    int32_t seq;
-    int32_t pos;
-    int32_t chunk;
-    int32_t nchunks;
-    int32_t part_base;
-    int32_t cb;
-    int32_t write_row;  // fused append: 1 if this item writes token tok's K/V row
+// One warp's share of one (token, KV head): blocks [b0, b1) of the token's
+// sequence, which has length pos + 1.  slot >= 0: the (token, head) is split
+// across warps and this piece writes partial `slot`; slot < 0: the piece
+// covers the whole sequence and writes the output.  last_block >= 0: the
+// piece holds the token's last block (physical id last_block) and writes
+// the token's new K/V row there (fused append).
+struct Piece {
+    int32_t tok, h, seq, pos;
+    int32_t b0, b1;
+    int32_t slot;
+    int32_t last_block;
 };
 
 struct AttnParams {
     const uint16_t* pool_layer;  // pool + layer offset
+    uint16_t* pool_layer_w;      // same, for the fused append
     const int32_t* tables;       // [max_seqs][max_blocks]
     int32_t max_blocks;
-    const WorkItem* items;
-    int32_t n_items;
+    const Piece* pieces;         // grouped by warp
+    const int32_t* warp_off;     // warp w owns pieces [warp_off[w], warp_off[w+1])
+    int32_t n_warps;
+    const int4* combine;         // (tok, h, n_pieces, first_slot) per split (token, head)
+    int32_t n_combine;
     int32_t n_kv_heads;
     int32_t group;
     const void* q;               // [n][n_heads*D]
@@ -37,20 +39,19 @@ struct AttnParams {
     void* out;                   // [n][n_heads*D]
     int32_t out_f32;
     float scale_log2;            // scale * log2(e)
-    float* part_o;               // [slots][n_kv_heads][group][D]
-    float* part_ml;              // [slots][n_kv_heads][group][2]
-    int32_t* counters;           // [max_batch][n_kv_heads]
+    float* part_o;               // [slots][group][D]
+    float* part_ml;              // [slots][group][2]
     int32_t* err;                // device error flag
-    // fused append (write_row items): new K/V rows [n][n_kv_heads*D]
-    uint16_t* pool_layer_w;
-    const void* k_new;
+    const void* k_new;           // fused append: new K/V rows [n][n_kv_heads*D]
     const void* v_new;
     int32_t kv_f32;
-    const int2* cells;           // (block, slot) per token
 };
 
-int attn_smem_bytes(int head_dim);
+// Warps of one attention launch on `device` (all resident at once), or 0.
+int attend_warps(int device, int group, int head_dim, int q_f32);
 cudaError_t launch_attend(const AttnParams& p, int head_dim, cudaStream_t s);
+// Kernel launches made by launch_attend(p).
+int attend_launches(const AttnParams& p);
 
 cudaError_t launch_write(uint16_t* pool_layer, const int2* cells, int n, int n_kv_heads, int head_dim,
                          const void* k, const void* v, int in_f32, cudaStream_t s);

@@ -2,6 +2,7 @@
 //
 //   kv_write_kernel      K1  KvCache::write (kv.rs:123-131): f32/f16 rows -> f16 pool cells
 //   paged_attn_kernel    K2  attention closure of Model::forward (model.rs:431-476)
+//   kv_combine_kernel        merge of split-K partials of K2
 //   apply_plan_kernel    K3/K4  whole-block copies (copy-on-write kv.rs:99-110,
 //                            compaction moves) + block-table scatter
 //   rows_kernel              KvCache::rows (kv.rs:135-150) gather, for parity/debug
@@ -18,9 +19,10 @@
 namespace ltkv {
 namespace {
 
-constexpr int kWarps = 4;                       // warps per attention CTA
-constexpr int kStages = 3;                      // bulk-copy stages per warp
+constexpr int kWarps = 4;                         // warps per attention CTA
+constexpr int kStages = 3;                        // bulk-copy stages per warp
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // bounded mbarrier wait: 2 s
+constexpr unsigned kFull = 0xffffffffu;
 
 // ------------------------------------------------------------- helpers ----
 
@@ -163,166 +165,85 @@ __global__ void __launch_bounds__(256) kv_write_kernel(uint16_t* __restrict__ po
 }
 
 // ------------------------------------------------------------------ K2 ----
-// grid (n_items, n_kv_heads), kWarps warps.  Warp w of an item handles
-// blocks b_begin + w, + kWarps, ... through its own kStages-deep ring of
-// bulk copies.  Scores S = Q K^T and O += P V run on mma.sync m16n8k16:
-// rows 0..7 of the A operand hold the (up to 8) query heads of this KV head
-// rounded to f16, rows 8..15 hold the f16 rounding residual of the same
-// values, so S and O carry ~22-bit q and P at no extra MMA cost.
+// Stream-K decode attention.  The host lays the (token, KV head) sequences
+// of a call end to end -- tokens in order, heads within a token, blocks
+// within a head -- and cuts that tile sequence into n_warps contiguous
+// ranges of equal length (+-1 tile).  Warp w processes the pieces of its
+// range: (token, head, blocks [b0, b1)).  A (token, head) cut across warps
+// leaves one (m, l, O) partial per piece, merged by kv_combine_kernel; an
+// uncut one writes its output directly.  No atomics, fences or CTA barriers
+// sit on the data path, and every warp gets the same number of tiles.
+//
+// Each warp streams its (block, head) tiles -- 4*16*D contiguous bytes, one
+// cp.async.bulk each, completion on an mbarrier -- through its own
+// kStages-deep ring.  The issuer runs up to kStages tiles ahead of the
+// consumer and at most one piece ahead of it; a piece's q rows are bulk-
+// copied next to its first tile into one of two q buffers (piece parity).
+// Block ids are read 32 at a time (one per lane) a whole window ahead, and
+// piece descriptors one piece ahead, so no dependent global load sits on the
+// stream.  Scores S = Q K^T and O += P V use mma.sync m16n8k16: rows 0..7
+// of the A operand hold the (up to 8) query heads of the KV head rounded to
+// f16, rows 8..15 the f16 rounding residual of the same values, so S and O
+// carry ~22-bit q and P at no extra MMA cost.
+
+struct PieceRegs {
+    int tok, h, seq, pos, b0, b1, slot, last_block;
+};
+
+__device__ __forceinline__ void decode_piece(int v, PieceRegs& r) {
+    r.tok = __shfl_sync(kFull, v, 0);
+    r.h = __shfl_sync(kFull, v, 1);
+    r.seq = __shfl_sync(kFull, v, 2);
+    r.pos = __shfl_sync(kFull, v, 3);
+    r.b0 = __shfl_sync(kFull, v, 4);
+    r.b1 = __shfl_sync(kFull, v, 5);
+    r.slot = __shfl_sync(kFull, v, 6);
+    r.last_block = __shfl_sync(kFull, v, 7);
+}
+
+// S = Q K^T, online softmax and O += P V for one staged (block, head) tile.
 template <int D>
-__global__ void __launch_bounds__(kWarps * 32, 2) paged_attn_kernel(const AttnParams p) {
-    constexpr int TILE = 2 * kBlock * D * 2;  // bytes of one (block, head) K+V tile
-    constexpr int ROW = D * 2;                // bytes per row
-    constexpr int KS = D / 16;                // k-steps of S = Q K^T
-    constexpr int NT = D / 8;                 // n-tiles of O
-    extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ int s_flag[2];
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.y;
-    const WorkItem it = p.items[blockIdx.x];
-    const int Hkv = p.n_kv_heads, G = p.group;
-    const int len = it.pos + 1;
-    const int nb = (len + kBlock - 1) / kBlock;
-    const int b_begin = it.chunk * it.cb;
-    const int b_end = min(b_begin + it.cb, nb);
-    const int32_t* trow = p.tables + (size_t)it.seq * p.max_blocks;
-    const size_t tile_elems = 2 * kBlock * D;
-
-    uint8_t* my_stages = smem + (size_t)warp * kStages * TILE;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kWarps * kStages * TILE);
-    const uint32_t my_bar0 = smem_u32(bars + warp * kStages);
-
-    if (threadIdx.x < kWarps * kStages) mbar_init(smem_u32(bars + threadIdx.x), 1);
-    if (threadIdx.x == 0) s_flag[0] = 0;
-    fence_mbar_init();
-    __syncthreads();
-
-    const int n_mine = (b_end - b_begin - warp + kWarps - 1) / kWarps;  // may be <= 0
-    auto issue = [&](int j) {
-        const int b = b_begin + warp + j * kWarps;
-        const int pb = __ldg(trow + b);
-        const uint16_t* src = p.pool_layer + ((size_t)pb * Hkv + h) * tile_elems;
-        const int s = j % kStages;
-        const uint32_t bar = my_bar0 + 8u * s;
-        mbar_arrive_expect_tx(bar, TILE);
-        bulk_g2s(smem_u32(my_stages + (size_t)s * TILE), src, TILE, bar);
-    };
-    int issued = 0;
-    if (n_mine > 0) {
-        issued = min(kStages, n_mine);
-        if (lane == 0)
-            for (int j = 0; j < issued; ++j) issue(j);
-    }
-
-    // Q fragments (A operand), loaded while the first copies are in flight.
-    const int g = lane >> 2, t = lane & 3;
-    uint32_t qa[KS][4];
+__device__ __forceinline__ void attend_tile(const uint8_t* tile, int valid, const uint32_t (&qa)[D / 16][4],
+                                            float (&o)[D / 8][4], float& m_run, float& l_run, float scale_log2,
+                                            int lane) {
+    constexpr int ROW = D * 2;
+    constexpr int KS = D / 16;
+    constexpr int NT = D / 8;
+    const int t = lane & 3;
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t kbase = smem_u32(tile);
     {
-        const size_t qrow = ((size_t)it.tok * Hkv * G + (size_t)h * G + g) * D;
+        const int mi = lane >> 3;
+        const int tok = ((mi >> 1) << 3) + (lane & 7);
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                float x0 = 0.f, x1 = 0.f;
-                if (g < G) {
-                    const size_t e = qrow + ks * 16 + hf * 8 + 2 * t;
-                    if (p.q_f32) {
-                        const float2 f = *reinterpret_cast<const float2*>(static_cast<const float*>(p.q) + e);
-                        x0 = f.x;
-                        x1 = f.y;
-                    } else {
-                        const float2 f =
-                            __half22float2(*reinterpret_cast<const __half2*>(static_cast<const __half*>(p.q) + e));
-                        x0 = f.x;
-                        x1 = f.y;
-                    }
-                }
-                const __half2 hi = __floats2half2_rn(x0, x1);
-                const float2 hf2 = __half22float2(hi);
-                const __half2 lo = __floats2half2_rn(x0 - hf2.x, x1 - hf2.y);
-                qa[ks][2 * hf] = h2_bits(hi);
-                qa[ks][2 * hf + 1] = h2_bits(lo);
-            }
+            const int c = 2 * ks + (mi & 1);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(kbase + tok * ROW + (swz(c, tok) << 4), b0, b1, b2, b3);
+            mma16816(s0, qa[ks], b0, b1);
+            mma16816(s1, qa[ks], b2, b3);
         }
     }
-
-    float o[NT][4];
+    float sc[4] = {(s0[0] + s0[2]) * scale_log2, (s0[1] + s0[3]) * scale_log2, (s1[0] + s1[2]) * scale_log2,
+                   (s1[1] + s1[3]) * scale_log2};
+    if (valid < kBlock) {
+        if (2 * t >= valid) sc[0] = -INFINITY;
+        if (2 * t + 1 >= valid) sc[1] = -INFINITY;
+        if (2 * t + 8 >= valid) sc[2] = -INFINITY;
+        if (2 * t + 9 >= valid) sc[3] = -INFINITY;
+    }
+    float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
+    const bool grow = mx > m_run;
+    const float m_new = grow ? mx : m_run;
+    const float alpha = grow ? ex2(m_run - m_new) : 1.f;
+    float pr[4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
-    int j = 0;
-    for (; j < n_mine; ++j) {
-        const int s = j % kStages;
-        if (!mbar_wait_bounded(my_bar0 + 8u * s, (j / kStages) & 1)) {
-            ok = false;
-            break;
-        }
-        const int b = b_begin + warp + j * kWarps;
-        uint8_t* tile = my_stages + (size_t)s * TILE;
-        const int valid = min(kBlock, len - b * kBlock);
-        bool touched = false;
-        if (it.write_row && b == nb - 1) {
-            // Fused append: this token's new K/V row for head h goes to the
-            // pool cell and into the staged tile (the copy read the old bytes).
-            constexpr int CH = D / 8;
-            const int slot = it.pos % kBlock;
-            if (lane < 2 * CH) {
-                const int kvsel = lane / CH, c = lane % CH;
-                const size_t src = (size_t)it.tok * Hkv * D + (size_t)h * D + (size_t)c * 8;
-                const uint4 val = load8_as_f16(kvsel ? p.v_new : p.k_new, src, p.kv_f32);
-                const int pc = swz(c, slot);
-                uint16_t* dst = p.pool_layer_w + ((size_t)__ldg(trow + b) * Hkv + h) * tile_elems +
-                                (size_t)kvsel * kBlock * D + (size_t)slot * D + (size_t)pc * 8;
-                *reinterpret_cast<uint4*>(dst) = val;
-                *reinterpret_cast<uint4*>(tile + kvsel * kBlock * ROW + slot * ROW + pc * 16) = val;
-            }
-            touched = true;
-        }
-        if (valid < kBlock) {
-            // Rows past the sequence end were never written for it: zero V so
-            // 0 * (stale NaN/Inf) cannot reach O; K rows are masked below.
-            const int n16 = (kBlock - valid) * ROW / 16;
-            uint4* vz = reinterpret_cast<uint4*>(tile + kBlock * ROW + valid * ROW);
-            for (int e = lane; e < n16; e += 32) vz[e] = make_uint4(0, 0, 0, 0);
-            touched = true;
-        }
-        __syncwarp();
-
-        // S = Q K^T over this block's 16 tokens (two n-tiles of 8 tokens).
-        float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t kbase = smem_u32(tile);
-        {
-            const int mi = lane >> 3;
-            const int tok = ((mi >> 1) << 3) + (lane & 7);
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) {
-                const int c = 2 * ks + (mi & 1);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4(kbase + tok * ROW + (swz(c, tok) << 4), b0, b1, b2, b3);
-                mma16816(s0, qa[ks], b0, b1);
-                mma16816(s1, qa[ks], b2, b3);
-            }
-        }
-        float sc[4] = {(s0[0] + s0[2]) * p.scale_log2, (s0[1] + s0[3]) * p.scale_log2,
-                       (s1[0] + s1[2]) * p.scale_log2, (s1[1] + s1[3]) * p.scale_log2};
-        if (valid < kBlock) {
-            if (2 * t >= valid) sc[0] = -INFINITY;
-            if (2 * t + 1 >= valid) sc[1] = -INFINITY;
-            if (2 * t + 8 >= valid) sc[2] = -INFINITY;
-            if (2 * t + 9 >= valid) sc[3] = -INFINITY;
-        }
-        float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float m_new = fmaxf(m_run, mx);
-        const float alpha = ex2(m_run - m_new);
-        float pr[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) pr[e] = ex2(sc[e] - m_new);
-        l_run = l_run * alpha + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
-        m_run = m_new;
+    for (int e = 0; e < 4; ++e) pr[e] = ex2(sc[e] - m_new);
+    l_run = l_run * alpha + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
+    m_run = m_new;
+    if (__any_sync(kFull, grow)) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             o[nt][0] *= alpha;
@@ -330,141 +251,308 @@ __global__ void __launch_bounds__(kWarps * 32, 2) paged_attn_kernel(const AttnPa
             o[nt][2] *= alpha;
             o[nt][3] *= alpha;
         }
-        uint32_t pa[4];
-        {
-            const __half2 h01 = __floats2half2_rn(pr[0], pr[1]);
-            const __half2 h23 = __floats2half2_rn(pr[2], pr[3]);
-            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
-            pa[0] = h2_bits(h01);
-            pa[1] = h2_bits(__floats2half2_rn(pr[0] - f01.x, pr[1] - f01.y));
-            pa[2] = h2_bits(h23);
-            pa[3] = h2_bits(__floats2half2_rn(pr[2] - f23.x, pr[3] - f23.y));
-        }
-        // O += P V (V^T fragments via ldmatrix.trans).
-        {
-            const uint32_t vbase = kbase + kBlock * ROW;
-            const int mi = lane >> 3;
-            const int tok = ((mi & 1) << 3) + (lane & 7);
+    }
+    uint32_t pa[4];
+    {
+        const __half2 h01 = __floats2half2_rn(pr[0], pr[1]);
+        const __half2 h23 = __floats2half2_rn(pr[2], pr[3]);
+        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+        pa[0] = h2_bits(h01);
+        pa[1] = h2_bits(__floats2half2_rn(pr[0] - f01.x, pr[1] - f01.y));
+        pa[2] = h2_bits(h23);
+        pa[3] = h2_bits(__floats2half2_rn(pr[2] - f23.x, pr[3] - f23.y));
+    }
+    {
+        const uint32_t vbase = kbase + kBlock * ROW;
+        const int mi = lane >> 3;
+        const int tok = ((mi & 1) << 3) + (lane & 7);
 #pragma unroll
-            for (int np = 0; np < NT / 2; ++np) {
-                const int c = 2 * np + (mi >> 1);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(vbase + tok * ROW + (swz(c, tok) << 4), b0, b1, b2, b3);
-                mma16816(o[2 * np], pa, b0, b1);
-                mma16816(o[2 * np + 1], pa, b2, b3);
+        for (int np = 0; np < NT / 2; ++np) {
+            const int c = 2 * np + (mi >> 1);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(vbase + tok * ROW + (swz(c, tok) << 4), b0, b1, b2, b3);
+            mma16816(o[2 * np], pa, b0, b1);
+            mma16816(o[2 * np + 1], pa, b2, b3);
+        }
+    }
+}
+
+// Shared memory of one warp: its tile ring plus two q buffers (pieces of
+// even / odd index) of group*D elements of the q dtype.
+__host__ __device__ inline int qbuf_bytes(int group, int head_dim, int q_f32) {
+    return (group * head_dim * (q_f32 ? 4 : 2) + 127) & ~127;
+}
+
+__host__ __device__ inline int warp_smem(int group, int head_dim, int q_f32) {
+    return kStages * (2 * kBlock * head_dim * 2) + 2 * qbuf_bytes(group, head_dim, q_f32);
+}
+
+__host__ __device__ inline int attn_smem(int group, int head_dim, int q_f32) {
+    return kWarps * warp_smem(group, head_dim, q_f32) + kWarps * kStages * 8;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const AttnParams p) {
+    constexpr int TILE = 2 * kBlock * D * 2;
+    constexpr int ROW = D * 2;
+    constexpr int KS = D / 16;
+    constexpr int NT = D / 8;
+    constexpr int S = kStages;
+    extern __shared__ __align__(1024) uint8_t smem[];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * kWarps + warp;
+    const int Hkv = p.n_kv_heads, G = p.group;
+    const int QBUF = qbuf_bytes(G, D, p.q_f32);
+    uint8_t* stages = smem + (size_t)warp * warp_smem(G, D, p.q_f32);
+    uint8_t* qbufs = stages + S * TILE;
+    const uint32_t bar0 =
+        smem_u32(reinterpret_cast<uint64_t*>(smem + (size_t)kWarps * warp_smem(G, D, p.q_f32)) + warp * S);
+    if (lane < S) mbar_init(bar0 + 8u * lane, 1);
+    fence_mbar_init();
+    __syncwarp();
+    if (gw >= p.n_warps) return;
+    const int p_begin = p.warp_off[gw], p_end = p.warp_off[gw + 1];
+    if (p_begin >= p_end) return;
+
+    const int g = lane >> 2, t4 = lane & 3;
+    const size_t tile_elems = 2 * kBlock * D;
+    const int qelem = p.q_f32 ? 4 : 2;
+    const uint32_t qbytes = (uint32_t)(G * D * qelem);
+
+    auto load_desc = [&](int i) {
+        return (i < p_end && lane < 8) ? __ldg(reinterpret_cast<const int*>(p.pieces + i) + lane) : 0;
+    };
+    // block ids [b, b + min(32, b1 - b)) of a piece, lane j holding b + j
+    auto load_window = [&](const PieceRegs& r, int b) {
+        return (b + lane < r.b1) ? __ldg(p.tables + (size_t)r.seq * p.max_blocks + b + lane) : 0;
+    };
+
+    // ---- issuer state ----
+    int ii = p_begin;  // issuer piece
+    PieceRegs di{};
+    decode_piece(load_desc(ii), di);
+    int raw_n = load_desc(ii + 1);  // descriptor of piece ii + 1
+    int it = 0;                     // next tile of piece ii to issue (relative to b0)
+    int wb = 0;                     // window base (relative to b0)
+    int win = load_window(di, di.b0);
+    int win_n = 0;                  // next window: same piece (wb + 32) or first of piece ii + 1
+    auto prefetch_window = [&]() {
+        if (wb + 32 < di.b1 - di.b0) {
+            win_n = load_window(di, di.b0 + wb + 32);
+        } else if (ii + 1 < p_end) {
+            PieceRegs dn;
+            decode_piece(raw_n, dn);
+            win_n = load_window(dn, dn.b0);
+        }
+    };
+    prefetch_window();
+
+    int issued = 0, consumed = 0;
+    auto issue_one = [&]() {
+        if (it - wb >= 32) {
+            win = win_n;
+            wb += 32;
+            prefetch_window();
+        }
+        const int b = __shfl_sync(kFull, win, it - wb);
+        if (lane == 0) {
+            const int s = issued % S;
+            const uint32_t bar = bar0 + 8u * s;
+            mbar_arrive_expect_tx(bar, TILE + (it == 0 ? qbytes : 0u));
+            bulk_g2s(smem_u32(stages + (size_t)s * TILE), p.pool_layer + ((size_t)b * Hkv + di.h) * tile_elems, TILE,
+                     bar);
+            if (it == 0)
+                bulk_g2s(smem_u32(qbufs + (ii & 1) * QBUF),
+                         static_cast<const uint8_t*>(p.q) + ((size_t)di.tok * Hkv + di.h) * G * D * qelem, qbytes,
+                         bar);
+        }
+        ++it;
+        ++issued;
+    };
+    auto issuer_advance = [&]() {  // piece ii is fully issued; move to ii + 1
+        ++ii;
+        decode_piece(raw_n, di);
+        raw_n = load_desc(ii + 1);
+        it = 0;
+        wb = 0;
+        win = win_n;
+        prefetch_window();
+    };
+
+    // ---- consumer state ----
+    int ci = p_begin;
+    PieceRegs dc = di;
+    int ct = 0;
+    // The issuer stays within one piece of the consumer (two q buffers).
+    auto try_issue = [&]() {
+        while (issued - consumed < S) {
+            if (it < di.b1 - di.b0) {
+                issue_one();
+                continue;
+            }
+            if (ii != ci || ii + 1 >= p_end) break;
+            issuer_advance();
+        }
+    };
+    try_issue();
+
+    uint32_t qa[KS][4];
+    float o[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (;;) {
+        const int s = consumed % S;
+        if (!mbar_wait_bounded(bar0 + 8u * s, (consumed / S) & 1)) {
+            ok = false;
+            break;
+        }
+        uint8_t* tile = stages + (size_t)s * TILE;
+        if (ct == 0) {
+            // q rows of this piece: rows 0..G-1 rounded to f16, rows 8.. the residual
+            const uint8_t* qb = qbufs + (ci & 1) * QBUF;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    float x0 = 0.f, x1 = 0.f;
+                    if (g < G) {
+                        const int e = g * D + ks * 16 + hf * 8 + 2 * t4;
+                        if (p.q_f32) {
+                            const float2 f = *reinterpret_cast<const float2*>(qb + e * 4);
+                            x0 = f.x;
+                            x1 = f.y;
+                        } else {
+                            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(qb + e * 2));
+                            x0 = f.x;
+                            x1 = f.y;
+                        }
+                    }
+                    const __half2 hi = __floats2half2_rn(x0, x1);
+                    const float2 hf2 = __half22float2(hi);
+                    qa[ks][2 * hf] = h2_bits(hi);
+                    qa[ks][2 * hf + 1] = h2_bits(__floats2half2_rn(x0 - hf2.x, x1 - hf2.y));
+                }
             }
         }
+        const int b = dc.b0 + ct;
+        const int valid = min(kBlock, dc.pos + 1 - b * kBlock);
+        bool touched = false;
+        if (dc.last_block >= 0 && b == dc.pos / kBlock) {
+            // Fused append: this token's new K/V row for head h goes to its
+            // pool cell and into the staged tile (the copy read the old bytes).
+            constexpr int CH = D / 8;
+            const int slot = dc.pos % kBlock;
+            if (lane < 2 * CH) {
+                const int kvsel = lane / CH, c = lane % CH;
+                const size_t src = (size_t)dc.tok * Hkv * D + (size_t)dc.h * D + (size_t)c * 8;
+                const uint4 val = load8_as_f16(kvsel ? p.v_new : p.k_new, src, p.kv_f32);
+                const int pc = swz(c, slot);
+                *reinterpret_cast<uint4*>(tile + kvsel * kBlock * ROW + slot * ROW + pc * 16) = val;
+                *reinterpret_cast<uint4*>(p.pool_layer_w + ((size_t)dc.last_block * Hkv + dc.h) * tile_elems +
+                                          (size_t)kvsel * kBlock * D + (size_t)slot * D + (size_t)pc * 8) = val;
+            }
+            touched = true;
+        }
+        if (valid < kBlock) {
+            // Rows past the sequence end were never written for it: zero V so
+            // 0 * (stale NaN/Inf) cannot reach O; K rows are masked.
+            const int n16 = (kBlock - valid) * ROW / 16;
+            uint4* vz = reinterpret_cast<uint4*>(tile + kBlock * ROW + valid * ROW);
+            for (int e = lane; e < n16; e += 32) vz[e] = make_uint4(0, 0, 0, 0);
+            touched = true;
+        }
+        __syncwarp();
+        attend_tile<D>(tile, valid, qa, o, m_run, l_run, p.scale_log2, lane);
+        ++consumed;
+        ++ct;
         // Generic-proxy writes into this stage must be ordered before the
         // async-proxy copy that may refill it.
         if (touched) fence_proxy_async_smem();
         __syncwarp();
-        if (j + kStages < n_mine) {
-            if (lane == 0) issue(j + kStages);
-            ++issued;
+
+        if (ct == dc.b1 - dc.b0) {
+            // ---- piece done: output, or a partial for kv_combine_kernel ----
+            float l = l_run;
+            l += __shfl_xor_sync(kFull, l, 1);
+            l += __shfl_xor_sync(kFull, l, 2);
+            const size_t GD = (size_t)G * D;
+            if (g < G) {
+                if (dc.slot < 0) {
+                    const size_t ob = ((size_t)dc.tok * Hkv + dc.h) * GD + (size_t)g * D + 2 * t4;
+                    const float inv = 1.f / l;
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        const float v0 = (o[nt][0] + o[nt][2]) * inv, v1 = (o[nt][1] + o[nt][3]) * inv;
+                        if (p.out_f32)
+                            *reinterpret_cast<float2*>(static_cast<float*>(p.out) + ob + nt * 8) = make_float2(v0, v1);
+                        else
+                            *reinterpret_cast<__half2*>(static_cast<__half*>(p.out) + ob + nt * 8) =
+                                __floats2half2_rn(v0, v1);
+                    }
+                } else {
+                    const size_t sl = (size_t)dc.slot;
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+                        *reinterpret_cast<float2*>(p.part_o + sl * GD + (size_t)g * D + nt * 8 + 2 * t4) =
+                            make_float2(o[nt][0] + o[nt][2], o[nt][1] + o[nt][3]);
+                    if (t4 == 0) {
+                        p.part_ml[(sl * G + g) * 2] = m_run;
+                        p.part_ml[(sl * G + g) * 2 + 1] = l;
+                    }
+                }
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+            m_run = -INFINITY;
+            l_run = 0.f;
+            if (ci + 1 >= p_end) break;  // every issued tile has been consumed
+            if (ii == ci) issuer_advance();
+            ++ci;
+            dc = di;
+            ct = 0;
         }
+        try_issue();
     }
     if (!ok) {
-        // Give the copies still in flight a bounded chance to land before
-        // this CTA's shared memory is released, then report the failure.
-        for (int jj = j + 1; jj < issued; ++jj) mbar_wait_bounded(my_bar0 + 8u * (jj % kStages), (jj / kStages) & 1);
-        if (lane == 0) {
-            s_flag[0] = 1;
-            atomicExch(p.err, 1);
-        }
+        // bounded drain of the copies still in flight, then report
+        for (int jj = consumed + 1; jj < issued; ++jj) mbar_wait_bounded(bar0 + 8u * (jj % S), (jj / S) & 1);
+        if (lane == 0) atomicExch(p.err, 1);
     }
-    __syncthreads();
-    if (s_flag[0]) return;
+}
 
-    // Combine the warps of this CTA (stage memory is free: every copy landed).
-    float* cm = reinterpret_cast<float*>(smem);
-    float* cl = cm + kWarps * kMaxGroup;
-    float* co = cl + kWarps * kMaxGroup;
-    float l_tot = l_run;
-    l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 1);
-    l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 2);
-    if (g < G) {
-        if (t == 0) {
-            cm[warp * kMaxGroup + g] = m_run;
-            cl[warp * kMaxGroup + g] = l_tot;
-        }
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-            *reinterpret_cast<float2*>(co + (size_t)(warp * kMaxGroup + g) * D + nt * 8 + 2 * t) =
-                make_float2(o[nt][0] + o[nt][2], o[nt][1] + o[nt][3]);
-    }
-    __syncthreads();
-
+// Merge the (m, l, O) partials of every split (token, KV head).  One thread
+// per output element (pair, g, d); the pieces of a pair are few, so every
+// load is independent and the kernel is a short bandwidth-bound pass.  It is
+// launched as a programmatic dependent of the attention kernel and waits for
+// that grid's completion before its first read.
+template <int D>
+__global__ void __launch_bounds__(256) kv_combine_kernel(const AttnParams p) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int G = p.group, Hkv = p.n_kv_heads;
     const int GD = G * D;
-    const size_t out_base = ((size_t)it.tok * Hkv + h) * GD;  // == tok*Hq*D + h*G*D
-    if (it.nchunks == 1) {
-        for (int e = threadIdx.x; e < GD; e += blockDim.x) {
-            const int gg = e / D, d = e % D;
-            float M = -INFINITY;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) M = fmaxf(M, cm[w * kMaxGroup + gg]);
-            float L = 0.f, O = 0.f;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
-                const float sw = ex2(cm[w * kMaxGroup + gg] - M);
-                L += cl[w * kMaxGroup + gg] * sw;
-                O += co[(size_t)(w * kMaxGroup + gg) * D + d] * sw;
-            }
-            const float r = O / L;
-            if (p.out_f32)
-                static_cast<float*>(p.out)[out_base + e] = r;
-            else
-                static_cast<__half*>(p.out)[out_base + e] = __float2half_rn(r);
-        }
-        return;
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)p.n_combine * GD) return;
+    const int pair = (int)(idx / GD), e = (int)(idx % GD), gg = e / D;
+    const int4 c = __ldg(p.combine + pair);  // (tok, h, n_pieces, first_slot)
+    const float* ml = p.part_ml + ((size_t)c.w * G + gg) * 2;
+    const float* po = p.part_o + (size_t)c.w * GD + e;
+    float M = -INFINITY;
+    for (int j = 0; j < c.z; ++j) M = fmaxf(M, __ldcg(ml + (size_t)j * G * 2));
+    float L = 0.f, O = 0.f;
+    for (int j = 0; j < c.z; ++j) {
+        const float sw = ex2(__ldcg(ml + (size_t)j * G * 2) - M);
+        L += __ldcg(ml + (size_t)j * G * 2 + 1) * sw;
+        O += __ldcg(po + (size_t)j * GD) * sw;
     }
-
-    const size_t slot = (size_t)(it.part_base + it.chunk) * Hkv + h;
-    for (int e = threadIdx.x; e < GD; e += blockDim.x) {
-        const int gg = e / D, d = e % D;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, cm[w * kMaxGroup + gg]);
-        float L = 0.f, O = 0.f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-            const float sw = ex2(cm[w * kMaxGroup + gg] - M);
-            L += cl[w * kMaxGroup + gg] * sw;
-            O += co[(size_t)(w * kMaxGroup + gg) * D + d] * sw;
-        }
-        p.part_o[slot * GD + e] = O;
-        if (d == 0) {
-            p.part_ml[(slot * G + gg) * 2] = M;
-            p.part_ml[(slot * G + gg) * 2 + 1] = L;
-        }
-    }
-    __threadfence();
-    __syncthreads();
-    int32_t* counter = p.counters + (size_t)it.tok * Hkv + h;
-    if (threadIdx.x == 0) s_flag[1] = (atomicAdd(counter, 1) == it.nchunks - 1);
-    __syncthreads();
-    if (!s_flag[1]) return;
-    __threadfence();
-    // Last item of (tok, head): merge all chunks' (m, l, o).
-    const size_t base = (size_t)it.part_base * Hkv + h;
-    for (int e = threadIdx.x; e < GD; e += blockDim.x) {
-        const int gg = e / D;
-        float M = -INFINITY;
-        for (int c = 0; c < it.nchunks; ++c)
-            M = fmaxf(M, __ldcg(p.part_ml + ((base + (size_t)c * Hkv) * G + gg) * 2));
-        float L = 0.f, O = 0.f;
-        for (int c = 0; c < it.nchunks; ++c) {
-            const size_t sl = base + (size_t)c * Hkv;
-            const float sw = ex2(__ldcg(p.part_ml + (sl * G + gg) * 2) - M);
-            L += __ldcg(p.part_ml + (sl * G + gg) * 2 + 1) * sw;
-            O += __ldcg(p.part_o + sl * GD + e) * sw;
-        }
-        const float r = O / L;
-        if (p.out_f32)
-            static_cast<float*>(p.out)[out_base + e] = r;
-        else
-            static_cast<__half*>(p.out)[out_base + e] = __float2half_rn(r);
-    }
-    if (threadIdx.x == 0) *counter = 0;
+    const float r = O / L;
+    const size_t o = ((size_t)c.x * Hkv + c.y) * GD + e;
+    if (p.out_f32)
+        static_cast<float*>(p.out)[o] = r;
+    else
+        static_cast<__half*>(p.out)[o] = __float2half_rn(r);
 }
 
 // -------------------------------------------------------------- K3/K4 ----
@@ -513,36 +601,90 @@ __global__ void __launch_bounds__(256) rows_kernel(const uint16_t* __restrict__ 
     *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
 }
 
-template <int D>
-int smem_bytes_for() {
-    return kWarps * kStages * (2 * kBlock * D * 2) + kWarps * kStages * 8;
-}
-
 }  // namespace
 
-int attn_smem_bytes(int head_dim) { return head_dim == 64 ? smem_bytes_for<64>() : smem_bytes_for<128>(); }
+namespace {
+
+int sm_count(int dev) {
+    static int sms[64] = {};
+    if (sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    return sms[dev];
+}
+
+template <int D>
+cudaError_t ensure_attr(int dev) {
+    // opt-in shared memory is a per-device attribute; size it for the largest
+    // layout (f32 q, group 8)
+    static bool set[64] = {};
+    if (set[dev]) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(paged_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               attn_smem(kMaxGroup, D, 1));
+    if (e == cudaSuccess) set[dev] = true;
+    return e;
+}
+
+template <int D>
+int warps_for(int dev, int group, int q_f32) {
+    // resident CTAs per SM for this layout, cached per (device, group, dtype)
+    static int cache[64][kMaxGroup + 1][2] = {};
+    int& c = cache[dev][group][q_f32 ? 1 : 0];
+    if (c == 0) {
+        if (ensure_attr<D>(dev) != cudaSuccess) return 0;
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_attn_kernel<D>, kWarps * 32,
+                                                          attn_smem(group, D, q_f32)) != cudaSuccess)
+            return 0;
+        c = (per_sm < 1 ? 1 : per_sm) * sm_count(dev) * kWarps;
+    }
+    return c;
+}
 
 template <int D>
 cudaError_t launch_attend_d(const AttnParams& p, cudaStream_t s) {
-    // The opt-in shared-memory size is a per-device function attribute.
-    static bool attr_set[64] = {};
-    const int sm = smem_bytes_for<D>();
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!attr_set[dev]) {
-        e = cudaFuncSetAttribute(paged_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-        if (e != cudaSuccess) return e;
-        attr_set[dev] = true;
-    }
-    paged_attn_kernel<D><<<dim3(p.n_items, p.n_kv_heads), kWarps * 32, sm, s>>>(p);
-    return cudaGetLastError();
+    if ((e = ensure_attr<D>(dev)) != cudaSuccess) return e;
+    const int grid = (p.n_warps + kWarps - 1) / kWarps;
+    paged_attn_kernel<D><<<grid, kWarps * 32, attn_smem(p.group, D, p.q_f32), s>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess || p.n_combine == 0) return e;
+    // programmatic dependent launch: the combine grid is set up while the
+    // attention grid runs and starts reading once it has completed
+    const long long threads = (long long)p.n_combine * p.group * D;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((threads + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kv_combine_kernel<D>, p);
+}
+
+}  // namespace
+
+int attend_warps(int device, int group, int head_dim, int q_f32) {
+    if (device < 0 || device >= 64 || group < 1 || group > kMaxGroup) return 0;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != device) cudaSetDevice(device);
+    const int w = head_dim == 64 ? warps_for<64>(device, group, q_f32) : warps_for<128>(device, group, q_f32);
+    if (prev != device && prev >= 0) cudaSetDevice(prev);
+    return w;
 }
 
 cudaError_t launch_attend(const AttnParams& p, int head_dim, cudaStream_t s) {
-    if (p.n_items == 0) return cudaSuccess;
+    if (p.n_warps == 0) return cudaSuccess;
     return head_dim == 64 ? launch_attend_d<64>(p, s) : launch_attend_d<128>(p, s);
+}
+
+int attend_launches(const AttnParams& p) {
+    if (p.n_warps == 0) return 0;
+    return p.n_combine > 0 ? 2 : 1;
 }
 
 cudaError_t launch_write(uint16_t* pool_layer, const int2* cells, int n, int n_kv_heads, int head_dim, const void* k,

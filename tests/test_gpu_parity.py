@@ -254,7 +254,7 @@ def test_fused_write_attend_equals_write_then_attend(oracle_mod, kv_dtype):
     kd, vd, qd = (torch.from_numpy(x).cuda() for x in (k, v, q))
     launches = a.kv.launch_count()
     out_f = a.kv.write_attend(0, b_, s_, kd, vd, qd, seqs, pos)
-    assert a.kv.launch_count() - launches <= 2  # one plan + one fused kernel
+    assert a.kv.launch_count() - launches <= 3  # plan + fused attention (+ split-K combine)
     a.ok.write_batch(0, b_, s_, k, v)
     a.check_pool()
     ref = a.ok.attend(0, q, seqs, pos, hq, hkv, hd)
