@@ -21,7 +21,6 @@
 
 #include "lt_kv.h"
 #include "lt_kv_internal.h"
-#include "lt_kv_plan.h"
 
 using ltkv::kBlock;
 
@@ -84,6 +83,8 @@ struct lt_kv {
     float* d_part_o = nullptr;
     float* d_part_ml = nullptr;
     int32_t* d_err = nullptr;
+    uint32_t* d_flags = nullptr;  // attention: per-warp range-done flags (epoch values)
+    uint32_t attn_epoch = 0;
     size_t ws_slots = 0;  // split-K partial slots (one per split piece)
     size_t slot_bytes = 0;
     Slot slots[kSlots];
@@ -107,10 +108,11 @@ struct lt_kv {
     uint64_t prof_count = 0;
 
     UploadCache cells_cache, items_cache;
-    std::vector<ltkv::Piece> pieces_tmp;
-    std::vector<int32_t> warp_off_tmp, last_tmp;
-    std::vector<int4> combine_tmp;
-    std::vector<char> upload_tmp;
+    std::vector<ltkv::TokenDesc> toks_tmp;
+    std::vector<std::pair<size_t, int32_t>> fold_tmp;  // (table index, previous shadow value)
+    std::vector<uint32_t> fold_mark, fold_pos;         // per sequence, for one call
+    uint32_t fold_epoch = 0;
+    ltkv::AttnParams params{};                         // large (inline descriptors): kept here
     std::vector<int2> cells_tmp;
     uint64_t launches = 0;
 };
@@ -139,6 +141,8 @@ void free_device(lt_kv* kv) {
     cudaFree(kv->d_part_o);
     cudaFree(kv->d_part_ml);
     cudaFree(kv->d_err);
+    cudaFree(kv->d_flags);
+    kv->d_flags = nullptr;
     for (auto& s : kv->slots) {
         if (s.host) cudaFreeHost(s.host);
         if (s.dev) cudaFree(s.dev);
@@ -374,51 +378,62 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
         (k && (reinterpret_cast<uintptr_t>(k) & 15)) || (v && (reinterpret_cast<uintptr_t>(v) & 15)))
         return fail(kv, LT_E_ARG, "q, out, k and v must be 16-byte aligned device pointers");
-    lt_status rc = flush(kv, st);
-    if (rc) return rc;
-    if (n == 0) return LT_OK;
-    // stream-K partition: pieces grouped by warp, warp offsets, split list
+    if (n == 0) return flush(kv, st);
+    // Per-token descriptors; the kernel derives its stream-K partition from them.
     const int q_f32 = q_dtype == LT_F32;
     const int max_warps = ltkv::attend_warps(kv->cfg.device, (int)kv->group, (int)kv->cfg.head_dim, q_f32);
     if (max_warps <= 0) return fail(kv, LT_E_CUDA, "could not size the attention launch on device %d", kv->cfg.device);
-    const size_t pairs = (size_t)n * kv->cfg.n_kv_heads;
-    kv->pieces_tmp.resize(pairs + max_warps);
-    kv->warp_off_tmp.resize((size_t)max_warps + 1);
-    kv->combine_tmp.resize(pairs);
-    const int32_t* last = nullptr;
-    if (fused) {
-        kv->last_tmp.resize(n);
-        for (uint32_t i = 0; i < n; ++i) kv->last_tmp[i] = kv->blocks[seq[i]][pos[i] / kBlock];
-        last = kv->last_tmp.data();
+    kv->toks_tmp.resize(n);
+    long long tiles = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        ltkv::TokenDesc& t = kv->toks_tmp[i];
+        t.seq = (int32_t)seq[i];
+        t.pos = (int32_t)pos[i];
+        t.last_block = kv->blocks[seq[i]][pos[i] / kBlock];
+        t.prefix = (int32_t)tiles;
+        tiles += pos[i] / kBlock + 1;
     }
-    const ltkv::StreamPlan pl = ltkv::plan_stream_k(seq, pos, n, (int)kv->cfg.n_kv_heads, max_warps, last,
-                                                    kv->pieces_tmp.data(), kv->warp_off_tmp.data(),
-                                                    kv->combine_tmp.data());
-    if ((size_t)pl.n_slots > kv->ws_slots)
-        return fail(kv, LT_E_ARG, "attention needs %d partial slots, the handle has %zu", pl.n_slots, kv->ws_slots);
-    // one upload: [pieces][warp offsets, 16-byte padded][split list]
-    const size_t pb = (size_t)pl.n_pieces * sizeof(ltkv::Piece);
-    const size_t wb = (((size_t)pl.n_warps + 1) * sizeof(int32_t) + 15) & ~size_t(15);
-    const size_t cbytes = (size_t)pl.n_combine * sizeof(int4);
-    kv->upload_tmp.resize(pb + wb + cbytes);
-    std::memcpy(kv->upload_tmp.data(), kv->pieces_tmp.data(), pb);
-    std::memcpy(kv->upload_tmp.data() + pb, kv->warp_off_tmp.data(), ((size_t)pl.n_warps + 1) * sizeof(int32_t));
-    if (cbytes) std::memcpy(kv->upload_tmp.data() + pb + wb, kv->combine_tmp.data(), cbytes);
-    const void* d_plan = nullptr;
-    int s_plan = -1;
-    rc = upload(kv, kv->items_cache, kv->upload_tmp.data(), pb + wb + cbytes, st, &d_plan, &s_plan);
-    if (rc) return rc;
-    const char* dp = static_cast<const char*>(d_plan);
-    ltkv::AttnParams p{};
+    if (tiles > 0x7FFFFFFFll / kv->cfg.n_kv_heads) return fail(kv, LT_E_ARG, "attention call too large");
+    // The kernel writes every token's last table entry itself.  For the
+    // highest position of each sequence in the call that entry is read by no
+    // other token from the table, so its pending upload is dropped; the
+    // shadow is restored if the launch fails.
+    kv->fold_tmp.clear();
+    if (++kv->fold_epoch == 0) {  // wrapped: start the marks afresh
+        std::fill(kv->fold_mark.begin(), kv->fold_mark.end(), 0u);
+        kv->fold_epoch = 1;
+    }
+    for (uint32_t i = n; i-- > 0;) {
+        if (kv->fold_mark[seq[i]] == kv->fold_epoch && kv->fold_pos[seq[i]] >= pos[i]) continue;
+        kv->fold_mark[seq[i]] = kv->fold_epoch;
+        kv->fold_pos[seq[i]] = pos[i];
+    }
+    for (uint32_t i = 0; i < n; ++i) {
+        if (kv->fold_pos[seq[i]] != pos[i] || kv->fold_mark[seq[i]] != kv->fold_epoch) continue;
+        kv->fold_mark[seq[i]] = 0;  // once per sequence
+        const size_t idx = (size_t)seq[i] * kv->max_blocks + pos[i] / kBlock;
+        const int32_t val = kv->toks_tmp[i].last_block;
+        if (kv->dev_shadow[idx] != val) {
+            kv->fold_tmp.push_back(std::make_pair(idx, kv->dev_shadow[idx]));
+            kv->dev_shadow[idx] = val;
+        }
+    }
+    lt_status rc = flush(kv, st);
+    auto rollback = [&]() {
+        for (auto& f : kv->fold_tmp) kv->dev_shadow[f.first] = f.second;
+    };
+    if (rc) {
+        rollback();
+        return rc;
+    }
+    ltkv::AttnParams& p = kv->params;
     p.pool_layer = kv->d_pool + (size_t)layer * kv->layer_elems;
     p.pool_layer_w = kv->d_pool + (size_t)layer * kv->layer_elems;
     p.tables = kv->d_tables;
     p.max_blocks = (int32_t)kv->max_blocks;
-    p.pieces = reinterpret_cast<const ltkv::Piece*>(dp);
-    p.warp_off = reinterpret_cast<const int32_t*>(dp + pb);
-    p.n_warps = pl.n_warps;
-    p.combine = reinterpret_cast<const int4*>(dp + pb + wb);
-    p.n_combine = pl.n_combine;
+    p.n_tok = (int32_t)n;
+    p.tiles_per_head = (int32_t)tiles;
+    p.n_warps = (int32_t)std::min<long long>(max_warps, tiles * kv->cfg.n_kv_heads);
     p.n_kv_heads = (int32_t)kv->cfg.n_kv_heads;
     p.group = (int32_t)kv->group;
     p.q = q;
@@ -428,19 +443,39 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     p.scale_log2 = scale * 1.4426950408889634f;
     p.part_o = kv->d_part_o;
     p.part_ml = kv->d_part_ml;
+    p.flags = kv->d_flags;
+    if (++kv->attn_epoch == 0) kv->attn_epoch = 1;  // 0 is the flags' initial value
+    p.epoch = kv->attn_epoch;
     p.err = kv->d_err;
     p.k_new = k;
     p.v_new = v;
     p.kv_f32 = kv_dtype == LT_F32;
+    int s_plan = -1;
+    if (n <= (uint32_t)ltkv::kInlineTokens) {
+        p.toks = nullptr;  // descriptors travel in the kernel parameters
+        std::memcpy(p.inl, kv->toks_tmp.data(), n * sizeof(ltkv::TokenDesc));
+    } else {
+        const void* d_toks = nullptr;
+        rc = upload(kv, kv->items_cache, kv->toks_tmp.data(), n * sizeof(ltkv::TokenDesc), st, &d_toks, &s_plan);
+        if (rc) {
+            rollback();
+            return rc;
+        }
+        p.toks = static_cast<const ltkv::TokenDesc*>(d_toks);
+    }
     cudaEvent_t ev_end = nullptr;
     if (kv->profiling) {
         lt_status prc = prof_begin(kv, st, &ev_end);
         if (prc) return prc;
     }
-    LT_CUDA(kv, ltkv::launch_attend(p, (int)kv->cfg.head_dim, st));
+    const cudaError_t le = ltkv::launch_attend(p, (int)kv->cfg.head_dim, st);
+    if (le != cudaSuccess) {
+        rollback();
+        return fail(kv, LT_E_CUDA, "attention launch: %s", cudaGetErrorString(le));
+    }
     kv->launches += ltkv::attend_launches(p);
     if (ev_end) LT_CUDA(kv, cudaEventRecord(ev_end, st));
-    return mark_slot_use(kv, s_plan, st);
+    return s_plan >= 0 ? mark_slot_use(kv, s_plan, st) : LT_OK;
 }
 
 }  // namespace
@@ -478,6 +513,8 @@ lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
     kv->free_list.resize(kv->n_blocks);
     for (uint32_t i = 0; i < kv->n_blocks; ++i) kv->free_list[i] = (int32_t)(kv->n_blocks - 1 - i);  // kv.rs:45
     kv->dirty_from.assign(c.max_seqs, kClean);
+    kv->fold_mark.assign(c.max_seqs, 0);
+    kv->fold_pos.assign(c.max_seqs, 0);
 
     if (c.device >= 0) {
         kv->dev = true;
@@ -491,11 +528,11 @@ lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
         };
         if (!g.ok) ck(cudaErrorInvalidDevice, "cudaSetDevice");
         const size_t pool_bytes = (size_t)c.n_layers * kv->layer_elems * 2;
-        // Split pieces of one call: at most one per (token, head) plus one per warp.
+        // Partial slots: a warp's first piece may be part of a split sequence.
         const int max_warps = std::max(ltkv::attend_warps(c.device, (int)kv->group, (int)c.head_dim, 1),
                                        ltkv::attend_warps(c.device, (int)kv->group, (int)c.head_dim, 0));
         if (max_warps <= 0) ck(cudaErrorInvalidDevice, "attend_warps");
-        kv->ws_slots = (size_t)c.max_batch * c.n_kv_heads + (size_t)std::max(max_warps, 0);
+        kv->ws_slots = (size_t)std::max(max_warps, 0);  // one partial slot per warp
         const size_t gd = (size_t)kv->group * c.head_dim;
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_pool, std::max<size_t>(pool_bytes, 16)), "cudaMalloc(pool)");
         if (rc == LT_OK) ck(cudaMemset(kv->d_pool, 0, std::max<size_t>(pool_bytes, 16)), "cudaMemset(pool)");
@@ -505,11 +542,11 @@ lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_part_o, kv->ws_slots * gd * sizeof(float)), "cudaMalloc(partials)");
         if (rc == LT_OK)
             ck(cudaMalloc(&kv->d_part_ml, kv->ws_slots * kv->group * 2 * sizeof(float)), "cudaMalloc(partials)");
+        if (rc == LT_OK) ck(cudaMalloc(&kv->d_flags, kv->ws_slots * sizeof(uint32_t) + 4), "cudaMalloc(flags)");
+        if (rc == LT_OK) ck(cudaMemset(kv->d_flags, 0, kv->ws_slots * sizeof(uint32_t) + 4), "cudaMemset(flags)");
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_err, sizeof(int32_t)), "cudaMalloc(err)");
         if (rc == LT_OK) ck(cudaMemset(kv->d_err, 0, sizeof(int32_t)), "cudaMemset(err)");
-        kv->slot_bytes = std::max<size_t>(
-            1u << 20, sizeof(ltkv::Piece) * kv->ws_slots + sizeof(int32_t) * ((size_t)max_warps + 1) +
-                          sizeof(int4) * (size_t)c.max_batch * c.n_kv_heads + 64);
+        kv->slot_bytes = std::max<size_t>(1u << 20, sizeof(ltkv::TokenDesc) * (size_t)c.max_batch + 64);
         for (auto& s : kv->slots) {
             if (rc != LT_OK) break;
             ck(cudaHostAlloc(&s.host, kv->slot_bytes, cudaHostAllocDefault), "cudaHostAlloc(staging)");

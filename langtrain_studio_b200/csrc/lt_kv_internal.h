@@ -9,29 +9,24 @@ namespace ltkv {
 constexpr int kBlock = 16;           // tokens per block (kv.rs:13)
 constexpr int kMaxGroup = 8;         // q heads per KV head the attention kernel handles
 
-// One warp's share of one (token, KV head): blocks [b0, b1) of the token's
-// sequence, which has length pos + 1.  slot >= 0: the (token, head) is split
-// across warps and this piece writes partial `slot`; slot < 0: the piece
-// covers the whole sequence and writes the output.  last_block >= 0: the
-// piece holds the token's last block (physical id last_block) and writes
-// the token's new K/V row there (fused append).
-struct Piece {
-    int32_t tok, h, seq, pos;
-    int32_t b0, b1;
-    int32_t slot;
-    int32_t last_block;
+// Per-token input of one attention launch: the token's sequence, its
+// position (it attends over blocks [0, pos/16]), the physical id of its last
+// block, and the tile prefix P = sum of (pos_j/16 + 1) over tokens j < i.
+struct TokenDesc {
+    int32_t seq, pos, last_block, prefix;
 };
+
+constexpr int kInlineTokens = 512;  // tokens passed inside the kernel parameters
 
 struct AttnParams {
     const uint16_t* pool_layer;  // pool + layer offset
     uint16_t* pool_layer_w;      // same, for the fused append
-    const int32_t* tables;       // [max_seqs][max_blocks]
+    int32_t* tables;             // [max_seqs][max_blocks]; each token's last entry is (re)written
     int32_t max_blocks;
-    const Piece* pieces;         // grouped by warp
-    const int32_t* warp_off;     // warp w owns pieces [warp_off[w], warp_off[w+1])
-    int32_t n_warps;
-    const int4* combine;         // (tok, h, n_pieces, first_slot) per split (token, head)
-    int32_t n_combine;
+    const TokenDesc* toks;       // n_tok entries in global memory, or null: use inl
+    int32_t n_tok;
+    int32_t tiles_per_head;      // prefix of n_tok (total blocks over the tokens)
+    int32_t n_warps;             // stream-K ranges; tile total = tiles_per_head * n_kv_heads
     int32_t n_kv_heads;
     int32_t group;
     const void* q;               // [n][n_heads*D]
@@ -39,12 +34,15 @@ struct AttnParams {
     void* out;                   // [n][n_heads*D]
     int32_t out_f32;
     float scale_log2;            // scale * log2(e)
-    float* part_o;               // [slots][group][D]
-    float* part_ml;              // [slots][group][2]
+    float* part_o;               // [n_warps][group][D]: partial of warp w's first piece
+    float* part_ml;              // [n_warps][group][2]
+    uint32_t* flags;             // [n_warps]: warp w stores `epoch` once its range is done
+    uint32_t epoch;              // distinct per launch on a flags array
     int32_t* err;                // device error flag
-    const void* k_new;           // fused append: new K/V rows [n][n_kv_heads*D]
+    const void* k_new;           // fused append: new K/V rows [n][n_kv_heads*D], or null
     const void* v_new;
     int32_t kv_f32;
+    TokenDesc inl[kInlineTokens];
 };
 
 // Warps of one attention launch on `device` (all resident at once), or 0.

@@ -2,7 +2,6 @@
 //
 //   kv_write_kernel      K1  KvCache::write (kv.rs:123-131): f32/f16 rows -> f16 pool cells
 //   paged_attn_kernel    K2  attention closure of Model::forward (model.rs:431-476)
-//   kv_combine_kernel        merge of split-K partials of K2
 //   apply_plan_kernel    K3/K4  whole-block copies (copy-on-write kv.rs:99-110,
 //                            compaction moves) + block-table scatter
 //   rows_kernel              KvCache::rows (kv.rs:135-150) gather, for parity/debug
@@ -80,6 +79,27 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
         "l"(src), "r"(bytes), "r"(bar)
         : "memory");
+}
+
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Wait until *flag == epoch, giving up after kWaitLimitNs.
+__device__ __forceinline__ int wait_flag_bounded(const uint32_t* flag, uint32_t epoch) {
+    if (ld_acquire_gpu(flag) == epoch) return 1;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        __nanosleep(64);
+        if (ld_acquire_gpu(flag) == epoch) return 1;
+        if (global_ns() - t0 > kWaitLimitNs) return 0;
+    }
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -165,41 +185,42 @@ __global__ void __launch_bounds__(256) kv_write_kernel(uint16_t* __restrict__ po
 }
 
 // ------------------------------------------------------------------ K2 ----
-// Stream-K decode attention.  The host lays the (token, KV head) sequences
-// of a call end to end -- tokens in order, heads within a token, blocks
-// within a head -- and cuts that tile sequence into n_warps contiguous
-// ranges of equal length (+-1 tile).  Warp w processes the pieces of its
-// range: (token, head, blocks [b0, b1)).  A (token, head) cut across warps
-// leaves one (m, l, O) partial per piece, merged by kv_combine_kernel; an
-// uncut one writes its output directly.  No atomics, fences or CTA barriers
-// sit on the data path, and every warp gets the same number of tiles.
+// Stream-K decode attention.  The tokens of a call are laid end to end --
+// tokens in order, KV heads within a token, blocks within a head -- and the
+// tile sequence is cut into n_warps contiguous ranges of equal length (+-1
+// tile).  Every warp derives its range and its pieces (token, head, blocks
+// [b0, b1)) from the per-token descriptors alone; those travel inside the
+// kernel parameters for up to kInlineTokens tokens, so a decode step needs
+// no upload.  An uncut (token, head) writes its output.  A cut one is merged
+// by the warp whose range holds its start: there it is that warp's last
+// piece, whose (m, l, O) stays in registers; its other pieces are the first
+// pieces of the following warps, which write an (m, l, O) partial to their
+// own slot.  Each warp publishes an epoch flag (release) once its range is
+// done; a merging warp then waits (bounded) for its neighbours' flags and
+// combines.  The launch is cooperative, so every warp it waits for is
+// resident.  No atomics, fences or CTA barriers sit on the streaming path.
 //
 // Each warp streams its (block, head) tiles -- 4*16*D contiguous bytes, one
 // cp.async.bulk each, completion on an mbarrier -- through its own
 // kStages-deep ring.  The issuer runs up to kStages tiles ahead of the
 // consumer and at most one piece ahead of it; a piece's q rows are bulk-
 // copied next to its first tile into one of two q buffers (piece parity).
-// Block ids are read 32 at a time (one per lane) a whole window ahead, and
-// piece descriptors one piece ahead, so no dependent global load sits on the
-// stream.  Scores S = Q K^T and O += P V use mma.sync m16n8k16: rows 0..7
+// Block ids are read 32 at a time (one per lane) a whole window ahead; a
+// token's last block id comes from its descriptor, and the warp holding it
+// (head 0) writes that table entry, so new blocks need no separate table
+// upload.  Scores S = Q K^T and O += P V use mma.sync m16n8k16: rows 0..7
 // of the A operand hold the (up to 8) query heads of the KV head rounded to
 // f16, rows 8..15 the f16 rounding residual of the same values, so S and O
 // carry ~22-bit q and P at no extra MMA cost.
 
+// kind: 0 the whole (token, head) -> output; 1 it started before this
+// warp's range (this is the warp's first piece) -> partial slot; 2 it
+// starts in this range and runs past its end (the warp's last piece) ->
+// this warp merges it.
 struct PieceRegs {
-    int tok, h, seq, pos, b0, b1, slot, last_block;
+    int tok, h, seq, pos, b0, b1, kind, last_block;
+    long long ps;  // first tile of the (token, head)
 };
-
-__device__ __forceinline__ void decode_piece(int v, PieceRegs& r) {
-    r.tok = __shfl_sync(kFull, v, 0);
-    r.h = __shfl_sync(kFull, v, 1);
-    r.seq = __shfl_sync(kFull, v, 2);
-    r.pos = __shfl_sync(kFull, v, 3);
-    r.b0 = __shfl_sync(kFull, v, 4);
-    r.b1 = __shfl_sync(kFull, v, 5);
-    r.slot = __shfl_sync(kFull, v, 6);
-    r.last_block = __shfl_sync(kFull, v, 7);
-}
 
 // S = Q K^T, online softmax and O += P V for one staged (block, head) tile.
 template <int D>
@@ -292,7 +313,7 @@ __host__ __device__ inline int attn_smem(int group, int head_dim, int q_f32) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid_constant__ AttnParams p) {
     constexpr int TILE = 2 * kBlock * D * 2;
     constexpr int ROW = D * 2;
     constexpr int KS = D / 16;
@@ -312,41 +333,83 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const AttnPa
     fence_mbar_init();
     __syncwarp();
     if (gw >= p.n_warps) return;
-    const int p_begin = p.warp_off[gw], p_end = p.warp_off[gw + 1];
-    if (p_begin >= p_end) return;
 
+    const TokenDesc* toks = p.toks ? p.toks : p.inl;
+    const long long T = (long long)p.tiles_per_head * Hkv;
+    const long long t0 = T * gw / p.n_warps, t1 = T * (gw + 1) / p.n_warps;
     const int g = lane >> 2, t4 = lane & 3;
     const size_t tile_elems = 2 * kBlock * D;
     const int qelem = p.q_f32 ? 4 : 2;
     const uint32_t qbytes = (uint32_t)(G * D * qelem);
 
-    auto load_desc = [&](int i) {
-        return (i < p_end && lane < 8) ? __ldg(reinterpret_cast<const int*>(p.pieces + i) + lane) : 0;
+    // ---- piece generator over [t0, t1) ----
+    int gi, gh, gb;  // token, head, block of tile gt
+    long long gt = t0;
+    {
+        int lo = 0, hi = p.n_tok - 1;  // last token whose first tile is <= t0
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if ((long long)toks[mid].prefix * Hkv <= t0) lo = mid; else hi = mid - 1;
+        }
+        gi = lo;
+        const TokenDesc td = toks[gi];
+        const int nb = td.pos / kBlock + 1;
+        const long long off = t0 - (long long)td.prefix * Hkv;
+        gh = (int)(off / nb);
+        gb = (int)(off % nb);
+    }
+    auto gen_piece = [&](PieceRegs& r) {  // the piece at the generator, then advance past it
+        const TokenDesc td = toks[gi];
+        const int nb = td.pos / kBlock + 1;
+        const int len = (int)min((long long)(nb - gb), t1 - gt);
+        r.tok = gi;
+        r.h = gh;
+        r.seq = td.seq;
+        r.pos = td.pos;
+        r.b0 = gb;
+        r.b1 = gb + len;
+        r.ps = (long long)td.prefix * Hkv + (long long)gh * nb;
+        r.kind = r.ps < t0 ? 1 : (r.ps + nb > t1 ? 2 : 0);
+        r.last_block = r.b1 == nb ? td.last_block : -1;
+        gt += len;
+        gb += len;
+        if (gb == nb) {
+            gb = 0;
+            if (++gh == Hkv) {
+                gh = 0;
+                ++gi;
+            }
+        }
     };
-    // block ids [b, b + min(32, b1 - b)) of a piece, lane j holding b + j
+    // block ids [b, min(b + 32, b1)) of a piece, lane j holding b + j
     auto load_window = [&](const PieceRegs& r, int b) {
-        return (b + lane < r.b1) ? __ldg(p.tables + (size_t)r.seq * p.max_blocks + b + lane) : 0;
+        const int bb = b + lane;
+        if (bb >= r.b1) return 0;
+        if (bb == r.b1 - 1 && r.last_block >= 0) return r.last_block;
+        return __ldg(p.tables + (size_t)r.seq * p.max_blocks + bb);
     };
 
     // ---- issuer state ----
-    int ii = p_begin;  // issuer piece
-    PieceRegs di{};
-    decode_piece(load_desc(ii), di);
-    int raw_n = load_desc(ii + 1);  // descriptor of piece ii + 1
-    int it = 0;                     // next tile of piece ii to issue (relative to b0)
-    int wb = 0;                     // window base (relative to b0)
+    PieceRegs di{}, dn{};
+    gen_piece(di);
+    bool dn_valid = gt < t1;
+    if (dn_valid) gen_piece(dn);
+    int ii = 0;  // issuer piece ordinal
+    int it = 0;  // next tile of piece di to issue (relative to b0)
+    int wb = 0;  // window base (relative to b0)
     int win = load_window(di, di.b0);
-    int win_n = 0;                  // next window: same piece (wb + 32) or first of piece ii + 1
+    int win_n = 0;  // next window: same piece (wb + 32) or first of piece dn
     auto prefetch_window = [&]() {
-        if (wb + 32 < di.b1 - di.b0) {
-            win_n = load_window(di, di.b0 + wb + 32);
-        } else if (ii + 1 < p_end) {
-            PieceRegs dn;
-            decode_piece(raw_n, dn);
-            win_n = load_window(dn, dn.b0);
-        }
+        if (wb + 32 < di.b1 - di.b0) win_n = load_window(di, di.b0 + wb + 32);
+        else if (dn_valid) win_n = load_window(dn, dn.b0);
     };
     prefetch_window();
+    auto table_write = [&](const PieceRegs& r) {
+        // the token's last block entry, written once per token (head 0)
+        if (r.h == 0 && r.last_block >= 0 && lane == 0)
+            p.tables[(size_t)r.seq * p.max_blocks + r.b1 - 1] = r.last_block;
+    };
+    table_write(di);
 
     int issued = 0, consumed = 0;
     auto issue_one = [&]() {
@@ -370,18 +433,20 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const AttnPa
         ++it;
         ++issued;
     };
-    auto issuer_advance = [&]() {  // piece ii is fully issued; move to ii + 1
+    auto issuer_advance = [&]() {  // piece di is fully issued; move to dn
         ++ii;
-        decode_piece(raw_n, di);
-        raw_n = load_desc(ii + 1);
+        di = dn;
+        dn_valid = gt < t1;
+        if (dn_valid) gen_piece(dn);
         it = 0;
         wb = 0;
         win = win_n;
         prefetch_window();
+        table_write(di);
     };
 
     // ---- consumer state ----
-    int ci = p_begin;
+    int ci = 0;
     PieceRegs dc = di;
     int ct = 0;
     // The issuer stays within one piece of the consumer (two q buffers).
@@ -391,7 +456,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const AttnPa
                 issue_one();
                 continue;
             }
-            if (ii != ci || ii + 1 >= p_end) break;
+            if (ii != ci || !dn_valid) break;
             issuer_advance();
         }
     };
@@ -440,7 +505,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const AttnPa
         const int b = dc.b0 + ct;
         const int valid = min(kBlock, dc.pos + 1 - b * kBlock);
         bool touched = false;
-        if (dc.last_block >= 0 && b == dc.pos / kBlock) {
+        if (p.k_new && dc.last_block >= 0 && b == dc.b1 - 1) {
             // Fused append: this token's new K/V row for head h goes to its
             // pool cell and into the staged tile (the copy read the old bytes).
             constexpr int CH = D / 8;
@@ -474,13 +539,14 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const AttnPa
         __syncwarp();
 
         if (ct == dc.b1 - dc.b0) {
-            // ---- piece done: output, or a partial for kv_combine_kernel ----
+            // ---- piece done ----
+            if (dc.kind == 2) break;  // the range's last piece: merged after the loop
             float l = l_run;
             l += __shfl_xor_sync(kFull, l, 1);
             l += __shfl_xor_sync(kFull, l, 2);
             const size_t GD = (size_t)G * D;
             if (g < G) {
-                if (dc.slot < 0) {
+                if (dc.kind == 0) {
                     const size_t ob = ((size_t)dc.tok * Hkv + dc.h) * GD + (size_t)g * D + 2 * t4;
                     const float inv = 1.f / l;
 #pragma unroll
@@ -493,7 +559,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const AttnPa
                                 __floats2half2_rn(v0, v1);
                     }
                 } else {
-                    const size_t sl = (size_t)dc.slot;
+                    const size_t sl = (size_t)gw;  // partial slot of this warp (its first piece)
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt)
                         *reinterpret_cast<float2*>(p.part_o + sl * GD + (size_t)g * D + nt * 8 + 2 * t4) =
@@ -508,8 +574,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const AttnPa
             for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
             m_run = -INFINITY;
             l_run = 0.f;
-            if (ci + 1 >= p_end) break;  // every issued tile has been consumed
-            if (ii == ci) issuer_advance();
+            if (ii == ci) {
+                if (!dn_valid) break;  // last piece of the range: every issued tile is consumed
+                issuer_advance();
+            }
             ++ci;
             dc = di;
             ct = 0;
@@ -521,38 +589,62 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const AttnPa
         for (int jj = consumed + 1; jj < issued; ++jj) mbar_wait_bounded(bar0 + 8u * (jj % S), (jj / S) & 1);
         if (lane == 0) atomicExch(p.err, 1);
     }
-}
+    // Publish: every partial this warp wrote is visible before its flag.
+    __syncwarp();
+    if (lane == 0) st_release_gpu(p.flags + gw, p.epoch);
+    if (!ok || dc.kind != 2 || ct != dc.b1 - dc.b0) return;
 
-// Merge the (m, l, O) partials of every split (token, KV head).  One thread
-// per output element (pair, g, d); the pieces of a pair are few, so every
-// load is independent and the kernel is a short bandwidth-bound pass.  It is
-// launched as a programmatic dependent of the attention kernel and waits for
-// that grid's completion before its first read.
-template <int D>
-__global__ void __launch_bounds__(256) kv_combine_kernel(const AttnParams p) {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int G = p.group, Hkv = p.n_kv_heads;
-    const int GD = G * D;
-    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (long long)p.n_combine * GD) return;
-    const int pair = (int)(idx / GD), e = (int)(idx % GD), gg = e / D;
-    const int4 c = __ldg(p.combine + pair);  // (tok, h, n_pieces, first_slot)
-    const float* ml = p.part_ml + ((size_t)c.w * G + gg) * 2;
-    const float* po = p.part_o + (size_t)c.w * GD + e;
-    float M = -INFINITY;
-    for (int j = 0; j < c.z; ++j) M = fmaxf(M, __ldcg(ml + (size_t)j * G * 2));
-    float L = 0.f, O = 0.f;
-    for (int j = 0; j < c.z; ++j) {
-        const float sw = ex2(__ldcg(ml + (size_t)j * G * 2) - M);
-        L += __ldcg(ml + (size_t)j * G * 2 + 1) * sw;
-        O += __ldcg(po + (size_t)j * GD) * sw;
+    // ---- merge the cut (token, head) this range ends with ----
+    const long long NW = p.n_warps;
+    const int nb = dc.pos / kBlock + 1;
+    const int w_last = (int)(((dc.ps + nb) * NW - 1) / T);  // warp holding its last tile
+    int ready = 1;
+    if (lane == 0)
+        for (int w = gw + 1; w <= w_last && ready; ++w) ready = wait_flag_bounded(p.flags + w, p.epoch);
+    ready = __shfl_sync(kFull, ready, 0);
+    __syncwarp();
+    if (!ready) {
+        if (lane == 0) atomicExch(p.err, 1);
+        return;
     }
-    const float r = O / L;
-    const size_t o = ((size_t)c.x * Hkv + c.y) * GD + e;
-    if (p.out_f32)
-        static_cast<float*>(p.out)[o] = r;
-    else
-        static_cast<__half*>(p.out)[o] = __float2half_rn(r);
+    float l = l_run;
+    l += __shfl_xor_sync(kFull, l, 1);
+    l += __shfl_xor_sync(kFull, l, 2);
+    if (g < G) {
+        const size_t GD = (size_t)G * D;
+        float M = m_run;
+        for (int w = gw + 1; w <= w_last; ++w) M = fmaxf(M, __ldcg(p.part_ml + ((size_t)w * G + g) * 2));
+        const float own = ex2(m_run - M);
+        float L = l * own;
+        float acc[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            acc[nt][0] = (o[nt][0] + o[nt][2]) * own;
+            acc[nt][1] = (o[nt][1] + o[nt][3]) * own;
+        }
+        for (int w = gw + 1; w <= w_last; ++w) {
+            const float sw = ex2(__ldcg(p.part_ml + ((size_t)w * G + g) * 2) - M);
+            L += __ldcg(p.part_ml + ((size_t)w * G + g) * 2 + 1) * sw;
+            const float* po = p.part_o + (size_t)w * GD + (size_t)g * D + 2 * t4;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const float2 v2 = __ldcg(reinterpret_cast<const float2*>(po + nt * 8));
+                acc[nt][0] += v2.x * sw;
+                acc[nt][1] += v2.y * sw;
+            }
+        }
+        const float inv = 1.f / L;
+        const size_t ob = ((size_t)dc.tok * Hkv + dc.h) * GD + (size_t)g * D + 2 * t4;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            if (p.out_f32)
+                *reinterpret_cast<float2*>(static_cast<float*>(p.out) + ob + nt * 8) =
+                    make_float2(acc[nt][0] * inv, acc[nt][1] * inv);
+            else
+                *reinterpret_cast<__half2*>(static_cast<__half*>(p.out) + ob + nt * 8) =
+                    __floats2half2_rn(acc[nt][0] * inv, acc[nt][1] * inv);
+        }
+    }
 }
 
 // -------------------------------------------------------------- K3/K4 ----
@@ -646,23 +738,12 @@ cudaError_t launch_attend_d(const AttnParams& p, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if ((e = ensure_attr<D>(dev)) != cudaSuccess) return e;
-    const int grid = (p.n_warps + kWarps - 1) / kWarps;
-    paged_attn_kernel<D><<<grid, kWarps * 32, attn_smem(p.group, D, p.q_f32), s>>>(p);
-    if ((e = cudaGetLastError()) != cudaSuccess || p.n_combine == 0) return e;
-    // programmatic dependent launch: the combine grid is set up while the
-    // attention grid runs and starts reading once it has completed
-    const long long threads = (long long)p.n_combine * p.group * D;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((threads + 255) / 256));
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kv_combine_kernel<D>, p);
+    // Cooperative: merging warps wait for other CTAs' flags, so the whole
+    // grid (sized to the resident capacity) must be co-resident.
+    const dim3 grid((p.n_warps + kWarps - 1) / kWarps), block(kWarps * 32);
+    void* args[] = {const_cast<AttnParams*>(&p)};
+    return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&paged_attn_kernel<D>), grid, block, args,
+                                       attn_smem(p.group, D, p.q_f32), s);
 }
 
 }  // namespace
@@ -682,10 +763,7 @@ cudaError_t launch_attend(const AttnParams& p, int head_dim, cudaStream_t s) {
     return head_dim == 64 ? launch_attend_d<64>(p, s) : launch_attend_d<128>(p, s);
 }
 
-int attend_launches(const AttnParams& p) {
-    if (p.n_warps == 0) return 0;
-    return p.n_combine > 0 ? 2 : 1;
-}
+int attend_launches(const AttnParams& p) { return p.n_warps == 0 ? 0 : 1; }
 
 cudaError_t launch_write(uint16_t* pool_layer, const int2* cells, int n, int n_kv_heads, int head_dim, const void* k,
                          const void* v, int in_f32, cudaStream_t s) {

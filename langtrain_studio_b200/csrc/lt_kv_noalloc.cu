@@ -30,24 +30,22 @@
 
 #include "lt_kv.h"
 #include "lt_kv_internal.h"
-#include "lt_kv_plan.h"
 
 namespace {
 
 constexpr size_t kScratchBytes = LT_NOALLOC_SCRATCH_BYTES;
 constexpr int kMaxDevices = 64;
-// Host-side plan buffers (file scope, guarded by a mutex): the stream-K
-// pieces, per-warp offsets and split list of one call.
-constexpr int kMaxPieces = 8192;
-constexpr int kMaxWarps = 4096;
 
 static __device__ __align__(256) unsigned char lt_noalloc_scratch[kScratchBytes];
 
 std::atomic<void*> g_scratch[kMaxDevices];
-std::mutex g_plan_mu;
-ltkv::Piece g_pieces[kMaxPieces];
-int32_t g_warp_off[kMaxWarps + 1];
-int4 g_combine[kMaxPieces];
+// Host-side descriptors of one call (file scope, guarded by a mutex): the
+// launch parameters carry up to kInlineTokens of them, the rest go through
+// the scratch array.
+std::mutex g_mu;
+uint32_t g_epoch[kMaxDevices];  // per-device launch epoch for the range-done flags
+ltkv::AttnParams g_params;
+ltkv::TokenDesc g_toks[LT_NOALLOC_MAX_TOKENS];
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -82,57 +80,67 @@ extern "C" lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_
     if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) return LT_E_ARG;
     if (n == 0) return LT_OK;
     if (n > LT_NOALLOC_MAX_TOKENS) return LT_E_SCRATCH;
-    for (uint32_t i = 0; i < n; ++i)
+    long long tiles = 0;
+    for (uint32_t i = 0; i < n; ++i) {
         if ((pos[i] + ltkv::kBlock) / ltkv::kBlock > max_blocks_per_seq) return LT_E_ARG;
+        tiles += pos[i] / ltkv::kBlock + 1;
+    }
+    if (tiles > 0x7FFFFFFFll / n_kv_heads) return LT_E_SCRATCH;
 
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return LT_E_CUDA;
     const int q_f32 = q_dtype == LT_F32;
-    const int max_warps = std::min(ltkv::attend_warps(dev, (int)group, (int)head_dim, q_f32), kMaxWarps);
-    if (max_warps <= 0) return LT_E_CUDA;
-    const size_t pairs = (size_t)n * n_kv_heads;
-    if (pairs + (size_t)max_warps > (size_t)kMaxPieces) return LT_E_SCRATCH;
+    int n_warps = ltkv::attend_warps(dev, (int)group, (int)head_dim, q_f32);
+    if (n_warps <= 0) return LT_E_CUDA;
+    n_warps = (int)std::min<long long>(n_warps, tiles * n_kv_heads);
 
-    std::lock_guard<std::mutex> lock(g_plan_mu);
-    const ltkv::StreamPlan pl =
-        ltkv::plan_stream_k(seq, pos, n, (int)n_kv_heads, max_warps, nullptr, g_pieces, g_warp_off, g_combine);
-
-    // Scratch layout: [error word][pieces][warp offsets][split list]
-    // [partial (m, l)][partial O], each 256-byte aligned.
+    // Scratch layout: [error word][descriptors beyond the inline ones]
+    // [range-done flags][partial (m, l)][partial O], 256-byte aligned; one
+    // flag and one partial slot per warp.  Fewer warps are used when the
+    // partials would not fit.
     const size_t gd = (size_t)group * head_dim;
-    const size_t o_pieces = 256;
-    const size_t o_warp = o_pieces + round256((size_t)pl.n_pieces * sizeof(ltkv::Piece));
-    const size_t o_comb = o_warp + round256(((size_t)pl.n_warps + 1) * sizeof(int32_t));
-    const size_t o_ml = o_comb + round256((size_t)pl.n_combine * sizeof(int4));
-    const size_t o_o = o_ml + round256((size_t)pl.n_slots * group * 2 * sizeof(float));
-    const size_t need = o_o + round256((size_t)pl.n_slots * gd * sizeof(float));
-    if (need > kScratchBytes) return LT_E_SCRATCH;
+    const size_t o_toks = 256;
+    const size_t o_flags = o_toks + round256(n > (uint32_t)ltkv::kInlineTokens ? n * sizeof(ltkv::TokenDesc) : 0);
+    const size_t per_warp = sizeof(uint32_t) + group * 2 * sizeof(float) + gd * sizeof(float);
+    if (o_flags + 1024 + per_warp > kScratchBytes) return LT_E_SCRATCH;
+    n_warps = (int)std::min<size_t>((size_t)n_warps, (kScratchBytes - o_flags - 1024) / per_warp);
+    const size_t o_ml = o_flags + round256((size_t)n_warps * sizeof(uint32_t));
+    const size_t o_o = o_ml + round256((size_t)n_warps * group * 2 * sizeof(float));
 
     void* base = nullptr;
     if (scratch_ptr(&base) != cudaSuccess) return LT_E_CUDA;
     unsigned char* b = static_cast<unsigned char*>(base);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+    std::lock_guard<std::mutex> lock(g_mu);
+    ltkv::AttnParams& p = g_params;
+    long long prefix = 0;
+    ltkv::TokenDesc* td = n <= (uint32_t)ltkv::kInlineTokens ? p.inl : g_toks;
+    for (uint32_t i = 0; i < n; ++i) {
+        td[i].seq = (int32_t)seq[i];
+        td[i].pos = (int32_t)pos[i];
+        td[i].last_block = -1;  // unknown here: the kernel reads every block id from the tables
+        td[i].prefix = (int32_t)prefix;
+        prefix += pos[i] / ltkv::kBlock + 1;
+    }
     // The error word must start at zero; the array keeps the previous call's bytes.
     if (cudaMemsetAsync(b, 0, sizeof(int32_t), st) != cudaSuccess) return LT_E_CUDA;
-    // Pageable sources: each call returns once its bytes are staged.
-    if (cudaMemcpyAsync(b + o_pieces, g_pieces, (size_t)pl.n_pieces * sizeof(ltkv::Piece), cudaMemcpyHostToDevice,
-                        st) != cudaSuccess ||
-        cudaMemcpyAsync(b + o_warp, g_warp_off, ((size_t)pl.n_warps + 1) * sizeof(int32_t), cudaMemcpyHostToDevice,
-                        st) != cudaSuccess ||
-        (pl.n_combine && cudaMemcpyAsync(b + o_comb, g_combine, (size_t)pl.n_combine * sizeof(int4),
-                                         cudaMemcpyHostToDevice, st) != cudaSuccess))
-        return LT_E_CUDA;
-
-    ltkv::AttnParams p{};
+    if (td == g_toks) {
+        // Pageable source: the call returns once the bytes are staged.
+        if (cudaMemcpyAsync(b + o_toks, g_toks, n * sizeof(ltkv::TokenDesc), cudaMemcpyHostToDevice, st) !=
+            cudaSuccess)
+            return LT_E_CUDA;
+        p.toks = reinterpret_cast<const ltkv::TokenDesc*>(b + o_toks);
+    } else {
+        p.toks = nullptr;
+    }
     p.pool_layer = static_cast<const uint16_t*>(pool_layer);
     p.pool_layer_w = nullptr;  // no fused append on this entry point
-    p.tables = tables;
+    p.tables = const_cast<int32_t*>(tables);  // not written: no descriptor carries a last block id
     p.max_blocks = (int32_t)max_blocks_per_seq;
-    p.pieces = reinterpret_cast<const ltkv::Piece*>(b + o_pieces);
-    p.warp_off = reinterpret_cast<const int32_t*>(b + o_warp);
-    p.n_warps = pl.n_warps;
-    p.combine = reinterpret_cast<const int4*>(b + o_comb);
-    p.n_combine = pl.n_combine;
+    p.n_tok = (int32_t)n;
+    p.tiles_per_head = (int32_t)tiles;
+    p.n_warps = n_warps;
     p.n_kv_heads = (int32_t)n_kv_heads;
     p.group = (int32_t)group;
     p.q = q;
@@ -142,6 +150,11 @@ extern "C" lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_
     p.scale_log2 = scale * 1.4426950408889634f;
     p.part_ml = reinterpret_cast<float*>(b + o_ml);
     p.part_o = reinterpret_cast<float*>(b + o_o);
+    // The flags keep the last call's epochs: a fresh epoch per call on this
+    // device (the array starts zeroed, and 0 is never used).
+    p.flags = reinterpret_cast<uint32_t*>(b + o_flags);
+    if (++g_epoch[dev] == 0) g_epoch[dev] = 1;
+    p.epoch = g_epoch[dev];
     // A bounded wait that gives up sets the error word (first int32 of the
     // array) and leaves this call's outputs invalid; nothing synchronises
     // here to report it, and the next call clears it.
