@@ -586,6 +586,250 @@ def run_c4(args, rank, world, local, mode):
     return res
 
 
+class ChurnDriver:
+    """continuous batching with the reference scheduler's KV
+    policy, restated in blocks over the C ABI (engine/crates/engine/src/
+    scheduler.rs:252-473, prefix.rs:58-125):
+      - admit FIFO into the least recently used idle slot while the prompt
+        plus min(output, DECODE_HEADROOM=256) tokens fit, evicting idle
+        slots' cached KV LRU first (kv_remove(slot, 0));
+      - each step: one decode token per sequence past its prompt, prompt
+        chunks of at most 256 tokens (EngineConfig.prefill_chunk);
+      - before the step, free enough blocks: evict LRU idle, then preempt the
+        youngest running sequence (it finishes with Length);
+      - retire: a finished slot keeps its KV for prefix reuse (idle);
+      - compaction every step (no reference counterpart).
+    Prompt ids are random, so no prefix is ever reused; prompt tokens are
+    appended and their K/V written, decode tokens run the fused
+    append + attention launch (prefill attention is a later addition)."""
+
+    HEADROOM = 256
+    CHUNK = 256
+
+    def __init__(self, kv, n_slots, lam, seed, kv_src, q_src, prompt_lo=64, prompt_hi=8192, out_lo=16, out_hi=512):
+        self.kv = kv
+        self.rng = np.random.default_rng(seed)
+        self.lam = lam
+        self.lo, self.hi, self.olo, self.ohi = prompt_lo, prompt_hi, out_lo, out_hi
+        self.busy = np.zeros(n_slots, bool)
+        self.held = np.zeros(n_slots, np.int64)  # tokens an idle slot keeps
+        self.last_used = np.zeros(n_slots, np.int64)
+        self.clock = 0
+        self.queue = []
+        self.active = {}  # slot -> [n_past, prompt, total, admit_step]
+        self.step_no = 0
+        self.kv_src, self.q_src = kv_src, q_src  # device tensors the K/V/q rows are cut from
+        self.stats = dict(decode=0, prefill=0, evicted=0, preempted=0, moved=0, admitted=0, finished=0)
+
+    def _evict_lru_idle(self):
+        idle = np.nonzero(~self.busy & (self.held > 0))[0]
+        if idle.size == 0:
+            return False
+        i = int(idle[np.argmin(self.last_used[idle])])
+        self.kv.truncate(i, 0)
+        self.held[i] = 0
+        self.stats["evicted"] += 1
+        return True
+
+    def _retire(self, slot, n_past):
+        self.busy[slot] = False
+        self.held[slot] = n_past
+        self.clock += 1
+        self.last_used[slot] = self.clock
+        del self.active[slot]
+
+    def arrivals(self):
+        for _ in range(self.rng.poisson(self.lam)):
+            prompt = int(np.exp(self.rng.uniform(np.log(self.lo), np.log(self.hi))))
+            out = int(self.rng.integers(self.olo, self.ohi + 1))
+            self.queue.append((prompt, out))
+
+    def admit(self):
+        while self.queue:
+            idle = np.nonzero(~self.busy)[0]
+            if idle.size == 0:
+                break
+            prompt, out = self.queue[0]
+            need = (prompt + min(out, self.HEADROOM) + BLOCK - 1) // BLOCK
+            while self.kv.free_blocks() < need and self._evict_lru_idle():
+                pass
+            if self.kv.free_blocks() < need and self.active:
+                break
+            self.queue.pop(0)
+            idle = np.nonzero(~self.busy)[0]
+            slot = int(idle[np.argmin(self.last_used[idle])])
+            self.kv.truncate(slot, 0)  # kv_remove(slot, reuse = 0): random prompts share nothing
+            self.held[slot] = 0
+            self.busy[slot] = True
+            self.clock += 1
+            self.last_used[slot] = self.clock
+            self.active[slot] = [0, prompt, prompt + out, self.step_no]
+            self.stats["admitted"] += 1
+
+    def plan(self):
+        """(slot, first position, token count) of this step's batch."""
+        dec, pre = [], []
+        for slot, (n_past, prompt, total, _) in self.active.items():
+            if n_past >= prompt:
+                dec.append((slot, n_past, 1))
+            else:
+                pre.append((slot, n_past, min(self.CHUNK, prompt - n_past)))
+        return dec, pre
+
+    @staticmethod
+    def _new_blocks(items):
+        n = 0
+        for _, p0, cnt in items:
+            n += (p0 + cnt + BLOCK - 1) // BLOCK - (p0 + BLOCK - 1) // BLOCK
+        return n
+
+    def ensure_room(self):
+        while True:
+            dec, pre = self.plan()
+            need = self._new_blocks(dec) + self._new_blocks(pre)
+            if self.kv.free_blocks() >= need:
+                return dec, pre
+            if self._evict_lru_idle():
+                continue
+            youngest = max(self.active, key=lambda s: self.active[s][3])
+            self.kv.truncate(youngest, 0)  # preempted: finishes with Length, nothing kept
+            self.busy[youngest] = False
+            self.held[youngest] = 0
+            del self.active[youngest]
+            self.stats["preempted"] += 1
+
+    def step(self, out):
+        """One scheduler step; returns the number of decode tokens."""
+        self.step_no += 1
+        self.arrivals()
+        self.admit()
+        dec, pre = self.ensure_room()
+        kv = self.kv
+        if pre:
+            seqs = np.concatenate([np.full(c, s) for s, _, c in pre])
+            pos = np.concatenate([np.arange(p0, p0 + c) for _, p0, c in pre])
+            b, sl = kv.append_batch(seqs, pos)
+            n = seqs.size
+            off = int(self.rng.integers(0, self.kv_src.shape[0] - n + 1))
+            kv.write(0, b, sl, self.kv_src[off:off + n], self.kv_src[off:off + n])
+            self.stats["prefill"] += n
+        nd = len(dec)
+        if dec:
+            seqs = np.array([s for s, _, _ in dec], np.uint32)
+            pos = np.array([p for _, p, _ in dec], np.uint32)
+            b, sl = kv.append_batch(seqs, pos)
+            off = int(self.rng.integers(0, self.kv_src.shape[0] - nd + 1))
+            kv.write_attend(0, b, sl, self.kv_src[off:off + nd], self.kv_src[off:off + nd], self.q_src[:nd], seqs,
+                            pos, out=out[:nd])
+            self.stats["decode"] += nd
+        for s, p0, c in dec + pre:
+            st = self.active[s]
+            st[0] = p0 + c
+            if st[0] >= st[2]:
+                self._retire(s, st[0])
+                self.stats["finished"] += 1
+        self.stats["moved"] += kv.compact()
+        return nd
+
+
+def run_c5(args, rank, world, local):
+    """continuous-batching churn, Llama-3-8B attention shape, one
+    layer; arrivals Poisson(32/N) per rank and step (sequence-sharded), prompts
+    log-uniform in [64, 8192], outputs U[16, 512], block pool at 60 % of the
+    peak demand of an uncapped dry run."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from langtrain_studio_b200 import kv as kv_mod
+
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    lam = args.c5_rate / world
+    seed = shard_seed(rank)
+    hq, hkv, d = 32, 8, 128
+    # uncapped dry run of the same arrival/length process: peak blocks held by running sequences
+    rng = np.random.default_rng(seed)
+    live, peak = [], 0
+    for _ in range(args.warmup + args.steps):
+        for _ in range(rng.poisson(lam)):
+            prompt = int(np.exp(rng.uniform(np.log(64), np.log(8192))))
+            live.append([prompt, prompt + int(rng.integers(16, 513)), 0])
+        nxt = []
+        for r in live:  # [prompt, total, n_past]
+            r[2] = min(r[2] + ChurnDriver.CHUNK, r[0]) if r[2] < r[0] else r[2] + 1
+            if r[2] < r[1]:
+                nxt.append(r)
+        live = nxt
+        peak = max(peak, sum((r[2] + BLOCK - 1) // BLOCK for r in live))
+    pool = max(int(0.6 * peak), 64)
+    n_slots = 16384
+    max_blocks = (8192 + 512 + 2 * BLOCK) // BLOCK
+    kv = kv_mod.KvCache(1, hkv, d, pool * BLOCK, n_heads=hq, max_seqs=n_slots, max_batch=1 << 17,
+                        max_blocks_per_seq=max_blocks, device=local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    kv_src = torch.randn((1 << 17, hkv * d), generator=g, device=dev, dtype=torch.float16)
+    q_src = torch.randn((n_slots, hq * d), generator=g, device=dev, dtype=torch.float16)
+    out = torch.empty((n_slots, hq * d), device=dev, dtype=torch.float16)
+    drv = ChurnDriver(kv, n_slots, lam, seed, kv_src, q_src)
+    for _ in range(args.warmup):
+        drv.step(out)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s0 = dict(drv.stats)
+    kv.profile(True)
+    l0 = kv.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    for _ in range(args.steps):
+        drv.step(out)
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    if world > 1:
+        dist.barrier()
+    ms = reduce_max(e0.elapsed_time(e1), dev, world)
+    attn_ms, attn_n = kv.profile_read()
+    kv.check()
+    delta = {k: drv.stats[k] - s0[k] for k in drv.stats}
+    tot = torch.tensor([float(delta["decode"]), float(delta["prefill"]), float(delta["moved"])], device=dev,
+                       dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tot)
+    res = None
+    if rank == 0:
+        moved_bytes = tot[2].item() * hkv * d * 2 * BLOCK * 2 * 2  # K+V block, read + write
+        res = _json_common(args, world, tot[0].item() / (ms * 1e-3), "tokens/s", ms / args.steps, {
+            "workload": "configs[4]: continuous-batching churn, Llama-3-8B attention shape, one layer, "
+                        f"Poisson({args.c5_rate:g}) arrivals/step over {world} rank(s), prompts log-U[64,8192], "
+                        "outputs U[16,512], pool 60% of peak demand, compaction every step",
+            "n_heads": hq, "n_kv_heads": hkv, "head_dim": d, "block_tokens": BLOCK,
+            "pool_blocks_per_rank": pool, "parallelism": f"seq-sharded x{world}"})
+        res.update({
+            "decode_tokens_per_s": tot[0].item() / (ms * 1e-3),
+            "prefill_tokens_per_s": tot[1].item() / (ms * 1e-3),
+            "rank0": {"steps": args.steps, "decode": delta["decode"], "prefill": delta["prefill"],
+                      "admitted": delta["admitted"], "finished": delta["finished"], "evicted": delta["evicted"],
+                      "preempted": delta["preempted"], "moved_blocks": delta["moved"], "attn_ms_per_step":
+                      attn_ms / max(attn_n, 1), "host_wall_ms_per_step": wall * 1e3 / args.steps},
+            "compaction_gb_moved_per_s": moved_bytes / (ms * 1e-3) / 1e9,
+            "gpu_launches": kv.launch_count() - l0,
+        })
+    if world > 1:
+        dist.barrier()
+        kv.close()
+        dist.destroy_process_group()
+    else:
+        kv.close()
+    return res
+
+
 # ---------------------------------------------------------------------------
 # CPU arm (restated reference path)
 
@@ -656,6 +900,8 @@ def run_reference(args, rank, world):
     # sequences), bounded to ~60 s in total.
     from oracle import oracle as ok_mod  # noqa: F401  (builds the oracle if needed)
 
+    if args.warmup > 0:
+        cpu_run(lens, 1234, budget_s=30.0, max_steps=args.warmup, threads=threads)  # untimed warm-up
     value, steps, dt = cpu_run(lens, 1234, budget_s=60.0, max_steps=max(args.steps, 1), threads=threads)
     sample = (f"{steps} full steps (64 seqs, one layer: append + f32->f16 write + attention) in {dt:.1f} s, "
               f"{threads} threads on {cpu_desc()}")
@@ -681,8 +927,9 @@ def main():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c3", "c4-batch", "c4-head"], default="c2",
-                    help="c2: configs[1] (default, the headline); c3: configs[2]; c4-*: configs[3]")
+    ap.add_argument("--config", choices=["c2", "c3", "c4-batch", "c4-head", "c5"], default="c2",
+                    help="c2: configs[1] (default, the headline); c3: configs[2]; c4-*: configs[3]; c5: configs[4]")
+    ap.add_argument("--c5-rate", type=float, default=32.0, help="c5: mean arrivals per step over the whole job")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="CPU-baseline sample budget in seconds (rank 0, N=1); 0 skips it")
     args = ap.parse_args()
@@ -694,6 +941,11 @@ def main():
         return
     if args.config == "c3":
         res = run_c3(args, rank, world, local)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
+    if args.config == "c5":
+        res = run_c5(args, rank, world, local)
         if rank == 0:
             print(json.dumps(res), flush=True)
         return
