@@ -203,15 +203,20 @@ class Stepper:
     """One decode step through the public API: append + fused write/attend."""
 
     def __init__(self, kv, lens, k, v, q, out):
+        import ctypes
+
+        import torch
+
         self.kv, self.lens = kv, lens
         self.seqs = np.arange(len(lens), dtype=np.uint32)
         self.k, self.v, self.q, self.out = k, v, q, out
         self.phase = 0
+        self.stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
     def step(self):
         pos = (self.lens + self.phase).astype(np.uint32)
-        b, s = self.kv.append_batch(self.seqs, pos)
-        self.kv.write_attend(0, b, s, self.k, self.v, self.q, self.seqs, pos, out=self.out)
+        b, s = self.kv.append_batch(self.seqs, pos, stream=self.stream)
+        self.kv.write_attend(0, b, s, self.k, self.v, self.q, self.seqs, pos, out=self.out, stream=self.stream)
         lens_now = self.lens + self.phase + 1
         self.phase += 1
         if self.phase == CYCLE:
@@ -238,9 +243,14 @@ def run_ours(args, rank, world, local):
     kv = build_cache(kv_mod, torch, local, lens, seed)
     g = torch.Generator(device=dev)
     g.manual_seed(seed + 7)
-    k = torch.randn((BATCH, N_KV_HEADS * HEAD_DIM), generator=g, device=dev, dtype=torch.float16)
-    v = torch.randn((BATCH, N_KV_HEADS * HEAD_DIM), generator=g, device=dev, dtype=torch.float16)
-    q = torch.randn((BATCH, N_HEADS * HEAD_DIM), generator=g, device=dev, dtype=torch.float16)
+    # q, k and v of a step live in one buffer, so the end-to-end path moves
+    # them with one host->device copy
+    kvd, qd = N_KV_HEADS * HEAD_DIM, N_HEADS * HEAD_DIM
+    packed = torch.randn((BATCH, 2 * kvd + qd), generator=g, device=dev, dtype=torch.float16)
+    flat = packed.view(-1)
+    k = flat[: BATCH * kvd].view(BATCH, kvd)
+    v = flat[BATCH * kvd: 2 * BATCH * kvd].view(BATCH, kvd)
+    q = flat[2 * BATCH * kvd:].view(BATCH, qd)
     out = torch.empty((BATCH, N_HEADS * HEAD_DIM), device=dev, dtype=torch.float16)
     st = Stepper(kv, lens, k, v, q, out)
 
@@ -284,20 +294,14 @@ def run_ours(args, rank, world, local):
     kv.check()
     ms_max = reduce_max(ms, dev, world)
     # ---------------- end-to-end through the public API ----------------
-    hq = torch.empty_like(q, device="cpu").pin_memory()
-    hk = torch.empty_like(k, device="cpu").pin_memory()
-    hv = torch.empty_like(v, device="cpu").pin_memory()
+    hpacked = torch.empty_like(packed, device="cpu").pin_memory()
     hout = torch.empty_like(out, device="cpu").pin_memory()
-    hq.copy_(q)
-    hk.copy_(k)
-    hv.copy_(v)
+    hpacked.copy_(packed)
     stream = torch.cuda.current_stream()
     e2e_steps = args.steps
 
     def e2e_step():
-        q.copy_(hq, non_blocking=True)
-        k.copy_(hk, non_blocking=True)
-        v.copy_(hv, non_blocking=True)
+        packed.copy_(hpacked, non_blocking=True)  # this step's q, k, v
         st.step()
         hout.copy_(out, non_blocking=True)
         stream.synchronize()  # the host reads this step's result
@@ -316,7 +320,7 @@ def run_ours(args, rank, world, local):
     barrier()
     e2e_ms = f0.elapsed_time(f1)
     e2e_ms = reduce_max(e2e_ms, dev, world)
-    h2d = (q.numel() + k.numel() + v.numel()) * 2
+    h2d = packed.numel() * 2
     d2h = out.numel() * 2
 
     result = None

@@ -45,6 +45,8 @@ def _dptr(t) -> C.c_void_p:
 
 
 def _stream(stream) -> C.c_void_p:
+    if isinstance(stream, C.c_void_p):
+        return stream
     if stream is None:
         import torch
 
@@ -63,10 +65,14 @@ def _dtype_code(t) -> int:
 
 
 def _u32(a) -> np.ndarray:
+    if isinstance(a, np.ndarray) and a.dtype == np.uint32 and a.flags.c_contiguous:
+        return a
     return np.ascontiguousarray(np.asarray(a, dtype=np.int64).astype(np.uint32))
 
 
 def _i32(a) -> np.ndarray:
+    if isinstance(a, np.ndarray) and a.dtype == np.int32 and a.flags.c_contiguous:
+        return a
     return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
 
 
