@@ -531,13 +531,19 @@ def run_c4(args, rank, world, local, mode):
     v = torch.randn((n_seq, kvd), generator=g, device=dev, dtype=torch.float16)
     q = torch.randn((n_seq, my_hq * d), generator=g, device=dev, dtype=torch.float16)
     out = torch.empty_like(q)
-    gathered = torch.empty((world, n_seq, my_hq * d), device=dev, dtype=torch.float16) if mode == "head" else None
+    comm = None
+    if mode == "head" and world > 1:
+        uid = [kv_mod.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = kv_mod.NcclComm(world, uid[0], rank, local)
+        gathered = torch.empty((world, n_seq, my_hq * d), device=dev, dtype=torch.float16)
+        full = torch.empty((n_seq, world * my_hq * d), device=dev, dtype=torch.float16)
     st = Stepper(kv, lens, k, v, q, out)
 
     def step():
         lens_now = st.step()
-        if gathered is not None and world > 1:
-            dist.all_gather_into_tensor(gathered, out)  # rank r's heads r*G..: [world][seq][heads*D]
+        if comm is not None:  # NCCL all-gather + permute to [seq][all heads * D]
+            kv_mod.gather_heads(kv, out, comm, out=full, gathered=gathered, stream=st.stream)
         return lens_now
 
     def barrier():
@@ -572,8 +578,8 @@ def run_c4(args, rank, world, local, mode):
                         f"{mode}-sharded x{world}, one layer",
             "n_heads": hq, "n_kv_heads": hkv, "head_dim": d, "block_tokens": BLOCK,
             "per_rank": {"seqs": n_seq, "kv_heads": my_hkv, "q_heads": my_hq},
-            "collective": "NCCL all_gather_into_tensor of [seqs, q_heads*D] f16 per step" if mode == "head" and world > 1
-            else "none"})
+            "collective": "lt_kv_gather_heads: NCCL all-gather of [seqs, q_heads*D] f16 per step + permute"
+            if mode == "head" and world > 1 else "none"})
         res["scaling"] = "strong" if mode == "head" else "weak"
         res["hbm_gbs_per_gpu"] = byts / args.steps / (ms / args.steps * 1e-3) / 1e9
         res["roofline"] = {"bound": "hbm", "kernel": "paged_attn_kernel<128> + kv_combine_kernel (rank 0)",
@@ -583,6 +589,8 @@ def run_c4(args, rank, world, local, mode):
         res["gpu_launches"] = kv.launch_count() - l0
     if world > 1:
         dist.barrier()
+        if comm is not None:
+            comm.close()
         kv.close()
         dist.destroy_process_group()
     else:

@@ -205,6 +205,28 @@ lt_status lt_kv_profile_read(lt_kv* kv, double* total_ms, uint64_t* launches);
 /* Kernel launches made by this handle since creation (all kinds). */
 uint64_t lt_kv_launch_count(const lt_kv* kv);
 
+/* ---- KV-head sharding across GPUs (NCCL) ---------------------------------- */
+/* No counterpart in the reference, which runs one process.  For long
+ * contexts the KV heads are split across ranks: rank r's handle holds KV
+ * heads [r*hl, (r+1)*hl) of every sequence (n_kv_heads = hl, n_heads = hl*G),
+ * every rank makes the same bookkeeping calls, and after each attention the
+ * ranks' outputs are all-gathered.  NCCL is resolved at run time from
+ * libnccl.so.2 (an already-loaded copy is reused); LT_E_NCCL if absent. */
+
+/* ncclGetUniqueId into 128 bytes, to be shared with every rank. */
+lt_status lt_kv_nccl_unique_id(void* id_out);
+/* ncclCommInitRank on `device`; blocks until all nranks ranks join. */
+lt_status lt_kv_nccl_init(void** comm_out, int nranks, const void* id, int rank, int device);
+void lt_kv_nccl_destroy(void* comm);
+/* Join the head-sharded attention outputs: `local` [n][n_heads*head_dim]
+ * (this rank's heads, from lt_kv_attend / lt_kv_write_attend) is
+ * all-gathered over `comm` into `gathered` [nranks][n][n_heads*head_dim] and
+ * permuted into `out` [n][nranks*n_heads*head_dim] -- the layout of the
+ * unsharded attention (head h*group+g of the full model).  Device buffers,
+ * 16-byte aligned; ordered on `stream`. */
+lt_status lt_kv_gather_heads(lt_kv* kv, const void* local, void* gathered, void* out, uint32_t n, lt_dtype dtype,
+                             void* comm, int nranks, void* stream);
+
 /* ---- allocation-free attention ------------------------------------------- */
 
 /* No counterpart in the reference.  The same paged decode attention as

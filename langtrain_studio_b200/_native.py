@@ -24,6 +24,7 @@ EXPORTS = (
     "lt_kv_truncate", "lt_kv_share", "lt_kv_compact", "lt_kv_flush", "lt_kv_rows", "lt_kv_check",
     "lt_kv_seq_blocks", "lt_kv_refs", "lt_kv_free_list", "lt_kv_n_blocks", "lt_kv_device_pool",
     "lt_kv_device_tables", "lt_kv_read_pool", "lt_kv_launch_count", "lt_kv_profile", "lt_kv_profile_read",
+    "lt_kv_nccl_unique_id", "lt_kv_nccl_init", "lt_kv_nccl_destroy", "lt_kv_gather_heads",
     "lt_paged_attend_noalloc",
 )
 
@@ -77,6 +78,10 @@ def _declare(L):
         "lt_kv_launch_count": (u64, [p]),
         "lt_kv_profile": (st, [p, C.c_int]),
         "lt_kv_profile_read": (st, [p, C.POINTER(C.c_double), C.POINTER(u64)]),
+        "lt_kv_nccl_unique_id": (st, [p]),
+        "lt_kv_nccl_init": (st, [C.POINTER(p), C.c_int, p, C.c_int, C.c_int]),
+        "lt_kv_nccl_destroy": (None, [p]),
+        "lt_kv_gather_heads": (st, [p, p, p, p, u32, C.c_int, p, C.c_int, p]),
         "lt_paged_attend_noalloc": (st, [p, u32, u32, u32, p, u32, p, p, u32, p, C.c_int, p, C.c_int,
                                          C.c_float, p]),
     }

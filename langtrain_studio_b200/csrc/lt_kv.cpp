@@ -480,6 +480,14 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
 
 }  // namespace
 
+namespace ltkv {
+size_t local_out_row_bytes(const lt_kv* kv, int dtype) {
+    return (size_t)kv->cfg.n_heads * kv->cfg.head_dim * (dtype == LT_F32 ? 4 : 2);
+}
+int handle_device(const lt_kv* kv) { return kv->cfg.device; }
+void count_launch(lt_kv* kv) { kv->launches++; }
+}  // namespace ltkv
+
 // ============================================================== C ABI ====
 
 extern "C" {

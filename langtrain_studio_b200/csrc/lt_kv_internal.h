@@ -51,6 +51,11 @@ cudaError_t launch_attend(const AttnParams& p, int head_dim, cudaStream_t s);
 // Kernel launches made by launch_attend(p).
 int attend_launches(const AttnParams& p);
 
+// Head-sharded output assembly: gathered [nranks][n][row bytes] ->
+// out [n][nranks][row bytes] (row = one token's local heads).
+cudaError_t launch_gather_permute(const void* gathered, void* out, int nranks, uint32_t n, size_t row_bytes,
+                                  cudaStream_t s);
+
 cudaError_t launch_write(uint16_t* pool_layer, const int2* cells, int n, int n_kv_heads, int head_dim,
                          const void* k, const void* v, int in_f32, cudaStream_t s);
 
@@ -63,4 +68,12 @@ cudaError_t launch_apply_plan(uint16_t* pool, size_t layer_stride_elems, size_t 
 cudaError_t launch_rows(const uint16_t* pool_layer, const int32_t* table_row, int n, int n_kv_heads,
                         int head_dim, uint16_t* k_out, uint16_t* v_out, cudaStream_t s);
 
+}  // namespace ltkv
+
+// Accessors of the opaque handle for the other translation units.
+struct lt_kv;
+namespace ltkv {
+size_t local_out_row_bytes(const lt_kv* kv, int dtype);  // n_heads*head_dim*elem of this handle
+int handle_device(const lt_kv* kv);
+void count_launch(lt_kv* kv);
 }  // namespace ltkv

@@ -13,6 +13,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "lt_kv_internal.h"
 
 namespace ltkv {
@@ -672,6 +674,18 @@ __global__ void __launch_bounds__(256) apply_plan_kernel(uint16_t* __restrict__ 
     }
 }
 
+// ---------------------------------------------------------- gather ----
+// out[t][r] = gathered[r][t] for 16-byte chunks of one token's local heads.
+__global__ void __launch_bounds__(256) gather_permute_kernel(const uint4* __restrict__ gathered, uint4* __restrict__ out,
+                                                             int nranks, uint32_t n, uint32_t row16) {
+    const size_t total = (size_t)nranks * n * row16;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t c = i % row16, rt = i / row16;
+        const size_t t = rt % n, r = rt / n;  // source order: [r][t][c]
+        out[(t * nranks + r) * row16 + c] = gathered[i];
+    }
+}
+
 // ------------------------------------------------------------- rows ----
 template <int D>
 __global__ void __launch_bounds__(256) rows_kernel(const uint16_t* __restrict__ pool_layer,
@@ -764,6 +778,17 @@ cudaError_t launch_attend(const AttnParams& p, int head_dim, cudaStream_t s) {
 }
 
 int attend_launches(const AttnParams& p) { return p.n_warps == 0 ? 0 : 1; }
+
+cudaError_t launch_gather_permute(const void* gathered, void* out, int nranks, uint32_t n, size_t row_bytes,
+                                  cudaStream_t s) {
+    const uint32_t row16 = (uint32_t)(row_bytes / 16);
+    const size_t total = (size_t)nranks * n * row16;
+    if (total == 0) return cudaSuccess;
+    const unsigned blocks = (unsigned)std::min<size_t>((total + 255) / 256, 4096);
+    gather_permute_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint4*>(gathered), static_cast<uint4*>(out), nranks,
+                                                 n, row16);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_write(uint16_t* pool_layer, const int2* cells, int n, int n_kv_heads, int head_dim, const void* k,
                          const void* v, int in_f32, cudaStream_t s) {

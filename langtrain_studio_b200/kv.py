@@ -275,6 +275,49 @@ class KvCache:
         return unswizzle_pool(self.read_pool(layer))
 
 
+class NcclComm:
+    """NCCL communicator for KV-head sharding (lt_kv_nccl_init).  Every rank
+    builds it with the same 128-byte id from `nccl_unique_id()` on rank 0."""
+
+    def __init__(self, nranks: int, uid: bytes, rank: int, device: int):
+        lib = N.lib()
+        buf = C.create_string_buffer(bytes(uid), 128)
+        h = C.c_void_p()
+        rc = lib.lt_kv_nccl_init(C.byref(h), nranks, buf, rank, device)
+        if rc != N.LT_OK:
+            raise KvError(rc, f"lt_kv_nccl_init failed with status {rc}")
+        self.handle, self.nranks, self.rank = h, nranks, rank
+
+    def close(self):
+        if self.handle:
+            N.lib().lt_kv_nccl_destroy(self.handle)
+            self.handle = None
+
+
+def nccl_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    rc = N.lib().lt_kv_nccl_unique_id(buf)
+    if rc != N.LT_OK:
+        raise KvError(rc, "NCCL is not available (libnccl.so.2)")
+    return buf.raw
+
+
+def gather_heads(kv: "KvCache", local, comm: NcclComm, out=None, gathered=None, stream=None):
+    """All-gather head-sharded attention outputs into the unsharded layout
+    [n][nranks * n_heads * head_dim] (lt_kv_gather_heads)."""
+    import torch
+
+    n = local.shape[0]
+    w = comm.nranks
+    if gathered is None:
+        gathered = torch.empty((w, n, local.shape[1]), dtype=local.dtype, device=local.device)
+    if out is None:
+        out = torch.empty((n, w * local.shape[1]), dtype=local.dtype, device=local.device)
+    kv._check(kv._lib.lt_kv_gather_heads(kv._h, _dptr(local), _dptr(gathered), _dptr(out), n, _dtype_code(local),
+                                         comm.handle, w, _stream(stream)))
+    return out
+
+
 def unswizzle_pool(raw: np.ndarray):
     """Invert the device pool layout: [block][head][2][16][D] with chunk c of
     slot s stored at c ^ (s & 7) -> reference (K, V) [block][16][head*D]."""

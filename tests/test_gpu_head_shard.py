@@ -1,0 +1,79 @@
+"""KV-head sharding across 2 GPUs: each rank holds half the KV heads of every
+sequence (identical bookkeeping calls on both ranks), attends with its own
+q heads, and lt_kv_gather_heads (NCCL all-gather + permute) must reproduce
+the unsharded attention of the oracle within the north-star tolerance."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, out_dir):
+    import datetime
+    import sys
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from langtrain_studio_b200 import kv as kvm
+    from oracle import oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    torch.cuda.set_device(rank)
+    hkv, hq, d = 4, 16, 128
+    hl, ql = hkv // world, hq // world
+    lens = [100, 333, 1000, 17]
+    rng = np.random.default_rng(0)  # the same full K/V and q on every rank
+    K = [rng.standard_normal((L, hkv * d)).astype(np.float32) for L in lens]
+    V = [rng.standard_normal((L, hkv * d)).astype(np.float32) for L in lens]
+    q = rng.standard_normal((len(lens), hq * d)).astype(np.float32)
+    nb = sum((L + 16) // 16 for L in lens) + 8
+    kv = kvm.KvCache(1, hl, d, nb * 16, n_heads=ql, max_seqs=len(lens), max_batch=4096, device=rank)
+    cols = slice(rank * hl * d, (rank + 1) * hl * d)
+    for s, L in enumerate(lens):
+        b, sl = kv.append_batch(np.full(L, s), np.arange(L))
+        kv.write(0, b, sl, torch.from_numpy(np.ascontiguousarray(K[s][:, cols])).cuda(),
+                 torch.from_numpy(np.ascontiguousarray(V[s][:, cols])).cuda())
+    qcols = slice(rank * ql * d, (rank + 1) * ql * d)
+    local = kv.attend(0, torch.from_numpy(np.ascontiguousarray(q[:, qcols])).cuda(), np.arange(len(lens)),
+                      np.array(lens) - 1, out_dtype=torch.float32)
+    uid = [kvm.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    comm = kvm.NcclComm(world, uid[0], rank, rank)
+    full = kvm.gather_heads(kv, local, comm).cpu().numpy()
+    ok = oracle.OracleKv(1, hkv * d, nb * 16, max_seqs=len(lens))
+    for s, L in enumerate(lens):
+        rc, _, b, sl = ok.append_batch(np.full(L, s), np.arange(L))
+        ok.write_batch(0, b, sl, K[s], V[s])
+    ref = ok.attend(0, q, np.arange(len(lens)), np.array(lens) - 1, hq, hkv, d)
+    err = float(np.abs(full - ref).max())
+    np.save(os.path.join(out_dir, f"err{rank}.npy"), np.array([err]))
+    comm.close()
+    kv.close()
+    dist.destroy_process_group()
+
+
+def test_head_sharded_attention_matches_unsharded(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_rank, args=(2, _port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    for r in range(2):
+        err = float(np.load(tmp_path / f"err{r}.npy")[0])
+        assert err < 2e-5, err  # f32 outputs; the north-star bar is 2e-3
