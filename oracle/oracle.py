@@ -24,13 +24,17 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 SRC = HERE / "lt_oracle.c"
 HDR = HERE / "lt_oracle.h"
+# The C1 end-to-end forward (model.rs restated) lives in the same library.
+MODEL_SRC = HERE / "lt_model.c"
+MODEL_HDR = HERE / "lt_model.h"
+SOURCES = (SRC, HDR, MODEL_SRC, MODEL_HDR)
 BUILD_DIR = HERE / "_build"
 LIB = BUILD_DIR / "liblt_oracle.so"
 
 # x86-64-v3 (AVX2/F16C) rather than -march=native: the built library travels to
 # other hosts.  -ffp-contract=off: Rust never fuses a*b+c, neither may we.
 CFLAGS = ["-O3", "-march=x86-64-v3", "-mf16c", "-ffp-contract=off", "-fno-fast-math",
-          "-std=c11", "-fPIC", "-shared", "-pthread", "-Wall"]
+          "-std=c11", "-fPIC", "-shared", "-pthread", "-fopenmp", "-Wall"]
 
 BLOCK = 16
 OK, FULL, NONCONTIG, ARG = 0, 1, 2, 3
@@ -39,10 +43,10 @@ OK, FULL, NONCONTIG, ARG = 0, 1, 2, 3
 def build(force: bool = False) -> Path:
     """Compile the oracle with gcc into oracle/_build/ (idempotent)."""
     BUILD_DIR.mkdir(exist_ok=True)
-    if not force and LIB.exists() and LIB.stat().st_mtime >= max(SRC.stat().st_mtime, HDR.stat().st_mtime):
+    if not force and LIB.exists() and LIB.stat().st_mtime >= max(f.stat().st_mtime for f in SOURCES):
         return LIB
     tmp = LIB.with_suffix(".so.tmp%d" % os.getpid())
-    subprocess.run(["gcc", *CFLAGS, "-o", str(tmp), str(SRC), "-lm"], check=True)
+    subprocess.run(["gcc", *CFLAGS, "-o", str(tmp), str(SRC), str(MODEL_SRC), "-lm"], check=True)
     os.replace(tmp, LIB)
     return LIB
 
