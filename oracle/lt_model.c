@@ -245,6 +245,74 @@ static void dequant_row(const qmat* m, int r, float* out) { /* quant.rs:464-490 
     }
 }
 
+/* ---- op-level entry points (the per-op parity tests call these) ---- */
+
+void om_quantize(const float* x, uint32_t n, uint32_t cols, int8_t* qs, float* scales) {
+    for (size_t b = 0; b < (size_t)n * cols / QK; b++) scales[b] = quantize_block(x + b * QK, qs + b * QK);
+}
+
+void om_matmul_q8(const int8_t* wq, const float* ws, uint32_t rows, uint32_t cols, const int8_t* xq, const float* xs,
+                  uint32_t n, float* out, int n_threads) {
+    qmat w = {(int)rows, (int)cols, (float*)ws, (int8_t*)wq};
+    qacts a = {(int)n, (int)cols, (int8_t*)xq, (float*)xs};
+    matmul(&w, &a, out, n_threads > 0 ? n_threads : 1);
+}
+
+void om_rms_norm(const float* x, const float* w, uint32_t dim, uint32_t n, float eps, float* out) {
+    rms_norm(x, w, (int)dim, (int)n, eps, out);
+}
+
+void om_rope(const omodel* m, float* x, uint32_t n_heads, uint32_t pos) { rope(m, x, (int)n_heads, pos); }
+
+void om_silu_mul(float* g, const float* u, size_t n) {
+    for (size_t e = 0; e < n; e++) g[e] = g[e] / (1.0f + expf(-g[e])) * u[e];
+}
+
+const float* om_inv_freq(const omodel* m) { return m->inv_freq; }
+
+static const qmat* tensor_qmat(const omodel* m, int which, int layer) {
+    if (which == OM_T_EMBED) return &m->embed;
+    if (which == OM_T_OUTPUT) return &m->output;
+    if (layer < 0 || layer >= m->n_layers) return NULL;
+    const olayer* L = &m->layers[layer];
+    switch (which) {
+        case OM_T_Q: return &L->q;
+        case OM_T_K: return &L->k;
+        case OM_T_V: return &L->v;
+        case OM_T_O: return &L->o;
+        case OM_T_GATE: return &L->gate;
+        case OM_T_UP: return &L->up;
+        case OM_T_DOWN: return &L->down;
+        default: return NULL;
+    }
+}
+
+/* One tensor in its GGUF encoding: Q8_0 blocks {f16 d; i8 qs[32]} (34 bytes,
+ * the layout quant.rs:265-273 repacks) for matrices, F32 for norm vectors.
+ * Returns the byte count (0 for an unknown tensor); writes only if out. */
+size_t om_export_tensor(const omodel* m, int which, int layer, void* out) {
+    const float* vec = NULL;
+    if (which == OM_T_OUTPUT_NORM) vec = m->output_norm;
+    if (which == OM_T_ATTN_NORM && layer >= 0 && layer < m->n_layers) vec = m->layers[layer].attn_norm;
+    if (which == OM_T_FFN_NORM && layer >= 0 && layer < m->n_layers) vec = m->layers[layer].ffn_norm;
+    if (vec) {
+        if (out) memcpy(out, vec, sizeof(float) * m->dim);
+        return sizeof(float) * m->dim;
+    }
+    const qmat* q = tensor_qmat(m, which, layer);
+    if (!q) return 0;
+    size_t nb = (size_t)q->rows * q->cols / QK;
+    if (out) {
+        uint8_t* o = (uint8_t*)out;
+        for (size_t b = 0; b < nb; b++) {
+            uint16_t d = okv_f32_to_f16(q->scales[b]);
+            memcpy(o + 34 * b, &d, 2);
+            memcpy(o + 34 * b + 2, q->qs + b * QK, QK);
+        }
+    }
+    return 34 * nb;
+}
+
 /* Model::forward (model.rs:366-518).  Returns 0, or the KV append error. */
 int om_forward(const omodel* m, const om_kv* kv, const int32_t* tokens, const uint32_t* seqs, const uint32_t* pos,
                uint32_t n, const uint32_t* want, uint32_t n_want, float* logits, int n_threads) {

@@ -10,6 +10,7 @@
  */
 #ifndef LT_MODEL_H
 #define LT_MODEL_H
+#include <stddef.h>
 #include <stdint.h>
 
 #include "lt_oracle.h"
@@ -48,6 +49,22 @@ int om_forward(const omodel* m, const om_kv* kv, const int32_t* tokens, const ui
 /* argmax under f32 total order, last index among equal maxima
  * (engine/crates/engine/src/sampling.rs:161-163). */
 int32_t om_argmax(const float* logits, int n);
+
+/* Tensor ids, the same numbering as the product's lt_tensor. */
+enum {
+    OM_T_EMBED = 0, OM_T_OUTPUT, OM_T_OUTPUT_NORM, OM_T_ATTN_NORM, OM_T_FFN_NORM,
+    OM_T_Q, OM_T_K, OM_T_V, OM_T_O, OM_T_GATE, OM_T_UP, OM_T_DOWN
+};
+size_t om_export_tensor(const omodel* m, int which, int layer, void* out);
+const float* om_inv_freq(const omodel* m);
+
+/* Op-level restatements, for per-op parity checks. */
+void om_quantize(const float* x, uint32_t n, uint32_t cols, int8_t* qs, float* scales); /* quant.rs:771-795 */
+void om_matmul_q8(const int8_t* wq, const float* ws, uint32_t rows, uint32_t cols, const int8_t* xq, const float* xs,
+                  uint32_t n, float* out, int n_threads);                                 /* quant.rs:405-428 */
+void om_rms_norm(const float* x, const float* w, uint32_t dim, uint32_t n, float eps, float* out); /* model.rs:174-183 */
+void om_rope(const omodel* m, float* x, uint32_t n_heads, uint32_t pos);                  /* model.rs:291-308 */
+void om_silu_mul(float* g, const float* u, size_t n);                                     /* model.rs:492-494 */
 
 /* The oracle KvCache as an om_kv (attention over n_threads threads). */
 om_kv* om_kv_oracle(okv* kv, int n_heads, int n_kv_heads, int head_dim, int n_threads);

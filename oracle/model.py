@@ -159,16 +159,28 @@ def c1_prompts(vocab: int, n_seqs: int = 4, prompt: int = 128, shared: int = 64,
                     ).astype(np.int32)
 
 
-def run_c1(model: OracleModel, kv, share, prompts: np.ndarray, shared: int, n_gen: int, n_threads: int = 0):
+def run_c1(model: OracleModel, kv, share, prompts: np.ndarray, shared: int, n_gen: int, n_threads: int = 0,
+           teacher: np.ndarray | None = None, logits_out: np.ndarray | None = None):
     """The C1 serving sequence: prefill seq 0, share its first `shared`
     positions into every other sequence (kv.rs:172-183), prefill their
     suffixes in one batch, then greedy decode with every sequence in each
     step.  `share(src, dst, n)` acts on the cache under `kv`.  Returns the
-    generated ids [n_seqs, n_gen]."""
+    generated ids [n_seqs, n_gen].
+
+    With `teacher` [n_seqs, n_gen], step j feeds teacher[:, j-1] instead of
+    the model's own previous pick (teacher forcing), so two runs whose
+    numerics differ slightly still see the same inputs.  `logits_out`
+    [n_seqs, n_gen, vocab] receives the logits of every pick."""
     n_seqs, plen = prompts.shape
     gen = np.zeros((n_seqs, n_gen), np.int32)
+
+    def pick(lg, rows, j):
+        if logits_out is not None:
+            logits_out[rows, j] = lg
+        gen[rows, j] = model.argmax(lg)
+
     lg = model.forward(kv, prompts[0], np.zeros(plen, np.uint32), np.arange(plen), [plen - 1], n_threads)
-    gen[0, 0] = model.argmax(lg)[0]
+    pick(lg, [0], 0)
     for s in range(1, n_seqs):
         share(0, s, shared)
     m = plen - shared
@@ -176,9 +188,16 @@ def run_c1(model: OracleModel, kv, share, prompts: np.ndarray, shared: int, n_ge
     seqs = np.repeat(np.arange(1, n_seqs), m)
     pos = np.tile(np.arange(shared, plen), n_seqs - 1)
     lg = model.forward(kv, toks, seqs, pos, [(i + 1) * m - 1 for i in range(n_seqs - 1)], n_threads)
-    gen[1:, 0] = model.argmax(lg)
+    pick(lg, list(range(1, n_seqs)), 0)
     for j in range(1, n_gen):
         p = np.full(n_seqs, plen + j - 1, np.uint32)
-        lg = model.forward(kv, gen[:, j - 1], np.arange(n_seqs), p, np.arange(n_seqs), n_threads)
-        gen[:, j] = model.argmax(lg)
+        feed = gen[:, j - 1] if teacher is None else teacher[:, j - 1]
+        lg = model.forward(kv, feed, np.arange(n_seqs), p, np.arange(n_seqs), n_threads)
+        pick(lg, list(range(n_seqs)), j)
     return gen
+
+
+def top2_margin(logits: np.ndarray) -> np.ndarray:
+    """Gap between the largest and second-largest logit of each row."""
+    part = np.partition(logits, -2, axis=-1)
+    return part[..., -1] - part[..., -2]
