@@ -26,6 +26,9 @@ EXPORTS = (
     "lt_kv_device_tables", "lt_kv_read_pool", "lt_kv_launch_count", "lt_kv_profile", "lt_kv_profile_read",
     "lt_kv_nccl_unique_id", "lt_kv_nccl_init", "lt_kv_nccl_destroy", "lt_kv_gather_heads",
     "lt_paged_attend_noalloc",
+    "lt_llama_create", "lt_llama_destroy", "lt_llama_last_error", "lt_llama_set_tensor", "lt_llama_forward",
+    "lt_llama_step_greedy", "lt_llama_launch_count", "lt_q8_quantize", "lt_q8_matmul", "lt_rms_norm_q8",
+    "lt_silu_q8", "lt_argmax_f32",
 )
 
 
@@ -39,6 +42,24 @@ class lt_kv_config(C.Structure):
         ("max_seqs", C.c_uint32),
         ("max_batch", C.c_uint32),
         ("max_blocks_per_seq", C.c_uint32),
+        ("device", C.c_int32),
+    ]
+
+
+class lt_llama_config(C.Structure):
+    _fields_ = [
+        ("n_layers", C.c_uint32),
+        ("dim", C.c_uint32),
+        ("n_heads", C.c_uint32),
+        ("n_kv_heads", C.c_uint32),
+        ("head_dim", C.c_uint32),
+        ("ffn_dim", C.c_uint32),
+        ("vocab", C.c_uint32),
+        ("rope_dim", C.c_uint32),
+        ("rope_neox", C.c_int32),
+        ("eps", C.c_float),
+        ("rope_base", C.c_float),
+        ("max_batch", C.c_uint32),
         ("device", C.c_int32),
     ]
 
@@ -84,6 +105,18 @@ def _declare(L):
         "lt_kv_gather_heads": (st, [p, p, p, p, u32, C.c_int, p, C.c_int, p]),
         "lt_paged_attend_noalloc": (st, [p, u32, u32, u32, p, u32, p, p, u32, p, C.c_int, p, C.c_int,
                                          C.c_float, p]),
+        "lt_llama_create": (st, [C.POINTER(lt_llama_config), C.POINTER(p)]),
+        "lt_llama_destroy": (None, [p]),
+        "lt_llama_last_error": (C.c_char_p, [p]),
+        "lt_llama_set_tensor": (st, [p, C.c_int, u32, p, C.c_size_t]),
+        "lt_llama_forward": (st, [p, p, p, p, p, u32, p, u32, p, p]),
+        "lt_llama_step_greedy": (st, [p, p, p, p, p, u32, p, u32, p, p]),
+        "lt_llama_launch_count": (u64, [p]),
+        "lt_q8_quantize": (st, [p, u32, u32, p, p, p]),
+        "lt_q8_matmul": (st, [p, p, u32, u32, p, p, u32, p, u32, C.c_int, p]),
+        "lt_rms_norm_q8": (st, [p, p, p, u32, u32, C.c_float, p, p, p, p]),
+        "lt_silu_q8": (st, [p, u32, u32, p, p, p, p]),
+        "lt_argmax_f32": (st, [p, u32, u32, p, p]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

@@ -18,8 +18,9 @@ INCLUDE = ROOT / "include"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "liblt_kv.so"
 
-SOURCES = [CSRC / "lt_kv_kernels.cu", CSRC / "lt_kv.cpp", CSRC / "lt_kv_nccl.cpp", CSRC / "lt_kv_noalloc.cu"]
-HEADERS = [CSRC / "lt_kv_internal.h", INCLUDE / "lt_kv.h"]
+SOURCES = [CSRC / "lt_kv_kernels.cu", CSRC / "lt_kv.cpp", CSRC / "lt_kv_nccl.cpp", CSRC / "lt_kv_noalloc.cu",
+           CSRC / "lt_llama.cu"]
+HEADERS = [CSRC / "lt_kv_internal.h", INCLUDE / "lt_kv.h", INCLUDE / "lt_llama.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall", "-shared",

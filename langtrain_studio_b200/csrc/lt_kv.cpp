@@ -485,6 +485,7 @@ size_t local_out_row_bytes(const lt_kv* kv, int dtype) {
     return (size_t)kv->cfg.n_heads * kv->cfg.head_dim * (dtype == LT_F32 ? 4 : 2);
 }
 int handle_device(const lt_kv* kv) { return kv->cfg.device; }
+const lt_kv_config* handle_config(const lt_kv* kv) { return &kv->cfg; }
 void count_launch(lt_kv* kv) { kv->launches++; }
 }  // namespace ltkv
 

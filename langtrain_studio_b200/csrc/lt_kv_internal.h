@@ -72,8 +72,10 @@ cudaError_t launch_rows(const uint16_t* pool_layer, const int32_t* table_row, in
 
 // Accessors of the opaque handle for the other translation units.
 struct lt_kv;
+struct lt_kv_config;
 namespace ltkv {
 size_t local_out_row_bytes(const lt_kv* kv, int dtype);  // n_heads*head_dim*elem of this handle
 int handle_device(const lt_kv* kv);
+const lt_kv_config* handle_config(const lt_kv* kv);
 void count_launch(lt_kv* kv);
 }  // namespace ltkv

@@ -1,0 +1,728 @@
+// sm_100a Llama step around the paged KV cache: the operations on either
+// side of the attention path in Model::forward (model.rs:366-518).
+//
+//   q8_matmul_kernel   QMatrix::matmul (quant.rs:405-428, 492-533): int8 dot
+//                      products on the tensor cores (mma.sync m16n8k32 s8,
+//                      one 32-wide Q8_0 block per instruction), scales applied
+//                      per block and summed block by block in the reference's
+//                      order, so results are bit-identical to row_dot
+//   quantize_kernel    QActs::quantize (quant.rs:771-795)
+//   rms_norm_q8_kernel rms_norm (model.rs:174-183) + quantize
+//   rope_split_kernel  RoPE of q and k (model.rs:291-308, 414-421) and the
+//                      split of the fused q|k|v projection into q, k, v
+//   silu_q8_kernel     SiLU(gate) * up (model.rs:492-494) + quantize
+//   embed_kernel       Q8_0 embedding rows (quant.rs:464-490)
+//   argmax_kernel      greedy pick (sampling.rs:161-163)
+//
+// Weights live on the device in a split Q8_0 layout: int8 [rows][cols] and
+// f16 scales [rows][cols/32] (the GGUF block's d, unchanged).  Projections
+// that share an input are stored as one matrix: q|k|v rows, and gate|up rows,
+// so each is one launch (the reference's matmul_many, quant.rs:722).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "lt_kv.h"
+#include "lt_kv_internal.h"
+#include "lt_llama.h"
+
+namespace {
+
+constexpr int kQK = 32;          // Q8_0 block
+constexpr int kMmWarps = 16;     // warps per matmul CTA (K blocks dealt round-robin)
+constexpr int kMmRows = 16;      // weight rows per matmul CTA (mma M)
+constexpr int kMmToks = 8;       // tokens per matmul CTA (mma N)
+
+// ------------------------------------------------------------ helpers -----
+
+__device__ __forceinline__ uint2 ld_stream(const void* p) {  // weights: read once
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                       uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// QActs::quantize of one 32-element block held as 8 values by each of 4
+// consecutive lanes (quantize_block, quant.rs:785-795): amax folded from 0
+// with f32::max (NaN-ignoring, as fmaxf), d = amax / 127, q = round(v * (1/d))
+// half away from zero, saturated to int8 (Rust `as i8`: NaN -> 0).
+// Every lane of the warp must call it (the group shuffles); only `live`
+// lanes store.
+__device__ __forceinline__ void quant8_store(const float (&v)[8], int8_t* q_dst, float* scale_dst, bool leader,
+                                             bool live = true) {
+    float a = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) a = fmaxf(a, fabsf(v[k]));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+    const float d = __fdiv_rn(a, 127.0f);
+    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const float r = roundf(__fmul_rn(v[k], id));
+        int qi = 0;
+        if (!(r != r)) qi = (int)fminf(fmaxf(r, -128.0f), 127.0f);
+        w[k >> 2] |= (uint32_t)(qi & 0xff) << (8 * (k & 3));
+    }
+    if (!live) return;
+    *reinterpret_cast<uint2*>(q_dst) = make_uint2(w[0], w[1]);
+    if (leader) *scale_dst = d;
+}
+
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// ------------------------------------------------------------ kernels -----
+
+// out[t][r] (+)= sum_b (ws[r][b] * xs[t][b]) * dot32(W[r][b], X[t][b]),
+// summed over b = 0, 1, ... from 0.0f (row_dot, quant.rs:418-421).
+// CTA: 16 rows x 8 tokens.  Its 16 warps take the 32-wide blocks round-robin
+// and run one s8 mma per block: lane (g, q) loads bytes [8q, 8q+8) of its
+// block for rows g and g+8 and token g; the same k permutation on both
+// operands leaves each dot32 unchanged.  The four f32 products of every lane
+// and block go to shared memory; warp 0 then adds them block by block.
+__global__ void __launch_bounds__(kMmWarps * 32) q8_matmul_kernel(
+    const int8_t* __restrict__ wq, const __half* __restrict__ ws, int rows, int cols,
+    const int8_t* __restrict__ xq, const float* __restrict__ xs, int n, float* __restrict__ out, int out_stride,
+    int accumulate) {
+    extern __shared__ float4 prod[];  // [nb][32]
+    const int nb = cols / kQK;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, q = lane & 3;
+    const int r0 = blockIdx.x * kMmRows, t0 = blockIdx.y * kMmToks;
+    const int ra = min(r0 + g, rows - 1), rb = min(r0 + g + 8, rows - 1);
+    const int tb_op = min(t0 + g, n - 1);                                // B operand token
+    const int ta = min(t0 + 2 * q, n - 1), tc = min(t0 + 2 * q + 1, n - 1);  // C columns
+    const int8_t* wa = wq + (size_t)ra * cols + 8 * q;
+    const int8_t* wb = wq + (size_t)rb * cols + 8 * q;
+    const int8_t* xb = xq + (size_t)tb_op * cols + 8 * q;
+    const __half* sa = ws + (size_t)ra * nb;
+    const __half* sb = ws + (size_t)rb * nb;
+    const float* xa = xs + (size_t)ta * nb;
+    const float* xc = xs + (size_t)tc * nb;
+#pragma unroll 4
+    for (int b = warp; b < nb; b += kMmWarps) {
+        const uint2 A0 = ld_stream(wa + (size_t)b * kQK);
+        const uint2 A1 = ld_stream(wb + (size_t)b * kQK);
+        const uint2 B = __ldg(reinterpret_cast<const uint2*>(xb + (size_t)b * kQK));
+        int d[4];
+        mma_s8(d, A0.x, A1.x, A0.y, A1.y, B.x, B.y);
+        const float wsa = __half2float(sa[b]), wsb = __half2float(sb[b]);
+        const float xsa = __ldg(xa + b), xsc = __ldg(xc + b);
+        float4 p;
+        p.x = __fmul_rn(__fmul_rn(wsa, xsa), __int2float_rn(d[0]));  // row g,   token 2q
+        p.y = __fmul_rn(__fmul_rn(wsa, xsc), __int2float_rn(d[1]));  // row g,   token 2q+1
+        p.z = __fmul_rn(__fmul_rn(wsb, xsa), __int2float_rn(d[2]));  // row g+8, token 2q
+        p.w = __fmul_rn(__fmul_rn(wsb, xsc), __int2float_rn(d[3]));  // row g+8, token 2q+1
+        prod[b * 32 + lane] = p;
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 8
+    for (int b = 0; b < nb; b++) {
+        const float4 p = prod[b * 32 + lane];
+        s.x = __fadd_rn(s.x, p.x);
+        s.y = __fadd_rn(s.y, p.y);
+        s.z = __fadd_rn(s.z, p.z);
+        s.w = __fadd_rn(s.w, p.w);
+    }
+    const int rr[2] = {r0 + g, r0 + g + 8};
+    const int tt[2] = {t0 + 2 * q, t0 + 2 * q + 1};
+    const float v[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = rr[i >> 1], t = tt[i & 1];
+        if (r < rows && t < n) {
+            float* o = out + (size_t)t * out_stride + r;
+            *o = accumulate ? __fadd_rn(*o, v[i]) : v[i];
+        }
+    }
+}
+
+// QActs::quantize over n*cols/8 threads, 8 values each.
+__global__ void quantize_kernel(const float* __restrict__ x, size_t n_threads, int8_t* __restrict__ qs,
+                                float* __restrict__ scales) {
+    // Lanes past the end stay for the group shuffles (n_threads is a multiple
+    // of 4, so a group is wholly in or out) but neither load nor store.
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool live = i < n_threads;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (live) load8(x + i * 8, v);
+    quant8_store(v, qs + i * 8, scales + i / 4, (threadIdx.x & 3) == 0, live);
+}
+
+// rms_norm then quantize: one CTA per output row, dim/8 threads.  The sum of
+// squares is a tree (the reference's is sequential: a few ulps apart).
+__global__ void rms_norm_q8_kernel(const float* __restrict__ x, const int32_t* __restrict__ rows_idx,
+                                   const float* __restrict__ w, int dim, float eps, float* __restrict__ normed,
+                                   int8_t* __restrict__ qs, float* __restrict__ scales) {
+    __shared__ float red[32];
+    const int row = blockIdx.x;
+    const int src = rows_idx ? rows_idx[row] : row;
+    const int i = threadIdx.x;
+    float v[8];
+    load8(x + (size_t)src * dim + i * 8, v);
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) ss = __fadd_rn(ss, __fmul_rn(v[k], v[k]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    if ((i & 31) == 0) red[i >> 5] = ss;
+    __syncthreads();
+    const int nw = blockDim.x >> 5;
+    if (i < 32) {
+        float t = i < nw ? red[i] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
+        if (i == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float ms = __fdiv_rn(red[0], (float)dim);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+    float wv[8];
+    load8(w + i * 8, wv);
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[k] = __fmul_rn(__fmul_rn(v[k], inv), wv[k]);
+    if (normed) store8(normed + (size_t)row * dim + i * 8, v);
+    quant8_store(v, qs + (size_t)row * dim + i * 8, scales + ((size_t)row * dim + i * 8) / kQK, (i & 3) == 0);
+}
+
+// SiLU(g) * u = g / (1 + exp(-g)) * u, then quantize.  exp is rounded once
+// to f32 from a double-precision exp: the correctly rounded f32 value.  The
+// C library expf that the reference calls is one ulp away from it on about
+// 0.03 % of inputs (near rounding midpoints).
+__global__ void silu_q8_kernel(const float* __restrict__ gu, int n, int ffn, float* __restrict__ h,
+                               int8_t* __restrict__ qs, float* __restrict__ scales) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t per_row = (size_t)ffn / 8;  // a multiple of 4: groups are wholly in or out
+    const bool live = i < per_row * n;
+    const size_t t = live ? i / per_row : 0, c = live ? (i % per_row) * 8 : 0;
+    float gv[8], uv[8];
+    load8(gu + t * 2 * ffn + c, gv);  // past the end: reload row 0, store nothing
+    load8(gu + t * 2 * ffn + ffn + c, uv);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const float e = (float)exp(-(double)gv[k]);
+        gv[k] = __fmul_rn(__fdiv_rn(gv[k], __fadd_rn(1.0f, e)), uv[k]);
+    }
+    if (h && live) store8(h + t * ffn + c, gv);
+    quant8_store(gv, qs + t * ffn + c, scales + (t * ffn + c) / kQK, (threadIdx.x & 3) == 0, live);
+}
+
+// RoPE of the q and k parts of one token's q|k|v row and the split into q,
+// k, v rows.  sincos [n][half][2] (sin, cos) of pos * inv_freq[i].
+__global__ void rope_split_kernel(const float* __restrict__ qkv, int q_dim, int kv_dim, int hd, int half, int neox,
+                                  const float* __restrict__ sincos, float* __restrict__ qo, float* __restrict__ ko,
+                                  float* __restrict__ vo) {
+    const int t = blockIdx.x;
+    const float* row = qkv + (size_t)t * (q_dim + 2 * kv_dim);
+    const float* sc = sincos + (size_t)t * half * 2;
+    for (int j = threadIdx.x; j < q_dim + 2 * kv_dim; j += blockDim.x) {
+        float r = row[j];
+        if (j < q_dim + kv_dim) {
+            const int base = j - j % hd, c = j % hd;
+            int i = -1, partner = 0;
+            bool first = true;
+            if (neox) {
+                if (c < half) { i = c; partner = c + half; }
+                else if (c < 2 * half) { i = c - half; partner = c - half; first = false; }
+            } else if (c < 2 * half) {
+                i = c >> 1; partner = c ^ 1; first = (c & 1) == 0;
+            }
+            if (i >= 0) {
+                const float sn = sc[2 * i], cs = sc[2 * i + 1];
+                const float other = row[base + partner];
+                r = first ? __fsub_rn(__fmul_rn(r, cs), __fmul_rn(other, sn))     // x0 cos - x1 sin
+                          : __fadd_rn(__fmul_rn(other, sn), __fmul_rn(r, cs));    // x0 sin + x1 cos
+            }
+        }
+        if (j < q_dim) qo[(size_t)t * q_dim + j] = r;
+        else if (j < q_dim + kv_dim) ko[(size_t)t * kv_dim + (j - q_dim)] = r;
+        else vo[(size_t)t * kv_dim + (j - q_dim - kv_dim)] = r;
+    }
+}
+
+// Embedding rows: x[i][j] = d[tok][j/32] * q[tok][j].
+__global__ void embed_kernel(const int8_t* __restrict__ qs, const __half* __restrict__ sc, int dim,
+                             const int32_t* __restrict__ tokens, float* __restrict__ x) {
+    const int i = blockIdx.x;
+    const size_t tok = (size_t)tokens[i];
+    for (int j = threadIdx.x; j < dim; j += blockDim.x)
+        x[(size_t)i * dim + j] = __fmul_rn(__half2float(sc[tok * (dim / kQK) + j / kQK]), (float)qs[tok * dim + j]);
+}
+
+// Greedy pick: max under f32 total order, the last index among equal keys.
+__device__ __forceinline__ int32_t total_key(float f) {
+    const int32_t b = __float_as_int(f);
+    return b < 0 ? (b ^ 0x7fffffff) : b;
+}
+
+__global__ void argmax_kernel(const float* __restrict__ x, int cols, int32_t* __restrict__ idx) {
+    __shared__ int32_t sk[32], si[32];
+    const float* row = x + (size_t)blockIdx.x * cols;
+    int32_t bk = INT32_MIN, bi = -1;
+    for (int j = threadIdx.x; j < cols; j += blockDim.x) {
+        const int32_t k = total_key(row[j]);
+        if (k >= bk) { bk = k; bi = j; }  // j rises: ties keep the later index
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const int32_t k2 = __shfl_xor_sync(0xffffffffu, bk, o), i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (k2 > bk || (k2 == bk && i2 > bi)) { bk = k2; bi = i2; }
+    }
+    if ((threadIdx.x & 31) == 0) { sk[threadIdx.x >> 5] = bk; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+            if (sk[w] > bk || (sk[w] == bk && si[w] > bi)) { bk = sk[w]; bi = si[w]; }
+        idx[blockIdx.x] = bi < 0 ? 0 : bi;
+    }
+}
+
+// ------------------------------------------------------------ launchers ---
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+cudaError_t launch_matmul(const int8_t* wq, const __half* ws, int rows, int cols, const int8_t* xq, const float* xs,
+                          int n, float* out, int out_stride, int accumulate, cudaStream_t st) {
+    if (rows <= 0 || n <= 0) return cudaSuccess;
+    static bool attr_set[64] = {};
+    const size_t smem = (size_t)(cols / kQK) * 32 * sizeof(float4);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(q8_matmul_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   200 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    dim3 grid((rows + kMmRows - 1) / kMmRows, (n + kMmToks - 1) / kMmToks);
+    q8_matmul_kernel<<<grid, kMmWarps * 32, smem, st>>>(wq, ws, rows, cols, xq, xs, n, out, out_stride, accumulate);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize(const float* x, size_t n_elems, int8_t* qs, float* scales, cudaStream_t st) {
+    const size_t threads = n_elems / 8;
+    if (!threads) return cudaSuccess;
+    quantize_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(x, threads, qs, scales);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rms_norm_q8(const float* x, const int32_t* rows_idx, const float* w, int dim, int n, float eps,
+                               float* normed, int8_t* qs, float* scales, cudaStream_t st) {
+    if (!n) return cudaSuccess;
+    rms_norm_q8_kernel<<<n, dim / 8, 0, st>>>(x, rows_idx, w, dim, eps, normed, qs, scales);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_silu_q8(const float* gu, int n, int ffn, float* h, int8_t* qs, float* scales, cudaStream_t st) {
+    const size_t threads = (size_t)n * ffn / 8;
+    if (!threads) return cudaSuccess;
+    silu_q8_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(gu, n, ffn, h, qs, scales);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float* x, int n, int cols, int32_t* idx, cudaStream_t st) {
+    if (!n) return cudaSuccess;
+    argmax_kernel<<<n, 1024, 0, st>>>(x, cols, idx);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+// ------------------------------------------------------------ the handle --
+
+struct QMat {
+    int8_t* qs = nullptr;
+    __half* sc = nullptr;
+    uint32_t rows = 0, cols = 0;
+};
+
+struct lt_llama {
+    lt_llama_config cfg{};
+    std::string err;
+    uint32_t q_dim = 0, kv_dim = 0, qkv_rows = 0, half = 0, maxc = 0;
+    QMat embed, output;
+    float* out_norm = nullptr;
+    std::vector<QMat> wqkv, wo, wgu, wdown;
+    std::vector<float*> attn_norm, ffn_norm;
+    std::vector<uint8_t> set;  // which (tensor, layer) were given
+    std::vector<float> inv_freq;
+    float *x = nullptr, *qkv = nullptr, *qb = nullptr, *kb = nullptr, *vb = nullptr, *att = nullptr, *gu = nullptr;
+    float *xs = nullptr, *logits = nullptr;
+    int8_t* xq = nullptr;
+    int32_t* ids = nullptr;
+    char* meta_dev = nullptr;
+    char* meta_host = nullptr;
+    int32_t* ids_host = nullptr;
+    size_t meta_bytes = 0;
+    cudaEvent_t meta_ev = nullptr;
+    std::vector<int32_t> blocks, slots;
+    uint64_t launches = 0;
+    std::vector<void*> allocs;
+};
+
+namespace {
+
+lt_status fail(lt_llama* m, lt_status rc, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    m->err = buf;
+    return rc;
+}
+
+#define LL_CUDA(m, call)                                                                             \
+    do {                                                                                             \
+        cudaError_t e_ = (call);                                                                     \
+        if (e_ != cudaSuccess) return fail((m), LT_E_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+template <typename T>
+lt_status dalloc(lt_llama* m, T** p, size_t count) {
+    void* q = nullptr;
+    if (cudaMalloc(&q, count * sizeof(T) + 16) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(m, LT_E_CUDA, "cudaMalloc of %zu bytes failed", count * sizeof(T));
+    }
+    m->allocs.push_back(q);
+    *p = static_cast<T*>(q);
+    return LT_OK;
+}
+
+lt_status alloc_mat(lt_llama* m, QMat& w, uint32_t rows, uint32_t cols) {
+    w.rows = rows;
+    w.cols = cols;
+    lt_status rc = dalloc(m, &w.qs, (size_t)rows * cols);
+    if (rc == LT_OK) rc = dalloc(m, &w.sc, (size_t)rows * cols / kQK);
+    return rc;
+}
+
+enum { kTensorKinds = 12 };
+
+size_t set_index(const lt_llama* m, int which, uint32_t layer) {
+    return which <= LT_T_OUTPUT_NORM ? (size_t)which : 3 + (size_t)layer * (kTensorKinds - 3) + (which - 3);
+}
+
+}  // namespace
+
+extern "C" {
+
+lt_status lt_llama_create(const lt_llama_config* cfg, lt_llama** out) {
+    if (!cfg || !out) return LT_E_ARG;
+    *out = nullptr;
+    const lt_llama_config& c = *cfg;
+    if (!c.n_layers || !c.dim || !c.n_heads || !c.n_kv_heads || !c.vocab || !c.max_batch || !c.ffn_dim)
+        return LT_E_ARG;
+    if (c.dim % kQK || c.ffn_dim % kQK || c.n_heads % c.n_kv_heads || (c.head_dim != 64 && c.head_dim != 128))
+        return LT_E_UNSUPPORTED;
+    if (c.dim / 8 > 1024 || (c.dim / 8) % 32) return LT_E_UNSUPPORTED;  // rms_norm: one CTA of dim/8 threads
+    const uint32_t rope_dim = c.rope_dim ? c.rope_dim : c.head_dim;
+    if (rope_dim > c.head_dim || rope_dim % 2) return LT_E_ARG;
+    if ((size_t)c.ffn_dim / kQK * 32 * sizeof(float4) > 200 * 1024) return LT_E_UNSUPPORTED;
+    auto* m = new lt_llama();
+    m->cfg = c;
+    m->cfg.rope_dim = rope_dim;
+    m->q_dim = c.n_heads * c.head_dim;
+    m->kv_dim = c.n_kv_heads * c.head_dim;
+    m->qkv_rows = m->q_dim + 2 * m->kv_dim;
+    m->half = rope_dim / 2;
+    m->maxc = std::max(std::max(c.dim, m->q_dim), c.ffn_dim);
+    if (m->q_dim % kQK || (size_t)m->q_dim / kQK * 32 * sizeof(float4) > 200 * 1024) {
+        delete m;
+        return LT_E_UNSUPPORTED;
+    }
+    for (uint32_t i = 0; i < m->half; i++)  // model.rs:263-265
+        m->inv_freq.push_back(powf(c.rope_base, -2.0f * (float)i / (float)rope_dim));
+    m->set.assign(3 + (size_t)c.n_layers * (kTensorKinds - 3), 0);
+    DeviceGuard dg(c.device);
+    const size_t B = c.max_batch;
+    lt_status rc = alloc_mat(m, m->embed, c.vocab, c.dim);
+    if (rc == LT_OK) rc = alloc_mat(m, m->output, c.vocab, c.dim);
+    if (rc == LT_OK) rc = dalloc(m, &m->out_norm, c.dim);
+    m->wqkv.resize(c.n_layers);
+    m->wo.resize(c.n_layers);
+    m->wgu.resize(c.n_layers);
+    m->wdown.resize(c.n_layers);
+    m->attn_norm.assign(c.n_layers, nullptr);
+    m->ffn_norm.assign(c.n_layers, nullptr);
+    for (uint32_t l = 0; l < c.n_layers && rc == LT_OK; l++) {
+        rc = alloc_mat(m, m->wqkv[l], m->qkv_rows, c.dim);
+        if (rc == LT_OK) rc = alloc_mat(m, m->wo[l], c.dim, m->q_dim);
+        if (rc == LT_OK) rc = alloc_mat(m, m->wgu[l], 2 * c.ffn_dim, c.dim);
+        if (rc == LT_OK) rc = alloc_mat(m, m->wdown[l], c.dim, c.ffn_dim);
+        if (rc == LT_OK) rc = dalloc(m, &m->attn_norm[l], c.dim);
+        if (rc == LT_OK) rc = dalloc(m, &m->ffn_norm[l], c.dim);
+    }
+    if (rc == LT_OK) rc = dalloc(m, &m->x, B * c.dim);
+    if (rc == LT_OK) rc = dalloc(m, &m->qkv, B * m->qkv_rows);
+    if (rc == LT_OK) rc = dalloc(m, &m->qb, B * m->q_dim);
+    if (rc == LT_OK) rc = dalloc(m, &m->kb, B * m->kv_dim);
+    if (rc == LT_OK) rc = dalloc(m, &m->vb, B * m->kv_dim);
+    if (rc == LT_OK) rc = dalloc(m, &m->att, B * m->q_dim);
+    if (rc == LT_OK) rc = dalloc(m, &m->gu, B * 2 * c.ffn_dim);
+    if (rc == LT_OK) rc = dalloc(m, &m->xq, B * m->maxc);
+    if (rc == LT_OK) rc = dalloc(m, &m->xs, B * m->maxc / kQK);
+    if (rc == LT_OK) rc = dalloc(m, &m->logits, B * c.vocab);
+    if (rc == LT_OK) rc = dalloc(m, &m->ids, B);
+    // step metadata: tokens [B] | want [B] | sincos [B][half][2]
+    m->meta_bytes = B * 4 * 2 + B * m->half * 2 * sizeof(float);
+    if (rc == LT_OK) rc = dalloc(m, &m->meta_dev, m->meta_bytes);
+    if (rc == LT_OK && (cudaMallocHost(&m->meta_host, m->meta_bytes) != cudaSuccess ||
+                        cudaMallocHost(&m->ids_host, B * sizeof(int32_t)) != cudaSuccess ||
+                        cudaEventCreateWithFlags(&m->meta_ev, cudaEventDisableTiming) != cudaSuccess))
+        rc = fail(m, LT_E_CUDA, "pinned staging allocation failed");
+    if (rc != LT_OK) {
+        lt_llama_destroy(m);
+        return rc;
+    }
+    m->blocks.resize(B);
+    m->slots.resize(B);
+    *out = m;
+    return LT_OK;
+}
+
+void lt_llama_destroy(lt_llama* m) {
+    if (!m) return;
+    DeviceGuard dg(m->cfg.device);
+    if (m->meta_ev) {
+        cudaEventSynchronize(m->meta_ev);
+        cudaEventDestroy(m->meta_ev);
+    }
+    for (void* p : m->allocs) cudaFree(p);
+    if (m->meta_host) cudaFreeHost(m->meta_host);
+    if (m->ids_host) cudaFreeHost(m->ids_host);
+    delete m;
+}
+
+const char* lt_llama_last_error(const lt_llama* m) { return m ? m->err.c_str() : "null handle"; }
+
+uint64_t lt_llama_launch_count(const lt_llama* m) { return m ? m->launches : 0; }
+
+lt_status lt_llama_set_tensor(lt_llama* m, lt_tensor which, uint32_t layer, const void* data, size_t bytes) {
+    if (!m || !data) return LT_E_ARG;
+    const lt_llama_config& c = m->cfg;
+    if ((int)which < 0 || (int)which >= kTensorKinds) return fail(m, LT_E_ARG, "unknown tensor %d", (int)which);
+    if (which > LT_T_OUTPUT_NORM && layer >= c.n_layers) return fail(m, LT_E_ARG, "layer %u out of range", layer);
+    DeviceGuard dg(c.device);
+    if (which == LT_T_OUTPUT_NORM || which == LT_T_ATTN_NORM || which == LT_T_FFN_NORM) {
+        if (bytes != (size_t)c.dim * sizeof(float)) return fail(m, LT_E_ARG, "norm vector: %zu bytes", bytes);
+        float* dst = which == LT_T_OUTPUT_NORM ? m->out_norm
+                     : which == LT_T_ATTN_NORM ? m->attn_norm[layer] : m->ffn_norm[layer];
+        LL_CUDA(m, cudaMemcpy(dst, data, bytes, cudaMemcpyHostToDevice));
+        m->set[set_index(m, which, layer)] = 1;
+        return LT_OK;
+    }
+    QMat* dst = nullptr;
+    uint32_t row0 = 0, rows = 0, cols = c.dim;
+    switch (which) {
+        case LT_T_EMBED: dst = &m->embed; rows = c.vocab; break;
+        case LT_T_OUTPUT: dst = &m->output; rows = c.vocab; break;
+        case LT_T_Q: dst = &m->wqkv[layer]; rows = m->q_dim; break;
+        case LT_T_K: dst = &m->wqkv[layer]; row0 = m->q_dim; rows = m->kv_dim; break;
+        case LT_T_V: dst = &m->wqkv[layer]; row0 = m->q_dim + m->kv_dim; rows = m->kv_dim; break;
+        case LT_T_O: dst = &m->wo[layer]; rows = c.dim; cols = m->q_dim; break;
+        case LT_T_GATE: dst = &m->wgu[layer]; rows = c.ffn_dim; break;
+        case LT_T_UP: dst = &m->wgu[layer]; row0 = c.ffn_dim; rows = c.ffn_dim; break;
+        case LT_T_DOWN: dst = &m->wdown[layer]; rows = c.dim; cols = c.ffn_dim; break;
+        default: return fail(m, LT_E_ARG, "unknown tensor %d", (int)which);
+    }
+    const size_t nb = (size_t)rows * cols / kQK;
+    if (bytes != nb * 34) return fail(m, LT_E_ARG, "Q8_0 tensor %d: %zu bytes, expected %zu", (int)which, bytes, nb * 34);
+    // quant.rs:265-273: split each 34-byte block into its f16 d and 32 int8
+    std::vector<int8_t> qs((size_t)rows * cols);
+    std::vector<uint16_t> sc(nb);
+    const uint8_t* src = static_cast<const uint8_t*>(data);
+    for (size_t b = 0; b < nb; b++) {
+        std::memcpy(&sc[b], src + 34 * b, 2);
+        std::memcpy(&qs[b * kQK], src + 34 * b + 2, kQK);
+    }
+    LL_CUDA(m, cudaMemcpy(dst->qs + (size_t)row0 * cols, qs.data(), qs.size(), cudaMemcpyHostToDevice));
+    LL_CUDA(m, cudaMemcpy(dst->sc + (size_t)row0 * cols / kQK, sc.data(), nb * 2, cudaMemcpyHostToDevice));
+    m->set[set_index(m, which, layer)] = 1;
+    return LT_OK;
+}
+
+lt_status lt_llama_forward(lt_llama* m, lt_kv* kv, const int32_t* tokens, const uint32_t* seqs, const uint32_t* pos,
+                           uint32_t n, const uint32_t* want, uint32_t n_want, float* logits, void* stream) {
+    if (!m || !kv) return LT_E_ARG;
+    const lt_llama_config& c = m->cfg;
+    if (n == 0) return LT_OK;
+    if (!tokens || !seqs || !pos) return fail(m, LT_E_ARG, "null token/seq/pos array");
+    if (n > c.max_batch) return fail(m, LT_E_ARG, "batch of %u tokens exceeds max_batch %u", n, c.max_batch);
+    if (n_want > n || (n_want && (!want || !logits))) return fail(m, LT_E_ARG, "bad logits request");
+    for (uint32_t j = 0; j < n_want; j++)
+        if (want[j] >= n) return fail(m, LT_E_ARG, "want[%u] = %u out of range", j, want[j]);
+    const lt_kv_config* kc = ltkv::handle_config(kv);
+    if (kc->n_layers != c.n_layers || kc->n_kv_heads != c.n_kv_heads || kc->head_dim != c.head_dim ||
+        kc->n_heads != c.n_heads || kc->device != c.device)
+        return fail(m, LT_E_ARG, "KV cache shape does not match the model");
+    for (uint8_t s : m->set)
+        if (!s) return fail(m, LT_E_ARG, "not every tensor was set");
+    DeviceGuard dg(c.device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+    // Claim every cell first (model.rs:380-383).
+    uint32_t done = 0;
+    lt_status rc = lt_kv_append(kv, seqs, pos, n, m->blocks.data(), m->slots.data(), &done, stream);
+    if (rc != LT_OK) return fail(m, rc, "%s", lt_kv_last_error(kv));
+    for (uint32_t i = 0; i < n; i++)  // embed_row (model.rs:520-526), after the claim as in the reference
+        if (tokens[i] < 0 || (uint32_t)tokens[i] >= c.vocab)
+            return fail(m, LT_E_ARG, "token id %d out of range", tokens[i]);
+
+    // Step metadata in one copy: tokens, want, RoPE sin/cos (host libm, as model.rs:297).
+    LL_CUDA(m, cudaEventSynchronize(m->meta_ev));  // the previous copy has left the staging buffer
+    const size_t B = c.max_batch;
+    int32_t* h_tok = reinterpret_cast<int32_t*>(m->meta_host);
+    int32_t* h_want = h_tok + B;
+    float* h_sc = reinterpret_cast<float*>(h_want + B);
+    std::memcpy(h_tok, tokens, n * sizeof(int32_t));
+    for (uint32_t j = 0; j < n_want; j++) h_want[j] = (int32_t)want[j];
+    for (uint32_t i = 0; i < n; i++)
+        for (uint32_t k = 0; k < m->half; k++) {
+            const float a = (float)pos[i] * m->inv_freq[k];
+            h_sc[((size_t)i * m->half + k) * 2] = sinf(a);
+            h_sc[((size_t)i * m->half + k) * 2 + 1] = cosf(a);
+        }
+    int32_t* d_tok = reinterpret_cast<int32_t*>(m->meta_dev);
+    int32_t* d_want = d_tok + B;
+    float* d_sc = reinterpret_cast<float*>(d_want + B);
+    LL_CUDA(m, cudaMemcpyAsync(m->meta_dev, m->meta_host, B * 8 + (size_t)n * m->half * 2 * sizeof(float),
+                               cudaMemcpyHostToDevice, st));
+    LL_CUDA(m, cudaEventRecord(m->meta_ev, st));
+
+    const int dim = (int)c.dim, ffn = (int)c.ffn_dim, qd = (int)m->q_dim, kvd = (int)m->kv_dim;
+    const float scale = 1.0f / sqrtf((float)c.head_dim);  // model.rs:402
+    embed_kernel<<<n, 256, 0, st>>>(m->embed.qs, m->embed.sc, dim, d_tok, m->x);
+    LL_CUDA(m, cudaGetLastError());
+    m->launches++;
+    for (uint32_t l = 0; l < c.n_layers; l++) {
+        LL_CUDA(m, launch_rms_norm_q8(m->x, nullptr, m->attn_norm[l], dim, (int)n, c.eps, nullptr, m->xq, m->xs, st));
+        LL_CUDA(m, launch_matmul(m->wqkv[l].qs, m->wqkv[l].sc, (int)m->qkv_rows, dim, m->xq, m->xs, (int)n, m->qkv,
+                                 (int)m->qkv_rows, 0, st));
+        rope_split_kernel<<<n, 256, 0, st>>>(m->qkv, qd, kvd, (int)c.head_dim, (int)m->half, c.rope_neox, d_sc, m->qb,
+                                            m->kb, m->vb);
+        LL_CUDA(m, cudaGetLastError());
+        m->launches += 3;
+        rc = lt_kv_write_attend(kv, l, m->blocks.data(), m->slots.data(), m->kb, m->vb, LT_F32, m->qb, LT_F32, seqs,
+                                pos, n, m->att, LT_F32, scale, stream);
+        if (rc != LT_OK) return fail(m, rc, "%s", lt_kv_last_error(kv));
+        LL_CUDA(m, launch_quantize(m->att, (size_t)n * qd, m->xq, m->xs, st));
+        LL_CUDA(m, launch_matmul(m->wo[l].qs, m->wo[l].sc, dim, qd, m->xq, m->xs, (int)n, m->x, dim, 1, st));
+        LL_CUDA(m, launch_rms_norm_q8(m->x, nullptr, m->ffn_norm[l], dim, (int)n, c.eps, nullptr, m->xq, m->xs, st));
+        LL_CUDA(m, launch_matmul(m->wgu[l].qs, m->wgu[l].sc, 2 * ffn, dim, m->xq, m->xs, (int)n, m->gu, 2 * ffn, 0, st));
+        LL_CUDA(m, launch_silu_q8(m->gu, (int)n, ffn, nullptr, m->xq, m->xs, st));
+        LL_CUDA(m, launch_matmul(m->wdown[l].qs, m->wdown[l].sc, dim, ffn, m->xq, m->xs, (int)n, m->x, dim, 1, st));
+        m->launches += 6;
+    }
+    if (n_want) {  // model.rs:502-517
+        LL_CUDA(m, launch_rms_norm_q8(m->x, d_want, m->out_norm, dim, (int)n_want, c.eps, nullptr, m->xq, m->xs, st));
+        LL_CUDA(m, launch_matmul(m->output.qs, m->output.sc, (int)c.vocab, dim, m->xq, m->xs, (int)n_want, logits,
+                                 (int)c.vocab, 0, st));
+        m->launches += 2;
+    }
+    return LT_OK;
+}
+
+lt_status lt_llama_step_greedy(lt_llama* m, lt_kv* kv, const int32_t* tokens, const uint32_t* seqs,
+                               const uint32_t* pos, uint32_t n, const uint32_t* want, uint32_t n_want,
+                               int32_t* next_host, void* stream) {
+    if (!m) return LT_E_ARG;
+    if (n_want && !next_host) return fail(m, LT_E_ARG, "null next_host");
+    lt_status rc = lt_llama_forward(m, kv, tokens, seqs, pos, n, want, n_want, m->logits, stream);
+    if (rc != LT_OK || n_want == 0) return rc;
+    DeviceGuard dg(m->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    LL_CUDA(m, launch_argmax(m->logits, (int)n_want, (int)m->cfg.vocab, m->ids, st));
+    m->launches++;
+    LL_CUDA(m, cudaMemcpyAsync(m->ids_host, m->ids, n_want * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    LL_CUDA(m, cudaStreamSynchronize(st));
+    std::memcpy(next_host, m->ids_host, n_want * sizeof(int32_t));
+    return LT_OK;
+}
+
+// ---- op-level entry points ----
+
+lt_status lt_q8_quantize(const float* x, uint32_t n, uint32_t cols, int8_t* qs, float* scales, void* stream) {
+    if (!x || !qs || !scales || cols % kQK) return LT_E_ARG;
+    if (!aligned16(x) || !aligned16(qs)) return LT_E_ARG;
+    return launch_quantize(x, (size_t)n * cols, qs, scales, static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? LT_OK : LT_E_CUDA;
+}
+
+lt_status lt_q8_matmul(const int8_t* w_qs, const uint16_t* w_scales, uint32_t rows, uint32_t cols, const int8_t* x_qs,
+                       const float* x_scales, uint32_t n, float* out, uint32_t out_stride, int accumulate,
+                       void* stream) {
+    if (!w_qs || !w_scales || !x_qs || !x_scales || !out || cols % kQK || out_stride < rows) return LT_E_ARG;
+    if ((reinterpret_cast<uintptr_t>(w_qs) | reinterpret_cast<uintptr_t>(x_qs)) & 7) return LT_E_ARG;
+    if ((size_t)cols / kQK * 32 * sizeof(float4) > 200 * 1024) return LT_E_UNSUPPORTED;
+    return launch_matmul(w_qs, reinterpret_cast<const __half*>(w_scales), (int)rows, (int)cols, x_qs, x_scales, (int)n,
+                         out, (int)out_stride, accumulate, static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? LT_OK : LT_E_CUDA;
+}
+
+lt_status lt_rms_norm_q8(const float* x, const int32_t* rows_idx, const float* w, uint32_t dim, uint32_t n, float eps,
+                         float* normed, int8_t* qs, float* scales, void* stream) {
+    if (!x || !w || !qs || !scales || dim % 256 || dim / 8 > 1024) return LT_E_ARG;
+    if (!aligned16(x) || !aligned16(w) || (normed && !aligned16(normed)) || !aligned16(qs)) return LT_E_ARG;
+    return launch_rms_norm_q8(x, rows_idx, w, (int)dim, (int)n, eps, normed, qs, scales,
+                              static_cast<cudaStream_t>(stream)) == cudaSuccess ? LT_OK : LT_E_CUDA;
+}
+
+lt_status lt_silu_q8(const float* gu, uint32_t n, uint32_t ffn, float* h, int8_t* qs, float* scales, void* stream) {
+    if (!gu || !qs || !scales || ffn % kQK) return LT_E_ARG;
+    if (!aligned16(gu) || (h && !aligned16(h)) || !aligned16(qs)) return LT_E_ARG;
+    return launch_silu_q8(gu, (int)n, (int)ffn, h, qs, scales, static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? LT_OK : LT_E_CUDA;
+}
+
+lt_status lt_argmax_f32(const float* x, uint32_t n, uint32_t cols, int32_t* idx, void* stream) {
+    if (!x || !idx || !cols) return LT_E_ARG;
+    return launch_argmax(x, (int)n, (int)cols, idx, static_cast<cudaStream_t>(stream)) == cudaSuccess ? LT_OK
+                                                                                                      : LT_E_CUDA;
+}
+
+}  // extern "C"

@@ -45,6 +45,12 @@ def _lib():
         L.om_kv_oracle.restype = p
         L.om_kv_oracle.argtypes = [p, C.c_int, C.c_int, C.c_int, C.c_int]
         L.om_kv_free.argtypes = [p]
+        L.om_export_tensor.restype = C.c_size_t
+        L.om_export_tensor.argtypes = [p, C.c_int, C.c_int, p]
+        L.om_quantize.argtypes = [p, C.c_uint32, C.c_uint32, p, p]
+        L.om_matmul_q8.argtypes = [p, p, C.c_uint32, C.c_uint32, p, p, C.c_uint32, p, C.c_int]
+        L.om_rms_norm.argtypes = [p, p, C.c_uint32, C.c_uint32, C.c_float, p]
+        L.om_silu_mul.argtypes = [p, p, C.c_size_t]
         L._om_ready = True
     return L
 
@@ -146,9 +152,63 @@ class OracleModel:
             raise O.OracleError(rc, f"KV append failed with status {rc}")
         return logits[: want.size]
 
+    def export_tensor(self, which: int, layer: int) -> bytes:
+        """One tensor in its GGUF encoding (Q8_0 blocks or F32)."""
+        n = self._L.om_export_tensor(self._h, which, layer, None)
+        if n == 0:
+            raise ValueError(f"no tensor {which} in layer {layer}")
+        buf = np.zeros(n, np.uint8)
+        self._L.om_export_tensor(self._h, which, layer, O._ptr(buf))
+        return buf.tobytes()
+
     def argmax(self, logits: np.ndarray) -> np.ndarray:
         logits = np.ascontiguousarray(logits, np.float32)
         return np.array([self._L.om_argmax(O._ptr(row), row.size) for row in logits], np.int32)
+
+
+# ---- op-level restatements (per-op parity checks) ----
+
+def quantize(x: np.ndarray):
+    """QActs::quantize (quant.rs:771-795): x f32 [n, cols] -> (qs int8, scales f32)."""
+    x = np.ascontiguousarray(x, np.float32)
+    n, cols = x.shape
+    qs = np.zeros((n, cols), np.int8)
+    sc = np.zeros((n, cols // 32), np.float32)
+    _lib().om_quantize(O._ptr(x), n, cols, O._ptr(qs), O._ptr(sc))
+    return qs, sc
+
+
+def matmul_q8(wq: np.ndarray, ws: np.ndarray, xq: np.ndarray, xs: np.ndarray, n_threads: int = 0) -> np.ndarray:
+    """QMatrix::matmul (quant.rs:405-428, 492-533): out [n, rows]."""
+    wq, xq = np.ascontiguousarray(wq, np.int8), np.ascontiguousarray(xq, np.int8)
+    ws, xs = np.ascontiguousarray(ws, np.float32), np.ascontiguousarray(xs, np.float32)
+    rows, cols = wq.shape
+    n = xq.shape[0]
+    out = np.zeros((n, rows), np.float32)
+    _lib().om_matmul_q8(O._ptr(wq), O._ptr(ws), rows, cols, O._ptr(xq), O._ptr(xs), n, O._ptr(out), n_threads)
+    return out
+
+
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """rms_norm (model.rs:174-183)."""
+    x, w = np.ascontiguousarray(x, np.float32), np.ascontiguousarray(w, np.float32)
+    out = np.zeros_like(x)
+    _lib().om_rms_norm(O._ptr(x), O._ptr(w), x.shape[1], x.shape[0], eps, O._ptr(out))
+    return out
+
+
+def silu_mul(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    """g / (1 + exp(-g)) * u (model.rs:492-494)."""
+    g = np.array(g, np.float32, copy=True, order="C")
+    u = np.ascontiguousarray(u, np.float32)
+    _lib().om_silu_mul(O._ptr(g), O._ptr(u), g.size)
+    return g
+
+
+def argmax(x: np.ndarray) -> np.ndarray:
+    """Greedy pick per row (sampling.rs:161-163)."""
+    x = np.ascontiguousarray(x, np.float32)
+    return np.array([_lib().om_argmax(O._ptr(r), r.size) for r in x], np.int32)
 
 
 def c1_prompts(vocab: int, n_seqs: int = 4, prompt: int = 128, shared: int = 64, seed: int = 0) -> np.ndarray:
