@@ -846,6 +846,176 @@ def run_c5(args, rank, world, local):
 # CPU arm (restated reference path)
 
 
+# ---------------------------------------------------------------------------
+# the end-to-end Llama decode (--config c1)
+
+C1_SHAPE = dict(n_layers=22, dim=2048, n_heads=32, n_kv_heads=4, head_dim=64, ffn_dim=5632, vocab=32000)
+C1_SEQS, C1_PROMPT, C1_SHARED = 4, 128, 64
+
+
+def c1_prompts(vocab: int, seed: int = 0) -> np.ndarray:
+    """4 uniform-random prompts of 128 ids whose first 64 are shared."""
+    rng = np.random.default_rng(seed)
+    common = rng.integers(0, vocab, C1_SHARED)
+    return np.stack([np.concatenate([common, rng.integers(0, vocab, C1_PROMPT - C1_SHARED)])
+                     for _ in range(C1_SEQS)]).astype(np.int32)
+
+
+def run_c1(args, rank, world, local):
+    """configs[0] on the device: random-init Llama (22 layers, hidden 2048,
+    32/4 heads, head_dim 64, FFN 5632, vocab 32000, Q8_0), 4 sequences whose
+    128-token prompts share their first 64 tokens (sequence 0 prefilled,
+    share(0, s, 64), the suffixes prefilled in one batch), then greedy decode
+    steps of 4 tokens.  value: decode steps queued back to back on the device
+    (forward + argmax, token ids not fed back: the work does not depend on
+    them); e2e: the greedy loop through lt_llama_step_greedy, host ids in and
+    out every step.  Roofline: the Q8_0 matmul kernel against HBM."""
+    import torch
+    import torch.distributed as dist
+
+    from langtrain_studio_b200 import llama as LL
+
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    seed = shard_seed(rank)
+    model = LL.Llama(**C1_SHAPE, max_batch=256, device=local)
+    model.load(LL.random_weights(model, seed=seed))
+    steps, warm = args.steps, args.warmup
+    e2e_steps = steps
+    n_prof = min(steps, 100)
+    per_seq = C1_PROMPT + warm + 2 * steps + n_prof + 2 * BLOCK  # positions every sequence reaches
+    kv = model.kv_cache(C1_SEQS * per_seq, C1_SEQS)
+    prompts = c1_prompts(model.vocab, seed)
+    seqs = np.arange(C1_SEQS, dtype=np.uint32)
+    first = model.step_greedy(kv, prompts[0], np.zeros(C1_PROMPT), np.arange(C1_PROMPT), [C1_PROMPT - 1])
+    for s_ in range(1, C1_SEQS):
+        kv.share(0, s_, C1_SHARED)
+    m = C1_PROMPT - C1_SHARED
+    rest = model.step_greedy(kv, prompts[1:, C1_SHARED:].reshape(-1), np.repeat(seqs[1:], m),
+                             np.tile(np.arange(C1_SHARED, C1_PROMPT), C1_SEQS - 1),
+                             [(i + 1) * m - 1 for i in range(C1_SEQS - 1)])
+    cur = np.concatenate([first, rest]).astype(np.int32)
+    pos = C1_PROMPT
+    logits = torch.empty((C1_SEQS, model.vocab), dtype=torch.float32, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def queued_step():
+        nonlocal pos
+        model.forward(kv, cur, seqs, np.full(C1_SEQS, pos), seqs, logits=logits)
+        LL.argmax_rows(logits)
+        pos += 1
+
+    for _ in range(warm):
+        queued_step()
+    try:
+        uuid = str(torch.cuda.get_device_properties(local).uuid)
+        dev_id = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+    except Exception:
+        dev_id = str(local)
+    clocks = Clocks(dev_id)
+    time.sleep(0.3)
+    l0 = model.launch_count() + kv.launch_count()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        queued_step()
+    e1.record()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    launches = model.launch_count() + kv.launch_count() - l0 + steps  # + one argmax per step
+    clk = clocks.stop()
+    ms_max = reduce_max(ms, dev, world)
+    # matmul roofline: the same steps with an event pair around each matmul
+    model.profile(True)
+    mm_ms = mm_n = mm_bytes = 0
+    for _ in range(n_prof):
+        queued_step()
+        a, b_, c_ = model.profile_read()
+        mm_ms, mm_n, mm_bytes = mm_ms + a, mm_n + b_, mm_bytes + c_
+    model.profile(False)
+    # e2e: the greedy loop, ids to the host and back every step
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        cur = model.step_greedy(kv, cur, seqs, np.full(C1_SEQS, pos), seqs)
+        pos += 1
+    barrier()
+    e2e_ms = reduce_max((time.perf_counter() - t0) * 1e3, dev, world)
+    result = None
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        tokens = C1_SEQS * steps * world
+        achieved = mm_bytes / (mm_ms * 1e-3) / 1e9
+        result = _json_common(args, world, tokens / (ms_max * 1e-3), "tokens/s", ms_max / steps, {
+            "workload": "configs[0]: end-to-end greedy decode, random-init Llama 22 layers / hidden 2048 / 32 q, "
+                        "4 KV heads / head_dim 64 / FFN 5632 / vocab 32000, Q8_0 weights; 4 sequences, 128-token "
+                        "prompts with the first 64 shared via share(0, s, 64)",
+            "batch_per_gpu": C1_SEQS, "parallelism": f"replicas x{world} (independent models and caches)",
+            "context_at_start": C1_PROMPT, "l2": "inputs larger than L2: 1.16 GB of weights read per step"})
+        result.update({
+            "dtype": "int8 x int8 -> int32 (Q8_0 matmuls), f32 elsewhere, f16 KV",
+            "data": "synthetic: random-init Q8_0 weights (seeded), uniform-random prompt ids (seeded)",
+            "roofline": {"bound": "hbm", "kernel": "q8_matmul_kernel (all projections and the output matrix)",
+                         "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "algorithmic_bytes_per_launch": int(mm_bytes / max(mm_n, 1)),
+                         "avg_launch_ms": mm_ms / max(mm_n, 1), "launches_per_step": mm_n / max(n_prof, 1),
+                         "matmul_ms_per_step": mm_ms / max(n_prof, 1)},
+            "e2e": {"value": C1_SEQS * e2e_steps * world / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 256 * 8 + C1_SEQS * (C1_SHAPE["head_dim"] // 2) * 8,
+                    "d2h_bytes_per_step": C1_SEQS * 4},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+        })
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    kv.close()
+    model.close()
+    return result
+
+
+def cpu_run_c1(budget_s: float, threads: int, seed: int = 0):
+    """The restated reference forward (oracle/lt_model.c) on `threads` host
+    threads: prefill as configs[0] (untimed), then greedy decode steps of 4
+    tokens until `budget_s`.  Returns (tokens/s, steps, seconds)."""
+    from oracle import model as om
+
+    model = om.OracleModel(**{k: C1_SHAPE[k] for k in ("dim", "n_layers", "n_heads", "n_kv_heads", "head_dim",
+                                                        "ffn_dim", "vocab")}, seed=seed)
+    kv = model.oracle_kv(C1_SEQS * 1024, C1_SEQS)
+    prompts = c1_prompts(model.vocab, seed)
+    lg = model.forward(kv, prompts[0], np.zeros(C1_PROMPT), np.arange(C1_PROMPT), [C1_PROMPT - 1], threads)
+    first = model.argmax(lg)
+    for s_ in range(1, C1_SEQS):
+        kv.share(0, s_, C1_SHARED)
+    m = C1_PROMPT - C1_SHARED
+    lg = model.forward(kv, prompts[1:, C1_SHARED:].reshape(-1), np.repeat(np.arange(1, C1_SEQS), m),
+                       np.tile(np.arange(C1_SHARED, C1_PROMPT), C1_SEQS - 1),
+                       [(i + 1) * m - 1 for i in range(C1_SEQS - 1)], threads)
+    cur = np.concatenate([first, model.argmax(lg)])
+    pos, steps = C1_PROMPT, 0
+    t0 = time.perf_counter()
+    while steps < 1000 - C1_PROMPT:
+        lg = model.forward(kv, cur, np.arange(C1_SEQS), np.full(C1_SEQS, pos), np.arange(C1_SEQS), threads)
+        cur = model.argmax(lg)
+        pos += 1
+        steps += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return C1_SEQS * steps / dt, steps, dt
+
+
 def cpu_fill(ok_mod, lens, seed):
     n_blocks = int(((lens + CYCLE + 1 + BLOCK - 1) // BLOCK).sum()) + BATCH
     ok = ok_mod.OracleKv(1, N_KV_HEADS * HEAD_DIM, n_blocks * BLOCK, max_seqs=BATCH)
@@ -907,6 +1077,22 @@ def run_reference(args, rank, world):
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
+    if args.config == "c1":
+        value, steps, dt = cpu_run_c1(60.0, threads)
+        sample = (f"{steps} greedy decode steps of 4 tokens after an untimed prefill, {dt:.1f} s on {threads} "
+                  f"threads of {cpu_desc()}; restated reference forward (oracle/lt_model.c)")
+        return {
+            "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": 0, "ms_per_step": dt * 1e3 / max(steps, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32 (Q8_0 matmuls), f32, f16 KV",
+            "data": "synthetic: random-init Q8_0 weights (seeded), uniform-random prompt ids (seeded)",
+            "config": {"workload": "configs[0]: end-to-end greedy decode, random-init Llama (22 layers, Q8_0), "
+                                   "4 sequences, 64 shared prompt tokens", "batch_per_gpu": C1_SEQS,
+                       "implementation": "restated reference CPU forward (oracle/lt_model.c); the Rust reference "
+                                         "is not buildable here"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
     lens = workload(1234)
     # warm-up steps are untimed; each timed step is the full workload (64
     # sequences), bounded to ~60 s in total.
@@ -939,8 +1125,9 @@ def main():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c3", "c4-batch", "c4-head", "c5"], default="c2",
-                    help="c2: configs[1] (default, the headline); c3: configs[2]; c4-*: configs[3]; c5: configs[4]")
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4-batch", "c4-head", "c5"], default="c2",
+                    help="c2: configs[1] (default, the headline); c1: configs[0]; c3: configs[2]; "
+                         "c4-*: configs[3]; c5: configs[4]")
     ap.add_argument("--c5-rate", type=float, default=32.0, help="c5: mean arrivals per step over the whole job")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="CPU-baseline sample budget in seconds (rank 0, N=1); 0 skips it")
@@ -949,6 +1136,20 @@ def main():
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    if args.config == "c1":
+        res = run_c1(args, rank, world, local)
+        if rank == 0:
+            if world == 1 and args.cpu_seconds > 0:
+                threads = os.cpu_count() or 1
+                value, steps, dt = cpu_run_c1(args.cpu_seconds, threads)
+                res["cpu_baseline"] = {
+                    "value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                    "sample": f"{steps} greedy decode steps of 4 tokens after an untimed prefill, {dt:.1f} s on "
+                              f"{threads} threads of {cpu_desc()}; restated reference forward (oracle/lt_model.c)"}
+            else:
+                res["cpu_baseline"] = None
             print(json.dumps(res), flush=True)
         return
     if args.config == "c3":

@@ -205,6 +205,12 @@ lt_status lt_kv_profile_read(lt_kv* kv, double* total_ms, uint64_t* launches);
 /* Kernel launches made by this handle since creation (all kinds). */
 uint64_t lt_kv_launch_count(const lt_kv* kv);
 
+/* Attention launch sizing: each warp of the stream-K attention launch takes
+ * at least `tiles` 16-position tiles (default 8), so small steps run on fewer
+ * warps; large steps use every resident warp regardless.  Results do not
+ * depend on it beyond f32 summation order of split merges. */
+lt_status lt_kv_set_min_tiles_per_warp(lt_kv* kv, uint32_t tiles);
+
 /* ---- KV-head sharding across GPUs (NCCL) ---------------------------------- */
 /* No counterpart in the reference, which runs one process.  For long
  * contexts the KV heads are split across ranks: rank r's handle holds KV

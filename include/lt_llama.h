@@ -103,6 +103,13 @@ lt_status lt_llama_step_greedy(lt_llama* m, lt_kv* kv, const int32_t* tokens_hos
 /* Kernel launches issued by this handle since creation. */
 uint64_t lt_llama_launch_count(const lt_llama* m);
 
+/* Profiling of the Q8_0 matmul launches of lt_llama_forward: when enabled,
+ * each is bracketed by CUDA events on its stream.  profile_read waits for the
+ * recorded launches, returns their summed device time, count and algorithmic
+ * bytes (weights + scales, activations, outputs), and starts a new window. */
+lt_status lt_llama_profile(lt_llama* m, int enable);
+lt_status lt_llama_profile_read(lt_llama* m, double* matmul_ms, uint64_t* matmul_launches, uint64_t* matmul_bytes);
+
 /* ---- op-level entry points (device arrays; the same kernels the forward
  * runs), for per-op parity checks and for hosts that run their own loop ---- */
 
@@ -117,6 +124,24 @@ lt_status lt_q8_quantize(const float* x, uint32_t n, uint32_t cols, int8_t* qs, 
 lt_status lt_q8_matmul(const int8_t* w_qs, const uint16_t* w_scales, uint32_t rows, uint32_t cols,
                        const int8_t* x_qs, const float* x_scales, uint32_t n, float* out, uint32_t out_stride,
                        int accumulate, void* stream);
+
+/* One projection of the forward on device arrays: an activation prologue on
+ * f32 input x, then the Q8_0 matmul (as lt_q8_matmul):
+ *   LT_PRO_QUANT    quantize x [n][cols];
+ *   LT_PRO_SILU     SiLU(x[:, :cols]) * x[:, cols:] (x is [n][2*cols]), quantize;
+ *   LT_PRO_RMSNORM  rms_norm of rows x[rows_idx[i]] (rows_idx NULL: 0..n-1)
+ *                   with weight gamma [cols] and eps, quantize.
+ * fused != 0 runs both in one launch when n <= 8 and cols % 256 == 0 (the
+ * decode path of lt_llama_forward); otherwise, or with fused == 0, as two
+ * launches.  Results are identical either way. */
+enum { LT_PRO_QUANT = 1, LT_PRO_SILU = 2, LT_PRO_RMSNORM = 3 };
+lt_status lt_q8_project(int prologue, const int8_t* w_qs, const uint16_t* w_scales, uint32_t rows, uint32_t cols,
+                        const float* x, const int32_t* rows_idx, const float* gamma, float eps, uint32_t n,
+                        float* out, uint32_t out_stride, int fused, int accumulate, void* stream);
+
+/* Synchronises `stream` and reports whether an op-level matmul's bounded
+ * wait for its weight copies gave up since the last check (LT_E_TIMEOUT). */
+lt_status lt_q8_check(void* stream);
 
 /* rms_norm (model.rs:174-183) of rows x[rows_idx[i]] (rows_idx NULL: rows
  * 0..n-1) with weight w [dim], then QActs::quantize; `normed` (may be NULL)

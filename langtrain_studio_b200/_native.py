@@ -25,10 +25,10 @@ EXPORTS = (
     "lt_kv_seq_blocks", "lt_kv_refs", "lt_kv_free_list", "lt_kv_n_blocks", "lt_kv_device_pool",
     "lt_kv_device_tables", "lt_kv_read_pool", "lt_kv_launch_count", "lt_kv_profile", "lt_kv_profile_read",
     "lt_kv_nccl_unique_id", "lt_kv_nccl_init", "lt_kv_nccl_destroy", "lt_kv_gather_heads",
-    "lt_paged_attend_noalloc",
+    "lt_paged_attend_noalloc", "lt_kv_set_min_tiles_per_warp",
     "lt_llama_create", "lt_llama_destroy", "lt_llama_last_error", "lt_llama_set_tensor", "lt_llama_forward",
-    "lt_llama_step_greedy", "lt_llama_launch_count", "lt_q8_quantize", "lt_q8_matmul", "lt_rms_norm_q8",
-    "lt_silu_q8", "lt_argmax_f32",
+    "lt_llama_step_greedy", "lt_llama_launch_count", "lt_llama_profile", "lt_llama_profile_read", "lt_q8_quantize", "lt_q8_matmul", "lt_rms_norm_q8",
+    "lt_silu_q8", "lt_argmax_f32", "lt_q8_project", "lt_q8_check",
 )
 
 
@@ -97,6 +97,7 @@ def _declare(L):
         "lt_kv_device_tables": (p, [p, C.POINTER(u32)]),
         "lt_kv_read_pool": (st, [p, u32, u32, u32, p]),
         "lt_kv_launch_count": (u64, [p]),
+        "lt_kv_set_min_tiles_per_warp": (st, [p, u32]),
         "lt_kv_profile": (st, [p, C.c_int]),
         "lt_kv_profile_read": (st, [p, C.POINTER(C.c_double), C.POINTER(u64)]),
         "lt_kv_nccl_unique_id": (st, [p]),
@@ -112,11 +113,15 @@ def _declare(L):
         "lt_llama_forward": (st, [p, p, p, p, p, u32, p, u32, p, p]),
         "lt_llama_step_greedy": (st, [p, p, p, p, p, u32, p, u32, p, p]),
         "lt_llama_launch_count": (u64, [p]),
+        "lt_llama_profile": (st, [p, C.c_int]),
+        "lt_llama_profile_read": (st, [p, C.POINTER(C.c_double), C.POINTER(u64), C.POINTER(u64)]),
         "lt_q8_quantize": (st, [p, u32, u32, p, p, p]),
         "lt_q8_matmul": (st, [p, p, u32, u32, p, p, u32, p, u32, C.c_int, p]),
         "lt_rms_norm_q8": (st, [p, p, p, u32, u32, C.c_float, p, p, p, p]),
         "lt_silu_q8": (st, [p, u32, u32, p, p, p, p]),
         "lt_argmax_f32": (st, [p, u32, u32, p, p]),
+        "lt_q8_project": (st, [C.c_int, p, p, u32, u32, p, p, p, C.c_float, u32, p, u32, C.c_int, C.c_int, p]),
+        "lt_q8_check": (st, [p]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

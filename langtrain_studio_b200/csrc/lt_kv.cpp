@@ -64,6 +64,7 @@ struct DeviceGuard {
 
 struct lt_kv {
     lt_kv_config cfg{};
+    uint32_t min_tiles_per_warp = 8;  // attention launch sizing (lt_kv_set_min_tiles_per_warp)
     uint32_t n_blocks = 0, kv_dim = 0, group = 0, max_blocks = 0;
     size_t block_elems = 0;   // f16 elements of one block in one layer (all heads, K and V)
     size_t layer_elems = 0;   // f16 elements of one layer of the pool
@@ -433,7 +434,12 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     p.max_blocks = (int32_t)kv->max_blocks;
     p.n_tok = (int32_t)n;
     p.tiles_per_head = (int32_t)tiles;
-    p.n_warps = (int32_t)std::min<long long>(max_warps, tiles * kv->cfg.n_kv_heads);
+    // At least min_tiles_per_warp tiles a warp: a small step (few tokens, short
+    // contexts) runs on fewer warps with fewer split merges instead of
+    // paying every warp's ramp for one tile.
+    const long long total_tiles = tiles * kv->cfg.n_kv_heads;
+    const long long want = (total_tiles + kv->min_tiles_per_warp - 1) / kv->min_tiles_per_warp;
+    p.n_warps = (int32_t)std::min<long long>(max_warps, std::max<long long>(want, total_tiles ? 1 : 0));
     p.n_kv_heads = (int32_t)kv->cfg.n_kv_heads;
     p.group = (int32_t)kv->group;
     p.q = q;
@@ -848,6 +854,12 @@ lt_status lt_kv_profile_read(lt_kv* kv, double* total_ms, uint64_t* launches) {
     if (rc) return rc;
     if (total_ms) *total_ms = kv->prof_ms;
     if (launches) *launches = kv->prof_count;
+    return LT_OK;
+}
+
+lt_status lt_kv_set_min_tiles_per_warp(lt_kv* kv, uint32_t tiles) {
+    if (!kv || tiles == 0) return LT_E_ARG;
+    kv->min_tiles_per_warp = tiles;
     return LT_OK;
 }
 

@@ -220,6 +220,8 @@ __global__ void rms_norm_q8_kernel(const float* __restrict__ x, const int32_t* _
 // 0.03 % of inputs (near rounding midpoints).
 __global__ void silu_q8_kernel(const float* __restrict__ gu, int n, int ffn, float* __restrict__ h,
                                int8_t* __restrict__ qs, float* __restrict__ scales) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // no-ops unless launched as a dependent
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const size_t per_row = (size_t)ffn / 8;  // a multiple of 4: groups are wholly in or out
     const bool live = i < per_row * n;
@@ -237,36 +239,40 @@ __global__ void silu_q8_kernel(const float* __restrict__ gu, int n, int ffn, flo
 }
 
 // RoPE of the q and k parts of one token's q|k|v row and the split into q,
-// k, v rows.  sincos [n][half][2] (sin, cos) of pos * inv_freq[i].
+// k, v rows.  sincos [n][half][2] (sin, cos) of pos * inv_freq[i].  Grid:
+// (tokens, ceil(row / 256)), one element a thread.  Launched as a dependent
+// of the q|k|v matmul: it waits for it before reading.
 __global__ void rope_split_kernel(const float* __restrict__ qkv, int q_dim, int kv_dim, int hd, int half, int neox,
                                   const float* __restrict__ sincos, float* __restrict__ qo, float* __restrict__ ko,
                                   float* __restrict__ vo) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int t = blockIdx.x;
+    const int j = blockIdx.y * blockDim.x + threadIdx.x;
+    if (j >= q_dim + 2 * kv_dim) return;
     const float* row = qkv + (size_t)t * (q_dim + 2 * kv_dim);
     const float* sc = sincos + (size_t)t * half * 2;
-    for (int j = threadIdx.x; j < q_dim + 2 * kv_dim; j += blockDim.x) {
-        float r = row[j];
-        if (j < q_dim + kv_dim) {
-            const int base = j - j % hd, c = j % hd;
-            int i = -1, partner = 0;
-            bool first = true;
-            if (neox) {
-                if (c < half) { i = c; partner = c + half; }
-                else if (c < 2 * half) { i = c - half; partner = c - half; first = false; }
-            } else if (c < 2 * half) {
-                i = c >> 1; partner = c ^ 1; first = (c & 1) == 0;
-            }
-            if (i >= 0) {
-                const float sn = sc[2 * i], cs = sc[2 * i + 1];
-                const float other = row[base + partner];
-                r = first ? __fsub_rn(__fmul_rn(r, cs), __fmul_rn(other, sn))     // x0 cos - x1 sin
-                          : __fadd_rn(__fmul_rn(other, sn), __fmul_rn(r, cs));    // x0 sin + x1 cos
-            }
+    float r = row[j];
+    if (j < q_dim + kv_dim) {
+        const int base = j - j % hd, c = j % hd;
+        int i = -1, partner = 0;
+        bool first = true;
+        if (neox) {
+            if (c < half) { i = c; partner = c + half; }
+            else if (c < 2 * half) { i = c - half; partner = c - half; first = false; }
+        } else if (c < 2 * half) {
+            i = c >> 1; partner = c ^ 1; first = (c & 1) == 0;
         }
-        if (j < q_dim) qo[(size_t)t * q_dim + j] = r;
-        else if (j < q_dim + kv_dim) ko[(size_t)t * kv_dim + (j - q_dim)] = r;
-        else vo[(size_t)t * kv_dim + (j - q_dim - kv_dim)] = r;
+        if (i >= 0) {
+            const float sn = sc[2 * i], cs = sc[2 * i + 1];
+            const float other = row[base + partner];
+            r = first ? __fsub_rn(__fmul_rn(r, cs), __fmul_rn(other, sn))     // x0 cos - x1 sin
+                      : __fadd_rn(__fmul_rn(other, sn), __fmul_rn(r, cs));    // x0 sin + x1 cos
+        }
     }
+    if (j < q_dim) qo[(size_t)t * q_dim + j] = r;
+    else if (j < q_dim + kv_dim) ko[(size_t)t * kv_dim + (j - q_dim)] = r;
+    else vo[(size_t)t * kv_dim + (j - q_dim - kv_dim)] = r;
 }
 
 // Embedding rows: x[i][j] = d[tok][j/32] * q[tok][j].
@@ -343,17 +349,342 @@ cudaError_t launch_rms_norm_q8(const float* x, const int32_t* rows_idx, const fl
     return cudaGetLastError();
 }
 
-cudaError_t launch_silu_q8(const float* gu, int n, int ffn, float* h, int8_t* qs, float* scales, cudaStream_t st) {
+cudaError_t launch_silu_q8(const float* gu, int n, int ffn, float* h, int8_t* qs, float* scales, cudaStream_t st,
+                           bool dependent = false) {
     const size_t threads = (size_t)n * ffn / 8;
     if (!threads) return cudaSuccess;
-    silu_q8_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(gu, n, ffn, h, qs, scales);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((threads + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dependent ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, silu_q8_kernel, gu, n, ffn, h, qs, scales);
+}
+
+cudaError_t launch_rope_split(const float* qkv, int n, int q_dim, int kv_dim, int hd, int half, int neox,
+                              const float* sincos, float* qo, float* ko, float* vo, cudaStream_t st) {
+    if (!n) return cudaSuccess;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n, (q_dim + 2 * kv_dim + 255) / 256);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, rope_split_kernel, qkv, q_dim, kv_dim, hd, half, neox, sincos, qo, ko, vo);
 }
 
 cudaError_t launch_argmax(const float* x, int n, int cols, int32_t* idx, cudaStream_t st) {
     if (!n) return cudaSuccess;
     argmax_kernel<<<n, 1024, 0, st>>>(x, cols, idx);
     return cudaGetLastError();
+}
+
+
+// ---------------------------------------------------------------------------
+// Decode matmul: q8_gemv_kernel, for n <= 8 tokens and cols % 256 == 0.
+//
+// One CTA owns 16 weight rows.  Thread 0 bulk-copies the rows and their f16
+// scales into shared memory (cp.async.bulk, one mbarrier) before the CTA
+// waits for the kernel that produced its activations (programmatic
+// dependent launch: griddepcontrol), so the weight stream of this matmul
+// overlaps the tail of the previous kernel.  The activation prologue is fused:
+// the CTA builds the int8 activations of its (up to 8) tokens in shared memory
+// from the producer's f32 output -- RMSNorm + quantize, quantize, or
+// SiLU * up + quantize -- with the same arithmetic, thread mapping and
+// reduction tree as the standalone kernels, so results are identical to
+// running them separately.  Then 16 warps run one s8 mma per 32-wide block
+// (block b to warp b % 16), overwrite the block's weight bytes with their f32
+// products, and warp 0 adds the products block by block from 0.0f in the
+// reference's order.
+
+constexpr int kGvWarps = 16;
+constexpr int kGvThreads = kGvWarps * 32;
+__device__ uint32_t g_op_err;  // error flag of the op-level entry points
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // bounded mbarrier wait: 2 s
+enum { PRO_Q8 = 0, PRO_QUANT = 1, PRO_SILU = 2, PRO_NORM = 3 };
+
+struct GemvArgs {
+    const int8_t* wq;
+    const __half* ws;
+    int rows, cols;
+    float* out;
+    int out_stride, accumulate, n;
+    const float* x;           // QUANT [n][cols]; SILU [n][2*cols]; NORM rows of [*][cols]
+    const int32_t* rows_idx;  // NORM: source row of each token (NULL: 0..n-1)
+    const float* gamma;       // NORM weight
+    float eps;
+    const int8_t* xq;         // Q8: activations given
+    const float* xs;
+    uint32_t* err;            // set to 1 when a bounded wait gives up
+};
+
+struct GemvSmem {
+    int pitch, ws_pitch, xs_pitch;
+    size_t off_w, off_ws, off_xq, off_xs, off_red, total;
+    __host__ __device__ explicit GemvSmem(int cols) {
+        const int nb = cols / kQK;
+        pitch = cols + 32;        // conflict-free 8-byte operand reads
+        ws_pitch = nb * 2 + 16;   // bytes; keeps the bulk-copy destinations 16-byte aligned
+        xs_pitch = nb + 4;        // floats
+        off_w = 128;
+        off_ws = off_w + (size_t)16 * pitch;
+        off_xq = off_ws + (size_t)16 * ws_pitch;
+        off_xs = off_xq + (size_t)8 * pitch;
+        off_red = off_xs + (size_t)8 * xs_pitch * 4;
+        total = off_red + 16 * 32 * 4;
+    }
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 15u) == 0 && global_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+__device__ __forceinline__ void pdl_trigger_and_wait() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// RMSNorm + quantize of token rows into shared memory: cols/8 threads per
+// token, the reduction tree of rms_norm_q8_kernel.
+__device__ __forceinline__ void prologue_norm(const GemvArgs& a, const GemvSmem& L, uint8_t* sm) {
+    const int tpt = a.cols / 8, per_pass = kGvThreads / tpt;
+    const int slot = threadIdx.x / tpt, i = threadIdx.x % tpt, nw = tpt / 32;
+    float* red = reinterpret_cast<float*>(sm + L.off_red);
+    for (int t0 = 0; t0 < a.n; t0 += per_pass) {
+        const int t = t0 + slot;
+        const bool live = t < a.n;
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (live) load8(a.x + (size_t)(a.rows_idx ? a.rows_idx[t] : t) * a.cols + i * 8, v);
+        float ss = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) ss = __fadd_rn(ss, __fmul_rn(v[k], v[k]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        if ((i & 31) == 0) red[slot * 32 + (i >> 5)] = ss;
+        __syncthreads();
+        if (i < 32) {
+            float s2 = i < nw ? red[slot * 32 + i] : 0.0f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s2 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, o));
+            if (i == 0) red[slot * 32] = s2;
+        }
+        __syncthreads();
+        const float ms = __fdiv_rn(red[slot * 32], (float)a.cols);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
+        float gv[8];
+        load8(a.gamma + i * 8, gv);
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = __fmul_rn(__fmul_rn(v[k], inv), gv[k]);
+        const int tt = live ? t : 0;
+        quant8_store(v, reinterpret_cast<int8_t*>(sm + L.off_xq) + (size_t)tt * L.pitch + i * 8,
+                     reinterpret_cast<float*>(sm + L.off_xs) + (size_t)tt * L.xs_pitch + i / 4, (i & 3) == 0, live);
+        __syncthreads();  // red is reused by the next pass
+    }
+}
+
+// Quantize (PRO_QUANT) or SiLU * up + quantize (PRO_SILU), 8 values a thread.
+template <int PRO>
+__device__ __forceinline__ void prologue_elementwise(const GemvArgs& a, const GemvSmem& L, uint8_t* sm) {
+    const int per_row = a.cols / 8;
+    const int total = a.n * per_row;
+    for (int base = 0; base < total; base += kGvThreads) {  // every lane takes every pass (group shuffles)
+        const int item = base + threadIdx.x;
+        const bool live = item < total;
+        const int t = live ? item / per_row : 0, c = live ? (item % per_row) * 8 : 0;
+        float v[8];
+        if (PRO == PRO_QUANT) {
+            load8(a.x + (size_t)t * a.cols + c, v);
+        } else {
+            float u[8];
+            load8(a.x + (size_t)t * 2 * a.cols + c, v);
+            load8(a.x + (size_t)t * 2 * a.cols + a.cols + c, u);
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const float e = (float)exp(-(double)v[k]);
+                v[k] = __fmul_rn(__fdiv_rn(v[k], __fadd_rn(1.0f, e)), u[k]);
+            }
+        }
+        quant8_store(v, reinterpret_cast<int8_t*>(sm + L.off_xq) + (size_t)t * L.pitch + c,
+                     reinterpret_cast<float*>(sm + L.off_xs) + (size_t)t * L.xs_pitch + c / kQK,
+                     (threadIdx.x & 3) == 0, live);
+    }
+}
+
+template <int PRO>
+__global__ void __launch_bounds__(kGvThreads) q8_gemv_kernel(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const GemvSmem L(a.cols);
+    const int nb = a.cols / kQK;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, q = lane & 3;
+    const int r0 = blockIdx.x * 16;
+    const uint32_t bar = smem_u32(sm);
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                     "r"((uint32_t)(16 * (a.cols + nb * 2)))
+                     : "memory");
+        for (int r = 0; r < 16; r++) {
+            const int rr = min(r0 + r, a.rows - 1);
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                    smem_u32(sm + L.off_w + (size_t)r * L.pitch)),
+                "l"(a.wq + (size_t)rr * a.cols), "r"((uint32_t)a.cols), "r"(bar)
+                : "memory");
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                    smem_u32(sm + L.off_ws + (size_t)r * L.ws_pitch)),
+                "l"(a.ws + (size_t)rr * nb), "r"((uint32_t)(nb * 2)), "r"(bar)
+                : "memory");
+        }
+    }
+    pdl_trigger_and_wait();  // activations come from the previous kernel
+    int8_t* xq_s = reinterpret_cast<int8_t*>(sm + L.off_xq);
+    float* xs_s = reinterpret_cast<float*>(sm + L.off_xs);
+    if (PRO == PRO_Q8) {
+        const int per_row = a.cols / 16;
+        for (int idx = tid; idx < a.n * per_row; idx += kGvThreads) {
+            const int t = idx / per_row, c = (idx % per_row) * 16;
+            *reinterpret_cast<int4*>(xq_s + (size_t)t * L.pitch + c) =
+                *reinterpret_cast<const int4*>(a.xq + (size_t)t * a.cols + c);
+        }
+        for (int idx = tid; idx < a.n * nb; idx += kGvThreads)
+            xs_s[(idx / nb) * L.xs_pitch + idx % nb] = a.xs[idx];
+    } else if (PRO == PRO_NORM) {
+        prologue_norm(a, L, sm);
+    } else {
+        prologue_elementwise<PRO>(a, L, sm);
+    }
+    // tokens n..7 read as zeros
+    for (int idx = tid; idx < (8 - a.n) * (a.cols / 16); idx += kGvThreads) {
+        const int t = a.n + idx / (a.cols / 16), c = (idx % (a.cols / 16)) * 16;
+        *reinterpret_cast<int4*>(xq_s + (size_t)t * L.pitch + c) = make_int4(0, 0, 0, 0);
+    }
+    for (int idx = tid; idx < (8 - a.n) * nb; idx += kGvThreads) xs_s[(a.n + idx / nb) * L.xs_pitch + idx % nb] = 0.f;
+    __syncthreads();
+    const bool ok = mbar_wait_bounded(bar, 0);
+    if (__syncthreads_or(!ok)) {
+        if (tid == 0) atomicExch(a.err, 1u);
+        return;
+    }
+    uint8_t* w_s = sm + L.off_w;
+    const __half* ws_s = reinterpret_cast<const __half*>(sm + L.off_ws);
+    for (int b = warp; b < nb; b += kGvWarps) {
+        const uint2 A0 = *reinterpret_cast<const uint2*>(w_s + (size_t)g * L.pitch + 32 * b + 8 * q);
+        const uint2 A1 = *reinterpret_cast<const uint2*>(w_s + (size_t)(g + 8) * L.pitch + 32 * b + 8 * q);
+        const uint2 B = *reinterpret_cast<const uint2*>(xq_s + (size_t)g * L.pitch + 32 * b + 8 * q);
+        int d[4];
+        mma_s8(d, A0.x, A1.x, A0.y, A1.y, B.x, B.y);
+        const float wsa = __half2float(ws_s[g * (L.ws_pitch / 2) + b]);
+        const float wsb = __half2float(ws_s[(g + 8) * (L.ws_pitch / 2) + b]);
+        const float xsa = xs_s[(2 * q) * L.xs_pitch + b], xsc = xs_s[(2 * q + 1) * L.xs_pitch + b];
+        float4 p;
+        p.x = __fmul_rn(__fmul_rn(wsa, xsa), __int2float_rn(d[0]));
+        p.y = __fmul_rn(__fmul_rn(wsa, xsc), __int2float_rn(d[1]));
+        p.z = __fmul_rn(__fmul_rn(wsb, xsa), __int2float_rn(d[2]));
+        p.w = __fmul_rn(__fmul_rn(wsb, xsc), __int2float_rn(d[3]));
+        __syncwarp();  // every lane has read block b before it is overwritten
+        *reinterpret_cast<float4*>(w_s + (size_t)(lane >> 1) * L.pitch + 32 * b + 16 * (lane & 1)) = p;
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const uint8_t* slot = w_s + (size_t)(lane >> 1) * L.pitch + 16 * (lane & 1);
+#pragma unroll 8
+    for (int b = 0; b < nb; b++) {
+        const float4 p = *reinterpret_cast<const float4*>(slot + 32 * b);
+        s.x = __fadd_rn(s.x, p.x);
+        s.y = __fadd_rn(s.y, p.y);
+        s.z = __fadd_rn(s.z, p.z);
+        s.w = __fadd_rn(s.w, p.w);
+    }
+    const float v[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = r0 + g + 8 * (i >> 1), t = 2 * q + (i & 1);
+        if (r < a.rows && t < a.n) {
+            float* o = a.out + (size_t)t * a.out_stride + r;
+            *o = a.accumulate ? __fadd_rn(*o, v[i]) : v[i];
+        }
+    }
+}
+
+bool gemv_ok(int cols, int n) {
+    return n >= 1 && n <= 8 && cols % 256 == 0 && GemvSmem(cols).total <= 220 * 1024;
+}
+
+bool norm_fusable(int cols) {
+    const int tpt = cols / 8;
+    return tpt >= 32 && tpt <= kGvThreads && kGvThreads % tpt == 0;
+}
+
+template <int PRO>
+cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t st) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(q8_gemv_kernel<PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((a.rows + 15) / 16);
+    cfg.blockDim = dim3(kGvThreads);
+    cfg.dynamicSmemBytes = GemvSmem(a.cols).total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, q8_gemv_kernel<PRO>, a);
+}
+
+cudaError_t launch_gemv(int pro, const GemvArgs& a, cudaStream_t st) {
+    switch (pro) {
+        case PRO_Q8: return launch_gemv_t<PRO_Q8>(a, st);
+        case PRO_QUANT: return launch_gemv_t<PRO_QUANT>(a, st);
+        case PRO_SILU: return launch_gemv_t<PRO_SILU>(a, st);
+        default: return launch_gemv_t<PRO_NORM>(a, st);
+    }
 }
 
 }  // namespace
@@ -388,6 +719,13 @@ struct lt_llama {
     std::vector<int32_t> blocks, slots;
     uint64_t launches = 0;
     std::vector<void*> allocs;
+    bool use_gemv = true;     // fused decode matmuls for up to 8 tokens
+    uint32_t* d_err = nullptr;  // device flag: a bounded wait gave up (ids[0], copied with the picks)
+    // matmul profiling: an event pair around each q8_matmul launch
+    bool prof = false;
+    std::vector<cudaEvent_t> prof_ev;
+    size_t prof_used = 0;
+    uint64_t prof_bytes = 0;
 };
 
 namespace {
@@ -420,6 +758,77 @@ struct DeviceGuard {
         if (prev >= 0 && cur != prev) cudaSetDevice(prev);
     }
 };
+
+// One projection of the forward: the activation prologue (RMSNorm +
+// quantize, quantize, or SiLU * up + quantize of the f32 input `x`) and the
+// Q8_0 matmul.  For up to 8 tokens both run in one q8_gemv_kernel launch;
+// otherwise the standalone prologue kernel, then q8_matmul_kernel.  With
+// profiling on, the matmul (or the fused launch) is bracketed by events.
+// Algorithmic bytes: weights and their f16 scales, the activations as the
+// matmul reads them, the f32 output (read too when accumulating).
+lt_status project(lt_llama* m, int pro, const QMat& w, const float* x, const int32_t* rows_idx, const float* gamma,
+                  int n, float* out, int out_stride, int accumulate, cudaStream_t st) {
+    const bool fused = m->use_gemv && gemv_ok((int)w.cols, n) && (pro != PRO_NORM || norm_fusable((int)w.cols));
+    if (fused && pro == PRO_SILU) {
+        // SiLU * up + quantize once, as a dependent launch, rather than in every
+        // matmul CTA (its double-precision exp is not cheap at ffn width)
+        LL_CUDA(m, launch_silu_q8(x, n, (int)w.cols, nullptr, m->xq, m->xs, st, true));
+        m->launches++;
+        pro = PRO_Q8;
+    }
+    if (!fused) {  // standalone prologue into m->xq / m->xs
+        cudaError_t e = cudaSuccess;
+        if (pro == PRO_NORM)
+            e = launch_rms_norm_q8(x, rows_idx, gamma, (int)w.cols, n, m->cfg.eps, nullptr, m->xq, m->xs, st);
+        else if (pro == PRO_QUANT)
+            e = launch_quantize(x, (size_t)n * w.cols, m->xq, m->xs, st);
+        else if (pro == PRO_SILU)
+            e = launch_silu_q8(x, n, (int)w.cols, nullptr, m->xq, m->xs, st);
+        if (e != cudaSuccess) return fail(m, LT_E_CUDA, "prologue launch: %s", cudaGetErrorString(e));
+        if (pro != PRO_Q8) m->launches++;
+    }
+    if (m->prof) {
+        if (m->prof_used + 2 > m->prof_ev.size()) {
+            for (int i = 0; i < 2; i++) {
+                cudaEvent_t e;
+                LL_CUDA(m, cudaEventCreate(&e));
+                m->prof_ev.push_back(e);
+            }
+        }
+        LL_CUDA(m, cudaEventRecord(m->prof_ev[m->prof_used], st));
+    }
+    if (fused) {
+        GemvArgs a = {};
+        a.wq = w.qs;
+        a.ws = w.sc;
+        a.rows = (int)w.rows;
+        a.cols = (int)w.cols;
+        a.out = out;
+        a.out_stride = out_stride;
+        a.accumulate = accumulate;
+        a.n = n;
+        a.x = x;
+        a.rows_idx = rows_idx;
+        a.gamma = gamma;
+        a.eps = m->cfg.eps;
+        a.xq = m->xq;
+        a.xs = m->xs;
+        a.err = m->d_err;
+        LL_CUDA(m, launch_gemv(pro, a, st));
+    } else {
+        LL_CUDA(m, launch_matmul(w.qs, w.sc, (int)w.rows, (int)w.cols, m->xq, m->xs, n, out, out_stride, accumulate,
+                                 st));
+    }
+    m->launches++;
+    if (m->prof) {
+        LL_CUDA(m, cudaEventRecord(m->prof_ev[m->prof_used + 1], st));
+        m->prof_used += 2;
+        const uint64_t rc = (uint64_t)w.rows * w.cols;
+        m->prof_bytes += rc + rc / kQK * 2 + (uint64_t)n * w.cols + (uint64_t)n * w.cols / kQK * 4 +
+                         (uint64_t)n * w.rows * 4 * (accumulate ? 2 : 1);
+    }
+    return LT_OK;
+}
 
 template <typename T>
 lt_status dalloc(lt_llama* m, T** p, size_t count) {
@@ -507,12 +916,16 @@ lt_status lt_llama_create(const lt_llama_config* cfg, lt_llama** out) {
     if (rc == LT_OK) rc = dalloc(m, &m->xq, B * m->maxc);
     if (rc == LT_OK) rc = dalloc(m, &m->xs, B * m->maxc / kQK);
     if (rc == LT_OK) rc = dalloc(m, &m->logits, B * c.vocab);
-    if (rc == LT_OK) rc = dalloc(m, &m->ids, B);
+    if (rc == LT_OK) rc = dalloc(m, &m->ids, B + 1);  // [0]: error flag, [1..]: picks
+    if (rc == LT_OK) {
+        m->d_err = reinterpret_cast<uint32_t*>(m->ids);
+        if (cudaMemset(m->ids, 0, sizeof(int32_t)) != cudaSuccess) rc = fail(m, LT_E_CUDA, "cudaMemset failed");
+    }
     // step metadata: tokens [B] | want [B] | sincos [B][half][2]
     m->meta_bytes = B * 4 * 2 + B * m->half * 2 * sizeof(float);
     if (rc == LT_OK) rc = dalloc(m, &m->meta_dev, m->meta_bytes);
     if (rc == LT_OK && (cudaMallocHost(&m->meta_host, m->meta_bytes) != cudaSuccess ||
-                        cudaMallocHost(&m->ids_host, B * sizeof(int32_t)) != cudaSuccess ||
+                        cudaMallocHost(&m->ids_host, (B + 1) * sizeof(int32_t)) != cudaSuccess ||
                         cudaEventCreateWithFlags(&m->meta_ev, cudaEventDisableTiming) != cudaSuccess))
         rc = fail(m, LT_E_CUDA, "pinned staging allocation failed");
     if (rc != LT_OK) {
@@ -532,6 +945,7 @@ void lt_llama_destroy(lt_llama* m) {
         cudaEventSynchronize(m->meta_ev);
         cudaEventDestroy(m->meta_ev);
     }
+    for (cudaEvent_t e : m->prof_ev) cudaEventDestroy(e);
     for (void* p : m->allocs) cudaFree(p);
     if (m->meta_host) cudaFreeHost(m->meta_host);
     if (m->ids_host) cudaFreeHost(m->ids_host);
@@ -541,6 +955,32 @@ void lt_llama_destroy(lt_llama* m) {
 const char* lt_llama_last_error(const lt_llama* m) { return m ? m->err.c_str() : "null handle"; }
 
 uint64_t lt_llama_launch_count(const lt_llama* m) { return m ? m->launches : 0; }
+
+lt_status lt_llama_profile(lt_llama* m, int enable) {
+    if (!m) return LT_E_ARG;
+    m->prof = enable != 0;
+    m->prof_used = 0;
+    m->prof_bytes = 0;
+    return LT_OK;
+}
+
+lt_status lt_llama_profile_read(lt_llama* m, double* matmul_ms, uint64_t* matmul_launches, uint64_t* matmul_bytes) {
+    if (!m || !matmul_ms || !matmul_launches || !matmul_bytes) return LT_E_ARG;
+    DeviceGuard dg(m->cfg.device);
+    double ms = 0.0;
+    for (size_t i = 0; i + 1 < m->prof_used; i += 2) {
+        float t = 0.0f;
+        LL_CUDA(m, cudaEventSynchronize(m->prof_ev[i + 1]));
+        LL_CUDA(m, cudaEventElapsedTime(&t, m->prof_ev[i], m->prof_ev[i + 1]));
+        ms += t;
+    }
+    *matmul_ms = ms;
+    *matmul_launches = m->prof_used / 2;
+    *matmul_bytes = m->prof_bytes;
+    m->prof_used = 0;
+    m->prof_bytes = 0;
+    return LT_OK;
+}
 
 lt_status lt_llama_set_tensor(lt_llama* m, lt_tensor which, uint32_t layer, const void* data, size_t bytes) {
     if (!m || !data) return LT_E_ARG;
@@ -640,29 +1080,23 @@ lt_status lt_llama_forward(lt_llama* m, lt_kv* kv, const int32_t* tokens, const 
     LL_CUDA(m, cudaGetLastError());
     m->launches++;
     for (uint32_t l = 0; l < c.n_layers; l++) {
-        LL_CUDA(m, launch_rms_norm_q8(m->x, nullptr, m->attn_norm[l], dim, (int)n, c.eps, nullptr, m->xq, m->xs, st));
-        LL_CUDA(m, launch_matmul(m->wqkv[l].qs, m->wqkv[l].sc, (int)m->qkv_rows, dim, m->xq, m->xs, (int)n, m->qkv,
-                                 (int)m->qkv_rows, 0, st));
-        rope_split_kernel<<<n, 256, 0, st>>>(m->qkv, qd, kvd, (int)c.head_dim, (int)m->half, c.rope_neox, d_sc, m->qb,
-                                            m->kb, m->vb);
-        LL_CUDA(m, cudaGetLastError());
-        m->launches += 3;
+        rc = project(m, PRO_NORM, m->wqkv[l], m->x, nullptr, m->attn_norm[l], (int)n, m->qkv, (int)m->qkv_rows, 0, st);
+        if (rc != LT_OK) return rc;
+        LL_CUDA(m, launch_rope_split(m->qkv, (int)n, qd, kvd, (int)c.head_dim, (int)m->half, c.rope_neox, d_sc, m->qb,
+                                     m->kb, m->vb, st));
+        m->launches++;
         rc = lt_kv_write_attend(kv, l, m->blocks.data(), m->slots.data(), m->kb, m->vb, LT_F32, m->qb, LT_F32, seqs,
                                 pos, n, m->att, LT_F32, scale, stream);
         if (rc != LT_OK) return fail(m, rc, "%s", lt_kv_last_error(kv));
-        LL_CUDA(m, launch_quantize(m->att, (size_t)n * qd, m->xq, m->xs, st));
-        LL_CUDA(m, launch_matmul(m->wo[l].qs, m->wo[l].sc, dim, qd, m->xq, m->xs, (int)n, m->x, dim, 1, st));
-        LL_CUDA(m, launch_rms_norm_q8(m->x, nullptr, m->ffn_norm[l], dim, (int)n, c.eps, nullptr, m->xq, m->xs, st));
-        LL_CUDA(m, launch_matmul(m->wgu[l].qs, m->wgu[l].sc, 2 * ffn, dim, m->xq, m->xs, (int)n, m->gu, 2 * ffn, 0, st));
-        LL_CUDA(m, launch_silu_q8(m->gu, (int)n, ffn, nullptr, m->xq, m->xs, st));
-        LL_CUDA(m, launch_matmul(m->wdown[l].qs, m->wdown[l].sc, dim, ffn, m->xq, m->xs, (int)n, m->x, dim, 1, st));
-        m->launches += 6;
+        if ((rc = project(m, PRO_QUANT, m->wo[l], m->att, nullptr, nullptr, (int)n, m->x, dim, 1, st)) != LT_OK) return rc;
+        rc = project(m, PRO_NORM, m->wgu[l], m->x, nullptr, m->ffn_norm[l], (int)n, m->gu, 2 * ffn, 0, st);
+        if (rc != LT_OK) return rc;
+        if ((rc = project(m, PRO_SILU, m->wdown[l], m->gu, nullptr, nullptr, (int)n, m->x, dim, 1, st)) != LT_OK)
+            return rc;
     }
     if (n_want) {  // model.rs:502-517
-        LL_CUDA(m, launch_rms_norm_q8(m->x, d_want, m->out_norm, dim, (int)n_want, c.eps, nullptr, m->xq, m->xs, st));
-        LL_CUDA(m, launch_matmul(m->output.qs, m->output.sc, (int)c.vocab, dim, m->xq, m->xs, (int)n_want, logits,
-                                 (int)c.vocab, 0, st));
-        m->launches += 2;
+        rc = project(m, PRO_NORM, m->output, m->x, d_want, m->out_norm, (int)n_want, logits, (int)c.vocab, 0, st);
+        if (rc != LT_OK) return rc;
     }
     return LT_OK;
 }
@@ -676,11 +1110,15 @@ lt_status lt_llama_step_greedy(lt_llama* m, lt_kv* kv, const int32_t* tokens, co
     if (rc != LT_OK || n_want == 0) return rc;
     DeviceGuard dg(m->cfg.device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    LL_CUDA(m, launch_argmax(m->logits, (int)n_want, (int)m->cfg.vocab, m->ids, st));
+    LL_CUDA(m, launch_argmax(m->logits, (int)n_want, (int)m->cfg.vocab, m->ids + 1, st));
     m->launches++;
-    LL_CUDA(m, cudaMemcpyAsync(m->ids_host, m->ids, n_want * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    LL_CUDA(m, cudaMemcpyAsync(m->ids_host, m->ids, (n_want + 1) * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
     LL_CUDA(m, cudaStreamSynchronize(st));
-    std::memcpy(next_host, m->ids_host, n_want * sizeof(int32_t));
+    if (m->ids_host[0] != 0) {
+        cudaMemsetAsync(m->ids, 0, sizeof(int32_t), st);
+        return fail(m, LT_E_TIMEOUT, "a matmul's bounded wait for its weight copies gave up");
+    }
+    std::memcpy(next_host, m->ids_host + 1, n_want * sizeof(int32_t));
     return LT_OK;
 }
 
@@ -698,9 +1136,26 @@ lt_status lt_q8_matmul(const int8_t* w_qs, const uint16_t* w_scales, uint32_t ro
                        void* stream) {
     if (!w_qs || !w_scales || !x_qs || !x_scales || !out || cols % kQK || out_stride < rows) return LT_E_ARG;
     if ((reinterpret_cast<uintptr_t>(w_qs) | reinterpret_cast<uintptr_t>(x_qs)) & 7) return LT_E_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (gemv_ok((int)cols, (int)n) && !((reinterpret_cast<uintptr_t>(w_qs) | reinterpret_cast<uintptr_t>(w_scales) |
+                                         reinterpret_cast<uintptr_t>(x_qs)) & 15)) {
+        GemvArgs a = {};
+        a.wq = w_qs;
+        a.ws = reinterpret_cast<const __half*>(w_scales);
+        a.rows = (int)rows;
+        a.cols = (int)cols;
+        a.out = out;
+        a.out_stride = (int)out_stride;
+        a.accumulate = accumulate;
+        a.n = (int)n;
+        a.xq = x_qs;
+        a.xs = x_scales;
+        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&a.err), g_op_err) != cudaSuccess) return LT_E_CUDA;
+        return launch_gemv(PRO_Q8, a, st) == cudaSuccess ? LT_OK : LT_E_CUDA;
+    }
     if ((size_t)cols / kQK * 32 * sizeof(float4) > 200 * 1024) return LT_E_UNSUPPORTED;
     return launch_matmul(w_qs, reinterpret_cast<const __half*>(w_scales), (int)rows, (int)cols, x_qs, x_scales, (int)n,
-                         out, (int)out_stride, accumulate, static_cast<cudaStream_t>(stream)) == cudaSuccess
+                         out, (int)out_stride, accumulate, st) == cudaSuccess
                ? LT_OK : LT_E_CUDA;
 }
 
@@ -723,6 +1178,72 @@ lt_status lt_argmax_f32(const float* x, uint32_t n, uint32_t cols, int32_t* idx,
     if (!x || !idx || !cols) return LT_E_ARG;
     return launch_argmax(x, (int)n, (int)cols, idx, static_cast<cudaStream_t>(stream)) == cudaSuccess ? LT_OK
                                                                                                       : LT_E_CUDA;
+}
+
+lt_status lt_q8_project(int prologue, const int8_t* w_qs, const uint16_t* w_scales, uint32_t rows, uint32_t cols,
+                        const float* x, const int32_t* rows_idx, const float* gamma, float eps, uint32_t n,
+                        float* out, uint32_t out_stride, int fused, int accumulate, void* stream) {
+    if (prologue < LT_PRO_QUANT || prologue > LT_PRO_RMSNORM || !w_qs || !w_scales || !x || !out || cols % kQK ||
+        out_stride < rows || n == 0)
+        return LT_E_ARG;
+    if (prologue == LT_PRO_RMSNORM && (!gamma || cols % 256 || cols / 8 > 1024)) return LT_E_ARG;
+    if ((reinterpret_cast<uintptr_t>(w_qs) | reinterpret_cast<uintptr_t>(w_scales) | reinterpret_cast<uintptr_t>(x)) &
+        15)
+        return LT_E_ARG;
+    const int pro = prologue == LT_PRO_QUANT ? PRO_QUANT : prologue == LT_PRO_SILU ? PRO_SILU : PRO_NORM;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (fused && gemv_ok((int)cols, (int)n) && (pro != PRO_NORM || norm_fusable((int)cols))) {
+        GemvArgs a = {};
+        a.wq = w_qs;
+        a.ws = reinterpret_cast<const __half*>(w_scales);
+        a.rows = (int)rows;
+        a.cols = (int)cols;
+        a.out = out;
+        a.out_stride = (int)out_stride;
+        a.accumulate = accumulate;
+        a.n = (int)n;
+        a.x = x;
+        a.rows_idx = rows_idx;
+        a.gamma = gamma;
+        a.eps = eps;
+        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&a.err), g_op_err) != cudaSuccess) return LT_E_CUDA;
+        return launch_gemv(pro, a, st) == cudaSuccess ? LT_OK : LT_E_CUDA;
+    }
+    // two launches: the standalone prologue kernel into scratch, then the matmul
+    int8_t* xq = nullptr;
+    float* xs = nullptr;
+    if (cudaMallocAsync(reinterpret_cast<void**>(&xq), (size_t)n * cols + 16, st) != cudaSuccess) return LT_E_CUDA;
+    if (cudaMallocAsync(reinterpret_cast<void**>(&xs), (size_t)n * cols / kQK * 4 + 16, st) != cudaSuccess) {
+        cudaFreeAsync(xq, st);
+        return LT_E_CUDA;
+    }
+    cudaError_t e;
+    if (pro == PRO_NORM)
+        e = launch_rms_norm_q8(x, rows_idx, gamma, (int)cols, (int)n, eps, nullptr, xq, xs, st);
+    else if (pro == PRO_QUANT)
+        e = launch_quantize(x, (size_t)n * cols, xq, xs, st);
+    else
+        e = launch_silu_q8(x, (int)n, (int)cols, nullptr, xq, xs, st);
+    lt_status rc = e == cudaSuccess ? lt_q8_matmul(w_qs, w_scales, rows, cols, xq, xs, n, out, out_stride, accumulate,
+                                                   stream)
+                                    : LT_E_CUDA;
+    cudaFreeAsync(xq, st);
+    cudaFreeAsync(xs, st);
+    return rc;
+}
+
+lt_status lt_q8_check(void* stream) {
+    uint32_t* p = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_op_err) != cudaSuccess) return LT_E_CUDA;
+    uint32_t v = 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(&v, p, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
+        return LT_E_CUDA;
+    if (v) {
+        cudaMemsetAsync(p, 0, 4, st);
+        return LT_E_TIMEOUT;
+    }
+    return LT_OK;
 }
 
 }  // extern "C"

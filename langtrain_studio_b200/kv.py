@@ -259,6 +259,10 @@ class KvCache:
         self._check(self._lib.lt_kv_profile_read(self._h, C.byref(ms), C.byref(n)))
         return ms.value, n.value
 
+    def set_min_tiles_per_warp(self, tiles: int):
+        """Attention launch sizing: at least `tiles` tiles per warp (default 8)."""
+        self._check(self._lib.lt_kv_set_min_tiles_per_warp(self._h, tiles))
+
     def launch_count(self) -> int:
         return self._lib.lt_kv_launch_count(self._h)
 

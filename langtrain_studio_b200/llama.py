@@ -120,6 +120,49 @@ class Llama:
     def launch_count(self) -> int:
         return self._lib.lt_llama_launch_count(self._h)
 
+    def profile(self, enable: bool = True):
+        _check_op(self._lib.lt_llama_profile(self._h, int(enable)), "lt_llama_profile")
+
+    def profile_read(self):
+        """(matmul device ms, launches, algorithmic bytes) since the last read."""
+        ms, n, b = C.c_double(), C.c_uint64(), C.c_uint64()
+        rc = self._lib.lt_llama_profile_read(self._h, C.byref(ms), C.byref(n), C.byref(b))
+        if rc != N.LT_OK:
+            raise self._err(rc)
+        return ms.value, n.value, b.value
+
+
+def random_q8_0(rows: int, cols: int, sigma: float, rng: np.random.Generator) -> bytes:
+    """A synthetic Q8_0 tensor in its GGUF encoding (34-byte blocks {f16 d;
+    int8 qs[32]}): int8 values uniform in [-127, 127] and per-block scales
+    around sigma * sqrt(3) / 127, so entries have standard deviation ~sigma."""
+    nb = rows * cols // 32
+    out = np.empty((nb, 34), np.uint8)
+    d = (sigma * np.sqrt(3.0) / 127.0 * rng.uniform(0.5, 1.5, nb)).astype(np.float16)
+    out[:, :2] = d.view(np.uint8).reshape(nb, 2)
+    out[:, 2:] = rng.integers(-127, 128, (nb, 32), dtype=np.int8).view(np.uint8)
+    return out.tobytes()
+
+
+def random_weights(model: "Llama", seed: int = 0):
+    """tensor(which, layer) -> bytes for a random-init model of model's shape:
+    matrices ~ 0.02 (embedding ~ 1), norm vectors of ones."""
+    rng = np.random.default_rng(seed)
+    qd, kvd = model.q_dim, model.kv_dim
+    shapes = {EMBED: (model.vocab, model.dim, 1.0), OUTPUT: (model.vocab, model.dim, 0.02),
+              Q: (qd, model.dim, 0.02), K: (kvd, model.dim, 0.02), V: (kvd, model.dim, 0.02),
+              O: (model.dim, qd, 0.02), GATE: (model.ffn_dim, model.dim, 0.02), UP: (model.ffn_dim, model.dim, 0.02),
+              DOWN: (model.dim, model.ffn_dim, 0.02)}
+    ones = np.ones(model.dim, np.float32).tobytes()
+
+    def tensor(which, layer):
+        if which in (OUTPUT_NORM, ATTN_NORM, FFN_NORM):
+            return ones
+        rows, cols, sigma = shapes[which]
+        return random_q8_0(rows, cols, sigma, rng)
+
+    return tensor
+
 
 def serve_shared_prefix(model: Llama, kv: KvCache, prompts: np.ndarray, shared: int, n_gen: int,
                         teacher: np.ndarray | None = None, logits_out=None, stream=None) -> np.ndarray:
@@ -176,6 +219,32 @@ def q8_matmul(w_qs, w_scales_f16, x_qs, x_scales, out=None, accumulate=False, st
     _check_op(N.lib().lt_q8_matmul(_dptr(w_qs), _dptr(w_scales_f16), rows, cols, _dptr(x_qs), _dptr(x_scales), n,
                                    _dptr(out), out.stride(0), int(accumulate), _stream(stream)), "lt_q8_matmul")
     return out
+
+
+PRO_QUANT, PRO_SILU, PRO_RMSNORM = 1, 2, 3
+
+
+def q8_project(prologue: int, w_qs, w_scales_f16, x, rows_idx=None, gamma=None, eps: float = 1e-5, out=None,
+               accumulate=False, fused=True, stream=None):
+    """Activation prologue (quantize / SiLU * up + quantize / RMSNorm +
+    quantize of f32 x) and the Q8_0 matmul; one launch when fused and n <= 8."""
+    import torch
+
+    rows, cols = w_qs.shape
+    n = rows_idx.numel() if rows_idx is not None else x.shape[0]
+    if out is None:
+        out = torch.empty((n, rows), dtype=torch.float32, device=w_qs.device)
+    idx = None if rows_idx is None else _dptr(rows_idx)
+    g = None if gamma is None else _dptr(gamma)
+    _check_op(N.lib().lt_q8_project(prologue, _dptr(w_qs), _dptr(w_scales_f16), rows, cols, _dptr(x), idx, g, eps, n,
+                                    _dptr(out), out.stride(0), int(fused), int(accumulate), _stream(stream)),
+              "lt_q8_project")
+    return out
+
+
+def q8_check(stream=None):
+    """Raise if an op-level matmul's bounded wait gave up (synchronises)."""
+    _check_op(N.lib().lt_q8_check(_stream(stream)), "lt_q8_check")
 
 
 def rms_norm_q8(x, w, eps: float, rows_idx=None, stream=None):

@@ -168,6 +168,37 @@ def test_rms_norm_quantize_within_ulps(dim, n):
     assert np.array_equal(sc.cpu().numpy().view(np.uint32), so.view(np.uint32))
 
 
+@pytest.mark.parametrize("pro,rows,cols,n", [(LL.PRO_QUANT, 2048, 2048, 4), (LL.PRO_QUANT, 40, 256, 1),
+                                             (LL.PRO_SILU, 2048, 5632, 4), (LL.PRO_SILU, 33, 512, 8),
+                                             (LL.PRO_RMSNORM, 2560, 2048, 4), (LL.PRO_RMSNORM, 1000, 2048, 3),
+                                             (LL.PRO_RMSNORM, 64, 256, 8), (LL.PRO_QUANT, 2048, 2048, 12)])
+def test_fused_projection_equals_two_launches(pro, rows, cols, n):
+    """The decode path (prologue fused into the matmul launch) gives the bits
+    of the standalone prologue kernel followed by the matmul."""
+    rng = np.random.default_rng(rows + cols + n + pro)
+    wq = _cuda(rng.integers(-128, 128, (rows, cols), dtype=np.int8))
+    ws = _cuda((rng.random((rows, cols // 32)) * 0.01).astype(np.float16).view(np.uint16))
+    width = 2 * cols if pro == LL.PRO_SILU else cols
+    x = _cuda((rng.standard_normal((n + 3, width)) * 2).astype(np.float32))
+    idx = gamma = None
+    if pro == LL.PRO_RMSNORM:
+        gamma = _cuda((1 + 0.1 * rng.standard_normal(cols)).astype(np.float32))
+        idx = _cuda(rng.permutation(n + 3)[:n].astype(np.int32))
+    else:
+        x = x[:n].contiguous()
+    base = rng.standard_normal((n, rows)).astype(np.float32)
+    outs = []
+    for fused in (True, False):
+        for acc in (False, True):
+            o = _cuda(base) if acc else None
+            outs.append(LL.q8_project(pro, wq, ws, x, rows_idx=idx, gamma=gamma, out=o, accumulate=acc,
+                                      fused=fused).cpu().numpy())
+    LL.q8_check()
+    assert np.array_equal(outs[0].view(np.uint32), outs[2].view(np.uint32))
+    assert np.array_equal(outs[1].view(np.uint32), outs[3].view(np.uint32))
+    assert np.array_equal(outs[1].view(np.uint32), (base + outs[0]).view(np.uint32))
+
+
 TINY = dict(dim=256, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=64, ffn_dim=512, vocab=1000)
 
 

@@ -189,11 +189,17 @@ ATT_CASES = [
 
 
 @pytest.mark.parametrize("hd,hq,hkv,lens", ATT_CASES)
-@pytest.mark.parametrize("q_dtype,out_dtype", [(torch.float32, torch.float32), (torch.float16, torch.float16)])
-def test_attention_matches_oracle(oracle_mod, hd, hq, hkv, lens, q_dtype, out_dtype):
+@pytest.mark.parametrize("q_dtype,out_dtype,min_tiles", [(torch.float32, torch.float32, 8),
+                                                         (torch.float16, torch.float16, 8),
+                                                         (torch.float32, torch.float32, 1),
+                                                         (torch.float16, torch.float32, 3)])
+def test_attention_matches_oracle(oracle_mod, hd, hq, hkv, lens, q_dtype, out_dtype, min_tiles):
+    """min_tiles 1 splits every (token, head) over the most warps (the most
+    merges); the default 8 is the launch sizing of small steps."""
     rng = np.random.default_rng(hd + hq + len(lens))
     total = sum((L + 16) // 16 for L in lens) + 8
     t = Twin(oracle_mod, 1, hkv, hd, 16 * total, n_heads=hq, max_seqs=len(lens))
+    t.kv.set_min_tiles_per_warp(min_tiles)
     for s, L in enumerate(lens):
         t.fill(s, L, rng)
     seqs = np.arange(len(lens))
@@ -296,6 +302,7 @@ def test_random_ops_full_parity(oracle_mod, seed):
     rng = np.random.default_rng(100 + seed)
     max_seqs = 10
     t = Twin(oracle_mod, 2, 2, 64, 16 * 60, n_heads=4, max_seqs=max_seqs)
+    t.kv.set_min_tiles_per_warp([1, 8, 2][seed % 3])
     for step in range(120):
         r = rng.random()
         if r < 0.5:
