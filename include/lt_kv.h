@@ -211,6 +211,19 @@ uint64_t lt_kv_launch_count(const lt_kv* kv);
  * depend on it beyond f32 summation order of split merges. */
 lt_status lt_kv_set_min_tiles_per_warp(lt_kv* kv, uint32_t tiles);
 
+/* Shared-prefix (cascade) attention.  In an attention call, tokens whose
+ * sequences begin with the same physical blocks (prefix sharing, kv.rs:172)
+ * -- at least `min_group_tokens` of them, sharing at least 4 leading blocks
+ * before every member's own last block -- have those blocks attended in one
+ * extra launch that stages each shared K/V tile once for the whole group;
+ * the decode launch then covers only each token's own blocks and folds the
+ * prefix result in (online-softmax merge, f32).  Default 8; 0 turns it off.
+ * Calls of more than 2048 tokens (or max_batch) never use it. */
+lt_status lt_kv_set_cascade(lt_kv* kv, uint32_t min_group_tokens);
+
+/* Prefix-pass launches issued by this handle since creation. */
+uint64_t lt_kv_cascade_launches(const lt_kv* kv);
+
 /* ---- KV-head sharding across GPUs (NCCL) ---------------------------------- */
 /* No counterpart in the reference, which runs one process.  For long
  * contexts the KV heads are split across ranks: rank r's handle holds KV

@@ -25,7 +25,7 @@ EXPORTS = (
     "lt_kv_seq_blocks", "lt_kv_refs", "lt_kv_free_list", "lt_kv_n_blocks", "lt_kv_device_pool",
     "lt_kv_device_tables", "lt_kv_read_pool", "lt_kv_launch_count", "lt_kv_profile", "lt_kv_profile_read",
     "lt_kv_nccl_unique_id", "lt_kv_nccl_init", "lt_kv_nccl_destroy", "lt_kv_gather_heads",
-    "lt_paged_attend_noalloc", "lt_kv_set_min_tiles_per_warp",
+    "lt_paged_attend_noalloc", "lt_kv_set_min_tiles_per_warp", "lt_kv_set_cascade", "lt_kv_cascade_launches",
     "lt_llama_create", "lt_llama_destroy", "lt_llama_last_error", "lt_llama_set_tensor", "lt_llama_forward",
     "lt_llama_step_greedy", "lt_llama_launch_count", "lt_llama_profile", "lt_llama_profile_read", "lt_q8_quantize", "lt_q8_matmul", "lt_rms_norm_q8",
     "lt_silu_q8", "lt_argmax_f32", "lt_q8_project", "lt_q8_check",
@@ -98,6 +98,8 @@ def _declare(L):
         "lt_kv_read_pool": (st, [p, u32, u32, u32, p]),
         "lt_kv_launch_count": (u64, [p]),
         "lt_kv_set_min_tiles_per_warp": (st, [p, u32]),
+        "lt_kv_set_cascade": (st, [p, u32]),
+        "lt_kv_cascade_launches": (u64, [p]),
         "lt_kv_profile": (st, [p, C.c_int]),
         "lt_kv_profile_read": (st, [p, C.POINTER(C.c_double), C.POINTER(u64)]),
         "lt_kv_nccl_unique_id": (st, [p]),

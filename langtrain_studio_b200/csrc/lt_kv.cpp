@@ -27,6 +27,8 @@ using ltkv::kBlock;
 namespace {
 
 constexpr int kSlots = 8;  // staging ring depth (pinned host + device pairs)
+constexpr uint32_t kCascadeMaxTokens = 2048;  // tokens of one call the prefix pass serves
+constexpr int kCascadeMinBlocks = 4;          // shortest shared prefix worth a pass (64 positions)
 constexpr uint32_t kClean = 0xFFFFFFFFu;
 
 struct Slot {
@@ -65,6 +67,15 @@ struct DeviceGuard {
 struct lt_kv {
     lt_kv_config cfg{};
     uint32_t min_tiles_per_warp = 8;  // attention launch sizing (lt_kv_set_min_tiles_per_warp)
+    // shared-prefix (cascade) pass: groups of >= cascade_min_tokens tokens
+    // whose sequences share >= kCascadeMinBlocks leading blocks (0: off)
+    uint32_t cascade_min_tokens = 8;
+    uint32_t pre_cap = 0;          // tokens the prefix partial buffers hold
+    float* d_pre_o = nullptr;      // [pre_cap][n_heads][head_dim]
+    float* d_pre_ml = nullptr;     // [pre_cap][n_heads][2]
+    std::vector<uint32_t> casc_order;
+    std::vector<int32_t> casc_buf;  // upload image: PrefixItems then the token list
+    uint64_t cascade_launches = 0;
     uint32_t n_blocks = 0, kv_dim = 0, group = 0, max_blocks = 0;
     size_t block_elems = 0;   // f16 elements of one block in one layer (all heads, K and V)
     size_t layer_elems = 0;   // f16 elements of one layer of the pool
@@ -108,7 +119,7 @@ struct lt_kv {
     double prof_ms = 0.0;
     uint64_t prof_count = 0;
 
-    UploadCache cells_cache, items_cache;
+    UploadCache cells_cache, items_cache, casc_cache;
     std::vector<ltkv::TokenDesc> toks_tmp;
     std::vector<std::pair<size_t, int32_t>> fold_tmp;  // (table index, previous shadow value)
     std::vector<uint32_t> fold_mark, fold_pos;         // per sequence, for one call
@@ -141,6 +152,9 @@ void free_device(lt_kv* kv) {
     cudaFree(kv->d_tables);
     cudaFree(kv->d_part_o);
     cudaFree(kv->d_part_ml);
+    cudaFree(kv->d_pre_o);
+    cudaFree(kv->d_pre_ml);
+    kv->d_pre_o = kv->d_pre_ml = nullptr;
     cudaFree(kv->d_err);
     cudaFree(kv->d_flags);
     kv->d_flags = nullptr;
@@ -373,6 +387,64 @@ lt_status prof_begin(lt_kv* kv, cudaStream_t st, cudaEvent_t* end) {
     return LT_OK;
 }
 
+// Shared-prefix groups of one attention call: tokens whose sequences start
+// with the same block, at least cascade_min_tokens of them, sharing at least
+// kCascadeMinBlocks leading blocks (all strictly before every member token's
+// own block).  Each group's tokens get skip = its shared block count; the
+// prefix pass items (KV head x chunks of the group's tokens) and the token
+// list go to casc_buf.  Returns the number of items (0: no pass).
+int plan_cascade(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n) {
+    if (kv->cascade_min_tokens == 0 || n < kv->cascade_min_tokens || n > kv->pre_cap) return 0;
+    auto& ord = kv->casc_order;
+    ord.resize(n);
+    for (uint32_t i = 0; i < n; ++i) ord[i] = i;
+    std::sort(ord.begin(), ord.end(), [&](uint32_t a, uint32_t b) {
+        const int32_t fa = kv->blocks[seq[a]][0], fb = kv->blocks[seq[b]][0];
+        return fa != fb ? fa < fb : a < b;
+    });
+    const int tpc = ltkv::prefix_tokens_per_cta((int)kv->group);
+    const uint32_t hkv = kv->cfg.n_kv_heads;
+    std::vector<ltkv::PrefixItem> items;
+    std::vector<int32_t> toks;
+    for (uint32_t a = 0; a < n;) {
+        const int32_t first = kv->blocks[seq[ord[a]]][0];
+        uint32_t b = a + 1;
+        while (b < n && kv->blocks[seq[ord[b]]][0] == first) ++b;
+        if (b - a >= kv->cascade_min_tokens) {
+            const uint32_t root = seq[ord[a]];
+            const std::vector<int32_t>& rb = kv->blocks[root];
+            size_t P = pos[ord[a]] / kBlock;
+            for (uint32_t k = a; k < b && P >= (size_t)kCascadeMinBlocks; ++k) {
+                const uint32_t i = ord[k];
+                P = std::min<size_t>(P, pos[i] / kBlock);
+                if (seq[i] != root) {
+                    const std::vector<int32_t>& sb = kv->blocks[seq[i]];
+                    const size_t lim = std::min(P, std::min(sb.size(), rb.size()));
+                    P = (size_t)(std::mismatch(rb.begin(), rb.begin() + lim, sb.begin()).first - rb.begin());
+                }
+            }
+            if (P >= (size_t)kCascadeMinBlocks) {
+                const int32_t off = (int32_t)toks.size();
+                for (uint32_t k = a; k < b; ++k) {
+                    toks.push_back((int32_t)ord[k]);
+                    kv->toks_tmp[ord[k]].skip = (int32_t)P;
+                }
+                const int32_t cnt = (int32_t)(b - a);
+                for (uint32_t h = 0; h < hkv; ++h)
+                    for (int32_t c0 = 0; c0 < cnt; c0 += tpc)
+                        items.push_back({(int32_t)root, (int32_t)P, (int32_t)h, off + c0, std::min(tpc, cnt - c0)});
+            }
+        }
+        a = b;
+    }
+    kv->casc_buf.resize(items.size() * (sizeof(ltkv::PrefixItem) / 4) + toks.size());
+    if (!items.empty()) std::memcpy(kv->casc_buf.data(), items.data(), items.size() * sizeof(ltkv::PrefixItem));
+    if (!toks.empty())
+        std::memcpy(kv->casc_buf.data() + items.size() * (sizeof(ltkv::PrefixItem) / 4), toks.data(),
+                    toks.size() * sizeof(int32_t));
+    return (int)items.size();
+}
+
 lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype, const uint32_t* seq,
                       const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale, const void* k,
                       const void* v, lt_dtype kv_dtype, bool fused, cudaStream_t st) {
@@ -385,14 +457,19 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     const int max_warps = ltkv::attend_warps(kv->cfg.device, (int)kv->group, (int)kv->cfg.head_dim, q_f32);
     if (max_warps <= 0) return fail(kv, LT_E_CUDA, "could not size the attention launch on device %d", kv->cfg.device);
     kv->toks_tmp.resize(n);
-    long long tiles = 0;
     for (uint32_t i = 0; i < n; ++i) {
         ltkv::TokenDesc& t = kv->toks_tmp[i];
         t.seq = (int32_t)seq[i];
         t.pos = (int32_t)pos[i];
         t.last_block = kv->blocks[seq[i]][pos[i] / kBlock];
+        t.skip = 0;
+    }
+    const int n_items = plan_cascade(kv, seq, pos, n);  // sets skip of the tokens it covers
+    long long tiles = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        ltkv::TokenDesc& t = kv->toks_tmp[i];
         t.prefix = (int32_t)tiles;
-        tiles += pos[i] / kBlock + 1;
+        tiles += pos[i] / kBlock + 1 - t.skip;
     }
     if (tiles > 0x7FFFFFFFll / kv->cfg.n_kv_heads) return fail(kv, LT_E_ARG, "attention call too large");
     // The kernel writes every token's last table entry itself.  For the
@@ -469,10 +546,43 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
         }
         p.toks = static_cast<const ltkv::TokenDesc*>(d_toks);
     }
+    p.pre_o = kv->d_pre_o;
+    p.pre_ml = kv->d_pre_ml;
     cudaEvent_t ev_end = nullptr;
     if (kv->profiling) {
         lt_status prc = prof_begin(kv, st, &ev_end);
         if (prc) return prc;
+    }
+    int s_casc = -1;
+    if (n_items > 0) {
+        const void* d_casc = nullptr;
+        rc = upload(kv, kv->casc_cache, kv->casc_buf.data(), kv->casc_buf.size() * sizeof(int32_t), st, &d_casc,
+                    &s_casc);
+        if (rc) {
+            rollback();
+            return rc;
+        }
+        ltkv::PrefixParams pp{};
+        pp.pool_layer = p.pool_layer;
+        pp.tables = kv->d_tables;
+        pp.max_blocks = (int32_t)kv->max_blocks;
+        pp.items = static_cast<const ltkv::PrefixItem*>(d_casc);
+        pp.tok_list = static_cast<const int32_t*>(d_casc) + (size_t)n_items * (sizeof(ltkv::PrefixItem) / 4);
+        pp.n_kv_heads = (int32_t)kv->cfg.n_kv_heads;
+        pp.group = (int32_t)kv->group;
+        pp.q = q;
+        pp.q_f32 = q_f32;
+        pp.scale_log2 = p.scale_log2;
+        pp.pre_o = kv->d_pre_o;
+        pp.pre_ml = kv->d_pre_ml;
+        pp.err = kv->d_err;
+        const cudaError_t pe = ltkv::launch_prefix(pp, n_items, (int)kv->cfg.head_dim, st);
+        if (pe != cudaSuccess) {
+            rollback();
+            return fail(kv, LT_E_CUDA, "prefix launch: %s", cudaGetErrorString(pe));
+        }
+        kv->launches++;
+        kv->cascade_launches++;
     }
     const cudaError_t le = ltkv::launch_attend(p, (int)kv->cfg.head_dim, st);
     if (le != cudaSuccess) {
@@ -481,6 +591,7 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     }
     kv->launches += ltkv::attend_launches(p);
     if (ev_end) LT_CUDA(kv, cudaEventRecord(ev_end, st));
+    if (s_casc >= 0 && (rc = mark_slot_use(kv, s_casc, st)) != LT_OK) return rc;
     return s_plan >= 0 ? mark_slot_use(kv, s_plan, st) : LT_OK;
 }
 
@@ -559,6 +670,10 @@ lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
             ck(cudaMalloc(&kv->d_part_ml, kv->ws_slots * kv->group * 2 * sizeof(float)), "cudaMalloc(partials)");
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_flags, kv->ws_slots * sizeof(uint32_t) + 4), "cudaMalloc(flags)");
         if (rc == LT_OK) ck(cudaMemset(kv->d_flags, 0, kv->ws_slots * sizeof(uint32_t) + 4), "cudaMemset(flags)");
+        kv->pre_cap = std::min<uint32_t>(c.max_batch, kCascadeMaxTokens);
+        const size_t pre_rows = (size_t)kv->pre_cap * c.n_heads;
+        if (rc == LT_OK) ck(cudaMalloc(&kv->d_pre_o, pre_rows * c.head_dim * sizeof(float) + 16), "cudaMalloc(prefix)");
+        if (rc == LT_OK) ck(cudaMalloc(&kv->d_pre_ml, pre_rows * 2 * sizeof(float) + 16), "cudaMalloc(prefix)");
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_err, sizeof(int32_t)), "cudaMalloc(err)");
         if (rc == LT_OK) ck(cudaMemset(kv->d_err, 0, sizeof(int32_t)), "cudaMemset(err)");
         kv->slot_bytes = std::max<size_t>(1u << 20, sizeof(ltkv::TokenDesc) * (size_t)c.max_batch + 64);
@@ -856,6 +971,14 @@ lt_status lt_kv_profile_read(lt_kv* kv, double* total_ms, uint64_t* launches) {
     if (launches) *launches = kv->prof_count;
     return LT_OK;
 }
+
+lt_status lt_kv_set_cascade(lt_kv* kv, uint32_t min_group_tokens) {
+    if (!kv) return LT_E_ARG;
+    kv->cascade_min_tokens = min_group_tokens;
+    return LT_OK;
+}
+
+uint64_t lt_kv_cascade_launches(const lt_kv* kv) { return kv ? kv->cascade_launches : 0; }
 
 lt_status lt_kv_set_min_tiles_per_warp(lt_kv* kv, uint32_t tiles) {
     if (!kv || tiles == 0) return LT_E_ARG;

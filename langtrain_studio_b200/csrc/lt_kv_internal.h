@@ -11,9 +11,11 @@ constexpr int kMaxGroup = 8;         // q heads per KV head the attention kernel
 
 // Per-token input of one attention launch: the token's sequence, its
 // position (it attends over blocks [0, pos/16]), the physical id of its last
-// block, and the tile prefix P = sum of (pos_j/16 + 1) over tokens j < i.
+// block, the tile prefix P = sum of (pos_j/16 + 1 - skip_j) over tokens
+// j < i, and skip: its first `skip` blocks are a shared prefix whose
+// attention the prefix pass already computed (partial in pre_o / pre_ml).
 struct TokenDesc {
-    int32_t seq, pos, last_block, prefix;
+    int32_t seq, pos, last_block, prefix, skip;
 };
 
 constexpr int kInlineTokens = 512;  // tokens passed inside the kernel parameters
@@ -42,8 +44,40 @@ struct AttnParams {
     const void* k_new;           // fused append: new K/V rows [n][n_kv_heads*D], or null
     const void* v_new;
     int32_t kv_f32;
+    const float* pre_o;          // [n][n_kv_heads][group][D]: shared-prefix partial O (tokens with skip > 0)
+    const float* pre_ml;         // [n][n_kv_heads][group][2]: its (m, l)
     TokenDesc inl[kInlineTokens];
 };
+
+// Shared-prefix (cascade) pass: one CTA per item attends up to kPreTokens
+// tokens of one prefix group to the group's first n_blocks blocks for one KV
+// head, each K/V tile staged once for all of them, and writes (m, l, O)
+// partials that the stream-K launch folds into the tokens' outputs.
+constexpr int kPreWarps = 8;  // warps per prefix CTA, each 8 query rows
+struct PrefixItem {
+    int32_t root_seq;  // a member whose table row holds the shared blocks
+    int32_t n_blocks;  // shared blocks [0, n_blocks)
+    int32_t head;      // KV head
+    int32_t tok_off;   // first of the item's tokens in the token list
+    int32_t n_tok;     // tokens of this item
+};
+struct PrefixParams {
+    const uint16_t* pool_layer;
+    const int32_t* tables;
+    int32_t max_blocks;
+    const PrefixItem* items;
+    const int32_t* tok_list;  // token indices of the call (into q, pre_o, pre_ml)
+    int32_t n_kv_heads, group;
+    const void* q;
+    int32_t q_f32;
+    float scale_log2;
+    float* pre_o;
+    float* pre_ml;
+    int32_t* err;
+};
+// Tokens one prefix CTA covers: kPreWarps warps x (8 / group) tokens.
+inline int prefix_tokens_per_cta(int group) { return kPreWarps * (8 / group); }
+cudaError_t launch_prefix(const PrefixParams& p, int n_items, int head_dim, cudaStream_t s);
 
 // Warps of one attention launch on `device` (all resident at once), or 0.
 int attend_warps(int device, int group, int head_dim, int q_f32);

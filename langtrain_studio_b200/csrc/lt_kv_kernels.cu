@@ -220,9 +220,29 @@ __global__ void __launch_bounds__(256) kv_write_kernel(uint16_t* __restrict__ po
 // starts in this range and runs past its end (the warp's last piece) ->
 // this warp merges it.
 struct PieceRegs {
-    int tok, h, seq, pos, b0, b1, kind, last_block;
+    int tok, h, seq, pos, b0, b1, kind, last_block, skip;  // b0, b1 count from block `skip`
     long long ps;  // first tile of the (token, head)
 };
+
+// Fold the shared-prefix partial (m, l, O) of row (tok, h, g) into the
+// running (M, L, acc) of the rest of the token's blocks (same log2 units).
+template <int D>
+__device__ __forceinline__ void fold_prefix(const AttnParams& p, int tok, int h, int g, int t4, float& M, float& L,
+                                            float (&acc)[D / 8][2]) {
+    const size_t r = ((size_t)tok * p.n_kv_heads + h) * p.group + g;
+    const float mp = __ldcg(p.pre_ml + r * 2), lp = __ldcg(p.pre_ml + r * 2 + 1);
+    const float M2 = fmaxf(M, mp);
+    const float a = ex2(M - M2), b = ex2(mp - M2);
+    L = L * a + lp * b;
+    M = M2;
+    const float* po = p.pre_o + r * D + 2 * t4;
+#pragma unroll
+    for (int nt = 0; nt < D / 8; ++nt) {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(po + nt * 8));
+        acc[nt][0] = acc[nt][0] * a + v.x * b;
+        acc[nt][1] = acc[nt][1] * a + v.y * b;
+    }
+}
 
 // S = Q K^T, online softmax and O += P V for one staged (block, head) tile.
 template <int D>
@@ -355,16 +375,17 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
         }
         gi = lo;
         const TokenDesc td = toks[gi];
-        const int nb = td.pos / kBlock + 1;
+        const int nb = td.pos / kBlock + 1 - td.skip;
         const long long off = t0 - (long long)td.prefix * Hkv;
         gh = (int)(off / nb);
         gb = (int)(off % nb);
     }
     auto gen_piece = [&](PieceRegs& r) {  // the piece at the generator, then advance past it
         const TokenDesc td = toks[gi];
-        const int nb = td.pos / kBlock + 1;
+        const int nb = td.pos / kBlock + 1 - td.skip;
         const int len = (int)min((long long)(nb - gb), t1 - gt);
         r.tok = gi;
+        r.skip = td.skip;
         r.h = gh;
         r.seq = td.seq;
         r.pos = td.pos;
@@ -388,7 +409,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
         const int bb = b + lane;
         if (bb >= r.b1) return 0;
         if (bb == r.b1 - 1 && r.last_block >= 0) return r.last_block;
-        return __ldg(p.tables + (size_t)r.seq * p.max_blocks + bb);
+        return __ldg(p.tables + (size_t)r.seq * p.max_blocks + r.skip + bb);
     };
 
     // ---- issuer state ----
@@ -409,7 +430,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
     auto table_write = [&](const PieceRegs& r) {
         // the token's last block entry, written once per token (head 0)
         if (r.h == 0 && r.last_block >= 0 && lane == 0)
-            p.tables[(size_t)r.seq * p.max_blocks + r.b1 - 1] = r.last_block;
+            p.tables[(size_t)r.seq * p.max_blocks + r.skip + r.b1 - 1] = r.last_block;
     };
     table_write(di);
 
@@ -504,8 +525,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
                 }
             }
         }
-        const int b = dc.b0 + ct;
-        const int valid = min(kBlock, dc.pos + 1 - b * kBlock);
+        const int b = dc.b0 + ct;  // from block dc.skip
+        const int valid = min(kBlock, dc.pos + 1 - (dc.skip + b) * kBlock);
         bool touched = false;
         if (p.k_new && dc.last_block >= 0 && b == dc.b1 - 1) {
             // Fused append: this token's new K/V row for head h goes to its
@@ -550,10 +571,17 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
             if (g < G) {
                 if (dc.kind == 0) {
                     const size_t ob = ((size_t)dc.tok * Hkv + dc.h) * GD + (size_t)g * D + 2 * t4;
+                    float acc[NT][2];
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        acc[nt][0] = o[nt][0] + o[nt][2];
+                        acc[nt][1] = o[nt][1] + o[nt][3];
+                    }
+                    if (dc.skip > 0) fold_prefix<D>(p, dc.tok, dc.h, g, t4, m_run, l, acc);
                     const float inv = 1.f / l;
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
-                        const float v0 = (o[nt][0] + o[nt][2]) * inv, v1 = (o[nt][1] + o[nt][3]) * inv;
+                        const float v0 = acc[nt][0] * inv, v1 = acc[nt][1] * inv;
                         if (p.out_f32)
                             *reinterpret_cast<float2*>(static_cast<float*>(p.out) + ob + nt * 8) = make_float2(v0, v1);
                         else
@@ -598,7 +626,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
 
     // ---- merge the cut (token, head) this range ends with ----
     const long long NW = p.n_warps;
-    const int nb = dc.pos / kBlock + 1;
+    const int nb = dc.pos / kBlock + 1 - dc.skip;
     const int w_last = (int)(((dc.ps + nb) * NW - 1) / T);  // warp holding its last tile
     int ready = 1;
     if (lane == 0)
@@ -635,6 +663,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
                 acc[nt][1] += v2.y * sw;
             }
         }
+        if (dc.skip > 0) fold_prefix<D>(p, dc.tok, dc.h, g, t4, M, L, acc);
         const float inv = 1.f / L;
         const size_t ob = ((size_t)dc.tok * Hkv + dc.h) * GD + (size_t)g * D + 2 * t4;
 #pragma unroll
@@ -645,6 +674,132 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
             else
                 *reinterpret_cast<__half2*>(static_cast<__half*>(p.out) + ob + nt * 8) =
                     __floats2half2_rn(acc[nt][0] * inv, acc[nt][1] * inv);
+        }
+    }
+}
+
+// ------------------------------------------------------------ prefix ----
+// Shared-prefix (cascade) pass.  One CTA per PrefixItem: up to
+// prefix_tokens_per_cta(G) tokens of one prefix group and one KV head.  The
+// group's shared (block, head) tiles are bulk-copied once into a CTA-wide
+// ring and every warp attends its 8 query rows (8/G tokens x G heads, f16
+// value in A rows 0..7 and residual in rows 8..15, as the stream-K kernel) to
+// each of them, so a shared tile leaves L2 once per CTA instead of once per
+// sequence.  Each row's (m, l, O) goes to pre_ml / pre_o; the stream-K launch
+// that follows skips those blocks and folds the partials in.
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(kPreWarps * 32, 1) prefix_attn_kernel(const __grid_constant__ PrefixParams p) {
+    constexpr int TILE = 2 * kBlock * D * 2;
+    constexpr int KS = D / 16, NT = D / 8;
+    constexpr int NS = 4;  // ring stages
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const PrefixItem item = p.items[blockIdx.x];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = p.group, Hkv = p.n_kv_heads;
+    const int tpw = 8 / G;
+    const int g = lane >> 2, t4 = lane & 3;
+    const uint32_t full0 = smem_u32(smem + NS * TILE), empty0 = full0 + 8u * NS;
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < NS; ++st) {
+            mbar_init(full0 + 8u * st, 1);
+            mbar_init(empty0 + 8u * st, kPreWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const size_t tile_elems = 2 * kBlock * D;
+    const int32_t* trow = p.tables + (size_t)item.root_seq * p.max_blocks;
+    const int nbk = item.n_blocks;
+    int issued = 0;  // thread 0 only
+    auto issue = [&](int j) {
+        const uint32_t bar = full0 + 8u * (j % NS);
+        const int blk = __ldg(trow + j);
+        mbar_arrive_expect_tx(bar, TILE);
+        bulk_g2s(smem_u32(smem + (size_t)(j % NS) * TILE), p.pool_layer + ((size_t)blk * Hkv + item.head) * tile_elems,
+                 TILE, bar);
+        ++issued;
+    };
+    if (threadIdx.x == 0)
+        for (int j = 0; j < min(NS, nbk); ++j) issue(j);
+
+    const int tok0 = warp * tpw;  // this warp's first token of the item
+    const bool warp_live = tok0 < item.n_tok;
+    const bool row_live = g < tpw * G && tok0 + g / G < item.n_tok;
+    const int tok = row_live ? p.tok_list[item.tok_off + tok0 + g / G] : 0;
+    const int hg = g % G;
+    const int qelem = p.q_f32 ? 4 : 2;
+    const uint8_t* qrow = static_cast<const uint8_t*>(p.q) + (((size_t)tok * Hkv + item.head) * G + hg) * D * qelem;
+    uint32_t qa[KS][4];
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            float x0 = 0.f, x1 = 0.f;
+            if (row_live) {
+                const int e = ks * 16 + hf * 8 + 2 * t4;
+                if (p.q_f32) {
+                    const float2 f = *reinterpret_cast<const float2*>(qrow + e * 4);
+                    x0 = f.x;
+                    x1 = f.y;
+                } else {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(qrow + e * 2));
+                    x0 = f.x;
+                    x1 = f.y;
+                }
+            }
+            const __half2 hi = __floats2half2_rn(x0, x1);
+            const float2 hf2 = __half22float2(hi);
+            qa[ks][2 * hf] = h2_bits(hi);
+            qa[ks][2 * hf + 1] = h2_bits(__floats2half2_rn(x0 - hf2.x, x1 - hf2.y));
+        }
+    }
+    float o[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    int j = 0;
+    for (; j < nbk; ++j) {
+        const int st = j % NS;
+        if (!mbar_wait_bounded(full0 + 8u * st, (j / NS) & 1)) {
+            ok = false;
+            break;
+        }
+        if (warp_live) attend_tile<D>(smem + (size_t)st * TILE, kBlock, qa, o, m_run, l_run, p.scale_log2, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8u * st);
+        if (threadIdx.x == 0 && j + NS < nbk) {
+            // refill this stage once every warp is done with tile j
+            if (!mbar_wait_bounded(empty0 + 8u * st, (j / NS) & 1)) {
+                ok = false;
+                break;
+            }
+            issue(j + NS);
+        }
+    }
+    if (!ok) {
+        // bounded drain of this CTA's copies still in flight, then report
+        if (threadIdx.x == 0)
+            for (int jj = j; jj < issued; ++jj) mbar_wait_bounded(full0 + 8u * (jj % NS), (jj / NS) & 1);
+        if (lane == 0) atomicExch(p.err, 1);
+        return;
+    }
+    float l = l_run;
+    l += __shfl_xor_sync(kFull, l, 1);
+    l += __shfl_xor_sync(kFull, l, 2);
+    if (row_live) {
+        const size_t r = ((size_t)tok * Hkv + item.head) * G + hg;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            *reinterpret_cast<float2*>(p.pre_o + r * D + nt * 8 + 2 * t4) =
+                make_float2(o[nt][0] + o[nt][2], o[nt][1] + o[nt][3]);
+        if (t4 == 0) {
+            p.pre_ml[r * 2] = m_run;
+            p.pre_ml[r * 2 + 1] = l;
         }
     }
 }
@@ -778,6 +933,16 @@ cudaError_t launch_attend(const AttnParams& p, int head_dim, cudaStream_t s) {
 }
 
 int attend_launches(const AttnParams& p) { return p.n_warps == 0 ? 0 : 1; }
+
+cudaError_t launch_prefix(const PrefixParams& p, int n_items, int head_dim, cudaStream_t s) {
+    if (n_items <= 0) return cudaSuccess;
+    const size_t smem = (size_t)4 * 2 * kBlock * head_dim * 2 + 2 * 4 * 8;
+    if (head_dim == 64)
+        prefix_attn_kernel<64><<<n_items, kPreWarps * 32, smem, s>>>(p);
+    else
+        prefix_attn_kernel<128><<<n_items, kPreWarps * 32, smem, s>>>(p);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_gather_permute(const void* gathered, void* out, int nranks, uint32_t n, size_t row_bytes,
                                   cudaStream_t s) {

@@ -121,6 +121,7 @@ extern "C" lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_
         td[i].pos = (int32_t)pos[i];
         td[i].last_block = -1;  // unknown here: the kernel reads every block id from the tables
         td[i].prefix = (int32_t)prefix;
+        td[i].skip = 0;
         prefix += pos[i] / ltkv::kBlock + 1;
     }
     // The error word must start at zero; the array keeps the previous call's bytes.
@@ -162,6 +163,8 @@ extern "C" lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_
     p.k_new = nullptr;
     p.v_new = nullptr;
     p.kv_f32 = 0;
+    p.pre_o = nullptr;
+    p.pre_ml = nullptr;
     if (ltkv::launch_attend(p, (int)head_dim, st) != cudaSuccess) return LT_E_CUDA;
     return LT_OK;
 }

@@ -263,6 +263,13 @@ class KvCache:
         """Attention launch sizing: at least `tiles` tiles per warp (default 8)."""
         self._check(self._lib.lt_kv_set_min_tiles_per_warp(self._h, tiles))
 
+    def set_cascade(self, min_group_tokens: int):
+        """Shared-prefix attention pass for groups of >= min_group_tokens tokens (0: off)."""
+        self._check(self._lib.lt_kv_set_cascade(self._h, min_group_tokens))
+
+    def cascade_launches(self) -> int:
+        return self._lib.lt_kv_cascade_launches(self._h)
+
     def launch_count(self) -> int:
         return self._lib.lt_kv_launch_count(self._h)
 

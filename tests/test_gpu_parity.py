@@ -349,3 +349,83 @@ def test_bad_arguments_are_rejected_without_launch(oracle_mod):
     with pytest.raises(KvError):
         t.kv.write(0, [99], [0], torch.zeros((1, 64), device="cuda"), torch.zeros((1, 64), device="cuda"))
     assert t.kv.launch_count() == n0
+
+
+CASCADE_CASES = [
+    (128, 32, 8, 40, 700, 37),    # Llama-3-8B shape, group 4
+    (64, 32, 4, 24, 1024, 5),     # config-1 shape, group 8
+    (128, 8, 8, 16, 333, 90),     # group 1
+    (64, 12, 4, 10, 200, 17),     # group 3
+]
+
+
+@pytest.mark.parametrize("hd,hq,hkv,n_seq,prefix,suffix", CASCADE_CASES)
+@pytest.mark.parametrize("fused", [False, True])
+def test_cascade_shared_prefix_matches_oracle(oracle_mod, hd, hq, hkv, n_seq, prefix, suffix, fused):
+    """Sequences made with share(0, s, prefix) and their own suffixes: the
+    shared blocks go through the prefix pass (one extra launch), the rest
+    through the decode launch, and the merged outputs match the oracle."""
+    rng = np.random.default_rng(hd + n_seq + prefix)
+    per = (prefix + suffix + 16) // 16 + 2
+    t = Twin(oracle_mod, 1, hkv, hd, 16 * (prefix // 16 + 2 + n_seq * per), n_heads=hq, max_seqs=n_seq + 1)
+    t.fill(0, prefix, rng)
+    lens = []
+    for s in range(1, n_seq + 1):
+        t.share(0, s, prefix)
+        L = prefix + suffix + s % 7
+        t.fill(s, L, rng)
+        lens.append(L)
+    seqs = np.arange(1, n_seq + 1)
+    pos = np.array(lens)
+    b, sl = t.append(seqs, pos)
+    k = rng.standard_normal((n_seq, hkv * hd)).astype(np.float32)
+    v = rng.standard_normal((n_seq, hkv * hd)).astype(np.float32)
+    q = rng.standard_normal((n_seq, hq * hd)).astype(np.float32)
+    c0 = t.kv.cascade_launches()
+    if fused:
+        out = t.kv.write_attend(0, b, sl, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(),
+                                torch.from_numpy(q).cuda(), seqs, pos).cpu().numpy()
+        t.ok.write_batch(0, b, sl, k, v)
+        ref = t.ok.attend(0, q, seqs, pos, hq, hkv, hd)
+    else:
+        t.write(0, b, sl, k, v)
+        out, ref = t.attend_both(0, seqs, pos, q)
+    assert t.kv.cascade_launches() == c0 + 1
+    np.testing.assert_allclose(out, ref, rtol=1e-4, atol=2e-5)
+    t.check_pool()
+    t.check_tables()
+    t.kv.check()
+
+
+def test_cascade_groups_mixed_with_private_sequences(oracle_mod):
+    """Two prefix groups, one of them with a member that shares only part of
+    the prefix (the group's shared run shortens to it), and sequences with no
+    sharing, in one call; also the same call with the pass turned off."""
+    rng = np.random.default_rng(77)
+    hd, hq, hkv = 128, 16, 4
+    t = Twin(oracle_mod, 1, hkv, hd, 16 * 900, n_heads=hq, max_seqs=40)
+    t.fill(0, 640, rng)     # group A root
+    t.fill(20, 515, rng)    # group B root
+    lens = {}
+    for s in range(1, 12):
+        t.share(0, s, 640 if s != 5 else 300)  # seq 5 shares 300 positions only
+        lens[s] = 700 + s
+    for s in range(21, 32):
+        t.share(20, s, 515)
+        lens[s] = 530 + 3 * s
+    for s in range(33, 38):
+        lens[s] = 100 + 40 * s % 300  # private
+    for s, L in lens.items():
+        t.fill(s, L, rng)
+    seqs = np.array(sorted(lens))
+    pos = np.array([lens[s] - 1 for s in seqs])
+    q = rng.standard_normal((seqs.size, hq * hd)).astype(np.float32)
+    c0 = t.kv.cascade_launches()
+    out, ref = t.attend_both(0, seqs, pos, q)
+    assert t.kv.cascade_launches() == c0 + 1
+    np.testing.assert_allclose(out, ref, rtol=1e-4, atol=2e-5)
+    t.kv.set_cascade(0)
+    out2, _ = t.attend_both(0, seqs, pos, q)
+    assert t.kv.cascade_launches() == c0 + 1
+    np.testing.assert_allclose(out2, ref, rtol=1e-4, atol=2e-5)
+    t.kv.check()
