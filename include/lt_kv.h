@@ -181,10 +181,12 @@ uint32_t lt_kv_free_list(const lt_kv* kv, int32_t* out_host, uint32_t cap);
 uint32_t lt_kv_n_blocks(const lt_kv* kv);
 
 /* Device pool layout, for tools that read it directly:
- * f16 [layer][block][kv_head][2 (K, V)][16 slots][head_dim], where the 16-byte
- * chunk c of row `slot` is stored at chunk position (c ^ (slot & 7)) within
- * its 128-byte group (a bank-conflict-free shared-memory image once a block
- * is bulk-copied).  Returns the device base address. */
+ * f16 [layer][block][kv_head][2 (K, V)][head_dim/64][16 slots][64]: each K
+ * or V part is head_dim/64 sub-tiles of 16 rows x 128 bytes, and inside a
+ * sub-tile the 16-byte chunk c of row `slot` is stored at chunk position
+ * (c ^ (slot & 7)) -- the 128-byte-swizzled layout of the tensor-core operand
+ * descriptors, bank-conflict free for ldmatrix once bulk-copied.  Returns the
+ * device base address. */
 void* lt_kv_device_pool(const lt_kv* kv);
 /* Device block tables: int32 [max_seqs][max_blocks_per_seq]. */
 const int32_t* lt_kv_device_tables(const lt_kv* kv, uint32_t* max_blocks_per_seq);

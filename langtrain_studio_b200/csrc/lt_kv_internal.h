@@ -49,11 +49,11 @@ struct AttnParams {
     TokenDesc inl[kInlineTokens];
 };
 
-// Shared-prefix (cascade) pass: one CTA per item attends up to kPreTokens
-// tokens of one prefix group to the group's first n_blocks blocks for one KV
-// head, each K/V tile staged once for all of them, and writes (m, l, O)
-// partials that the stream-K launch folds into the tokens' outputs.
-constexpr int kPreWarps = 8;  // warps per prefix CTA, each 8 query rows
+// Shared-prefix (cascade) pass: one CTA per item attends up to
+// prefix_tokens_per_cta(group) tokens of one prefix group (128 query rows on
+// the tensor cores) to the group's first n_blocks blocks for one KV head,
+// each K/V tile staged once for all of them, and writes (m, l, O) partials
+// that the stream-K launch folds into the tokens' outputs.
 struct PrefixItem {
     int32_t root_seq;  // a member whose table row holds the shared blocks
     int32_t n_blocks;  // shared blocks [0, n_blocks)
@@ -75,8 +75,8 @@ struct PrefixParams {
     float* pre_ml;
     int32_t* err;
 };
-// Tokens one prefix CTA covers: kPreWarps warps x (8 / group) tokens.
-inline int prefix_tokens_per_cta(int group) { return kPreWarps * (8 / group); }
+// Tokens one prefix CTA covers: 128 query rows / group.
+inline int prefix_tokens_per_cta(int group) { return 128 / group; }
 cudaError_t launch_prefix(const PrefixParams& p, int n_items, int head_dim, cudaStream_t s);
 
 // Warps of one attention launch on `device` (all resident at once), or 0.

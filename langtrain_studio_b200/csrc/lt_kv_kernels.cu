@@ -6,10 +6,12 @@
 //                            compaction moves) + block-table scatter
 //   rows_kernel              KvCache::rows (kv.rs:135-150) gather, for parity/debug
 //
-// Pool layout (per layer): f16 [block][kv_head][2 (K,V)][16 slots][D].  The
-// 16-byte chunk c of the row of slot s sits at chunk position c ^ (s & 7):
-// one (block, head) K+V tile is a contiguous 4*D*16-byte run whose
-// bulk-copied shared-memory image is bank-conflict free for ldmatrix.
+// Pool layout (per layer): f16 [block][kv_head][2 (K,V)][D/64][16 slots][64].
+// Within each 16 x 64 sub-tile, the 16-byte chunk c of the row of slot s
+// sits at chunk position c ^ (s & 7) (the 128-byte swizzle of the tensor-core
+// operand layouts): one (block, head) K+V tile is a contiguous 4*D*16-byte run
+// whose bulk-copied shared-memory image is bank-conflict free for ldmatrix
+// and, 64-wide sub-tile by sub-tile, a valid tcgen05 operand.
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -160,7 +162,14 @@ __device__ __forceinline__ uint4 load8_as_f16(const void* base, size_t idx, int 
     return r;
 }
 
-__device__ __forceinline__ int swz(int chunk, int slot) { return chunk ^ (slot & 7); }
+// Element offset of 16-byte chunk c (8 f16) of slot s inside the K (or V)
+// part of a (block, head) tile: the part is head_dim/64 sub-tiles of 16 rows
+// x 128 bytes, chunk c in sub-tile c/8, at chunk position (c%8) ^ (s%8).
+// Each sub-tile is the 128-byte-swizzled row-major layout of the tensor-core
+// operand descriptors, and ldmatrix over it is bank-conflict free.
+__device__ __forceinline__ int chunk_off(int c, int slot) {
+    return (c >> 3) * (kBlock * 64) + slot * 64 + (((c & 7) ^ (slot & 7)) << 3);
+}
 
 // ------------------------------------------------------------------ K1 ----
 // One thread per 16-byte chunk of one (token, head, K|V) row.
@@ -181,8 +190,7 @@ __global__ void __launch_bounds__(256) kv_write_kernel(uint16_t* __restrict__ po
     const int2 cell = cells[i];
     const size_t src = (size_t)i * n_kv_heads * D + (size_t)h * D + (size_t)c * 8;
     const uint4 val = load8_as_f16(kvsel ? v : k, src, in_f32);
-    uint16_t* dst = pool_layer + (((size_t)cell.x * n_kv_heads + h) * 2 + kvsel) * (kBlock * D) +
-                    (size_t)cell.y * D + (size_t)swz(c, cell.y) * 8;
+    uint16_t* dst = pool_layer + (((size_t)cell.x * n_kv_heads + h) * 2 + kvsel) * (kBlock * D) + chunk_off(c, cell.y);
     *reinterpret_cast<uint4*>(dst) = val;
 }
 
@@ -262,7 +270,7 @@ __device__ __forceinline__ void attend_tile(const uint8_t* tile, int valid, cons
         for (int ks = 0; ks < KS; ++ks) {
             const int c = 2 * ks + (mi & 1);
             uint32_t b0, b1, b2, b3;
-            ldsm_x4(kbase + tok * ROW + (swz(c, tok) << 4), b0, b1, b2, b3);
+            ldsm_x4(kbase + chunk_off(c, tok) * 2, b0, b1, b2, b3);
             mma16816(s0, qa[ks], b0, b1);
             mma16816(s1, qa[ks], b2, b3);
         }
@@ -313,7 +321,7 @@ __device__ __forceinline__ void attend_tile(const uint8_t* tile, int valid, cons
         for (int np = 0; np < NT / 2; ++np) {
             const int c = 2 * np + (mi >> 1);
             uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(vbase + tok * ROW + (swz(c, tok) << 4), b0, b1, b2, b3);
+            ldsm_x4_t(vbase + chunk_off(c, tok) * 2, b0, b1, b2, b3);
             mma16816(o[2 * np], pa, b0, b1);
             mma16816(o[2 * np + 1], pa, b2, b3);
         }
@@ -537,19 +545,21 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
                 const int kvsel = lane / CH, c = lane % CH;
                 const size_t src = (size_t)dc.tok * Hkv * D + (size_t)dc.h * D + (size_t)c * 8;
                 const uint4 val = load8_as_f16(kvsel ? p.v_new : p.k_new, src, p.kv_f32);
-                const int pc = swz(c, slot);
-                *reinterpret_cast<uint4*>(tile + kvsel * kBlock * ROW + slot * ROW + pc * 16) = val;
+                const int off = chunk_off(c, slot);
+                *reinterpret_cast<uint4*>(tile + kvsel * kBlock * ROW + off * 2) = val;
                 *reinterpret_cast<uint4*>(p.pool_layer_w + ((size_t)dc.last_block * Hkv + dc.h) * tile_elems +
-                                          (size_t)kvsel * kBlock * D + (size_t)slot * D + (size_t)pc * 8) = val;
+                                          (size_t)kvsel * kBlock * D + off) = val;
             }
             touched = true;
         }
         if (valid < kBlock) {
             // Rows past the sequence end were never written for it: zero V so
             // 0 * (stale NaN/Inf) cannot reach O; K rows are masked.
-            const int n16 = (kBlock - valid) * ROW / 16;
-            uint4* vz = reinterpret_cast<uint4*>(tile + kBlock * ROW + valid * ROW);
-            for (int e = lane; e < n16; e += 32) vz[e] = make_uint4(0, 0, 0, 0);
+            const int per_half = (kBlock - valid) * 8;  // 16-byte chunks past the end in each 64-wide sub-tile
+            for (int e = lane; e < per_half * (D / 64); e += 32) {
+                uint4* vz = reinterpret_cast<uint4*>(tile + kBlock * ROW + (e / per_half) * (kBlock * 128) + valid * 128);
+                vz[e % per_half] = make_uint4(0, 0, 0, 0);
+            }
             touched = true;
         }
         __syncwarp();
@@ -679,128 +689,390 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
 }
 
 // ------------------------------------------------------------ prefix ----
-// Shared-prefix (cascade) pass.  One CTA per PrefixItem: up to
-// prefix_tokens_per_cta(G) tokens of one prefix group and one KV head.  The
-// group's shared (block, head) tiles are bulk-copied once into a CTA-wide
-// ring and every warp attends its 8 query rows (8/G tokens x G heads, f16
-// value in A rows 0..7 and residual in rows 8..15, as the stream-K kernel) to
-// each of them, so a shared tile leaves L2 once per CTA instead of once per
-// sequence.  Each row's (m, l, O) goes to pre_ml / pre_o; the stream-K launch
-// that follows skips those blocks and folds the partials in.
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+// Shared-prefix (cascade) pass on the 5th-generation tensor cores.
+//
+// One CTA per PrefixItem: one KV head and up to 128 query rows (row r =
+// item token r / G, q head r % G), tcgen05 M = 128 with row r in TMEM lane r.
+// The group's shared blocks stream through a 3-stage shared-memory ring, four
+// blocks (64 positions) a step, each (block, head) K and V sub-tile
+// bulk-copied once for all 128 rows.  Per step:
+//   S = Q K^T      tcgen05.mma, A = Q (f16 value, then its f16 residual,
+//                  both accumulating into S: ~22-bit q), B = K, D = S in TMEM;
+//   softmax        thread r reads its S row from TMEM, keeps a running
+//                  maximum m that only moves up by more than 2^8 (so O and l
+//                  are rescaled rarely), writes P = 2^(s*scale - m) as f16
+//                  value + residual rows into shared memory;
+//   O += P V       tcgen05.mma, A = P (value, then residual), B = V (MN-major),
+//                  D = O in TMEM.
+// The pool's 16 x 64 sub-tiles are already the 128-byte-swizzled K-major (K)
+// and MN-major (V) operand layouts, so the tiles go from the bulk copy
+// straight to the tensor cores.  At the end each row writes (m, l, O).
+// Every wait is bounded; on a timeout the CTA sets the error flag, drains
+// its copies and still frees its TMEM.  The warp-collective tcgen05 ops
+// (alloc, ld, st, wait, dealloc) are only ever reached by whole warps.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;  // 128-byte swizzle
+    return d;
 }
 
+// kind::f16 instruction descriptor: f16 A/B, f32 D, M = 128, N = n.
+__device__ __forceinline__ uint32_t f16_idesc(int n, bool b_mn_major) {
+    return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Warp-collective: every lane of the warp calls these with the same column.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    __syncwarp();
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    __syncwarp();
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+        "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+        "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])),
+        "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])),
+        "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])),
+        "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])),
+        "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+constexpr int kPreRows = 128;       // tcgen05 M
+constexpr int kPreStepBlocks = 4;   // blocks (16 positions each) per step: N = 64
+constexpr int kPreStages = 3;
+constexpr int kPreTmemCols = 256;   // S: [0, 64), O: [64, 64 + D)
+constexpr float kRescaleLog2 = 8.f; // the running maximum moves only by more than this
+
+// Shared-memory layout of the prefix CTA (offsets from a 1024-aligned base).
+struct PreSmem {
+    uint32_t q_hi, q_lo, stage0, p_hi, p_lo, bars, total;
+    __host__ __device__ explicit PreSmem(int D) {
+        const uint32_t qbytes = (uint32_t)kPreRows * D * 2;                 // [D/64][128 rows][128 B]
+        const uint32_t stage = (uint32_t)2 * kPreStepBlocks * kBlock * D * 2;  // K and V: [D/64][64 rows][128 B]
+        q_hi = 0;
+        q_lo = q_hi + qbytes;
+        stage0 = q_lo + qbytes;
+        p_hi = stage0 + kPreStages * stage;
+        p_lo = p_hi + kPreRows * 128;
+        bars = p_lo + kPreRows * 128;
+        total = bars + 128;
+    }
+};
+
 template <int D>
-__global__ void __launch_bounds__(kPreWarps * 32, 1) prefix_attn_kernel(const __grid_constant__ PrefixParams p) {
-    constexpr int TILE = 2 * kBlock * D * 2;
-    constexpr int KS = D / 16, NT = D / 8;
-    constexpr int NS = 4;  // ring stages
-    extern __shared__ __align__(1024) uint8_t smem[];
+__global__ void __launch_bounds__(kPreRows, 1) prefix_attn_kernel(const __grid_constant__ PrefixParams p) {
+    constexpr int HALVES = D / 64;
+    constexpr uint32_t STAGE = 2 * kPreStepBlocks * kBlock * D * 2;
+    constexpr uint32_t KPART = STAGE / 2;                    // K sub-tiles of a stage; V follows
+    constexpr uint32_t HALF_ROWS_BYTES = kPreStepBlocks * kBlock * 128;  // one 64-wide sub-tile column of a stage
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    uint8_t* sbase = smem_raw + (base - smem_u32(smem_raw));
+    const PreSmem L(D);
     const PrefixItem item = p.items[blockIdx.x];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tid = threadIdx.x, warp = tid >> 5;
     const int G = p.group, Hkv = p.n_kv_heads;
-    const int tpw = 8 / G;
-    const int g = lane >> 2, t4 = lane & 3;
-    const uint32_t full0 = smem_u32(smem + NS * TILE), empty0 = full0 + 8u * NS;
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < NS; ++st) {
+    const uint32_t full0 = base + L.bars, empty0 = full0 + 8u * kPreStages, mma_bar = empty0 + 8u * kPreStages;
+    uint32_t* tmem_word = reinterpret_cast<uint32_t*>(sbase + L.bars + 8 * (2 * kPreStages + 1));
+    if (tid == 0) {
+        for (int st = 0; st < kPreStages; ++st) {
             mbar_init(full0 + 8u * st, 1);
-            mbar_init(empty0 + 8u * st, kPreWarps);
+            mbar_init(empty0 + 8u * st, 1);
         }
+        mbar_init(mma_bar, 1);
         fence_mbar_init();
     }
+    __syncwarp();  // tcgen05.alloc is warp-collective: warp 0 converged again after thread 0's setup
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_word)),
+                     "r"(kPreTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
     __syncthreads();
-    const size_t tile_elems = 2 * kBlock * D;
-    const int32_t* trow = p.tables + (size_t)item.root_seq * p.max_blocks;
+    tc_fence_after();
+    const uint32_t tmem = *tmem_word;
+    const uint32_t tmem_s = tmem, tmem_o = tmem + 64;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;  // this warp's TMEM lanes
+
     const int nbk = item.n_blocks;
-    int issued = 0;  // thread 0 only
-    auto issue = [&](int j) {
-        const uint32_t bar = full0 + 8u * (j % NS);
-        const int blk = __ldg(trow + j);
-        mbar_arrive_expect_tx(bar, TILE);
-        bulk_g2s(smem_u32(smem + (size_t)(j % NS) * TILE), p.pool_layer + ((size_t)blk * Hkv + item.head) * tile_elems,
-                 TILE, bar);
+    const int n_steps = (nbk + kPreStepBlocks - 1) / kPreStepBlocks;
+    const int32_t* trow = p.tables + (size_t)item.root_seq * p.max_blocks;
+    const size_t tile_elems = 2 * kBlock * D;
+    int issued = 0;  // thread 0: steps whose copies were issued
+    auto issue_step = [&](int j) {
+        const int st = j % kPreStages;
+        const int nblk = min(kPreStepBlocks, nbk - j * kPreStepBlocks);
+        const uint32_t bar = full0 + 8u * st;
+        mbar_arrive_expect_tx(bar, (uint32_t)nblk * 2 * kBlock * D * 2);
+        const uint32_t sk = base + L.stage0 + st * STAGE;
+        for (int bb = 0; bb < nblk; ++bb) {
+            const int blk = __ldg(trow + j * kPreStepBlocks + bb);
+            const uint16_t* src = p.pool_layer + ((size_t)blk * Hkv + item.head) * tile_elems;
+            for (int hh = 0; hh < HALVES; ++hh) {
+                // K sub-tile hh -> K region column hh, rows 16bb..; V likewise
+                bulk_g2s(sk + hh * HALF_ROWS_BYTES + bb * (kBlock * 128), src + hh * (kBlock * 64), kBlock * 128, bar);
+                bulk_g2s(sk + KPART + hh * HALF_ROWS_BYTES + bb * (kBlock * 128), src + kBlock * D + hh * (kBlock * 64),
+                         kBlock * 128, bar);
+            }
+        }
         ++issued;
     };
-    if (threadIdx.x == 0)
-        for (int j = 0; j < min(NS, nbk); ++j) issue(j);
+    if (tid == 0)
+        for (int j = 0; j < min(kPreStages, n_steps); ++j) issue_step(j);
 
-    const int tok0 = warp * tpw;  // this warp's first token of the item
-    const bool warp_live = tok0 < item.n_tok;
-    const bool row_live = g < tpw * G && tok0 + g / G < item.n_tok;
-    const int tok = row_live ? p.tok_list[item.tok_off + tok0 + g / G] : 0;
-    const int hg = g % G;
-    const int qelem = p.q_f32 ? 4 : 2;
-    const uint8_t* qrow = static_cast<const uint8_t*>(p.q) + (((size_t)tok * Hkv + item.head) * G + hg) * D * qelem;
-    uint32_t qa[KS][4];
+    // Q rows: row r = token r / G, head r % G; value and f16 residual, 128-byte swizzled
+    const int r = tid;
+    const int t_item = r / G, hg = r % G;
+    const bool live = t_item < item.n_tok && t_item < kPreRows / G;
+    const int tok = live ? p.tok_list[item.tok_off + t_item] : 0;
+    {
+        const int qelem = p.q_f32 ? 4 : 2;
+        const uint8_t* qrow = static_cast<const uint8_t*>(p.q) + (((size_t)tok * Hkv + item.head) * G + hg) * D * qelem;
+#pragma unroll 1
+        for (int c = 0; c < D / 8; ++c) {
+            float x[8];
 #pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-            float x0 = 0.f, x1 = 0.f;
-            if (row_live) {
-                const int e = ks * 16 + hf * 8 + 2 * t4;
+            for (int e = 0; e < 8; ++e) x[e] = 0.f;
+            if (live) {
                 if (p.q_f32) {
-                    const float2 f = *reinterpret_cast<const float2*>(qrow + e * 4);
-                    x0 = f.x;
-                    x1 = f.y;
+                    const float4 a = *reinterpret_cast<const float4*>(qrow + c * 32);
+                    const float4 b2 = *reinterpret_cast<const float4*>(qrow + c * 32 + 16);
+                    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b2.x; x[5] = b2.y; x[6] = b2.z; x[7] = b2.w;
                 } else {
-                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(qrow + e * 2));
-                    x0 = f.x;
-                    x1 = f.y;
+                    const uint4 u = *reinterpret_cast<const uint4*>(qrow + c * 16);
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __half22float2(h2[e]);
+                        x[2 * e] = f.x;
+                        x[2 * e + 1] = f.y;
+                    }
                 }
             }
-            const __half2 hi = __floats2half2_rn(x0, x1);
-            const float2 hf2 = __half22float2(hi);
-            qa[ks][2 * hf] = h2_bits(hi);
-            qa[ks][2 * hf + 1] = h2_bits(__floats2half2_rn(x0 - hf2.x, x1 - hf2.y));
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const __half2 h = __floats2half2_rn(x[2 * e], x[2 * e + 1]);
+                const float2 hf = __half22float2(h);
+                hi[e] = h2_bits(h);
+                lo[e] = h2_bits(__floats2half2_rn(x[2 * e] - hf.x, x[2 * e + 1] - hf.y));
+            }
+            const uint32_t off = (uint32_t)(c >> 3) * (kPreRows * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(sbase + L.q_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(sbase + L.q_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
     }
-    float o[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
+    fence_proxy_async_smem();  // generic writes of Q -> visible to the tensor core
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    const uint32_t idesc_pv = f16_idesc(D, true);
+    const float scale_log2 = p.scale_log2;
+    float m_use = -INFINITY, l_run = 0.f;
+    uint32_t mma_phase = 0;
     bool ok = true;
     int j = 0;
-    for (; j < nbk; ++j) {
-        const int st = j % NS;
-        if (!mbar_wait_bounded(full0 + 8u * st, (j / NS) & 1)) {
+    for (; j < n_steps; ++j) {
+        const int st = j % kPreStages;
+        const int nblk = min(kPreStepBlocks, nbk - j * kPreStepBlocks);
+        const uint32_t sk = base + L.stage0 + st * STAGE, sv = sk + KPART;
+        // ---- S = Q K^T (thread 0 issues) ----
+        bool t_ok = true;
+        if (tid == 0) {
+            t_ok = mbar_wait_bounded(full0 + 8u * st, (j / kPreStages) & 1);
+            if (t_ok) {
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t koff = (uint32_t)(kk >> 2) * (kPreRows * 128) + (kk & 3) * 32;
+                    const uint32_t boff = (uint32_t)(kk >> 2) * HALF_ROWS_BYTES + (kk & 3) * 32;
+                    const uint64_t bdesc = sw128_desc(sk + boff, 16, 1024);
+                    umma_f16(tmem_s, sw128_desc(base + L.q_hi + koff, 16, 1024), bdesc,
+                             f16_idesc(nblk * kBlock, false), kk > 0 ? 1u : 0u);
+                    umma_f16(tmem_s, sw128_desc(base + L.q_lo + koff, 16, 1024), bdesc,
+                             f16_idesc(nblk * kBlock, false), 1u);
+                }
+                umma_commit(mma_bar);
+            }
+        }
+        if (!__syncthreads_and(t_ok)) {
             ok = false;
             break;
         }
-        if (warp_live) attend_tile<D>(smem + (size_t)st * TILE, kBlock, qa, o, m_run, l_run, p.scale_log2, lane);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty0 + 8u * st);
-        if (threadIdx.x == 0 && j + NS < nbk) {
-            // refill this stage once every warp is done with tile j
-            if (!mbar_wait_bounded(empty0 + 8u * st, (j / NS) & 1)) {
-                ok = false;
-                break;
-            }
-            issue(j + NS);
+        // ---- softmax of row r ----
+        t_ok = mbar_wait_bounded(mma_bar, mma_phase);
+        mma_phase ^= 1;
+        if (!__syncthreads_and(t_ok)) {
+            ok = false;
+            break;
         }
-    }
-    if (!ok) {
-        // bounded drain of this CTA's copies still in flight, then report
-        if (threadIdx.x == 0)
-            for (int jj = j; jj < issued; ++jj) mbar_wait_bounded(full0 + 8u * (jj % NS), (jj / NS) & 1);
-        if (lane == 0) atomicExch(p.err, 1);
-        return;
-    }
-    float l = l_run;
-    l += __shfl_xor_sync(kFull, l, 1);
-    l += __shfl_xor_sync(kFull, l, 2);
-    if (row_live) {
-        const size_t r = ((size_t)tok * Hkv + item.head) * G + hg;
+        tc_fence_after();
+        const int npos = nblk * kBlock;
+        float sv_[64];
+        {
+            float tmp[32];
+            tmem_ld32(tmem_s + lane_off, tmp);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-            *reinterpret_cast<float2*>(p.pre_o + r * D + nt * 8 + 2 * t4) =
-                make_float2(o[nt][0] + o[nt][2], o[nt][1] + o[nt][3]);
-        if (t4 == 0) {
-            p.pre_ml[r * 2] = m_run;
-            p.pre_ml[r * 2 + 1] = l;
+            for (int i = 0; i < 32; ++i) sv_[i] = tmp[i];
+            if (npos > 32) {
+                tmem_ld32(tmem_s + lane_off + 32, tmp);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sv_[32 + i] = tmp[i];
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sv_[32 + i] = 0.f;
+            }
         }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+            sv_[i] = i < npos ? sv_[i] * scale_log2 : -INFINITY;
+            mx = fmaxf(mx, sv_[i]);
+        }
+        float alpha = 1.f;
+        bool rescale = false;
+        if (mx > m_use + kRescaleLog2 || m_use == -INFINITY) {
+            const float m_new = mx;
+            alpha = m_use == -INFINITY ? 0.f : ex2(m_use - m_new);
+            rescale = j > 0 && m_use != -INFINITY;
+            m_use = m_new;
+        }
+        float lsum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float p0 = ex2(sv_[8 * c + 2 * e] - m_use), p1 = ex2(sv_[8 * c + 2 * e + 1] - m_use);
+                lsum += p0 + p1;
+                const __half2 h = __floats2half2_rn(p0, p1);
+                const float2 hf = __half22float2(h);
+                hi[e] = h2_bits(h);
+                lo[e] = h2_bits(__floats2half2_rn(p0 - hf.x, p1 - hf.y));
+            }
+            const uint32_t off = r * 128 + (((c & 7) ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(sbase + L.p_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(sbase + L.p_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+        l_run = l_run * alpha + lsum;
+        if (__syncthreads_or(rescale)) {
+            // some row moved its maximum: every row scales its O by its alpha
+            // (1 where it did not); the PV of the previous step has completed
+            // (the S commit above tracked it)
+#pragma unroll 1
+            for (int c0 = 0; c0 < D; c0 += 32) {
+                float o[32];
+                tmem_ld32(tmem_o + lane_off + c0, o);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                tmem_st32(tmem_o + lane_off + c0, o);
+            }
+        }
+        fence_proxy_async_smem();  // P rows -> visible to the tensor core
+        tc_fence_before();
+        __syncthreads();
+        // ---- O += P V (thread 0 issues), then refill the stage ----
+        if (tid == 0) {
+            tc_fence_after();
+            for (int ks = 0; ks < nblk; ++ks) {
+                const uint64_t bdesc = sw128_desc(sv + ks * (kBlock * 128), HALF_ROWS_BYTES, 1024);
+                umma_f16(tmem_o, sw128_desc(base + L.p_hi + ks * 32, 16, 1024), bdesc, idesc_pv,
+                         (j > 0 || ks > 0) ? 1u : 0u);
+                umma_f16(tmem_o, sw128_desc(base + L.p_lo + ks * 32, 16, 1024), bdesc, idesc_pv, 1u);
+            }
+            umma_commit(empty0 + 8u * st);
+            if (j + kPreStages < n_steps) {
+                // the stage is free once this step's MMAs have read it
+                if (mbar_wait_bounded(empty0 + 8u * st, (j / kPreStages) & 1)) issue_step(j + kPreStages);
+                else t_ok = false;
+            }
+        }
+        if (!__syncthreads_and(t_ok)) {
+            ok = false;
+            break;
+        }
+    }
+    // ---- epilogue: wait for the last MMAs, write (m, l, O) of live rows ----
+    if (ok) {
+        if (tid == 0) umma_commit(mma_bar);
+        const bool t_ok = mbar_wait_bounded(mma_bar, mma_phase);
+        ok = __syncthreads_and(t_ok);
+    }
+    if (ok) {
+        tc_fence_after();
+        // tcgen05.ld is warp-collective: every lane loads, live rows store
+        const size_t row = ((size_t)tok * Hkv + item.head) * G + hg;
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+            float o[32];
+            tmem_ld32(tmem_o + lane_off + c0, o);
+            if (live) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                    *reinterpret_cast<float4*>(p.pre_o + row * D + c0 + i) =
+                        make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+            }
+        }
+        if (live) {
+            p.pre_ml[row * 2] = m_use;
+            p.pre_ml[row * 2 + 1] = l_run;
+        }
+    } else {
+        if (tid == 0) {
+            for (int jj = j; jj < issued; ++jj)
+                mbar_wait_bounded(full0 + 8u * (jj % kPreStages), (jj / kPreStages) & 1);
+            atomicExch(p.err, 1);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPreTmemCols) : "memory");
     }
 }
 
@@ -856,8 +1128,7 @@ __global__ void __launch_bounds__(256) rows_kernel(const uint16_t* __restrict__ 
     const int h = r % n_kv_heads;
     const int pos = r / n_kv_heads;
     const int b = trow[pos / kBlock], slot = pos % kBlock;
-    const uint16_t* src = pool_layer + (((size_t)b * n_kv_heads + h) * 2 + kvsel) * (kBlock * D) + (size_t)slot * D +
-                          (size_t)swz(c, slot) * 8;
+    const uint16_t* src = pool_layer + (((size_t)b * n_kv_heads + h) * 2 + kvsel) * (kBlock * D) + chunk_off(c, slot);
     uint16_t* dst = (kvsel ? v_out : k_out) + (size_t)pos * n_kv_heads * D + (size_t)h * D + (size_t)c * 8;
     *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
 }
@@ -936,11 +1207,24 @@ int attend_launches(const AttnParams& p) { return p.n_warps == 0 ? 0 : 1; }
 
 cudaError_t launch_prefix(const PrefixParams& p, int n_items, int head_dim, cudaStream_t s) {
     if (n_items <= 0) return cudaSuccess;
-    const size_t smem = (size_t)4 * 2 * kBlock * head_dim * 2 + 2 * 4 * 8;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    static bool attr[64][2] = {};
+    const size_t smem = PreSmem(head_dim).total + 1024;  // + alignment slack
+    const int hi = head_dim == 64 ? 0 : 1;
+    if (!attr[dev][hi]) {
+        e = head_dim == 64
+                ? cudaFuncSetAttribute(prefix_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                : cudaFuncSetAttribute(prefix_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr[dev][hi] = true;
+    }
     if (head_dim == 64)
-        prefix_attn_kernel<64><<<n_items, kPreWarps * 32, smem, s>>>(p);
+        prefix_attn_kernel<64><<<n_items, kPreRows, smem, s>>>(p);
     else
-        prefix_attn_kernel<128><<<n_items, kPreWarps * 32, smem, s>>>(p);
+        prefix_attn_kernel<128><<<n_items, kPreRows, smem, s>>>(p);
     return cudaGetLastError();
 }
 

@@ -330,16 +330,19 @@ def gather_heads(kv: "KvCache", local, comm: NcclComm, out=None, gathered=None, 
 
 
 def unswizzle_pool(raw: np.ndarray):
-    """Invert the device pool layout: [block][head][2][16][D] with chunk c of
-    slot s stored at c ^ (s & 7) -> reference (K, V) [block][16][head*D]."""
+    """Invert the device pool layout -> reference (K, V) [block][16][head*D].
+
+    Device layout: [block][head][2 (K, V)][D/64][16 slots][64]; inside each
+    16 x 64 sub-tile the 16-byte chunk c of slot s is stored at chunk
+    position c ^ (s & 7)."""
     nb, hkv, _, blk, d = raw.shape
-    ch = d // 8
-    chunks = raw.reshape(nb, hkv, 2, blk, ch, 8)
+    hs = d // 64
+    sub = raw.reshape(nb, hkv, 2, hs, blk, 8, 8)  # [.., half, slot, physical chunk, 8]
     slot = np.arange(blk)[:, None]
-    c = np.arange(ch)[None, :]
-    phys = c ^ (slot & 7)  # logical chunk c lives at physical chunk phys
-    logical = chunks[:, :, :, np.arange(blk)[:, None], phys, :]  # [nb, hkv, 2, blk, ch, 8]
-    logical = logical.reshape(nb, hkv, 2, blk, d)
+    c = np.arange(8)[None, :]
+    phys = c ^ (slot & 7)  # logical chunk c of slot s lives at physical chunk phys
+    logical = sub[:, :, :, :, np.arange(blk)[:, None], phys, :]  # [nb, hkv, 2, hs, blk, 8, 8]
+    logical = logical.transpose(0, 1, 2, 4, 3, 5, 6).reshape(nb, hkv, 2, blk, d)
     k = logical[:, :, 0].transpose(0, 2, 1, 3).reshape(nb, blk, hkv * d)
     v = logical[:, :, 1].transpose(0, 2, 1, 3).reshape(nb, blk, hkv * d)
     return np.ascontiguousarray(k), np.ascontiguousarray(v)
