@@ -220,7 +220,7 @@ lt_status lt_kv_set_min_tiles_per_warp(lt_kv* kv, uint32_t tiles);
  * extra launch that stages each shared K/V tile once for the whole group;
  * the decode launch then covers only each token's own blocks and folds the
  * prefix result in (online-softmax merge, f32).  Default 8; 0 turns it off.
- * Calls of more than 2048 tokens (or max_batch) never use it. */
+ * Calls of more than 1024 tokens (or max_batch) never use it. */
 lt_status lt_kv_set_cascade(lt_kv* kv, uint32_t min_group_tokens);
 
 /* Prefix-pass launches issued by this handle since creation. */

@@ -27,7 +27,7 @@ using ltkv::kBlock;
 namespace {
 
 constexpr int kSlots = 8;  // staging ring depth (pinned host + device pairs)
-constexpr uint32_t kCascadeMaxTokens = 2048;  // tokens of one call the prefix pass serves
+constexpr uint32_t kCascadeMaxTokens = 1024;  // tokens of one call the prefix pass serves
 constexpr int kCascadeMinBlocks = 4;          // shortest shared prefix worth a pass (64 positions)
 constexpr uint32_t kClean = 0xFFFFFFFFu;
 
@@ -71,11 +71,13 @@ struct lt_kv {
     // whose sequences share >= kCascadeMinBlocks leading blocks (0: off)
     uint32_t cascade_min_tokens = 8;
     uint32_t pre_cap = 0;          // tokens the prefix partial buffers hold
+    int sm_count = 0;              // of the device: the prefix pass splits blocks to fill it
     float* d_pre_o = nullptr;      // [pre_cap][n_heads][head_dim]
     float* d_pre_ml = nullptr;     // [pre_cap][n_heads][2]
     std::vector<uint32_t> casc_order;
     std::vector<int32_t> casc_buf;  // upload image: PrefixItems then the token list
     uint64_t cascade_launches = 0;
+    int casc_splits = 1;
     uint32_t n_blocks = 0, kv_dim = 0, group = 0, max_blocks = 0;
     size_t block_elems = 0;   // f16 elements of one block in one layer (all heads, K and V)
     size_t layer_elems = 0;   // f16 elements of one layer of the pool
@@ -404,7 +406,10 @@ int plan_cascade(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n
     });
     const int tpc = ltkv::prefix_tokens_per_cta((int)kv->group);
     const uint32_t hkv = kv->cfg.n_kv_heads;
-    std::vector<ltkv::PrefixItem> items;
+    struct Group {
+        int32_t root, P, off, cnt;
+    };
+    std::vector<Group> groups;
     std::vector<int32_t> toks;
     for (uint32_t a = 0; a < n;) {
         const int32_t first = kv->blocks[seq[ord[a]]][0];
@@ -424,19 +429,36 @@ int plan_cascade(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n
                 }
             }
             if (P >= (size_t)kCascadeMinBlocks) {
-                const int32_t off = (int32_t)toks.size();
+                groups.push_back({(int32_t)root, (int32_t)P, (int32_t)toks.size(), (int32_t)(b - a)});
                 for (uint32_t k = a; k < b; ++k) {
                     toks.push_back((int32_t)ord[k]);
                     kv->toks_tmp[ord[k]].skip = (int32_t)P;
                 }
-                const int32_t cnt = (int32_t)(b - a);
-                for (uint32_t h = 0; h < hkv; ++h)
-                    for (int32_t c0 = 0; c0 < cnt; c0 += tpc)
-                        items.push_back({(int32_t)root, (int32_t)P, (int32_t)h, off + c0, std::min(tpc, cnt - c0)});
             }
         }
         a = b;
     }
+    // Split every group's blocks over S CTAs so the pass fills the SMs; each
+    // split keeps at least one 4-block step.
+    long long base_items = 0;
+    int min_p = 1 << 30;
+    for (const Group& g : groups) {
+        base_items += (long long)hkv * ((g.cnt + tpc - 1) / tpc);
+        min_p = std::min(min_p, (int)g.P);
+    }
+    int S = 1;
+    if (base_items > 0)
+        S = (int)std::max<long long>(1, std::min<long long>(ltkv::kPreMaxSplits, kv->sm_count / base_items));
+    S = std::max(1, std::min(S, min_p / 4));
+    kv->casc_splits = S;
+    std::vector<ltkv::PrefixItem> items;
+    for (const Group& g : groups)
+        for (uint32_t h = 0; h < hkv; ++h)
+            for (int32_t c0 = 0; c0 < g.cnt; c0 += tpc)
+                for (int sp = 0; sp < S; ++sp) {
+                    const int32_t b0 = (int32_t)((long long)g.P * sp / S), b1 = (int32_t)((long long)g.P * (sp + 1) / S);
+                    items.push_back({g.root, b0, b1, sp, (int32_t)h, g.off + c0, std::min(tpc, g.cnt - c0)});
+                }
     kv->casc_buf.resize(items.size() * (sizeof(ltkv::PrefixItem) / 4) + toks.size());
     if (!items.empty()) std::memcpy(kv->casc_buf.data(), items.data(), items.size() * sizeof(ltkv::PrefixItem));
     if (!toks.empty())
@@ -548,6 +570,8 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     }
     p.pre_o = kv->d_pre_o;
     p.pre_ml = kv->d_pre_ml;
+    p.pre_splits = n_items > 0 ? kv->casc_splits : 0;
+    p.pre_split_rows = (int64_t)kv->pre_cap * kv->cfg.n_heads;
     cudaEvent_t ev_end = nullptr;
     if (kv->profiling) {
         lt_status prc = prof_begin(kv, st, &ev_end);
@@ -575,6 +599,7 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
         pp.scale_log2 = p.scale_log2;
         pp.pre_o = kv->d_pre_o;
         pp.pre_ml = kv->d_pre_ml;
+        pp.split_rows = p.pre_split_rows;
         pp.err = kv->d_err;
         const cudaError_t pe = ltkv::launch_prefix(pp, n_items, (int)kv->cfg.head_dim, st);
         if (pe != cudaSuccess) {
@@ -671,7 +696,9 @@ lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_flags, kv->ws_slots * sizeof(uint32_t) + 4), "cudaMalloc(flags)");
         if (rc == LT_OK) ck(cudaMemset(kv->d_flags, 0, kv->ws_slots * sizeof(uint32_t) + 4), "cudaMemset(flags)");
         kv->pre_cap = std::min<uint32_t>(c.max_batch, kCascadeMaxTokens);
-        const size_t pre_rows = (size_t)kv->pre_cap * c.n_heads;
+        const size_t pre_rows = (size_t)kv->pre_cap * c.n_heads * ltkv::kPreMaxSplits;
+        if (rc == LT_OK) ck(cudaDeviceGetAttribute(&kv->sm_count, cudaDevAttrMultiProcessorCount, c.device),
+                            "cudaDeviceGetAttribute");
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_pre_o, pre_rows * c.head_dim * sizeof(float) + 16), "cudaMalloc(prefix)");
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_pre_ml, pre_rows * 2 * sizeof(float) + 16), "cudaMalloc(prefix)");
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_err, sizeof(int32_t)), "cudaMalloc(err)");

@@ -44,8 +44,10 @@ struct AttnParams {
     const void* k_new;           // fused append: new K/V rows [n][n_kv_heads*D], or null
     const void* v_new;
     int32_t kv_f32;
-    const float* pre_o;          // [n][n_kv_heads][group][D]: shared-prefix partial O (tokens with skip > 0)
-    const float* pre_ml;         // [n][n_kv_heads][group][2]: its (m, l)
+    const float* pre_o;          // [pre_splits][rows][D]: shared-prefix partial O (tokens with skip > 0),
+    const float* pre_ml;         // [pre_splits][rows][2]: its (m, l); row = (token*n_kv_heads + h)*group + g
+    int32_t pre_splits;          // partials per row (the prefix blocks split over that many CTAs)
+    int64_t pre_split_rows;      // rows between split slabs
     TokenDesc inl[kInlineTokens];
 };
 
@@ -56,11 +58,14 @@ struct AttnParams {
 // that the stream-K launch folds into the tokens' outputs.
 struct PrefixItem {
     int32_t root_seq;  // a member whose table row holds the shared blocks
-    int32_t n_blocks;  // shared blocks [0, n_blocks)
+    int32_t blk0;      // this item's part of the shared blocks: [blk0, blk1)
+    int32_t blk1;
+    int32_t split;     // which partial slab it writes
     int32_t head;      // KV head
     int32_t tok_off;   // first of the item's tokens in the token list
     int32_t n_tok;     // tokens of this item
 };
+constexpr int kPreMaxSplits = 4;
 struct PrefixParams {
     const uint16_t* pool_layer;
     const int32_t* tables;
@@ -73,6 +78,7 @@ struct PrefixParams {
     float scale_log2;
     float* pre_o;
     float* pre_ml;
+    int64_t split_rows;  // rows between split slabs of pre_o / pre_ml
     int32_t* err;
 };
 // Tokens one prefix CTA covers: 128 query rows / group.

@@ -238,17 +238,20 @@ template <int D>
 __device__ __forceinline__ void fold_prefix(const AttnParams& p, int tok, int h, int g, int t4, float& M, float& L,
                                             float (&acc)[D / 8][2]) {
     const size_t r = ((size_t)tok * p.n_kv_heads + h) * p.group + g;
-    const float mp = __ldcg(p.pre_ml + r * 2), lp = __ldcg(p.pre_ml + r * 2 + 1);
-    const float M2 = fmaxf(M, mp);
-    const float a = ex2(M - M2), b = ex2(mp - M2);
-    L = L * a + lp * b;
-    M = M2;
-    const float* po = p.pre_o + r * D + 2 * t4;
+    for (int sp = 0; sp < p.pre_splits; ++sp) {
+        const size_t rs = r + (size_t)sp * p.pre_split_rows;
+        const float mp = __ldcg(p.pre_ml + rs * 2), lp = __ldcg(p.pre_ml + rs * 2 + 1);
+        const float M2 = fmaxf(M, mp);
+        const float a = ex2(M - M2), b = ex2(mp - M2);
+        L = L * a + lp * b;
+        M = M2;
+        const float* po = p.pre_o + rs * D + 2 * t4;
 #pragma unroll
-    for (int nt = 0; nt < D / 8; ++nt) {
-        const float2 v = __ldcg(reinterpret_cast<const float2*>(po + nt * 8));
-        acc[nt][0] = acc[nt][0] * a + v.x * b;
-        acc[nt][1] = acc[nt][1] * a + v.y * b;
+        for (int nt = 0; nt < D / 8; ++nt) {
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(po + nt * 8));
+            acc[nt][0] = acc[nt][0] * a + v.x * b;
+            acc[nt][1] = acc[nt][1] * a + v.y * b;
+        }
     }
 }
 
@@ -778,52 +781,69 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-constexpr int kPreRows = 128;       // tcgen05 M
-constexpr int kPreStepBlocks = 4;   // blocks (16 positions each) per step: N = 64
-constexpr int kPreStages = 3;
-constexpr int kPreTmemCols = 256;   // S: [0, 64), O: [64, 64 + D)
-constexpr float kRescaleLog2 = 8.f; // the running maximum moves only by more than this
+constexpr int kPreRows = 128;        // tcgen05 M: query rows of a CTA
+constexpr int kPreStepBlocks = 4;    // blocks (16 positions each) per step: N = 64
+constexpr int kPreStages = 3;        // K/V ring: copies run kPreStages - 2 steps ahead of their use
+constexpr int kPreThreads = 160;     // warps 0..3: softmax of rows 32w..32w+31; warp 4: copies + MMAs
+constexpr int kPreTmemCols = 256;    // S buffers at columns 0 and 64, O at 128
+constexpr float kRescaleLog2 = 8.f;  // a row's maximum moves only when it grows by more than this
 
-// Shared-memory layout of the prefix CTA (offsets from a 1024-aligned base).
+// Shared-memory layout of the prefix CTA (offsets from a 1024-aligned base):
+// Q value and residual [D/64][128 rows][128 B]; kPreStages K/V stages, each
+// K [D/64][64 rows][128 B] then V alike; two P buffers, each value and
+// residual [128 rows][128 B]; the mbarriers.
 struct PreSmem {
-    uint32_t q_hi, q_lo, stage0, p_hi, p_lo, bars, total;
+    uint32_t q_hi, q_lo, stage0, stage_bytes, p0, bars, total;
     __host__ __device__ explicit PreSmem(int D) {
-        const uint32_t qbytes = (uint32_t)kPreRows * D * 2;                 // [D/64][128 rows][128 B]
-        const uint32_t stage = (uint32_t)2 * kPreStepBlocks * kBlock * D * 2;  // K and V: [D/64][64 rows][128 B]
+        const uint32_t qbytes = (uint32_t)kPreRows * D * 2;
+        stage_bytes = (uint32_t)2 * kPreStepBlocks * kBlock * D * 2;
         q_hi = 0;
         q_lo = q_hi + qbytes;
         stage0 = q_lo + qbytes;
-        p_hi = stage0 + kPreStages * stage;
-        p_lo = p_hi + kPreRows * 128;
-        bars = p_lo + kPreRows * 128;
-        total = bars + 128;
+        p0 = stage0 + kPreStages * stage_bytes;  // P buffer b: value at p0 + b*2*16K, residual +16K
+        bars = p0 + 2 * 2 * kPreRows * 128;
+        total = bars + 256;
     }
 };
 
+// mbarrier arrive (count 1) from a thread.
+__device__ __forceinline__ void mbar_arrive1(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 template <int D>
-__global__ void __launch_bounds__(kPreRows, 1) prefix_attn_kernel(const __grid_constant__ PrefixParams p) {
+__global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __grid_constant__ PrefixParams p) {
     constexpr int HALVES = D / 64;
-    constexpr uint32_t STAGE = 2 * kPreStepBlocks * kBlock * D * 2;
-    constexpr uint32_t KPART = STAGE / 2;                    // K sub-tiles of a stage; V follows
     constexpr uint32_t HALF_ROWS_BYTES = kPreStepBlocks * kBlock * 128;  // one 64-wide sub-tile column of a stage
+    constexpr uint32_t PBUF = 2 * kPreRows * 128;                         // one P buffer: value + residual
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t* sbase = smem_raw + (base - smem_u32(smem_raw));
     const PreSmem L(D);
+    const uint32_t STAGE = L.stage_bytes, KPART = STAGE / 2;
     const PrefixItem item = p.items[blockIdx.x];
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = p.group, Hkv = p.n_kv_heads;
-    const uint32_t full0 = base + L.bars, empty0 = full0 + 8u * kPreStages, mma_bar = empty0 + 8u * kPreStages;
-    uint32_t* tmem_word = reinterpret_cast<uint32_t*>(sbase + L.bars + 8 * (2 * kPreStages + 1));
+    // barriers: kv_full[3], kv_empty[3], s_full[2], s_free[2], p_full[2], p_free[2], pv_done, tmem word
+    const uint32_t kv_full = base + L.bars, kv_empty = kv_full + 8u * kPreStages;
+    const uint32_t s_full = kv_empty + 8u * kPreStages, s_free = s_full + 16u, p_full = s_free + 16u,
+                   p_free = p_full + 16u, pv_done = p_free + 16u;
+    uint32_t* tmem_word = reinterpret_cast<uint32_t*>(sbase + L.bars + 8 * (2 * kPreStages + 9));
     if (tid == 0) {
         for (int st = 0; st < kPreStages; ++st) {
-            mbar_init(full0 + 8u * st, 1);
-            mbar_init(empty0 + 8u * st, 1);
+            mbar_init(kv_full + 8u * st, 1);
+            mbar_init(kv_empty + 8u * st, 1);
         }
-        mbar_init(mma_bar, 1);
+        for (int bb = 0; bb < 2; ++bb) {
+            mbar_init(s_full + 8u * bb, 1);
+            mbar_init(s_free + 8u * bb, 4);  // one arrival per softmax warp
+            mbar_init(p_full + 8u * bb, 4);
+            mbar_init(p_free + 8u * bb, 1);
+        }
+        mbar_init(pv_done, 1);
         fence_mbar_init();
     }
-    __syncwarp();  // tcgen05.alloc is warp-collective: warp 0 converged again after thread 0's setup
+    __syncwarp();  // tcgen05.alloc is warp-collective: warp 0 converged after thread 0's setup
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_word)),
                      "r"(kPreTmemCols)
@@ -834,25 +854,32 @@ __global__ void __launch_bounds__(kPreRows, 1) prefix_attn_kernel(const __grid_c
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_word;
-    const uint32_t tmem_s = tmem, tmem_o = tmem + 64;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;  // this warp's TMEM lanes
+    const uint32_t tmem_o = tmem + 128;
 
-    const int nbk = item.n_blocks;
+    const int nbk = item.blk1 - item.blk0;  // >= 1: the host gives every split at least one step
     const int n_steps = (nbk + kPreStepBlocks - 1) / kPreStepBlocks;
-    const int32_t* trow = p.tables + (size_t)item.root_seq * p.max_blocks;
+    const int32_t* trow = p.tables + (size_t)item.root_seq * p.max_blocks + item.blk0;
     const size_t tile_elems = 2 * kBlock * D;
-    int issued = 0;  // thread 0: steps whose copies were issued
-    auto issue_step = [&](int j) {
+    auto step_blocks = [&](int j) { return min(kPreStepBlocks, nbk - j * kPreStepBlocks); };
+    int issued = 0;  // warp 4 lane 0: steps whose copies were issued
+    // The step's block ids, loaded together (independent loads) a step ahead
+    // of the copies that use them.
+    auto load_ids = [&](int j, int (&ids)[kPreStepBlocks]) {
+        if (j >= n_steps) return;
+        const int nblk = step_blocks(j);
+#pragma unroll
+        for (int bb = 0; bb < kPreStepBlocks; ++bb)
+            ids[bb] = bb < nblk ? __ldg(trow + j * kPreStepBlocks + bb) : 0;
+    };
+    auto issue_step = [&](int j, const int (&ids)[kPreStepBlocks]) {
         const int st = j % kPreStages;
-        const int nblk = min(kPreStepBlocks, nbk - j * kPreStepBlocks);
-        const uint32_t bar = full0 + 8u * st;
+        const int nblk = step_blocks(j);
+        const uint32_t bar = kv_full + 8u * st;
         mbar_arrive_expect_tx(bar, (uint32_t)nblk * 2 * kBlock * D * 2);
         const uint32_t sk = base + L.stage0 + st * STAGE;
         for (int bb = 0; bb < nblk; ++bb) {
-            const int blk = __ldg(trow + j * kPreStepBlocks + bb);
-            const uint16_t* src = p.pool_layer + ((size_t)blk * Hkv + item.head) * tile_elems;
+            const uint16_t* src = p.pool_layer + ((size_t)ids[bb] * Hkv + item.head) * tile_elems;
             for (int hh = 0; hh < HALVES; ++hh) {
-                // K sub-tile hh -> K region column hh, rows 16bb..; V likewise
                 bulk_g2s(sk + hh * HALF_ROWS_BYTES + bb * (kBlock * 128), src + hh * (kBlock * 64), kBlock * 128, bar);
                 bulk_g2s(sk + KPART + hh * HALF_ROWS_BYTES + bb * (kBlock * 128), src + kBlock * D + hh * (kBlock * 64),
                          kBlock * 128, bar);
@@ -860,15 +887,22 @@ __global__ void __launch_bounds__(kPreRows, 1) prefix_attn_kernel(const __grid_c
         }
         ++issued;
     };
-    if (tid == 0)
-        for (int j = 0; j < min(kPreStages, n_steps); ++j) issue_step(j);
+    int nxt_ids[kPreStepBlocks] = {};  // ids of the next refill (step kPreStages, ...)
+    if (tid == kPreRows) {
+        for (int j = 0; j < min(kPreStages, n_steps); ++j) {
+            int ids[kPreStepBlocks] = {};
+            load_ids(j, ids);
+            issue_step(j, ids);
+        }
+        load_ids(kPreStages, nxt_ids);
+    }
 
-    // Q rows: row r = token r / G, head r % G; value and f16 residual, 128-byte swizzled
+    // Q rows (warps 0..3): row r = token r / G, head r % G; value and f16 residual
     const int r = tid;
     const int t_item = r / G, hg = r % G;
-    const bool live = t_item < item.n_tok && t_item < kPreRows / G;
+    const bool live = r < kPreRows && t_item < item.n_tok && t_item < kPreRows / G;
     const int tok = live ? p.tok_list[item.tok_off + t_item] : 0;
-    {
+    if (r < kPreRows) {
         const int qelem = p.q_f32 ? 4 : 2;
         const uint8_t* qrow = static_cast<const uint8_t*>(p.q) + (((size_t)tok * Hkv + item.head) * G + hg) * D * qelem;
 #pragma unroll 1
@@ -905,166 +939,185 @@ __global__ void __launch_bounds__(kPreRows, 1) prefix_attn_kernel(const __grid_c
             *reinterpret_cast<uint4*>(sbase + L.q_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
     }
-    fence_proxy_async_smem();  // generic writes of Q -> visible to the tensor core
+    fence_proxy_async_smem();  // Q -> visible to the tensor core
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
 
-    const uint32_t idesc_pv = f16_idesc(D, true);
-    const float scale_log2 = p.scale_log2;
-    float m_use = -INFINITY, l_run = 0.f;
-    uint32_t mma_phase = 0;
     bool ok = true;
-    int j = 0;
-    for (; j < n_steps; ++j) {
-        const int st = j % kPreStages;
-        const int nblk = min(kPreStepBlocks, nbk - j * kPreStepBlocks);
-        const uint32_t sk = base + L.stage0 + st * STAGE, sv = sk + KPART;
-        // ---- S = Q K^T (thread 0 issues) ----
-        bool t_ok = true;
-        if (tid == 0) {
-            t_ok = mbar_wait_bounded(full0 + 8u * st, (j / kPreStages) & 1);
-            if (t_ok) {
+    int j_fail = 0;
+    if (warp == 4) {
+        // ===== producer / MMA issuer (one lane) =====
+        if (lane == 0) {
+            const uint32_t idesc_pv = f16_idesc(D, true);
+            auto issue_pv = [&](int j) {  // O += P(j) V(j), then free its stage and P buffer
+                const int st = j % kPreStages, bb = j & 1;
+                const int nblk = step_blocks(j);
+                const uint32_t sv = base + L.stage0 + st * STAGE + KPART;
+                const uint32_t pv = base + L.p0 + bb * PBUF;
+                for (int ks = 0; ks < nblk; ++ks) {
+                    const uint64_t bdesc = sw128_desc(sv + ks * (kBlock * 128), HALF_ROWS_BYTES, 1024);
+                    umma_f16(tmem_o, sw128_desc(pv + ks * 32, 16, 1024), bdesc, idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
+                    umma_f16(tmem_o, sw128_desc(pv + kPreRows * 128 + ks * 32, 16, 1024), bdesc, idesc_pv, 1u);
+                }
+                umma_commit(kv_empty + 8u * st);
+                umma_commit(p_free + 8u * bb);
+                umma_commit(pv_done);
+            };
+            // S(j) = Q K(j)^T into S buffer j&1, once its copies landed and
+            // softmax(j-2) has read that buffer
+            auto issue_s = [&](int j) -> bool {
+                const int st = j % kPreStages, bb = j & 1;
+                if (!mbar_wait_bounded(kv_full + 8u * st, (j / kPreStages) & 1)) return false;
+                if (j >= 2 && !mbar_wait_bounded(s_free + 8u * bb, ((j - 2) >> 1) & 1)) return false;
                 tc_fence_after();
+                const uint32_t sk = base + L.stage0 + st * STAGE;
+                const uint32_t idesc_s = f16_idesc(step_blocks(j) * kBlock, false);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t koff = (uint32_t)(kk >> 2) * (kPreRows * 128) + (kk & 3) * 32;
-                    const uint32_t boff = (uint32_t)(kk >> 2) * HALF_ROWS_BYTES + (kk & 3) * 32;
-                    const uint64_t bdesc = sw128_desc(sk + boff, 16, 1024);
-                    umma_f16(tmem_s, sw128_desc(base + L.q_hi + koff, 16, 1024), bdesc,
-                             f16_idesc(nblk * kBlock, false), kk > 0 ? 1u : 0u);
-                    umma_f16(tmem_s, sw128_desc(base + L.q_lo + koff, 16, 1024), bdesc,
-                             f16_idesc(nblk * kBlock, false), 1u);
+                    const uint32_t qoff = (uint32_t)(kk >> 2) * (kPreRows * 128) + (kk & 3) * 32;
+                    const uint32_t koff = (uint32_t)(kk >> 2) * HALF_ROWS_BYTES + (kk & 3) * 32;
+                    const uint64_t bdesc = sw128_desc(sk + koff, 16, 1024);
+                    umma_f16(tmem + 64 * bb, sw128_desc(base + L.q_hi + qoff, 16, 1024), bdesc, idesc_s,
+                             kk > 0 ? 1u : 0u);
+                    umma_f16(tmem + 64 * bb, sw128_desc(base + L.q_lo + qoff, 16, 1024), bdesc, idesc_s, 1u);
                 }
-                umma_commit(mma_bar);
+                umma_commit(s_full + 8u * bb);
+                return true;
+            };
+            // The tensor cores run S two steps ahead of P V: S(0), S(1), PV(0),
+            // S(2), PV(1), ... so softmax(j+1) never waits on PV(j).
+            for (int j = 0; j < min(2, n_steps) && ok; ++j) ok = issue_s(j);
+            for (int j = 0; j < n_steps && ok; ++j) {
+                ok = mbar_wait_bounded(p_full + 8u * (j & 1), (j >> 1) & 1);
+                if (!ok) { j_fail = j; break; }
+                tc_fence_after();
+                issue_pv(j);
+                if (j + 2 < n_steps && !(ok = issue_s(j + 2))) { j_fail = j; break; }
+                if (j + kPreStages < n_steps) {
+                    // refill step j's stage once its MMAs have read it (the
+                    // ring keeps the copies kPreStages - 2 steps ahead)
+                    ok = mbar_wait_bounded(kv_empty + 8u * (j % kPreStages), (j / kPreStages) & 1);
+                    if (!ok) { j_fail = j; break; }
+                    issue_step(j + kPreStages, nxt_ids);
+                    load_ids(j + kPreStages + 1, nxt_ids);
+                }
+            }
+            if (!ok) {
+                // bounded drain of the copies still in flight, then report
+                for (int jj = j_fail; jj < issued; ++jj)
+                    mbar_wait_bounded(kv_full + 8u * (jj % kPreStages), (jj / kPreStages) & 1);
+                atomicExch(p.err, 1);
             }
         }
-        if (!__syncthreads_and(t_ok)) {
-            ok = false;
-            break;
-        }
-        // ---- softmax of row r ----
-        t_ok = mbar_wait_bounded(mma_bar, mma_phase);
-        mma_phase ^= 1;
-        if (!__syncthreads_and(t_ok)) {
-            ok = false;
-            break;
-        }
-        tc_fence_after();
-        const int npos = nblk * kBlock;
-        float sv_[64];
-        {
-            float tmp[32];
-            tmem_ld32(tmem_s + lane_off, tmp);
+    } else {
+        // ===== softmax warps: thread r owns query row r (TMEM lane r) =====
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        const float scale_log2 = p.scale_log2;
+        float m_use = -INFINITY, l_run = 0.f;
+        for (int j = 0; j < n_steps; ++j) {
+            const int bb = j & 1;
+            const int npos = step_blocks(j) * kBlock;
+            bool w_ok = mbar_wait_bounded(s_full + 8u * bb, (j >> 1) & 1);
+            if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
+            tc_fence_after();
+            float sv_[64];
+            {
+                float tmp[32];
+                tmem_ld32(tmem + 64 * bb + lane_off, tmp);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) sv_[i] = tmp[i];
-            if (npos > 32) {
-                tmem_ld32(tmem_s + lane_off + 32, tmp);
+                for (int i = 0; i < 32; ++i) sv_[i] = tmp[i];
+                if (npos > 32) {
+                    tmem_ld32(tmem + 64 * bb + lane_off + 32, tmp);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) sv_[32 + i] = tmp[i];
-            } else {
+                    for (int i = 0; i < 32; ++i) sv_[32 + i] = tmp[i];
+                } else {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) sv_[32 + i] = 0.f;
+                    for (int i = 0; i < 32; ++i) sv_[32 + i] = 0.f;
+                }
             }
-        }
-        float mx = -INFINITY;
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive1(s_free + 8u * bb);  // S buffer bb may be overwritten
+            float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-            sv_[i] = i < npos ? sv_[i] * scale_log2 : -INFINITY;
-            mx = fmaxf(mx, sv_[i]);
-        }
-        float alpha = 1.f;
-        bool rescale = false;
-        if (mx > m_use + kRescaleLog2 || m_use == -INFINITY) {
-            const float m_new = mx;
-            alpha = m_use == -INFINITY ? 0.f : ex2(m_use - m_new);
-            rescale = j > 0 && m_use != -INFINITY;
-            m_use = m_new;
-        }
-        float lsum = 0.f;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            uint32_t hi[4], lo[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float p0 = ex2(sv_[8 * c + 2 * e] - m_use), p1 = ex2(sv_[8 * c + 2 * e + 1] - m_use);
-                lsum += p0 + p1;
-                const __half2 h = __floats2half2_rn(p0, p1);
-                const float2 hf = __half22float2(h);
-                hi[e] = h2_bits(h);
-                lo[e] = h2_bits(__floats2half2_rn(p0 - hf.x, p1 - hf.y));
+            for (int i = 0; i < 64; ++i) {
+                sv_[i] = i < npos ? sv_[i] * scale_log2 : -INFINITY;
+                mx = fmaxf(mx, sv_[i]);
             }
-            const uint32_t off = r * 128 + (((c & 7) ^ (r & 7)) << 4);
-            *reinterpret_cast<uint4*>(sbase + L.p_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *reinterpret_cast<uint4*>(sbase + L.p_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            float alpha = 1.f;
+            bool rescale = false;
+            if (mx > m_use + kRescaleLog2 || m_use == -INFINITY) {
+                alpha = m_use == -INFINITY ? 0.f : ex2(m_use - mx);
+                rescale = m_use != -INFINITY;
+                m_use = mx;
+            }
+            if (__any_sync(0xffffffffu, rescale)) {
+                // this warp's O rows are scaled once PV(j-1) has finished
+                w_ok = mbar_wait_bounded(pv_done, (j - 1) & 1);
+                if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll 1
+                for (int c0 = 0; c0 < D; c0 += 32) {
+                    float o[32];
+                    tmem_ld32(tmem_o + lane_off + c0, o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                    tmem_st32(tmem_o + lane_off + c0, o);
+                }
+            }
+            // P buffer bb is free once PV(j-2) has read it
+            if (j >= 2) {
+                w_ok = mbar_wait_bounded(p_free + 8u * bb, ((j - 2) >> 1) & 1);
+                if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
+            }
+            const uint32_t pb = L.p0 + bb * PBUF;
+            float lsum = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint32_t hi[4], lo[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float p0 = ex2(sv_[8 * c + 2 * e] - m_use), p1 = ex2(sv_[8 * c + 2 * e + 1] - m_use);
+                    lsum += p0 + p1;
+                    const __half2 h = __floats2half2_rn(p0, p1);
+                    const float2 hf = __half22float2(h);
+                    hi[e] = h2_bits(h);
+                    lo[e] = h2_bits(__floats2half2_rn(p0 - hf.x, p1 - hf.y));
+                }
+                const uint32_t off = r * 128 + (((c & 7) ^ (r & 7)) << 4);
+                *reinterpret_cast<uint4*>(sbase + pb + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4*>(sbase + pb + kPreRows * 128 + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
+            l_run = l_run * alpha + lsum;
+            fence_proxy_async_smem();  // P rows (and O rescale) -> visible to the tensor core
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive1(p_full + 8u * bb);
         }
-        l_run = l_run * alpha + lsum;
-        if (__syncthreads_or(rescale)) {
-            // some row moved its maximum: every row scales its O by its alpha
-            // (1 where it did not); the PV of the previous step has completed
-            // (the S commit above tracked it)
+        if (ok && n_steps > 0) {
+            const bool w_ok = mbar_wait_bounded(pv_done, (n_steps - 1) & 1);
+            ok = __all_sync(0xffffffffu, w_ok);
+        }
+        if (ok) {
+            tc_fence_after();
+            const size_t row = ((size_t)tok * Hkv + item.head) * G + hg + (size_t)item.split * p.split_rows;
 #pragma unroll 1
             for (int c0 = 0; c0 < D; c0 += 32) {
                 float o[32];
                 tmem_ld32(tmem_o + lane_off + c0, o);
+                if (live) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                tmem_st32(tmem_o + lane_off + c0, o);
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4*>(p.pre_o + row * D + c0 + i) =
+                            make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+                }
             }
-        }
-        fence_proxy_async_smem();  // P rows -> visible to the tensor core
-        tc_fence_before();
-        __syncthreads();
-        // ---- O += P V (thread 0 issues), then refill the stage ----
-        if (tid == 0) {
-            tc_fence_after();
-            for (int ks = 0; ks < nblk; ++ks) {
-                const uint64_t bdesc = sw128_desc(sv + ks * (kBlock * 128), HALF_ROWS_BYTES, 1024);
-                umma_f16(tmem_o, sw128_desc(base + L.p_hi + ks * 32, 16, 1024), bdesc, idesc_pv,
-                         (j > 0 || ks > 0) ? 1u : 0u);
-                umma_f16(tmem_o, sw128_desc(base + L.p_lo + ks * 32, 16, 1024), bdesc, idesc_pv, 1u);
-            }
-            umma_commit(empty0 + 8u * st);
-            if (j + kPreStages < n_steps) {
-                // the stage is free once this step's MMAs have read it
-                if (mbar_wait_bounded(empty0 + 8u * st, (j / kPreStages) & 1)) issue_step(j + kPreStages);
-                else t_ok = false;
-            }
-        }
-        if (!__syncthreads_and(t_ok)) {
-            ok = false;
-            break;
-        }
-    }
-    // ---- epilogue: wait for the last MMAs, write (m, l, O) of live rows ----
-    if (ok) {
-        if (tid == 0) umma_commit(mma_bar);
-        const bool t_ok = mbar_wait_bounded(mma_bar, mma_phase);
-        ok = __syncthreads_and(t_ok);
-    }
-    if (ok) {
-        tc_fence_after();
-        // tcgen05.ld is warp-collective: every lane loads, live rows store
-        const size_t row = ((size_t)tok * Hkv + item.head) * G + hg;
-#pragma unroll 1
-        for (int c0 = 0; c0 < D; c0 += 32) {
-            float o[32];
-            tmem_ld32(tmem_o + lane_off + c0, o);
             if (live) {
-#pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                    *reinterpret_cast<float4*>(p.pre_o + row * D + c0 + i) =
-                        make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+                p.pre_ml[row * 2] = m_use;
+                p.pre_ml[row * 2 + 1] = l_run;
             }
-        }
-        if (live) {
-            p.pre_ml[row * 2] = m_use;
-            p.pre_ml[row * 2 + 1] = l_run;
-        }
-    } else {
-        if (tid == 0) {
-            for (int jj = j; jj < issued; ++jj)
-                mbar_wait_bounded(full0 + 8u * (jj % kPreStages), (jj / kPreStages) & 1);
+        } else if (lane == 0) {
             atomicExch(p.err, 1);
         }
     }
@@ -1222,9 +1275,9 @@ cudaError_t launch_prefix(const PrefixParams& p, int n_items, int head_dim, cuda
         attr[dev][hi] = true;
     }
     if (head_dim == 64)
-        prefix_attn_kernel<64><<<n_items, kPreRows, smem, s>>>(p);
+        prefix_attn_kernel<64><<<n_items, kPreThreads, smem, s>>>(p);
     else
-        prefix_attn_kernel<128><<<n_items, kPreRows, smem, s>>>(p);
+        prefix_attn_kernel<128><<<n_items, kPreThreads, smem, s>>>(p);
     return cudaGetLastError();
 }
 

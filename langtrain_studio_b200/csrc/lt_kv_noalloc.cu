@@ -165,6 +165,8 @@ extern "C" lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_
     p.kv_f32 = 0;
     p.pre_o = nullptr;
     p.pre_ml = nullptr;
+    p.pre_splits = 0;
+    p.pre_split_rows = 0;
     if (ltkv::launch_attend(p, (int)head_dim, st) != cudaSuccess) return LT_E_CUDA;
     return LT_OK;
 }
