@@ -602,163 +602,39 @@ def run_c4(args, rank, world, local, mode):
     return res
 
 
-class ChurnDriver:
-    """continuous batching with the reference scheduler's KV
-    policy, restated in blocks over the C ABI (engine/crates/engine/src/
-    scheduler.rs:252-473, prefix.rs:58-125):
-      - admit FIFO into the least recently used idle slot while the prompt
-        plus min(output, DECODE_HEADROOM=256) tokens fit, evicting idle
-        slots' cached KV LRU first (kv_remove(slot, 0));
-      - each step: one decode token per sequence past its prompt, prompt
-        chunks of at most 256 tokens (EngineConfig.prefill_chunk);
-      - before the step, free enough blocks: evict LRU idle, then preempt the
-        youngest running sequence (it finishes with Length);
-      - retire: a finished slot keeps its KV for prefix reuse (idle);
-      - compaction every step (no reference counterpart).
-    Prompt ids are random, so no prefix is ever reused; prompt tokens are
-    appended and their K/V written, decode tokens run the fused
-    append + attention launch (prefill attention is a later addition)."""
+class Arrivals:
+    """The configs[4] request process: Poisson(lam) arrivals per step, prompt
+    lengths log-uniform in [lo, hi], output lengths uniform in [olo, ohi]."""
 
-    HEADROOM = 256
-    CHUNK = 256
-
-    def __init__(self, kv, n_slots, lam, seed, kv_src, q_src, prompt_lo=64, prompt_hi=8192, out_lo=16, out_hi=512):
-        self.kv = kv
+    def __init__(self, lam, seed, lo=64, hi=8192, olo=16, ohi=512):
         self.rng = np.random.default_rng(seed)
-        self.lam = lam
-        self.lo, self.hi, self.olo, self.ohi = prompt_lo, prompt_hi, out_lo, out_hi
-        self.busy = np.zeros(n_slots, bool)
-        self.held = np.zeros(n_slots, np.int64)  # tokens an idle slot keeps
-        self.last_used = np.zeros(n_slots, np.int64)
-        self.clock = 0
-        self.queue = []
-        self.active = {}  # slot -> [n_past, prompt, total, admit_step]
-        self.step_no = 0
-        self.kv_src, self.q_src = kv_src, q_src  # device tensors the K/V/q rows are cut from
-        self.stats = dict(decode=0, prefill=0, evicted=0, preempted=0, moved=0, admitted=0, finished=0)
+        self.lam, self.lo, self.hi, self.olo, self.ohi = lam, lo, hi, olo, ohi
 
-    def _evict_lru_idle(self):
-        idle = np.nonzero(~self.busy & (self.held > 0))[0]
-        if idle.size == 0:
-            return False
-        i = int(idle[np.argmin(self.last_used[idle])])
-        self.kv.truncate(i, 0)
-        self.held[i] = 0
-        self.stats["evicted"] += 1
-        return True
-
-    def _retire(self, slot, n_past):
-        self.busy[slot] = False
-        self.held[slot] = n_past
-        self.clock += 1
-        self.last_used[slot] = self.clock
-        del self.active[slot]
-
-    def arrivals(self):
+    def step(self):
+        out = []
         for _ in range(self.rng.poisson(self.lam)):
             prompt = int(np.exp(self.rng.uniform(np.log(self.lo), np.log(self.hi))))
-            out = int(self.rng.integers(self.olo, self.ohi + 1))
-            self.queue.append((prompt, out))
+            out.append((prompt, int(self.rng.integers(self.olo, self.ohi + 1))))
+        return out
 
-    def admit(self):
-        while self.queue:
-            idle = np.nonzero(~self.busy)[0]
-            if idle.size == 0:
-                break
-            prompt, out = self.queue[0]
-            need = (prompt + min(out, self.HEADROOM) + BLOCK - 1) // BLOCK
-            while self.kv.free_blocks() < need and self._evict_lru_idle():
-                pass
-            if self.kv.free_blocks() < need and self.active:
-                break
-            self.queue.pop(0)
-            idle = np.nonzero(~self.busy)[0]
-            slot = int(idle[np.argmin(self.last_used[idle])])
-            self.kv.truncate(slot, 0)  # kv_remove(slot, reuse = 0): random prompts share nothing
-            self.held[slot] = 0
-            self.busy[slot] = True
-            self.clock += 1
-            self.last_used[slot] = self.clock
-            self.active[slot] = [0, prompt, prompt + out, self.step_no]
-            self.stats["admitted"] += 1
 
-    def plan(self):
-        """(slot, first position, token count) of this step's batch."""
-        dec, pre = [], []
-        for slot, (n_past, prompt, total, _) in self.active.items():
-            if n_past >= prompt:
-                dec.append((slot, n_past, 1))
-            else:
-                pre.append((slot, n_past, min(self.CHUNK, prompt - n_past)))
-        return dec, pre
-
-    @staticmethod
-    def _new_blocks(items):
-        n = 0
-        for _, p0, cnt in items:
-            n += (p0 + cnt + BLOCK - 1) // BLOCK - (p0 + BLOCK - 1) // BLOCK
-        return n
-
-    def ensure_room(self):
-        while True:
-            dec, pre = self.plan()
-            need = self._new_blocks(dec) + self._new_blocks(pre)
-            if self.kv.free_blocks() >= need:
-                return dec, pre
-            if self._evict_lru_idle():
-                continue
-            youngest = max(self.active, key=lambda s: self.active[s][3])
-            self.kv.truncate(youngest, 0)  # preempted: finishes with Length, nothing kept
-            self.busy[youngest] = False
-            self.held[youngest] = 0
-            del self.active[youngest]
-            self.stats["preempted"] += 1
-
-    def step(self, out):
-        """One scheduler step; returns the number of decode tokens."""
-        self.step_no += 1
-        self.arrivals()
-        self.admit()
-        dec, pre = self.ensure_room()
-        kv = self.kv
-        if pre:
-            seqs = np.concatenate([np.full(c, s) for s, _, c in pre])
-            pos = np.concatenate([np.arange(p0, p0 + c) for _, p0, c in pre])
-            b, sl = kv.append_batch(seqs, pos)
-            n = seqs.size
-            off = int(self.rng.integers(0, self.kv_src.shape[0] - n + 1))
-            kv.write(0, b, sl, self.kv_src[off:off + n], self.kv_src[off:off + n])
-            self.stats["prefill"] += n
-        nd = len(dec)
-        if dec:
-            seqs = np.array([s for s, _, _ in dec], np.uint32)
-            pos = np.array([p for _, p, _ in dec], np.uint32)
-            b, sl = kv.append_batch(seqs, pos)
-            off = int(self.rng.integers(0, self.kv_src.shape[0] - nd + 1))
-            kv.write_attend(0, b, sl, self.kv_src[off:off + nd], self.kv_src[off:off + nd], self.q_src[:nd], seqs,
-                            pos, out=out[:nd])
-            self.stats["decode"] += nd
-        for s, p0, c in dec + pre:
-            st = self.active[s]
-            st[0] = p0 + c
-            if st[0] >= st[2]:
-                self._retire(s, st[0])
-                self.stats["finished"] += 1
-        self.stats["moved"] += kv.compact()
-        return nd
+PREFILL_CHUNK = 256
 
 
 def run_c5(args, rank, world, local):
     """continuous-batching churn, Llama-3-8B attention shape, one
     layer; arrivals Poisson(32/N) per rank and step (sequence-sharded), prompts
     log-uniform in [64, 8192], outputs U[16, 512], block pool at 60 % of the
-    peak demand of an uncapped dry run."""
+    peak demand of an uncapped dry run.  The scheduler policy runs in the
+    native driver (lt_sched): admission, LRU eviction, preemption, chunked
+    prefill, retire, compaction every step."""
     import datetime
 
     import torch
     import torch.distributed as dist
 
     from langtrain_studio_b200 import kv as kv_mod
+    from langtrain_studio_b200.sched import Scheduler
 
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
@@ -768,15 +644,14 @@ def run_c5(args, rank, world, local):
     seed = shard_seed(rank)
     hq, hkv, d = 32, 8, 128
     # uncapped dry run of the same arrival/length process: peak blocks held by running sequences
-    rng = np.random.default_rng(seed)
+    dry = Arrivals(lam, seed + 101)
     live, peak = [], 0
     for _ in range(args.warmup + args.steps):
-        for _ in range(rng.poisson(lam)):
-            prompt = int(np.exp(rng.uniform(np.log(64), np.log(8192))))
-            live.append([prompt, prompt + int(rng.integers(16, 513)), 0])
+        for prompt, out_len in dry.step():
+            live.append([prompt, prompt + out_len, 0])
         nxt = []
         for r in live:  # [prompt, total, n_past]
-            r[2] = min(r[2] + ChurnDriver.CHUNK, r[0]) if r[2] < r[0] else r[2] + 1
+            r[2] = min(r[2] + PREFILL_CHUNK, r[0]) if r[2] < r[0] else r[2] + 1
             if r[2] < r[1]:
                 nxt.append(r)
         live = nxt
@@ -791,20 +666,27 @@ def run_c5(args, rank, world, local):
     kv_src = torch.randn((1 << 17, hkv * d), generator=g, device=dev, dtype=torch.float16)
     q_src = torch.randn((n_slots, hq * d), generator=g, device=dev, dtype=torch.float16)
     out = torch.empty((n_slots, hq * d), device=dev, dtype=torch.float16)
-    drv = ChurnDriver(kv, n_slots, lam, seed, kv_src, q_src)
+    sched = Scheduler(kv, n_slots)
+    arrivals = Arrivals(lam, seed + 101)
+
+    def step():
+        for prompt, out_len in arrivals.step():
+            sched.submit(prompt, out_len)
+        sched.step(kv_src, q_src, out)
+
     for _ in range(args.warmup):
-        drv.step(out)
+        step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    s0 = dict(drv.stats)
+    s0 = sched.stats
     kv.profile(True)
     l0 = kv.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
     e0.record()
     for _ in range(args.steps):
-        drv.step(out)
+        step()
     e1.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
@@ -813,9 +695,10 @@ def run_c5(args, rank, world, local):
     ms = reduce_max(e0.elapsed_time(e1), dev, world)
     attn_ms, attn_n = kv.profile_read()
     kv.check()
-    delta = {k: drv.stats[k] - s0[k] for k in drv.stats}
-    tot = torch.tensor([float(delta["decode"]), float(delta["prefill"]), float(delta["moved"])], device=dev,
-                       dtype=torch.float64)
+    s1 = sched.stats
+    delta = {k: s1[k] - s0[k] for k in s1}
+    tot = torch.tensor([float(delta["decode_tokens"]), float(delta["prefill_tokens"]), float(delta["moved_blocks"])],
+                       device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(tot)
     res = None
@@ -830,13 +713,15 @@ def run_c5(args, rank, world, local):
         res.update({
             "decode_tokens_per_s": tot[0].item() / (ms * 1e-3),
             "prefill_tokens_per_s": tot[1].item() / (ms * 1e-3),
-            "rank0": {"steps": args.steps, "decode": delta["decode"], "prefill": delta["prefill"],
+            "rank0": {"steps": args.steps, "decode": delta["decode_tokens"], "prefill": delta["prefill_tokens"],
                       "admitted": delta["admitted"], "finished": delta["finished"], "evicted": delta["evicted"],
-                      "preempted": delta["preempted"], "moved_blocks": delta["moved"], "attn_ms_per_step":
-                      attn_ms / max(attn_n, 1), "host_wall_ms_per_step": wall * 1e3 / args.steps},
+                      "preempted": delta["preempted"], "moved_blocks": delta["moved_blocks"],
+                      "running_at_end": s1["running"], "queued_at_end": s1["queued"],
+                      "attn_ms_per_step": attn_ms / max(attn_n, 1), "host_wall_ms_per_step": wall * 1e3 / args.steps},
             "compaction_gb_moved_per_s": moved_bytes / (ms * 1e-3) / 1e9,
             "gpu_launches": kv.launch_count() - l0,
         })
+    sched.close()
     if world > 1:
         dist.barrier()
         kv.close()

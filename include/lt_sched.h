@@ -1,0 +1,77 @@
+/*
+ * lt_sched.h -- the KV-cache side of the reference's continuous-batching
+ * scheduler as a native driver over lt_kv.h.
+ *
+ * Restates the slot / prefix policy of engine/crates/engine/src/scheduler.rs
+ * (admit :252-275, ensure_kv_room :321-334, the step :356-451, retire :452-473) and
+ * engine/crates/engine/src/prefix.rs (LRU slot cache :58-125) in blocks:
+ *   - a request waits in a FIFO queue; it is admitted into the least
+ *     recently used idle slot once its prompt plus min(output,
+ *     decode_headroom) tokens fit, evicting idle slots' cached KV least
+ *     recently used first (kv_remove(slot, 0) = lt_kv_truncate(slot, 0));
+ *   - each step: one decode token for every sequence past its prompt, a
+ *     prompt chunk of at most prefill_chunk tokens for the others;
+ *   - before the step, enough blocks are freed for it: evict LRU idle slots,
+ *     then preempt the youngest running sequence (it ends with Length);
+ *   - a finished sequence keeps its KV in its now idle slot for prefix reuse;
+ *   - optionally lt_kv_compact after every step (no reference counterpart).
+ * Requests carry lengths only: the prompts are random ids, so no prefix is
+ * ever reused and the driver never calls kv_copy.
+ *
+ * The step's K/V rows and q rows are cut from caller-provided device arrays
+ * (synthetic inputs of the benchmark): prompt tokens are appended and their
+ * rows written (lt_kv_write), decode tokens run the fused append + attention
+ * (lt_kv_write_attend).  With cfg.data == 0 only the bookkeeping runs, on a
+ * host-only handle too.
+ *
+ * Threading: a driver and its cache belong to one thread.
+ */
+#ifndef LT_SCHED_H
+#define LT_SCHED_H
+
+#include <stdint.h>
+
+#include "lt_kv.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct lt_sched lt_sched;
+
+typedef struct lt_sched_config {
+    uint32_t n_slots;         /* parallel slots: sequence ids [0, n_slots) (Backend::n_seq_max) */
+    uint32_t decode_headroom; /* scheduler.rs DECODE_HEADROOM (256) */
+    uint32_t prefill_chunk;   /* EngineConfig::prefill_chunk (256) */
+    int32_t compact;          /* 1: lt_kv_compact after every step */
+    int32_t data;             /* 1: write K/V rows and attend; 0: bookkeeping only */
+} lt_sched_config;
+
+typedef struct lt_sched_stats {
+    uint64_t steps, admitted, finished, evicted, preempted;
+    uint64_t decode_tokens, prefill_tokens, moved_blocks;
+    uint32_t running, queued;
+} lt_sched_stats;
+
+lt_status lt_sched_create(lt_kv* kv, const lt_sched_config* cfg, lt_sched** out);
+void lt_sched_destroy(lt_sched* s);
+const char* lt_sched_last_error(const lt_sched* s);
+
+/* Queue a request of prompt_len prompt tokens and out_len output tokens. */
+lt_status lt_sched_submit(lt_sched* s, uint32_t prompt_len, uint32_t out_len);
+
+/* One scheduler step (see the header comment).  kv_src: device f16
+ * [src_rows][n_kv_heads*head_dim] rows for the appended tokens (a contiguous
+ * window of them per call); q_src: device f16 [n_slots][n_heads*head_dim],
+ * row i is the i-th decode token's q; out: device f16 [n_slots][n_heads*
+ * head_dim].  Unused (may be NULL) with cfg.data == 0.  *n_decode receives
+ * the step's decode tokens (may be NULL). */
+lt_status lt_sched_step(lt_sched* s, const void* kv_src, uint32_t src_rows, const void* q_src, void* out,
+                        uint32_t* n_decode, void* stream);
+
+lt_status lt_sched_get_stats(const lt_sched* s, lt_sched_stats* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -29,6 +29,8 @@ EXPORTS = (
     "lt_llama_create", "lt_llama_destroy", "lt_llama_last_error", "lt_llama_set_tensor", "lt_llama_forward",
     "lt_llama_step_greedy", "lt_llama_launch_count", "lt_llama_profile", "lt_llama_profile_read", "lt_q8_quantize", "lt_q8_matmul", "lt_rms_norm_q8",
     "lt_silu_q8", "lt_argmax_f32", "lt_q8_project", "lt_q8_check",
+    "lt_sched_create", "lt_sched_destroy", "lt_sched_last_error", "lt_sched_submit", "lt_sched_step",
+    "lt_sched_get_stats",
 )
 
 
@@ -62,6 +64,22 @@ class lt_llama_config(C.Structure):
         ("max_batch", C.c_uint32),
         ("device", C.c_int32),
     ]
+
+
+class lt_sched_config(C.Structure):
+    _fields_ = [
+        ("n_slots", C.c_uint32),
+        ("decode_headroom", C.c_uint32),
+        ("prefill_chunk", C.c_uint32),
+        ("compact", C.c_int32),
+        ("data", C.c_int32),
+    ]
+
+
+class lt_sched_stats(C.Structure):
+    _fields_ = [(name, C.c_uint64) for name in ("steps", "admitted", "finished", "evicted", "preempted",
+                                                 "decode_tokens", "prefill_tokens", "moved_blocks")] + \
+               [("running", C.c_uint32), ("queued", C.c_uint32)]
 
 
 _lock = threading.Lock()
@@ -124,6 +142,12 @@ def _declare(L):
         "lt_argmax_f32": (st, [p, u32, u32, p, p]),
         "lt_q8_project": (st, [C.c_int, p, p, u32, u32, p, p, p, C.c_float, u32, p, u32, C.c_int, C.c_int, p]),
         "lt_q8_check": (st, [p]),
+        "lt_sched_create": (st, [p, C.POINTER(lt_sched_config), C.POINTER(p)]),
+        "lt_sched_destroy": (None, [p]),
+        "lt_sched_last_error": (C.c_char_p, [p]),
+        "lt_sched_submit": (st, [p, u32, u32]),
+        "lt_sched_step": (st, [p, p, u32, p, p, C.POINTER(u32), p]),
+        "lt_sched_get_stats": (st, [p, C.POINTER(lt_sched_stats)]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
