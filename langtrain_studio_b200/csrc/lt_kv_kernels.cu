@@ -784,7 +784,7 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
 constexpr int kPreRows = 128;        // tcgen05 M: query rows of a CTA
 constexpr int kPreStepBlocks = 4;    // blocks (16 positions each) per step: N = 64
 constexpr int kPreStages = 3;        // K/V ring: copies run kPreStages - 2 steps ahead of their use
-constexpr int kPreThreads = 160;     // warps 0..3: softmax of rows 32w..32w+31; warp 4: copies + MMAs
+constexpr int kPreThreads = 192;     // warps 0..3: softmax of rows 32w..32w+31; warp 4: MMA issue; warp 5: copies
 constexpr int kPreTmemCols = 256;    // S buffers at columns 0 and 64, O at 128
 constexpr float kRescaleLog2 = 8.f;  // a row's maximum moves only when it grows by more than this
 
@@ -861,7 +861,7 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
     const int32_t* trow = p.tables + (size_t)item.root_seq * p.max_blocks + item.blk0;
     const size_t tile_elems = 2 * kBlock * D;
     auto step_blocks = [&](int j) { return min(kPreStepBlocks, nbk - j * kPreStepBlocks); };
-    int issued = 0;  // warp 4 lane 0: steps whose copies were issued
+    int issued = 0;  // warp 5 lane 0: steps whose copies were issued
     // The step's block ids, loaded together (independent loads) a step ahead
     // of the copies that use them.
     auto load_ids = [&](int j, int (&ids)[kPreStepBlocks]) {
@@ -888,7 +888,7 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
         ++issued;
     };
     int nxt_ids[kPreStepBlocks] = {};  // ids of the next refill (step kPreStages, ...)
-    if (tid == kPreRows) {
+    if (tid == kPreRows + 32) {
         for (int j = 0; j < min(kPreStages, n_steps); ++j) {
             int ids[kPreStepBlocks] = {};
             load_ids(j, ids);
@@ -946,19 +946,39 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
 
     bool ok = true;
     int j_fail = 0;
-    if (warp == 4) {
-        // ===== producer / MMA issuer (one lane) =====
+    if (warp == 5) {
+        // ===== copy producer (one lane): refill a stage once its MMAs have read it =====
         if (lane == 0) {
+            for (int j = 0; j + kPreStages < n_steps && ok; ++j) {
+                ok = mbar_wait_bounded(kv_empty + 8u * (j % kPreStages), (j / kPreStages) & 1);
+                if (!ok) { j_fail = j + kPreStages; break; }
+                issue_step(j + kPreStages, nxt_ids);
+                load_ids(j + kPreStages + 1, nxt_ids);
+            }
+            if (!ok) {
+                // bounded drain of the copies still in flight, then report
+                for (int jj = 0; jj < issued; ++jj)
+                    mbar_wait_bounded(kv_full + 8u * (jj % kPreStages), (jj / kPreStages) & 1);
+                atomicExch(p.err, 1);
+            }
+        }
+    } else if (warp == 4) {
+        // ===== MMA issuer (one lane) =====
+        if (lane == 0) {
+            // descriptors: the start-address field is the low 14 bits (address >> 4),
+            // so offsets inside shared memory are added to a base descriptor
+            const uint64_t dq_hi = sw128_desc(base + L.q_hi, 16, 1024), dq_lo = sw128_desc(base + L.q_lo, 16, 1024);
+            const uint64_t dp0 = sw128_desc(base + L.p0, 16, 1024);
             const uint32_t idesc_pv = f16_idesc(D, true);
             auto issue_pv = [&](int j) {  // O += P(j) V(j), then free its stage and P buffer
                 const int st = j % kPreStages, bb = j & 1;
                 const int nblk = step_blocks(j);
-                const uint32_t sv = base + L.stage0 + st * STAGE + KPART;
-                const uint32_t pv = base + L.p0 + bb * PBUF;
+                const uint64_t dv = sw128_desc(base + L.stage0 + st * STAGE + KPART, HALF_ROWS_BYTES, 1024);
+                const uint64_t dp = dp0 + ((uint64_t)(bb * PBUF) >> 4);
                 for (int ks = 0; ks < nblk; ++ks) {
-                    const uint64_t bdesc = sw128_desc(sv + ks * (kBlock * 128), HALF_ROWS_BYTES, 1024);
-                    umma_f16(tmem_o, sw128_desc(pv + ks * 32, 16, 1024), bdesc, idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
-                    umma_f16(tmem_o, sw128_desc(pv + kPreRows * 128 + ks * 32, 16, 1024), bdesc, idesc_pv, 1u);
+                    const uint64_t bdesc = dv + ((uint64_t)(ks * (kBlock * 128)) >> 4);
+                    umma_f16(tmem_o, dp + (uint64_t)(ks * 2), bdesc, idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
+                    umma_f16(tmem_o, dp + ((uint64_t)(kPreRows * 128 + ks * 32) >> 4), bdesc, idesc_pv, 1u);
                 }
                 umma_commit(kv_empty + 8u * st);
                 umma_commit(p_free + 8u * bb);
@@ -971,16 +991,14 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
                 if (!mbar_wait_bounded(kv_full + 8u * st, (j / kPreStages) & 1)) return false;
                 if (j >= 2 && !mbar_wait_bounded(s_free + 8u * bb, ((j - 2) >> 1) & 1)) return false;
                 tc_fence_after();
-                const uint32_t sk = base + L.stage0 + st * STAGE;
+                const uint64_t dk = sw128_desc(base + L.stage0 + st * STAGE, 16, 1024);
                 const uint32_t idesc_s = f16_idesc(step_blocks(j) * kBlock, false);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t qoff = (uint32_t)(kk >> 2) * (kPreRows * 128) + (kk & 3) * 32;
-                    const uint32_t koff = (uint32_t)(kk >> 2) * HALF_ROWS_BYTES + (kk & 3) * 32;
-                    const uint64_t bdesc = sw128_desc(sk + koff, 16, 1024);
-                    umma_f16(tmem + 64 * bb, sw128_desc(base + L.q_hi + qoff, 16, 1024), bdesc, idesc_s,
-                             kk > 0 ? 1u : 0u);
-                    umma_f16(tmem + 64 * bb, sw128_desc(base + L.q_lo + qoff, 16, 1024), bdesc, idesc_s, 1u);
+                    const uint64_t qoff = ((uint64_t)(kk >> 2) * (kPreRows * 128) + (kk & 3) * 32) >> 4;
+                    const uint64_t koff = ((uint64_t)(kk >> 2) * HALF_ROWS_BYTES + (kk & 3) * 32) >> 4;
+                    umma_f16(tmem + 64 * bb, dq_hi + qoff, dk + koff, idesc_s, kk > 0 ? 1u : 0u);
+                    umma_f16(tmem + 64 * bb, dq_lo + qoff, dk + koff, idesc_s, 1u);
                 }
                 umma_commit(s_full + 8u * bb);
                 return true;
@@ -994,21 +1012,8 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
                 tc_fence_after();
                 issue_pv(j);
                 if (j + 2 < n_steps && !(ok = issue_s(j + 2))) { j_fail = j; break; }
-                if (j + kPreStages < n_steps) {
-                    // refill step j's stage once its MMAs have read it (the
-                    // ring keeps the copies kPreStages - 2 steps ahead)
-                    ok = mbar_wait_bounded(kv_empty + 8u * (j % kPreStages), (j / kPreStages) & 1);
-                    if (!ok) { j_fail = j; break; }
-                    issue_step(j + kPreStages, nxt_ids);
-                    load_ids(j + kPreStages + 1, nxt_ids);
-                }
             }
-            if (!ok) {
-                // bounded drain of the copies still in flight, then report
-                for (int jj = j_fail; jj < issued; ++jj)
-                    mbar_wait_bounded(kv_full + 8u * (jj % kPreStages), (jj / kPreStages) & 1);
-                atomicExch(p.err, 1);
-            }
+            if (!ok) atomicExch(p.err, 1);
         }
     } else {
         // ===== softmax warps: thread r owns query row r (TMEM lane r) =====
@@ -1052,6 +1057,12 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
                 rescale = m_use != -INFINITY;
                 m_use = mx;
             }
+            // P buffer bb is free once PV(j-2) has read it (waited before the
+            // rescale, so pv_done is at most one phase behind PV(j-1))
+            if (j >= 2) {
+                w_ok = mbar_wait_bounded(p_free + 8u * bb, ((j - 2) >> 1) & 1);
+                if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
+            }
             if (__any_sync(0xffffffffu, rescale)) {
                 // this warp's O rows are scaled once PV(j-1) has finished
                 w_ok = mbar_wait_bounded(pv_done, (j - 1) & 1);
@@ -1065,11 +1076,6 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
                     for (int i = 0; i < 32; ++i) o[i] *= alpha;
                     tmem_st32(tmem_o + lane_off + c0, o);
                 }
-            }
-            // P buffer bb is free once PV(j-2) has read it
-            if (j >= 2) {
-                w_ok = mbar_wait_bounded(p_free + 8u * bb, ((j - 2) >> 1) & 1);
-                if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
             }
             const uint32_t pb = L.p0 + bb * PBUF;
             float lsum = 0.f;
@@ -1143,8 +1149,18 @@ __global__ void __launch_bounds__(256) apply_plan_kernel(uint16_t* __restrict__ 
         const int2 cp = copies[ci];
         const uint4* src = reinterpret_cast<const uint4*>(pool + (size_t)l * layer_stride + (size_t)cp.x * block_elems);
         uint4* dst = reinterpret_cast<uint4*>(pool + (size_t)l * layer_stride + (size_t)cp.y * block_elems);
+        // 8 independent 16-byte loads in flight per thread before their stores
         const size_t n16 = block_elems * 2 / 16;
-        for (size_t i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = __ldg(src + i);
+        constexpr int U = 8;
+        size_t i = threadIdx.x;
+        for (; i + (U - 1) * blockDim.x < n16; i += U * blockDim.x) {
+            uint4 t[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) t[u] = __ldg(src + i + u * blockDim.x);
+#pragma unroll
+            for (int u = 0; u < U; ++u) dst[i + u * blockDim.x] = t[u];
+        }
+        for (; i < n16; i += blockDim.x) dst[i] = __ldg(src + i);
     } else {
         const int i = (blockIdx.x - n_copy_ctas) * blockDim.x + threadIdx.x;
         if (i < n_tw) {
