@@ -86,16 +86,22 @@ def workload(seed: int):
     return lens
 
 
-def step_bytes(lens_now: np.ndarray) -> dict:
+def kv_row_bytes(kv_dim: int, kv_format: str = "f16") -> float:
+    """Cached bytes of one K (or V) row: f16 values, or Q8_0 int8 values plus
+    one f16 scale per 32."""
+    return kv_dim * 2 if kv_format == "f16" else kv_dim * 34 / 32
+
+
+def step_bytes(lens_now: np.ndarray, kv_format: str = "f16") -> dict:
     """Algorithmic bytes of one step (one layer) at current lengths `lens_now`
     (after the step's append): K and V of every cached position once, q, out,
-    block-table entries, and the appended rows (f16 in, f16 out)."""
-    kv_row = N_KV_HEADS * HEAD_DIM * 2  # bytes of one K (or V) row
-    attn = int(lens_now.sum()) * kv_row * 2
+    block-table entries, and the appended rows (f16 in, cached format out)."""
+    kv_row = kv_row_bytes(N_KV_HEADS * HEAD_DIM, kv_format)  # bytes of one cached K (or V) row
+    attn = int(int(lens_now.sum()) * kv_row * 2)
     q = BATCH * N_HEADS * HEAD_DIM * 2
     out = BATCH * N_HEADS * HEAD_DIM * 2
     tables = int(((lens_now + BLOCK - 1) // BLOCK).sum()) * 4
-    append = BATCH * 2 * kv_row * 2  # read f16 input + write f16 cell, K and V
+    append = int(BATCH * 2 * (N_KV_HEADS * HEAD_DIM * 2 + kv_row))  # read f16 input + write the cell, K and V
     return {"attn": attn, "q": q, "out": out, "tables": tables, "append": append,
             "total": attn + q + out + tables + append}
 
@@ -109,10 +115,10 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic():
-    """DRAM bytes per launch of the attention kernel from the committed ncu
-    summary (profiles/paged_attn_c2.md, line 'traffic_bytes_per_launch: N')."""
-    p = ROOT / "profiles" / "paged_attn_c2.md"
+def ncu_traffic(name: str = "paged_attn_c2.md"):
+    """DRAM bytes per launch of the attention kernel from a committed ncu
+    summary (profiles/<name>, line 'traffic_bytes_per_launch: N')."""
+    p = ROOT / "profiles" / name
     try:
         for line in p.read_text().splitlines():
             if line.strip().startswith("traffic_bytes_per_launch:"):
@@ -177,14 +183,14 @@ class Clocks:
 # our arm
 
 
-def build_cache(kv_mod, torch, device: int, lens: np.ndarray, seed: int):
+def build_cache(kv_mod, torch, device: int, lens: np.ndarray, seed: int, kv_format: str = "f16"):
     """Fill a cache with the workload: every sequence's context appended in
     16-token pieces in a random interleaving (seed+1), so physical block ids
     are scattered across sequences, then K/V written as f16 N(0,1)."""
     headroom = CYCLE + 1
     n_blocks = int(((lens + headroom + BLOCK - 1) // BLOCK).sum()) + BATCH
     kv = kv_mod.KvCache(1, N_KV_HEADS, HEAD_DIM, n_blocks * BLOCK, n_heads=N_HEADS, max_seqs=BATCH,
-                        max_batch=8192, device=device)
+                        max_batch=8192, device=device, kv_format=kv_format)
     seqs, pos = fill_plan(lens, seed)
     gen = torch.Generator(device=f"cuda:{device}")
     gen.manual_seed(seed)
@@ -240,7 +246,7 @@ def run_ours(args, rank, world, local):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     seed = shard_seed(rank)
     lens = workload(seed)
-    kv = build_cache(kv_mod, torch, local, lens, seed)
+    kv = build_cache(kv_mod, torch, local, lens, seed, args.kv_format)
     g = torch.Generator(device=dev)
     g.manual_seed(seed + 7)
     # q, k and v of a step live in one buffer, so the end-to-end path moves
@@ -281,7 +287,7 @@ def run_ours(args, rank, world, local):
     e0.record()
     for _ in range(args.steps):
         lens_now = st.step()
-        b = step_bytes(lens_now)
+        b = step_bytes(lens_now, args.kv_format)
         total_bytes += b["total"]
         attn_bytes += b["total"]
     e1.record()
@@ -325,6 +331,7 @@ def run_ours(args, rank, world, local):
 
     result = None
     if rank == 0:
+        q8 = args.kv_format == "q8_0"
         peak, peak_kind = measured_peak()
         avg_attn_ms = attn_ms / max(attn_n, 1)
         per_launch_bytes = attn_bytes / max(args.steps, 1)
@@ -347,16 +354,21 @@ def run_ours(args, rank, world, local):
                 "workload": "configs[1]: isolated paged decode microbench, Llama-3-8B attention shape, one layer",
                 "batch_per_gpu": BATCH, "ctx": f"U[{CTX_LO},{CTX_HI}]", "n_heads": N_HEADS,
                 "n_kv_heads": N_KV_HEADS, "head_dim": HEAD_DIM, "block_tokens": BLOCK,
-                "step": "append 1 token/seq + fused K/V write + decode attention (f32 softmax/accumulate)",
+                "kv_format": args.kv_format,
+                "step": "append 1 token/seq + fused K/V write + decode attention (f32 softmax/accumulate)"
+                        + ("; K/V cached as Q8_0 (int8 + f16 scale per 32 values)" if q8 else ""),
                 "kv_bytes_per_step": int(attn_bytes / max(args.steps, 1)),
-                "l2": "inputs larger than L2: ~0.6 GB of K/V read per step vs 126 MB L2",
+                "l2": "inputs larger than L2: ~%.1f GB of K/V read per step vs 126 MB L2"
+                      % (attn_bytes / max(args.steps, 1) / 1e9),
                 "parallelism": f"seq-sharded x{world} (independent pools, no collective)",
             },
             "hbm_gbs": total_bytes / (ms_max * 1e-3) / 1e9 / 1.0 * world,
             "roofline": {
-                "bound": "hbm", "kernel": "paged_attn_kernel<128> (fused append + attention)",
+                "bound": "hbm",
+                "kernel": "paged_attn_kernel<128, %s> (fused append + attention)" % ("q8" if q8 else "f16"),
                 "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                "frac": achieved / peak, "traffic": ncu_traffic(),
+                "frac": achieved / peak,
+                "traffic": ncu_traffic("paged_attn_q8_c2.md" if q8 else "paged_attn_c2.md"),
                 "algorithmic_bytes_per_launch": int(per_launch_bytes), "avg_launch_ms": avg_attn_ms,
             },
             "e2e": {"value": tokens / (e2e_ms * 1e-3) if world == 1 else BATCH * e2e_steps * world / (e2e_ms * 1e-3),
@@ -520,7 +532,8 @@ def run_c4(args, rank, world, local, mode):
         n_seq, my_hkv, my_hq = B, hkv // world, hq // world
     kvd = my_hkv * d
     n_blocks = n_seq * ((L + CYCLE + 1 + BLOCK - 1) // BLOCK) + 8
-    kv = kv_mod.KvCache(1, my_hkv, d, n_blocks * BLOCK, n_heads=my_hq, max_seqs=n_seq, max_batch=8192, device=local)
+    kv = kv_mod.KvCache(1, my_hkv, d, n_blocks * BLOCK, n_heads=my_hq, max_seqs=n_seq, max_batch=8192, device=local,
+                        kv_format=args.kv_format)
     g = torch.Generator(device=dev)
     g.manual_seed(shard_seed(rank))
     chunk = 8192
@@ -567,7 +580,8 @@ def run_c4(args, rank, world, local, mode):
     e0.record()
     for _ in range(args.steps):
         lens_now = step()
-        byts += int(lens_now.sum()) * kvd * 2 * 2 + n_seq * (my_hq * d * 2 * 2 + 2 * kvd * 2 * 2)
+        row = kv_row_bytes(kvd, args.kv_format)
+        byts += int(int(lens_now.sum()) * row * 2 + n_seq * (my_hq * d * 2 * 2 + 2 * (kvd * 2 + row)))
     e1.record()
     barrier()
     ms = reduce_max(e0.elapsed_time(e1), dev, world)
@@ -580,7 +594,7 @@ def run_c4(args, rank, world, local, mode):
         res = _json_common(args, world, B * args.steps / (ms * 1e-3), "tokens/s", ms / args.steps, {
             "workload": f"configs[3]: long-context decode, Llama-3-70B attention shape, 16 seqs x 32768 tokens, "
                         f"{mode}-sharded x{world}, one layer",
-            "n_heads": hq, "n_kv_heads": hkv, "head_dim": d, "block_tokens": BLOCK,
+            "n_heads": hq, "n_kv_heads": hkv, "head_dim": d, "block_tokens": BLOCK, "kv_format": args.kv_format,
             "per_rank": {"seqs": n_seq, "kv_heads": my_hkv, "q_heads": my_hq},
             "collective": "lt_kv_gather_heads: NCCL all-gather of [seqs, q_heads*D] f16 per step + permute"
             if mode == "head" and world > 1 else "none"})
@@ -905,9 +919,9 @@ def cpu_run_c1(budget_s: float, threads: int, seed: int = 0):
     return C1_SEQS * steps / dt, steps, dt
 
 
-def cpu_fill(ok_mod, lens, seed):
+def cpu_fill(ok_mod, lens, seed, kv_format="f16"):
     n_blocks = int(((lens + CYCLE + 1 + BLOCK - 1) // BLOCK).sum()) + BATCH
-    ok = ok_mod.OracleKv(1, N_KV_HEADS * HEAD_DIM, n_blocks * BLOCK, max_seqs=BATCH)
+    ok = ok_mod.OracleKv(1, N_KV_HEADS * HEAD_DIM, n_blocks * BLOCK, max_seqs=BATCH, kv_format=kv_format)
     seqs, pos = fill_plan(lens, seed)
     drng = np.random.default_rng(seed)
     chunk = 16384
@@ -921,13 +935,13 @@ def cpu_fill(ok_mod, lens, seed):
     return ok
 
 
-def cpu_run(lens, seed, budget_s, max_steps, threads):
+def cpu_run(lens, seed, budget_s, max_steps, threads, kv_format="f16"):
     """Time the restated reference step (append + write + attention over every
     sequence, model.rs:380-476) on `threads` host threads.  Steps run until
     `budget_s` seconds or `max_steps`; returns (tokens/s, steps, seconds)."""
     from oracle import oracle as ok_mod
 
-    ok = cpu_fill(ok_mod, lens, seed)
+    ok = cpu_fill(ok_mod, lens, seed, kv_format)
     rng = np.random.default_rng(seed + 9)
     kin = rng.standard_normal((BATCH, N_KV_HEADS * HEAD_DIM), np.float32)
     vin = rng.standard_normal((BATCH, N_KV_HEADS * HEAD_DIM), np.float32)
@@ -1018,6 +1032,8 @@ def main():
                     help="c2: configs[1] (default, the headline); c1: configs[0]; c3: configs[2]; "
                          "c4-*: configs[3]; c5: configs[4]")
     ap.add_argument("--c5-rate", type=float, default=32.0, help="c5: mean arrivals per step over the whole job")
+    ap.add_argument("--kv-format", choices=["f16", "q8_0"], default="f16",
+                    help="c2 / c4-*: cached K/V format (f16: the reference's; q8_0: int8 + f16 scale per 32)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="CPU-baseline sample budget in seconds (rank 0, N=1); 0 skips it")
     args = ap.parse_args()
@@ -1061,11 +1077,12 @@ def main():
         if world == 1 and args.cpu_seconds > 0:
             threads = os.cpu_count() or 1
             value, steps, dt = cpu_run(workload(1234), 1234, budget_s=args.cpu_seconds, max_steps=10 ** 6,
-                                       threads=threads)
+                                       threads=threads, kv_format=args.kv_format)
             res["cpu_baseline"] = {
                 "value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                "sample": f"{steps} full steps of the same workload (64 seqs, one layer) in {dt:.1f} s on "
-                          f"{threads} threads of {cpu_desc()}; restated reference (oracle/lt_oracle.c)"}
+                "sample": f"{steps} full steps of the same workload (64 seqs, one layer, {args.kv_format} cache) "
+                          f"in {dt:.1f} s on {threads} threads of {cpu_desc()}; restated reference "
+                          f"(oracle/lt_oracle.c)"}
         else:
             res["cpu_baseline"] = None
         print(json.dumps(res), flush=True)

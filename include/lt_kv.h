@@ -61,6 +61,24 @@ typedef enum lt_dtype {
     LT_F16 = 1
 } lt_dtype;
 
+/* Storage format of the cached K/V rows (lt_kv_config.kv_format).
+ *   LT_KV_F16   the reference's cache (kv.rs:20-21): f16 per value.
+ *   LT_KV_Q8_0  each row cut into 32-value groups, stored as the Q8_0 block
+ *               of the reference's GGUF reader (quant.rs:254-275: one f16
+ *               scale d + 32 int8) -- the "q8_0" KV type the engine's
+ *               llama.cpp profile selects (engine/crates/engine/src/
+ *               hardware.rs:173) and its roadmap asks of the native cache
+ *               (engine/README.md:115).  A group x is quantised by the
+ *               engine's own int8 quantiser (quant.rs:785-795): d =
+ *               max|x| / 127, q = round(x / d) half away from zero, saturating
+ *               to int8 (q = 0 when d = 0); d is kept as f16 (round to
+ *               nearest even) and a value reads back as q * d.  0.53 of the
+ *               f16 bytes per cached token. */
+typedef enum lt_kv_format {
+    LT_KV_F16 = 0,
+    LT_KV_Q8_0 = 1
+} lt_kv_format;
+
 typedef struct lt_kv lt_kv;
 
 /* Creation parameters.  KvCache::new(n_layers, kv_dim, n_tokens) (kv.rs:35-48)
@@ -78,6 +96,7 @@ typedef struct lt_kv_config {
     uint32_t max_batch;         /* most tokens per append / write / attend call  */
     uint32_t max_blocks_per_seq;/* 0: n_blocks (never limits)                    */
     int32_t device;             /* CUDA ordinal; -1 = bookkeeping only (no GPU)  */
+    uint32_t kv_format;         /* lt_kv_format; 0 (f16) when zero-initialised    */
 } lt_kv_config;
 
 /* KvCache::new (kv.rs:35-48): zero-filled pool, free list (0..n_blocks).rev()
@@ -90,7 +109,8 @@ const char* lt_kv_last_error(const lt_kv* kv);
 
 /* KvCache::capacity (kv.rs:50-52): n_blocks * 16 tokens. Backend::n_ctx. */
 uint32_t lt_kv_capacity(const lt_kv* kv);
-/* KvCache::bytes (kv.rs:54-56): K + V pool bytes. */
+/* KvCache::bytes (kv.rs:54-56): K + V pool bytes (LT_KV_Q8_0: values and
+ * scales). */
 uint64_t lt_kv_bytes(const lt_kv* kv);
 /* KvCache::len (kv.rs:58-60): 0 for an unknown sequence. */
 uint32_t lt_kv_len(const lt_kv* kv, uint32_t seq);
@@ -111,9 +131,10 @@ lt_status lt_kv_append(lt_kv* kv, const uint32_t* seq_host, const uint32_t* pos_
 
 /* KvCache::write (kv.rs:123-131) for n cells of one layer, as the per-layer
  * loop of Model::forward does (model.rs:414-429).  k and v are device arrays
- * [n][n_kv_heads * head_dim] of `dtype`; f32 is rounded to f16 with
- * round-to-nearest-even (bit-identical to half::f16::from_f32), f16 is
- * stored unchanged. */
+ * [n][n_kv_heads * head_dim] of `dtype`.  LT_KV_F16: f32 is rounded to f16
+ * with round-to-nearest-even (bit-identical to half::f16::from_f32), f16 is
+ * stored unchanged.  LT_KV_Q8_0: each 32-value group of the given values
+ * (f16 widened exactly) is quantised as lt_kv_format describes. */
 lt_status lt_kv_write(lt_kv* kv, uint32_t layer, const int32_t* block_host, const int32_t* slot_host,
                       uint32_t n, const void* k, const void* v, lt_dtype dtype, void* stream);
 
@@ -162,7 +183,8 @@ lt_status lt_kv_flush(lt_kv* kv, void* stream);
 
 /* KvCache::rows (kv.rs:135-150): gather rows [0, n) of seq in `layer` into
  * device arrays k_out / v_out [n][n_kv_heads * head_dim] (f16, reference
- * row layout). */
+ * row layout).  LT_KV_Q8_0: each value is q * d rounded to f16 (nearest
+ * even). */
 lt_status lt_kv_rows(lt_kv* kv, uint32_t layer, uint32_t seq, uint32_t n, void* k_out, void* v_out,
                      void* stream);
 
@@ -180,13 +202,26 @@ uint32_t lt_kv_refs(const lt_kv* kv, uint32_t* out_host, uint32_t cap);
 uint32_t lt_kv_free_list(const lt_kv* kv, int32_t* out_host, uint32_t cap);
 uint32_t lt_kv_n_blocks(const lt_kv* kv);
 
-/* Device pool layout, for tools that read it directly:
- * f16 [layer][block][kv_head][2 (K, V)][head_dim/64][16 slots][64]: each K
- * or V part is head_dim/64 sub-tiles of 16 rows x 128 bytes, and inside a
- * sub-tile the 16-byte chunk c of row `slot` is stored at chunk position
- * (c ^ (slot & 7)) -- the 128-byte-swizzled layout of the tensor-core operand
- * descriptors, bank-conflict free for ldmatrix once bulk-copied.  Returns the
- * device base address. */
+/* Device pool layout, for tools that read it directly.
+ * LT_KV_F16: f16 [layer][block][kv_head][2 (K, V)][head_dim/64][16 slots][64]:
+ * each K or V part is head_dim/64 sub-tiles of 16 rows x 128 bytes, and
+ * inside a sub-tile the 16-byte chunk c of row `slot` is stored at chunk
+ * position (c ^ (slot & 7)) -- the 128-byte-swizzled layout of the
+ * tensor-core operand descriptors, bank-conflict free for ldmatrix once
+ * bulk-copied.
+ * LT_KV_Q8_0: [layer][block][kv_head] tiles of 34*head_dim bytes, D =
+ * head_dim, with the order within 16 of a 16-byte run
+ * pos(i) = ((i & 7) >> 1) * 4 + ((i >> 3) << 1) + (i & 1):
+ *   [0, 16D)    K int8, row-major [16 slots][D]: the 16-byte run that holds
+ *               values 16k..16k+15 of slot s is run L = (s*D)/16 + k of the
+ *               part, stored at byte 128*(L/8) + 16*((L%8) ^ ((L/8) & 7)),
+ *               value 16k+i at byte pos(i) of the run;
+ *   [16D, 32D)  V int8, transposed: 16 bytes per column d, slot s at byte
+ *               16*d + pos(s);
+ *   [32D, 33D)  K scales, f16 [D/32 groups][16]: group c of slot s at
+ *               element 16*c + pos(s);
+ *   [33D, 34D)  V scales, the same.
+ * Returns the device base address. */
 void* lt_kv_device_pool(const lt_kv* kv);
 /* Device block tables: int32 [max_seqs][max_blocks_per_seq]. */
 const int32_t* lt_kv_device_tables(const lt_kv* kv, uint32_t* max_blocks_per_seq);
@@ -220,7 +255,8 @@ lt_status lt_kv_set_min_tiles_per_warp(lt_kv* kv, uint32_t tiles);
  * extra launch that stages each shared K/V tile once for the whole group;
  * the decode launch then covers only each token's own blocks and folds the
  * prefix result in (online-softmax merge, f32).  Default 8; 0 turns it off.
- * Calls of more than 1024 tokens (or max_batch) never use it. */
+ * Calls of more than 1024 tokens (or max_batch) never use it, nor does an
+ * LT_KV_Q8_0 cache (its tiles are not tensor-core f16 operands). */
 lt_status lt_kv_set_cascade(lt_kv* kv, uint32_t min_group_tokens);
 
 /* Prefix-pass launches issued by this handle since creation. */

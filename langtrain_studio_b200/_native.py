@@ -15,6 +15,7 @@ LT_OK, LT_E_FULL, LT_E_NONCONTIG, LT_E_ARG, LT_E_CUDA, LT_E_NCCL, LT_E_TIMEOUT, 
 LT_NOALLOC_SCRATCH_BYTES = 8 << 20
 LT_NOALLOC_MAX_TOKENS = 1024
 LT_F32, LT_F16 = 0, 1
+LT_KV_F16, LT_KV_Q8_0 = 0, 1
 BLOCK = 16
 
 # Every function include/lt_kv.h declares (tests check the export table).
@@ -45,6 +46,7 @@ class lt_kv_config(C.Structure):
         ("max_batch", C.c_uint32),
         ("max_blocks_per_seq", C.c_uint32),
         ("device", C.c_int32),
+        ("kv_format", C.c_uint32),
     ]
 
 

@@ -79,8 +79,9 @@ struct lt_kv {
     uint64_t cascade_launches = 0;
     int casc_splits = 1;
     uint32_t n_blocks = 0, kv_dim = 0, group = 0, max_blocks = 0;
-    size_t block_elems = 0;   // f16 elements of one block in one layer (all heads, K and V)
-    size_t layer_elems = 0;   // f16 elements of one layer of the pool
+    bool q8 = false;          // LT_KV_Q8_0 pool
+    size_t block_elems = 0;   // 16-bit units of one block in one layer (all heads, K and V)
+    size_t layer_elems = 0;   // 16-bit units of one layer of the pool
 
     // ---- reference bookkeeping (kv.rs:15-26) ----
     std::vector<std::vector<int32_t>> blocks;  // per sequence
@@ -476,7 +477,7 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     if (n == 0) return flush(kv, st);
     // Per-token descriptors; the kernel derives its stream-K partition from them.
     const int q_f32 = q_dtype == LT_F32;
-    const int max_warps = ltkv::attend_warps(kv->cfg.device, (int)kv->group, (int)kv->cfg.head_dim, q_f32);
+    const int max_warps = ltkv::attend_warps(kv->cfg.device, (int)kv->group, (int)kv->cfg.head_dim, q_f32, kv->q8);
     if (max_warps <= 0) return fail(kv, LT_E_CUDA, "could not size the attention launch on device %d", kv->cfg.device);
     kv->toks_tmp.resize(n);
     for (uint32_t i = 0; i < n; ++i) {
@@ -486,7 +487,8 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
         t.last_block = kv->blocks[seq[i]][pos[i] / kBlock];
         t.skip = 0;
     }
-    const int n_items = plan_cascade(kv, seq, pos, n);  // sets skip of the tokens it covers
+    // sets skip of the tokens it covers; Q8_0 tiles are not f16 tensor-core operands
+    const int n_items = kv->q8 ? 0 : plan_cascade(kv, seq, pos, n);
     long long tiles = 0;
     for (uint32_t i = 0; i < n; ++i) {
         ltkv::TokenDesc& t = kv->toks_tmp[i];
@@ -571,6 +573,7 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     p.pre_o = kv->d_pre_o;
     p.pre_ml = kv->d_pre_ml;
     p.pre_splits = n_items > 0 ? kv->casc_splits : 0;
+    p.q8 = kv->q8;
     p.pre_split_rows = (int64_t)kv->pre_cap * kv->cfg.n_heads;
     cudaEvent_t ev_end = nullptr;
     if (kv->profiling) {
@@ -644,6 +647,7 @@ lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
     if (c.n_heads % c.n_kv_heads != 0) return LT_E_ARG;
     if (c.head_dim != 64 && c.head_dim != 128) return LT_E_UNSUPPORTED;
     if (c.n_heads / c.n_kv_heads > (uint32_t)ltkv::kMaxGroup) return LT_E_UNSUPPORTED;
+    if (c.kv_format != LT_KV_F16 && c.kv_format != LT_KV_Q8_0) return LT_E_ARG;
     lt_kv* kv = new (std::nothrow) lt_kv();
     if (!kv) return LT_E_ARG;
     kv->cfg = c;
@@ -656,7 +660,10 @@ lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
         delete kv;
         return LT_E_ARG;
     }
-    kv->block_elems = (size_t)c.n_kv_heads * 2 * kBlock * c.head_dim;
+    // 16-bit units of one block (all heads, K and V): f16 tiles of 2*16*D
+    // values, or Q8_0 tiles of 34*D bytes.
+    kv->q8 = c.kv_format == LT_KV_Q8_0;
+    kv->block_elems = (size_t)c.n_kv_heads * (kv->q8 ? 17 : 2 * kBlock) * c.head_dim;
     kv->layer_elems = (size_t)kv->n_blocks * kv->block_elems;
     kv->blocks.resize(c.max_seqs);
     kv->lens.assign(c.max_seqs, 0);
@@ -680,8 +687,8 @@ lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
         if (!g.ok) ck(cudaErrorInvalidDevice, "cudaSetDevice");
         const size_t pool_bytes = (size_t)c.n_layers * kv->layer_elems * 2;
         // Partial slots: a warp's first piece may be part of a split sequence.
-        const int max_warps = std::max(ltkv::attend_warps(c.device, (int)kv->group, (int)c.head_dim, 1),
-                                       ltkv::attend_warps(c.device, (int)kv->group, (int)c.head_dim, 0));
+        const int max_warps = std::max(ltkv::attend_warps(c.device, (int)kv->group, (int)c.head_dim, 1, kv->q8),
+                                       ltkv::attend_warps(c.device, (int)kv->group, (int)c.head_dim, 0, kv->q8));
         if (max_warps <= 0) ck(cudaErrorInvalidDevice, "attend_warps");
         kv->ws_slots = (size_t)std::max(max_warps, 0);  // one partial slot per warp
         const size_t gd = (size_t)kv->group * c.head_dim;
@@ -774,7 +781,8 @@ lt_status lt_kv_write(lt_kv* kv, uint32_t layer, const int32_t* block, const int
     int s = -1;
     if ((rc = upload(kv, kv->cells_cache, kv->cells_tmp.data(), n * sizeof(int2), st, &d_cells, &s))) return rc;
     LT_CUDA(kv, ltkv::launch_write(kv->d_pool + (size_t)layer * kv->layer_elems, static_cast<const int2*>(d_cells),
-                                   (int)n, (int)kv->cfg.n_kv_heads, (int)kv->cfg.head_dim, k, v, dtype == LT_F32, st));
+                                   (int)n, (int)kv->cfg.n_kv_heads, (int)kv->cfg.head_dim, k, v, dtype == LT_F32, kv->q8,
+                                   st));
     kv->launches++;
     return mark_slot_use(kv, s, st);
 }
@@ -914,7 +922,7 @@ lt_status lt_kv_rows(lt_kv* kv, uint32_t layer, uint32_t seq, uint32_t n, void* 
     LT_CUDA(kv, ltkv::launch_rows(kv->d_pool + (size_t)layer * kv->layer_elems,
                                   kv->d_tables + (size_t)seq * kv->max_blocks, (int)n, (int)kv->cfg.n_kv_heads,
                                   (int)kv->cfg.head_dim, static_cast<uint16_t*>(k_out), static_cast<uint16_t*>(v_out),
-                                  st));
+                                  kv->q8, st));
     kv->launches++;
     return LT_OK;
 }

@@ -48,6 +48,7 @@ struct AttnParams {
     const float* pre_ml;         // [pre_splits][rows][2]: its (m, l); row = (token*n_kv_heads + h)*group + g
     int32_t pre_splits;          // partials per row (the prefix blocks split over that many CTAs)
     int64_t pre_split_rows;      // rows between split slabs
+    int32_t q8;                  // pool tiles are Q8_0 (lt_kv.h LT_KV_Q8_0); no prefix partials then
     TokenDesc inl[kInlineTokens];
 };
 
@@ -86,7 +87,7 @@ inline int prefix_tokens_per_cta(int group) { return 128 / group; }
 cudaError_t launch_prefix(const PrefixParams& p, int n_items, int head_dim, cudaStream_t s);
 
 // Warps of one attention launch on `device` (all resident at once), or 0.
-int attend_warps(int device, int group, int head_dim, int q_f32);
+int attend_warps(int device, int group, int head_dim, int q_f32, int q8);
 cudaError_t launch_attend(const AttnParams& p, int head_dim, cudaStream_t s);
 // Kernel launches made by launch_attend(p).
 int attend_launches(const AttnParams& p);
@@ -97,7 +98,7 @@ cudaError_t launch_gather_permute(const void* gathered, void* out, int nranks, u
                                   cudaStream_t s);
 
 cudaError_t launch_write(uint16_t* pool_layer, const int2* cells, int n, int n_kv_heads, int head_dim,
-                         const void* k, const void* v, int in_f32, cudaStream_t s);
+                         const void* k, const void* v, int in_f32, int q8, cudaStream_t s);
 
 // Block copies (copy-on-write and compaction moves) and table scatter.
 // copies: (src, dst) pairs; tw: (flat table index, value) pairs.
@@ -106,7 +107,7 @@ cudaError_t launch_apply_plan(uint16_t* pool, size_t layer_stride_elems, size_t 
                               cudaStream_t s);
 
 cudaError_t launch_rows(const uint16_t* pool_layer, const int32_t* table_row, int n, int n_kv_heads,
-                        int head_dim, uint16_t* k_out, uint16_t* v_out, cudaStream_t s);
+                        int head_dim, uint16_t* k_out, uint16_t* v_out, int q8, cudaStream_t s);
 
 }  // namespace ltkv
 

@@ -12,6 +12,13 @@
 // operand layouts): one (block, head) K+V tile is a contiguous 4*D*16-byte run
 // whose bulk-copied shared-memory image is bank-conflict free for ldmatrix
 // and, 64-wide sub-tile by sub-tile, a valid tcgen05 operand.
+//
+// Q8_0 pool (LT_KV_Q8_0): one 34*D-byte tile per (block, head) -- K int8
+// row-major with 128-byte-swizzled 16-byte runs, V int8 transposed (one
+// 16-byte run per column), then the f16 scales of K and of V, one per
+// (32-value group, slot).  Inside every 16-byte run the 16 entries sit in the
+// order of the mma.sync B-fragment (pos(i) below), so one ldmatrix of the
+// int8 bytes hands each lane exactly the four values of its fragment.
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -23,7 +30,9 @@ namespace ltkv {
 namespace {
 
 constexpr int kWarps = 4;                         // warps per attention CTA
-constexpr int kStages = 3;                        // bulk-copy stages per warp
+constexpr int kStages = 3;                        // bulk-copy stages per warp (f16 tiles)
+constexpr int kStagesQ8 = 5;                      // the same for Q8_0 tiles (about half the bytes;
+                                                  // 5 keeps two group-8 CTAs per SM)
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // bounded mbarrier wait: 2 s
 constexpr unsigned kFull = 0xffffffffu;
 
@@ -171,6 +180,102 @@ __device__ __forceinline__ int chunk_off(int c, int slot) {
     return (c >> 3) * (kBlock * 64) + slot * 64 + (((c & 7) ^ (slot & 7)) << 3);
 }
 
+// ---------------------------------------------------------- Q8_0 tile ----
+__host__ __device__ constexpr int q8_tile_bytes(int D) { return 34 * D; }
+
+// Position of entry i (0..15) inside a 16-byte run: the order
+// 0,1,8,9, 2,3,10,11, 4,5,12,13, 6,7,14,15, so bytes 4t..4t+3 of a run hold
+// entries 2t, 2t+1, 2t+8, 2t+9 -- one lane's part of an m16n8k16 B fragment.
+__device__ __forceinline__ int q8_pos(int i) { return ((i & 7) >> 1) * 4 + ((i >> 3) << 1) + (i & 1); }
+
+// Byte offset of the 16-byte run of K values 16k..16k+15 of slot s: run
+// L = s*D/16 + k of the row-major K part, 128-byte lines swizzled by line.
+template <int D>
+__device__ __forceinline__ int q8_krun(int s, int k) {
+    const int L = s * (D / 16) + k;
+    return ((L >> 3) << 7) + (((L & 7) ^ ((L >> 3) & 7)) << 4);
+}
+
+// Four int8 (one 32-bit word) -> two f16x2, exactly: each biased byte
+// b = x + 128 becomes the f16 1024 + b (exponent 10, b in the mantissa),
+// then 1152 is subtracted.
+__device__ __forceinline__ void i8x4_to_f16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+    uint32_t a = __byte_perm(u, 0x64646464u, 0x5140), b = __byte_perm(u, 0x64646464u, 0x7362);
+    const __half2 ha = __hsub2(*reinterpret_cast<__half2*>(&a), bias);
+    const __half2 hb = __hsub2(*reinterpret_cast<__half2*>(&b), bias);
+    lo = h2_bits(ha);
+    hi = h2_bits(hb);
+}
+
+// Load 8 consecutive input values (f32, or f16 widened exactly).
+__device__ __forceinline__ void load8_f32(const void* base, size_t idx, int in_f32, float (&x)[8]) {
+    if (in_f32) {
+        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(base) + idx);
+        const float4 a = __ldg(p), b = __ldg(p + 1);
+        x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+    } else {
+        const uint4 r = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + idx));
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+            x[2 * j] = f.x;
+            x[2 * j + 1] = f.y;
+        }
+    }
+}
+
+// One 32-value group held as 8 values by each of the lanes 4j..4j+3 (all 32
+// lanes call this): the engine's int8 quantiser (quant.rs:785-795) --
+// d = max|x| / 127 (NaN ignored), q = round(x / d) half away from zero via
+// the reciprocal id, saturating to int8, NaN -> 0.  Returns d; the lane's
+// eight values come back packed in w0 (values 0-3) and w1 (4-7).
+__device__ __forceinline__ float q8_quant8(const float (&x)[8], uint32_t& w0, uint32_t& w1) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
+    const float d = amax / 127.0f;
+    const float id = d > 0.f ? 1.0f / d : 0.f;
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float r = roundf(x[i] * id);
+        const int q = r != r ? 0 : r >= 127.f ? 127 : r <= -128.f ? -128 : (int)r;
+        w[i >> 2] |= (uint32_t)(q & 0xff) << (8 * (i & 3));
+    }
+    w0 = w[0];
+    w1 = w[1];
+    return d;
+}
+
+// Store the lane's eight quantised values (value unit c = values 8c..8c+7 of
+// the row) of slot `slot` into a Q8_0 tile (K part for kvsel 0, V part for
+// 1), plus the group scale from the group's first lane.  Lane c^1 holds the
+// other half of the same K run; p0/p1 are its w0/w1.
+template <int D>
+__device__ __forceinline__ void q8_store8(uint8_t* tile, int kvsel, int c, int slot, uint32_t w0, uint32_t w1,
+                                          uint32_t p0, uint32_t p1, float d) {
+    if (kvsel == 0) {
+        const bool odd = c & 1;
+        const uint32_t A0 = odd ? p0 : w0, A1 = odd ? p1 : w1, B0 = odd ? w0 : p0, B1 = odd ? w1 : p1;
+        const uint2 val = odd ? make_uint2(__byte_perm(A1, B1, 0x5410), __byte_perm(A1, B1, 0x7632))
+                              : make_uint2(__byte_perm(A0, B0, 0x5410), __byte_perm(A0, B0, 0x7632));
+        *reinterpret_cast<uint2*>(tile + q8_krun<D>(slot, c >> 1) + (odd ? 8 : 0)) = val;
+    } else {
+        const int sp = q8_pos(slot);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            tile[16 * D + (8 * c + i) * 16 + sp] = (uint8_t)(((i < 4 ? w0 : w1) >> (8 * (i & 3))) & 0xff);
+    }
+    if ((c & 3) == 0)
+        *reinterpret_cast<uint16_t*>(tile + (kvsel ? 33 : 32) * D + ((c >> 2) * 16 + q8_pos(slot)) * 2) =
+            __half_as_ushort(__float2half_rn(d));
+}
+
 // ------------------------------------------------------------------ K1 ----
 // One thread per 16-byte chunk of one (token, head, K|V) row.
 template <int D>
@@ -192,6 +297,34 @@ __global__ void __launch_bounds__(256) kv_write_kernel(uint16_t* __restrict__ po
     const uint4 val = load8_as_f16(kvsel ? v : k, src, in_f32);
     uint16_t* dst = pool_layer + (((size_t)cell.x * n_kv_heads + h) * 2 + kvsel) * (kBlock * D) + chunk_off(c, cell.y);
     *reinterpret_cast<uint4*>(dst) = val;
+}
+
+// Q8_0 pool: the same thread mapping (eight values a thread, c fastest), so
+// lanes 4j..4j+3 share a 32-value group and lanes c, c^1 a K run.  Every lane
+// of a warp takes part in the shuffles; lanes past the end only compute.
+template <int D>
+__global__ void __launch_bounds__(256) kv_write_q8_kernel(uint8_t* __restrict__ pool_layer,
+                                                          const int2* __restrict__ cells, int n, int n_kv_heads,
+                                                          const void* __restrict__ k, const void* __restrict__ v,
+                                                          int in_f32) {
+    constexpr int CH = D / 8;
+    const int gid = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool live = gid < n * n_kv_heads * 2 * CH;
+    const int c = gid % CH;
+    int r = gid / CH;
+    const int kvsel = r & 1;
+    r >>= 1;
+    const int h = r % n_kv_heads;
+    const int i = r / n_kv_heads;
+    float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (live) load8_f32(kvsel ? v : k, (size_t)i * n_kv_heads * D + (size_t)h * D + (size_t)c * 8, in_f32, x);
+    uint32_t w0, w1;
+    const float d = q8_quant8(x, w0, w1);
+    const uint32_t p0 = __shfl_xor_sync(kFull, w0, 1), p1 = __shfl_xor_sync(kFull, w1, 1);
+    if (!live) return;
+    const int2 cell = cells[i];
+    q8_store8<D>(pool_layer + ((size_t)cell.x * n_kv_heads + h) * q8_tile_bytes(D), kvsel, c, cell.y, w0, w1, p0, p1,
+                 d);
 }
 
 // ------------------------------------------------------------------ K2 ----
@@ -331,37 +464,138 @@ __device__ __forceinline__ void attend_tile(const uint8_t* tile, int valid, cons
     }
 }
 
+// The same step for a staged Q8_0 tile.  S: per 32-value group c, one
+// ldmatrix hands each lane its K bytes for two k-steps (slots 0-7 and 8-15),
+// converted to f16 exactly; the group's partial scores are scaled by the
+// slots' K scales in f32.  O += P V: per group c the P row is multiplied by
+// the slots' V scales (in f32, then split into f16 value + residual), so the
+// V bytes (again exact f16) go to the MMA unscaled.  Slots past `valid`
+// are masked out of S and contribute nothing to O, whatever their bytes.
+template <int D>
+__device__ __forceinline__ void attend_tile_q8(const uint8_t* tile, int valid, const uint32_t (&qa)[D / 16][4],
+                                               float (&o)[D / 8][4], float& m_run, float& l_run, float scale_log2,
+                                               int lane) {
+    constexpr int G32 = D / 32;
+    const int t = lane & 3;
+    const int mi = lane >> 3, r = lane & 7;
+    const uint32_t base = smem_u32(tile);
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int c = 0; c < G32; ++c) {
+        float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t w0, w1, w2, w3, b0, b1;
+        // matrices: (slots 0-7, run 2c), (8-15, 2c), (0-7, 2c+1), (8-15, 2c+1)
+        ldsm_x4(base + q8_krun<D>(((mi & 1) << 3) + r, 2 * c + (mi >> 1)), w0, w1, w2, w3);
+        i8x4_to_f16x2(w0, b0, b1);
+        mma16816(t0, qa[2 * c], b0, b1);
+        i8x4_to_f16x2(w1, b0, b1);
+        mma16816(t1, qa[2 * c], b0, b1);
+        i8x4_to_f16x2(w2, b0, b1);
+        mma16816(t0, qa[2 * c + 1], b0, b1);
+        i8x4_to_f16x2(w3, b0, b1);
+        mma16816(t1, qa[2 * c + 1], b0, b1);
+        // K scales of slots 2t, 2t+1, 2t+8, 2t+9 (entries 4t..4t+3 of group c)
+        const uint2 kd = *reinterpret_cast<const uint2*>(tile + 32 * D + (c * 16 + 4 * t) * 2);
+        const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&kd.x));
+        const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&kd.y));
+        sc[0] += d01.x * (t0[0] + t0[2]);
+        sc[1] += d01.y * (t0[1] + t0[3]);
+        sc[2] += d23.x * (t1[0] + t1[2]);
+        sc[3] += d23.y * (t1[1] + t1[3]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sc[e] *= scale_log2;
+    const bool ok0 = 2 * t < valid, ok1 = 2 * t + 1 < valid, ok2 = 2 * t + 8 < valid, ok3 = 2 * t + 9 < valid;
+    if (!ok0) sc[0] = -INFINITY;
+    if (!ok1) sc[1] = -INFINITY;
+    if (!ok2) sc[2] = -INFINITY;
+    if (!ok3) sc[3] = -INFINITY;
+    float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
+    const bool grow = mx > m_run;
+    const float m_new = grow ? mx : m_run;
+    const float alpha = grow ? ex2(m_run - m_new) : 1.f;
+    float pr[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) pr[e] = ex2(sc[e] - m_new);
+    l_run = l_run * alpha + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
+    m_run = m_new;
+    if (__any_sync(kFull, grow)) {
+#pragma unroll
+        for (int nt = 0; nt < D / 8; ++nt) {
+            o[nt][0] *= alpha;
+            o[nt][1] *= alpha;
+            o[nt][2] *= alpha;
+            o[nt][3] *= alpha;
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < G32; ++c) {
+        const uint2 vd = *reinterpret_cast<const uint2*>(tile + 33 * D + (c * 16 + 4 * t) * 2);
+        const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&vd.x));
+        const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&vd.y));
+        const float p0 = ok0 ? pr[0] * d01.x : 0.f, p1 = ok1 ? pr[1] * d01.y : 0.f;
+        const float p2 = ok2 ? pr[2] * d23.x : 0.f, p3 = ok3 ? pr[3] * d23.y : 0.f;
+        uint32_t pa[4];
+        {
+            const __half2 h01 = __floats2half2_rn(p0, p1), h23 = __floats2half2_rn(p2, p3);
+            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+            pa[0] = h2_bits(h01);
+            pa[1] = h2_bits(__floats2half2_rn(p0 - f01.x, p1 - f01.y));
+            pa[2] = h2_bits(h23);
+            pa[3] = h2_bits(__floats2half2_rn(p2 - f23.x, p3 - f23.y));
+        }
+        // columns 32c + 8*mi + r: one 16-byte run (16 slots) each
+        uint32_t w0, w1, w2, w3, b0, b1;
+        ldsm_x4(base + 16 * D + (32 * c + 8 * mi + r) * 16, w0, w1, w2, w3);
+        i8x4_to_f16x2(w0, b0, b1);
+        mma16816(o[4 * c], pa, b0, b1);
+        i8x4_to_f16x2(w1, b0, b1);
+        mma16816(o[4 * c + 1], pa, b0, b1);
+        i8x4_to_f16x2(w2, b0, b1);
+        mma16816(o[4 * c + 2], pa, b0, b1);
+        i8x4_to_f16x2(w3, b0, b1);
+        mma16816(o[4 * c + 3], pa, b0, b1);
+    }
+}
+
 // Shared memory of one warp: its tile ring plus two q buffers (pieces of
 // even / odd index) of group*D elements of the q dtype.
 __host__ __device__ inline int qbuf_bytes(int group, int head_dim, int q_f32) {
     return (group * head_dim * (q_f32 ? 4 : 2) + 127) & ~127;
 }
 
-__host__ __device__ inline int warp_smem(int group, int head_dim, int q_f32) {
-    return kStages * (2 * kBlock * head_dim * 2) + 2 * qbuf_bytes(group, head_dim, q_f32);
+__host__ __device__ inline int stage_count(int q8) { return q8 ? kStagesQ8 : kStages; }
+__host__ __device__ inline int tile_bytes(int head_dim, int q8) {
+    return q8 ? q8_tile_bytes(head_dim) : 2 * kBlock * head_dim * 2;
 }
 
-__host__ __device__ inline int attn_smem(int group, int head_dim, int q_f32) {
-    return kWarps * warp_smem(group, head_dim, q_f32) + kWarps * kStages * 8;
+__host__ __device__ inline int warp_smem(int group, int head_dim, int q_f32, int q8) {
+    return stage_count(q8) * tile_bytes(head_dim, q8) + 2 * qbuf_bytes(group, head_dim, q_f32);
 }
 
-template <int D>
+__host__ __device__ inline int attn_smem(int group, int head_dim, int q_f32, int q8) {
+    return kWarps * warp_smem(group, head_dim, q_f32, q8) + kWarps * stage_count(q8) * 8;
+}
+
+template <int D, bool Q8>
 __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid_constant__ AttnParams p) {
-    constexpr int TILE = 2 * kBlock * D * 2;
+    constexpr int TILE = Q8 ? q8_tile_bytes(D) : 2 * kBlock * D * 2;
     constexpr int ROW = D * 2;
     constexpr int KS = D / 16;
     constexpr int NT = D / 8;
-    constexpr int S = kStages;
+    constexpr int S = Q8 ? kStagesQ8 : kStages;
     extern __shared__ __align__(1024) uint8_t smem[];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gw = blockIdx.x * kWarps + warp;
     const int Hkv = p.n_kv_heads, G = p.group;
     const int QBUF = qbuf_bytes(G, D, p.q_f32);
-    uint8_t* stages = smem + (size_t)warp * warp_smem(G, D, p.q_f32);
+    uint8_t* stages = smem + (size_t)warp * warp_smem(G, D, p.q_f32, Q8);
     uint8_t* qbufs = stages + S * TILE;
     const uint32_t bar0 =
-        smem_u32(reinterpret_cast<uint64_t*>(smem + (size_t)kWarps * warp_smem(G, D, p.q_f32)) + warp * S);
+        smem_u32(reinterpret_cast<uint64_t*>(smem + (size_t)kWarps * warp_smem(G, D, p.q_f32, Q8)) + warp * S);
     if (lane < S) mbar_init(bar0 + 8u * lane, 1);
     fence_mbar_init();
     __syncwarp();
@@ -371,7 +605,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
     const long long T = (long long)p.tiles_per_head * Hkv;
     const long long t0 = T * gw / p.n_warps, t1 = T * (gw + 1) / p.n_warps;
     const int g = lane >> 2, t4 = lane & 3;
-    const size_t tile_elems = 2 * kBlock * D;
+    const size_t tile_elems = TILE / 2;  // pool addressing in 16-bit units
     const int qelem = p.q_f32 ? 4 : 2;
     const uint32_t qbytes = (uint32_t)(G * D * qelem);
 
@@ -539,7 +773,30 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
         const int b = dc.b0 + ct;  // from block dc.skip
         const int valid = min(kBlock, dc.pos + 1 - (dc.skip + b) * kBlock);
         bool touched = false;
-        if (p.k_new && dc.last_block >= 0 && b == dc.b1 - 1) {
+        if (Q8 && p.k_new && dc.last_block >= 0 && b == dc.b1 - 1) {
+            // Fused append, Q8_0: lanes 0..2*CH-1 quantise this token's new
+            // K (then V) row for head h, eight values each, and store it to
+            // its pool cell and into the staged tile.
+            constexpr int CH = D / 8;
+            const int slot = dc.pos % kBlock;
+            const bool live = lane < 2 * CH;
+            const int kvsel = lane / CH, c = lane % CH;
+            float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (live)
+                load8_f32(kvsel ? p.v_new : p.k_new, (size_t)dc.tok * Hkv * D + (size_t)dc.h * D + (size_t)c * 8,
+                          p.kv_f32, x);
+            uint32_t w0, w1;
+            const float d = q8_quant8(x, w0, w1);
+            const uint32_t p0 = __shfl_xor_sync(kFull, w0, 1), p1 = __shfl_xor_sync(kFull, w1, 1);
+            if (live) {
+                q8_store8<D>(tile, kvsel, c, slot, w0, w1, p0, p1, d);
+                q8_store8<D>(reinterpret_cast<uint8_t*>(p.pool_layer_w + ((size_t)dc.last_block * Hkv + dc.h) *
+                                                                             tile_elems),
+                             kvsel, c, slot, w0, w1, p0, p1, d);
+            }
+            touched = true;
+        }
+        if (!Q8 && p.k_new && dc.last_block >= 0 && b == dc.b1 - 1) {
             // Fused append: this token's new K/V row for head h goes to its
             // pool cell and into the staged tile (the copy read the old bytes).
             constexpr int CH = D / 8;
@@ -555,7 +812,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
             }
             touched = true;
         }
-        if (valid < kBlock) {
+        if (!Q8 && valid < kBlock) {
             // Rows past the sequence end were never written for it: zero V so
             // 0 * (stale NaN/Inf) cannot reach O; K rows are masked.
             const int per_half = (kBlock - valid) * 8;  // 16-byte chunks past the end in each 64-wide sub-tile
@@ -566,7 +823,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
             touched = true;
         }
         __syncwarp();
-        attend_tile<D>(tile, valid, qa, o, m_run, l_run, p.scale_log2, lane);
+        if constexpr (Q8)
+            attend_tile_q8<D>(tile, valid, qa, o, m_run, l_run, p.scale_log2, lane);
+        else
+            attend_tile<D>(tile, valid, qa, o, m_run, l_run, p.scale_log2, lane);
         ++consumed;
         ++ct;
         // Generic-proxy writes into this stage must be ordered before the
@@ -1202,6 +1462,36 @@ __global__ void __launch_bounds__(256) rows_kernel(const uint16_t* __restrict__ 
     *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
 }
 
+// Q8_0 pool: value q * d of each cell, rounded to f16 (nearest even).
+template <int D>
+__global__ void __launch_bounds__(256) rows_q8_kernel(const uint8_t* __restrict__ pool_layer,
+                                                      const int32_t* __restrict__ trow, int n, int n_kv_heads,
+                                                      uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out) {
+    constexpr int CH = D / 8;
+    const int gid = blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= n * n_kv_heads * 2 * CH) return;
+    const int c = gid % CH;
+    int r = gid / CH;
+    const int kvsel = r & 1;
+    r >>= 1;
+    const int h = r % n_kv_heads;
+    const int pos = r / n_kv_heads;
+    const int b = trow[pos / kBlock], slot = pos % kBlock;
+    const uint8_t* tile = pool_layer + ((size_t)b * n_kv_heads + h) * q8_tile_bytes(D);
+    const float d = __half2float(__ushort_as_half(
+        *reinterpret_cast<const uint16_t*>(tile + (kvsel ? 33 : 32) * D + ((c >> 2) * 16 + q8_pos(slot)) * 2)));
+    uint16_t vals[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = 8 * c + i;
+        const int off = kvsel ? 16 * D + e * 16 + q8_pos(slot) : q8_krun<D>(slot, e >> 4) + q8_pos(e & 15);
+        vals[i] = f32_to_f16_ref((float)(int8_t)tile[off] * d);
+    }
+    uint16_t* dst = (kvsel ? v_out : k_out) + (size_t)pos * n_kv_heads * D + (size_t)h * D + (size_t)c * 8;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(vals[0] | (uint32_t(vals[1]) << 16), vals[2] | (uint32_t(vals[3]) << 16),
+                                                vals[4] | (uint32_t(vals[5]) << 16), vals[6] | (uint32_t(vals[7]) << 16));
+}
+
 }  // namespace
 
 namespace {
@@ -1212,64 +1502,69 @@ int sm_count(int dev) {
     return sms[dev];
 }
 
-template <int D>
+template <int D, bool Q8>
 cudaError_t ensure_attr(int dev) {
     // opt-in shared memory is a per-device attribute; size it for the largest
     // layout (f32 q, group 8)
     static bool set[64] = {};
     if (set[dev]) return cudaSuccess;
-    const cudaError_t e = cudaFuncSetAttribute(paged_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               attn_smem(kMaxGroup, D, 1));
+    const cudaError_t e = cudaFuncSetAttribute(paged_attn_kernel<D, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               attn_smem(kMaxGroup, D, 1, Q8));
     if (e == cudaSuccess) set[dev] = true;
     return e;
 }
 
-template <int D>
+template <int D, bool Q8>
 int warps_for(int dev, int group, int q_f32) {
     // resident CTAs per SM for this layout, cached per (device, group, dtype)
     static int cache[64][kMaxGroup + 1][2] = {};
     int& c = cache[dev][group][q_f32 ? 1 : 0];
     if (c == 0) {
-        if (ensure_attr<D>(dev) != cudaSuccess) return 0;
+        if (ensure_attr<D, Q8>(dev) != cudaSuccess) return 0;
         int per_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_attn_kernel<D>, kWarps * 32,
-                                                          attn_smem(group, D, q_f32)) != cudaSuccess)
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_attn_kernel<D, Q8>, kWarps * 32,
+                                                          attn_smem(group, D, q_f32, Q8)) != cudaSuccess)
             return 0;
         c = (per_sm < 1 ? 1 : per_sm) * sm_count(dev) * kWarps;
     }
     return c;
 }
 
-template <int D>
+template <int D, bool Q8>
 cudaError_t launch_attend_d(const AttnParams& p, cudaStream_t s) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if ((e = ensure_attr<D>(dev)) != cudaSuccess) return e;
+    if ((e = ensure_attr<D, Q8>(dev)) != cudaSuccess) return e;
     // Cooperative: merging warps wait for other CTAs' flags, so the whole
     // grid (sized to the resident capacity) must be co-resident.
     const dim3 grid((p.n_warps + kWarps - 1) / kWarps), block(kWarps * 32);
     void* args[] = {const_cast<AttnParams*>(&p)};
-    return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&paged_attn_kernel<D>), grid, block, args,
-                                       attn_smem(p.group, D, p.q_f32), s);
+    return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&paged_attn_kernel<D, Q8>), grid, block, args,
+                                       attn_smem(p.group, D, p.q_f32, Q8), s);
 }
 
 }  // namespace
 
-int attend_warps(int device, int group, int head_dim, int q_f32) {
+int attend_warps(int device, int group, int head_dim, int q_f32, int q8) {
     if (device < 0 || device >= 64 || group < 1 || group > kMaxGroup) return 0;
     int prev = -1;
     cudaGetDevice(&prev);
     if (prev != device) cudaSetDevice(device);
-    const int w = head_dim == 64 ? warps_for<64>(device, group, q_f32) : warps_for<128>(device, group, q_f32);
+    int w;
+    if (q8)
+        w = head_dim == 64 ? warps_for<64, true>(device, group, q_f32) : warps_for<128, true>(device, group, q_f32);
+    else
+        w = head_dim == 64 ? warps_for<64, false>(device, group, q_f32) : warps_for<128, false>(device, group, q_f32);
     if (prev != device && prev >= 0) cudaSetDevice(prev);
     return w;
 }
 
 cudaError_t launch_attend(const AttnParams& p, int head_dim, cudaStream_t s) {
     if (p.n_warps == 0) return cudaSuccess;
-    return head_dim == 64 ? launch_attend_d<64>(p, s) : launch_attend_d<128>(p, s);
+    if (p.q8) return head_dim == 64 ? launch_attend_d<64, true>(p, s) : launch_attend_d<128, true>(p, s);
+    return head_dim == 64 ? launch_attend_d<64, false>(p, s) : launch_attend_d<128, false>(p, s);
 }
 
 int attend_launches(const AttnParams& p) { return p.n_warps == 0 ? 0 : 1; }
@@ -1309,11 +1604,16 @@ cudaError_t launch_gather_permute(const void* gathered, void* out, int nranks, u
 }
 
 cudaError_t launch_write(uint16_t* pool_layer, const int2* cells, int n, int n_kv_heads, int head_dim, const void* k,
-                         const void* v, int in_f32, cudaStream_t s) {
+                         const void* v, int in_f32, int q8, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
     const int threads = n * n_kv_heads * 2 * (head_dim / 8);
     const int blocks = (threads + 255) / 256;
-    if (head_dim == 64)
+    uint8_t* pool_bytes = reinterpret_cast<uint8_t*>(pool_layer);
+    if (q8 && head_dim == 64)
+        kv_write_q8_kernel<64><<<blocks, 256, 0, s>>>(pool_bytes, cells, n, n_kv_heads, k, v, in_f32);
+    else if (q8)
+        kv_write_q8_kernel<128><<<blocks, 256, 0, s>>>(pool_bytes, cells, n, n_kv_heads, k, v, in_f32);
+    else if (head_dim == 64)
         kv_write_kernel<64><<<blocks, 256, 0, s>>>(pool_layer, cells, n, n_kv_heads, k, v, in_f32);
     else
         kv_write_kernel<128><<<blocks, 256, 0, s>>>(pool_layer, cells, n, n_kv_heads, k, v, in_f32);
@@ -1331,11 +1631,16 @@ cudaError_t launch_apply_plan(uint16_t* pool, size_t layer_stride_elems, size_t 
 }
 
 cudaError_t launch_rows(const uint16_t* pool_layer, const int32_t* table_row, int n, int n_kv_heads, int head_dim,
-                        uint16_t* k_out, uint16_t* v_out, cudaStream_t s) {
+                        uint16_t* k_out, uint16_t* v_out, int q8, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
     const int threads = n * n_kv_heads * 2 * (head_dim / 8);
     const int blocks = (threads + 255) / 256;
-    if (head_dim == 64)
+    const uint8_t* pool_bytes = reinterpret_cast<const uint8_t*>(pool_layer);
+    if (q8 && head_dim == 64)
+        rows_q8_kernel<64><<<blocks, 256, 0, s>>>(pool_bytes, table_row, n, n_kv_heads, k_out, v_out);
+    else if (q8)
+        rows_q8_kernel<128><<<blocks, 256, 0, s>>>(pool_bytes, table_row, n, n_kv_heads, k_out, v_out);
+    else if (head_dim == 64)
         rows_kernel<64><<<blocks, 256, 0, s>>>(pool_layer, table_row, n, n_kv_heads, k_out, v_out);
     else
         rows_kernel<128><<<blocks, 256, 0, s>>>(pool_layer, table_row, n, n_kv_heads, k_out, v_out);

@@ -90,7 +90,7 @@ extern "C" lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return LT_E_CUDA;
     const int q_f32 = q_dtype == LT_F32;
-    int n_warps = ltkv::attend_warps(dev, (int)group, (int)head_dim, q_f32);
+    int n_warps = ltkv::attend_warps(dev, (int)group, (int)head_dim, q_f32, 0);
     if (n_warps <= 0) return LT_E_CUDA;
     n_warps = (int)std::min<long long>(n_warps, tiles * n_kv_heads);
 
@@ -167,6 +167,7 @@ extern "C" lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_
     p.pre_ml = nullptr;
     p.pre_splits = 0;
     p.pre_split_rows = 0;
+    p.q8 = 0;  // f16 pool layout only
     if (ltkv::launch_attend(p, (int)head_dim, st) != cudaSuccess) return LT_E_CUDA;
     return LT_OK;
 }

@@ -76,21 +76,31 @@ def _i32(a) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
 
 
+KV_FORMATS = {"f16": N.LT_KV_F16, "q8_0": N.LT_KV_Q8_0}
+
+
 class KvCache:
-    """Paged f16 KV cache of 16-token blocks on one CUDA device.
+    """Paged KV cache of 16-token blocks on one CUDA device.
 
     ``KvCache(n_layers, n_kv_heads, head_dim, n_tokens)`` is the reference's
     ``KvCache::new(n_layers, n_kv_heads * head_dim, n_tokens)``.  ``device=-1``
     builds a bookkeeping-only handle (no GPU), for host-side tests.
+    ``kv_format="q8_0"`` stores rows as Q8_0 groups (include/lt_kv.h,
+    LT_KV_Q8_0) instead of f16.
     """
 
     def __init__(self, n_layers: int, n_kv_heads: int, head_dim: int, n_tokens: int, *, n_heads: int | None = None,
-                 max_seqs: int = 256, max_batch: int = 512, max_blocks_per_seq: int = 0, device: int = 0):
+                 max_seqs: int = 256, max_batch: int = 512, max_blocks_per_seq: int = 0, device: int = 0,
+                 kv_format: str = "f16"):
         self._lib = N.lib()
+        if kv_format not in KV_FORMATS:
+            raise ValueError(f"kv_format must be one of {sorted(KV_FORMATS)}")
         cfg = N.lt_kv_config(
             n_layers=n_layers, n_kv_heads=n_kv_heads, head_dim=head_dim,
             n_heads=n_heads if n_heads is not None else n_kv_heads, n_tokens=n_tokens, max_seqs=max_seqs,
-            max_batch=max_batch, max_blocks_per_seq=max_blocks_per_seq, device=device)
+            max_batch=max_batch, max_blocks_per_seq=max_blocks_per_seq, device=device,
+            kv_format=KV_FORMATS[kv_format])
+        self.kv_format = kv_format
         h = C.c_void_p()
         rc = self._lib.lt_kv_create(C.byref(cfg), C.byref(h))
         if rc != N.LT_OK:
@@ -274,15 +284,23 @@ class KvCache:
         return self._lib.lt_kv_launch_count(self._h)
 
     def read_pool(self, layer: int) -> np.ndarray:
-        """Raw device pool of one layer: uint16 [block][kv_head][2][16][head_dim]
-        with the chunk swizzle of include/lt_kv.h still applied."""
-        out = np.zeros((self.n_blocks, self.n_kv_heads, 2, BLOCK, self.head_dim), np.uint16)
+        """Raw device pool of one layer: f16 caches give uint16
+        [block][kv_head][2][16][head_dim] with the chunk swizzle of
+        include/lt_kv.h still applied; Q8_0 caches give the uint8 tiles
+        [block][kv_head][34 * head_dim]."""
+        if self.kv_format == "q8_0":
+            out = np.zeros((self.n_blocks, self.n_kv_heads, 34 * self.head_dim), np.uint8)
+        else:
+            out = np.zeros((self.n_blocks, self.n_kv_heads, 2, BLOCK, self.head_dim), np.uint16)
         self._check(self._lib.lt_kv_read_pool(self._h, layer, 0, self.n_blocks, _ptr(out)))
         return out
 
     def pool_reference_layout(self, layer: int):
         """This layer's pool as the reference lays it out (kv.rs:20):
-        (K, V) uint16 [block][slot][kv_dim]."""
+        (K, V) uint16 [block][slot][kv_dim]; for Q8_0 (Kq, Vq) int8
+        [block][slot][kv_dim] and (Kd, Vd) f16 bits [block][slot][kv_dim/32]."""
+        if self.kv_format == "q8_0":
+            return unswizzle_pool_q8(self.read_pool(layer), self.head_dim)
         return unswizzle_pool(self.read_pool(layer))
 
 
@@ -346,3 +364,32 @@ def unswizzle_pool(raw: np.ndarray):
     k = logical[:, :, 0].transpose(0, 2, 1, 3).reshape(nb, blk, hkv * d)
     v = logical[:, :, 1].transpose(0, 2, 1, 3).reshape(nb, blk, hkv * d)
     return np.ascontiguousarray(k), np.ascontiguousarray(v)
+
+
+def _q8_pos(i):
+    """Place of entry i (0..15) inside a 16-byte run of a Q8_0 tile."""
+    return ((i & 7) >> 1) * 4 + ((i >> 3) << 1) + (i & 1)
+
+
+def unswizzle_pool_q8(raw: np.ndarray, head_dim: int):
+    """Invert the Q8_0 tile layout of include/lt_kv.h -> (Kq, Vq) int8
+    [block][16][kv_heads*D] and (Kd, Vd) f16 bits [block][16][kv_heads*D/32]."""
+    nb, hkv, tb = raw.shape
+    d = head_dim
+    assert tb == 34 * d
+    pos = np.array([_q8_pos(i) for i in range(16)])
+    s = np.arange(BLOCK)[:, None]
+    e = np.arange(d)[None, :]
+    run = s * (d // 16) + e // 16
+    koff = (run // 8) * 128 + ((run % 8) ^ ((run // 8) & 7)) * 16 + pos[e % 16]  # [16, D]
+    voff = 16 * d + e * 16 + pos[s]  # [16, D]
+    kq = raw[:, :, koff].view(np.int8)  # [nb, hkv, 16, D]
+    vq = raw[:, :, voff].view(np.int8)
+    g = np.arange(d // 32)[None, :]
+    soff = g * 16 + pos[s]  # [16, D/32] in f16 entries
+    kd = raw[:, :, 32 * d:33 * d].copy().view(np.uint16)[:, :, soff]
+    vd = raw[:, :, 33 * d:34 * d].copy().view(np.uint16)[:, :, soff]
+    def rows(a):
+        return np.ascontiguousarray(a.transpose(0, 2, 1, 3).reshape(nb, BLOCK, -1))
+    return rows(kq), rows(vq), rows(kd), rows(vd)
+

@@ -14,6 +14,10 @@
  *   - dot with 8 partial sums + tail                            model.rs:159-172
  *   - scores * scale, max fold, expf, sequential sum, 1/sum     model.rs:447-463
  *   - V accumulation  o += w * v  (no contraction)              model.rs:464-473
+ * A Q8_0 cache (okv_new_q8) keeps each row as 32-value groups of int8 + an
+ * f16 scale: the Q8_0 block of the reference's GGUF reader (quant.rs:254-275)
+ * filled by the engine's own int8 quantiser (quant.rs:785-795); reads widen
+ * q * d, which is exact in f32 (8-bit q times an 11-bit scale).
  * Build with -ffp-contract=off and without fast-math (Rust does not fuse).
  */
 #define _GNU_SOURCE
@@ -39,6 +43,11 @@ struct okv {
     uint32_t n_layers, kv_dim, n_blocks, max_seqs;
     uint16_t* k;
     uint16_t* v;
+    int q8;           /* Q8_0 rows: kq/vq values, kd/vd f16 scales (k, v unused) */
+    int8_t* kq;
+    int8_t* vq;
+    uint16_t* kd;
+    uint16_t* vd;
     uint32_t* refs;
     int32_t* free_list;
     uint32_t n_free;
@@ -117,26 +126,44 @@ static void widen(const uint16_t* src, float* dst, uint32_t n) {
 
 /* ------------------------------------------------------------ KvCache ---- */
 
-okv* okv_new(uint32_t n_layers, uint32_t kv_dim, uint32_t n_tokens, uint32_t max_seqs) {
+static okv* okv_new_fmt(uint32_t n_layers, uint32_t kv_dim, uint32_t n_tokens, uint32_t max_seqs, int q8) {
+    if (q8 && kv_dim % 32) return NULL;
     okv* kv = (okv*)calloc(1, sizeof(okv));
     if (!kv) return NULL;
     kv->n_layers = n_layers;
     kv->kv_dim = kv_dim;
     kv->n_blocks = (n_tokens + OKV_BLOCK - 1) / OKV_BLOCK; /* div_ceil, kv.rs:36 */
     kv->max_seqs = max_seqs;
+    kv->q8 = q8;
     size_t size = (size_t)n_layers * kv->n_blocks * OKV_BLOCK * kv_dim; /* kv.rs:37 */
-    kv->k = (uint16_t*)calloc(size ? size : 1, 2);
-    kv->v = (uint16_t*)calloc(size ? size : 1, 2);
+    size_t fsize = q8 ? 1 : (size ? size : 1);
+    kv->k = (uint16_t*)calloc(fsize, 2);
+    kv->v = (uint16_t*)calloc(fsize, 2);
+    if (q8) {
+        kv->kq = (int8_t*)calloc(size ? size : 1, 1);
+        kv->vq = (int8_t*)calloc(size ? size : 1, 1);
+        kv->kd = (uint16_t*)calloc(size / 32 ? size / 32 : 1, 2);
+        kv->vd = (uint16_t*)calloc(size / 32 ? size / 32 : 1, 2);
+    }
     kv->refs = (uint32_t*)calloc(kv->n_blocks ? kv->n_blocks : 1, 4);
     kv->free_list = (int32_t*)malloc((kv->n_blocks ? kv->n_blocks : 1) * 4);
     kv->seqs = (oseq*)calloc(max_seqs ? max_seqs : 1, sizeof(oseq));
-    if (!kv->k || !kv->v || !kv->refs || !kv->free_list || !kv->seqs) {
+    if (!kv->k || !kv->v || !kv->refs || !kv->free_list || !kv->seqs ||
+        (q8 && (!kv->kq || !kv->vq || !kv->kd || !kv->vd))) {
         okv_delete(kv);
         return NULL;
     }
     for (uint32_t i = 0; i < kv->n_blocks; i++) kv->free_list[i] = (int32_t)(kv->n_blocks - 1 - i);
     kv->n_free = kv->n_blocks;
     return kv;
+}
+
+okv* okv_new(uint32_t n_layers, uint32_t kv_dim, uint32_t n_tokens, uint32_t max_seqs) {
+    return okv_new_fmt(n_layers, kv_dim, n_tokens, max_seqs, 0);
+}
+
+okv* okv_new_q8(uint32_t n_layers, uint32_t kv_dim, uint32_t n_tokens, uint32_t max_seqs) {
+    return okv_new_fmt(n_layers, kv_dim, n_tokens, max_seqs, 1);
 }
 
 void okv_delete(okv* kv) {
@@ -146,6 +173,10 @@ void okv_delete(okv* kv) {
     free(kv->seqs);
     free(kv->k);
     free(kv->v);
+    free(kv->kq);
+    free(kv->vq);
+    free(kv->kd);
+    free(kv->vd);
     free(kv->refs);
     free(kv->free_list);
     free(kv);
@@ -153,7 +184,9 @@ void okv_delete(okv* kv) {
 
 uint32_t okv_capacity(const okv* kv) { return kv->n_blocks * OKV_BLOCK; }
 uint64_t okv_bytes(const okv* kv) {
-    return (uint64_t)kv->n_layers * kv->n_blocks * OKV_BLOCK * kv->kv_dim * 2u * 2u;
+    const uint64_t rows = (uint64_t)kv->n_layers * kv->n_blocks * OKV_BLOCK;
+    if (kv->q8) return rows * 2u * (kv->kv_dim + kv->kv_dim / 32 * 2u);
+    return rows * kv->kv_dim * 2u * 2u;
 }
 uint32_t okv_len(const okv* kv, uint32_t seq) { return seq < kv->max_seqs ? kv->seqs[seq].len : 0; }
 uint32_t okv_free_blocks(const okv* kv) { return kv->n_free; }
@@ -161,6 +194,23 @@ uint32_t okv_n_blocks(const okv* kv) { return kv->n_blocks; }
 
 static size_t offset(const okv* kv, uint32_t layer, uint32_t block, uint32_t slot) { /* kv.rs:63-65 */
     return (((size_t)layer * kv->n_blocks + block) * OKV_BLOCK + slot) * kv->kv_dim;
+}
+
+/* All K and V bytes of block src onto block dst in every layer. */
+static void copy_block(okv* kv, uint32_t src, uint32_t dst) {
+    for (uint32_t l = 0; l < kv->n_layers; l++) {
+        size_t so = offset(kv, l, src, 0), dof = offset(kv, l, dst, 0);
+        size_t n = (size_t)OKV_BLOCK * kv->kv_dim;
+        if (kv->q8) {
+            memmove(kv->kq + dof, kv->kq + so, n);
+            memmove(kv->vq + dof, kv->vq + so, n);
+            memmove(kv->kd + dof / 32, kv->kd + so / 32, n / 32 * 2);
+            memmove(kv->vd + dof / 32, kv->vd + so / 32, n / 32 * 2);
+        } else {
+            memmove(kv->k + dof, kv->k + so, n * 2);
+            memmove(kv->v + dof, kv->v + so, n * 2);
+        }
+    }
 }
 
 static int alloc_block(okv* kv, int32_t* out) { /* kv.rs:67-74 */
@@ -198,12 +248,7 @@ int okv_append(okv* kv, uint32_t seq, uint32_t pos, int32_t* block, int32_t* slo
         if (kv->refs[last] > 1) { /* copy-on-write, kv.rs:99-110 */
             int32_t nb;
             if (alloc_block(kv, &nb)) return OKV_FULL;
-            for (uint32_t l = 0; l < kv->n_layers; l++) {
-                size_t src = offset(kv, l, (uint32_t)last, 0), dst = offset(kv, l, (uint32_t)nb, 0);
-                size_t n = (size_t)OKV_BLOCK * kv->kv_dim;
-                memmove(kv->k + dst, kv->k + src, n * 2);
-                memmove(kv->v + dst, kv->v + src, n * 2);
-            }
+            copy_block(kv, (uint32_t)last, (uint32_t)nb);
             release_block(kv, last);
             s->blocks[s->n - 1] = nb;
         }
@@ -226,8 +271,32 @@ int okv_append_batch(okv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t
     return rc;
 }
 
+float okv_q8_group(const float* x, int8_t* q) { /* quant.rs:785-795 */
+    float amax = 0.0f;
+    for (int i = 0; i < 32; i++) {
+        float a = fabsf(x[i]);
+        if (a > amax) amax = a; /* f32::max: a NaN operand loses */
+    }
+    float d = amax / 127.0f;
+    float id = d > 0.0f ? 1.0f / d : 0.0f;
+    for (int i = 0; i < 32; i++) {
+        float r = roundf(x[i] * id); /* f32::round: half away from zero */
+        q[i] = r != r ? 0 : r >= 127.0f ? 127 : r <= -128.0f ? -128 : (int8_t)r; /* `as i8` saturates */
+    }
+    return d;
+}
+
+static void q8_row(const float* x, uint32_t n, int8_t* q, uint16_t* d) {
+    for (uint32_t g = 0; g < n / 32; g++) d[g] = okv_f32_to_f16(okv_q8_group(x + 32 * g, q + 32 * g));
+}
+
 void okv_write(okv* kv, uint32_t layer, int32_t block, int32_t slot, const float* k, const float* v) {
     size_t o = offset(kv, layer, (uint32_t)block, (uint32_t)slot);
+    if (kv->q8) {
+        q8_row(k, kv->kv_dim, kv->kq + o, kv->kd + o / 32);
+        q8_row(v, kv->kv_dim, kv->vq + o, kv->vd + o / 32);
+        return;
+    }
     for (uint32_t d = 0; d < kv->kv_dim; d++) kv->k[o + d] = okv_f32_to_f16(k[d]);
     for (uint32_t d = 0; d < kv->kv_dim; d++) kv->v[o + d] = okv_f32_to_f16(v[d]);
 }
@@ -240,6 +309,18 @@ void okv_write_batch(okv* kv, uint32_t layer, const int32_t* block, const int32_
 
 void okv_write_batch_f16(okv* kv, uint32_t layer, const int32_t* block, const int32_t* slot,
                          uint32_t n, const uint16_t* k, const uint16_t* v) {
+    if (kv->q8) {
+        float* kf = (float*)malloc(kv->kv_dim * sizeof(float));
+        float* vf = (float*)malloc(kv->kv_dim * sizeof(float));
+        for (uint32_t i = 0; i < n; i++) {
+            widen(k + (size_t)i * kv->kv_dim, kf, kv->kv_dim);
+            widen(v + (size_t)i * kv->kv_dim, vf, kv->kv_dim);
+            okv_write(kv, layer, block[i], slot[i], kf, vf);
+        }
+        free(kf);
+        free(vf);
+        return;
+    }
     for (uint32_t i = 0; i < n; i++) {
         size_t o = offset(kv, layer, (uint32_t)block[i], (uint32_t)slot[i]);
         memcpy(kv->k + o, k + (size_t)i * kv->kv_dim, kv->kv_dim * 2);
@@ -286,12 +367,7 @@ uint32_t okv_compact(okv* kv, int32_t* moves) {
         if (kv->refs[b] != 0) lv[nl++] = (int32_t)b;
     for (uint32_t j = 0; j < nf && j < nl && fr[j] < lv[j]; j++) {
         int32_t src = lv[j], dst = fr[j];
-        for (uint32_t l = 0; l < kv->n_layers; l++) {
-            size_t so = offset(kv, l, (uint32_t)src, 0), dof = offset(kv, l, (uint32_t)dst, 0);
-            size_t n = (size_t)OKV_BLOCK * kv->kv_dim;
-            memcpy(kv->k + dof, kv->k + so, n * 2);
-            memcpy(kv->v + dof, kv->v + so, n * 2);
-        }
+        copy_block(kv, (uint32_t)src, (uint32_t)dst);
         kv->refs[dst] = kv->refs[src];
         kv->refs[src] = 0;
         remap[src] = dst;
@@ -328,14 +404,41 @@ uint32_t okv_free_list(const okv* kv, int32_t* out, uint32_t cap) {
 
 const uint16_t* okv_pool_k(const okv* kv) { return kv->k; }
 const uint16_t* okv_pool_v(const okv* kv) { return kv->v; }
+const int8_t* okv_pool_kq(const okv* kv) { return kv->kq; }
+const int8_t* okv_pool_vq(const okv* kv) { return kv->vq; }
+const uint16_t* okv_pool_kd(const okv* kv) { return kv->kd; }
+const uint16_t* okv_pool_vd(const okv* kv) { return kv->vd; }
+
+/* q * d of n values of a Q8_0 row (exact in f32). */
+static void dequant(const int8_t* q, const uint16_t* d, float* out, uint32_t n) {
+    for (uint32_t i = 0; i < n; i++) out[i] = (float)q[i] * okv_f16_to_f32(d[i / 32]);
+}
+
+/* Row o (element offset) of K or V, head `kvh`, widened to f32. */
+static void read_row(const okv* kv, int is_v, size_t o, uint32_t kvh, uint32_t hd, float* row) {
+    o += (size_t)kvh * hd;
+    if (kv->q8)
+        dequant((is_v ? kv->vq : kv->kq) + o, (is_v ? kv->vd : kv->kd) + o / 32, row, hd);
+    else
+        widen((is_v ? kv->v : kv->k) + o, row, hd);
+}
 
 void okv_rows(const okv* kv, uint32_t layer, uint32_t seq, uint32_t n, uint16_t* k_out, uint16_t* v_out) {
     const oseq* s = &kv->seqs[seq];
+    float* row = kv->q8 ? (float*)malloc(kv->kv_dim * sizeof(float)) : NULL;
     for (uint32_t p = 0; p < n; p++) {
         size_t o = offset(kv, layer, (uint32_t)s->blocks[p / OKV_BLOCK], p % OKV_BLOCK);
+        if (kv->q8) {
+            read_row(kv, 0, o, 0, kv->kv_dim, row);
+            okv_f32_to_f16_array(row, k_out + (size_t)p * kv->kv_dim, kv->kv_dim);
+            read_row(kv, 1, o, 0, kv->kv_dim, row);
+            okv_f32_to_f16_array(row, v_out + (size_t)p * kv->kv_dim, kv->kv_dim);
+            continue;
+        }
         memcpy(k_out + (size_t)p * kv->kv_dim, kv->k + o, kv->kv_dim * 2);
         memcpy(v_out + (size_t)p * kv->kv_dim, kv->v + o, kv->kv_dim * 2);
     }
+    free(row);
 }
 
 /* ---------------------------------------------------------- attention ---- */
@@ -383,7 +486,7 @@ static void attend_task(const attn_job* j, uint32_t idx, float** scores, size_t*
     float* sc = *scores;
     for (uint32_t p = 0; p < len; p++) { /* K pass, model.rs:447-452 */
         size_t o = offset(kv, j->layer, (uint32_t)s->blocks[p / OKV_BLOCK], p % OKV_BLOCK);
-        widen(kv->k + o + (size_t)kvh * hd, row, hd);
+        read_row(kv, 0, o, kvh, hd, row);
         for (uint32_t g = 0; g < group; g++) sc[(size_t)g * len + p] = dot(qs + (size_t)g * hd, row, hd) * j->scale;
     }
     for (uint32_t g = 0; g < group; g++) { /* softmax, model.rs:453-463 */
@@ -401,7 +504,7 @@ static void attend_task(const attn_job* j, uint32_t idx, float** scores, size_t*
     for (uint32_t e = 0; e < group * hd; e++) out[e] = 0.0f;
     for (uint32_t p = 0; p < len; p++) { /* V pass, model.rs:464-473 */
         size_t o = offset(kv, j->layer, (uint32_t)s->blocks[p / OKV_BLOCK], p % OKV_BLOCK);
-        widen(kv->v + o + (size_t)kvh * hd, row, hd);
+        read_row(kv, 1, o, kvh, hd, row);
         for (uint32_t g = 0; g < group; g++) {
             float w = sc[(size_t)g * len + p];
             float* og = out + (size_t)g * hd;

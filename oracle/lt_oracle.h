@@ -32,6 +32,18 @@ enum { OKV_OK = 0, OKV_FULL = 1, OKV_NONCONTIG = 2, OKV_ARG = 3 };
 
 /* KvCache::new (kv.rs:35-48).  Sequence ids must be < max_seqs. */
 okv* okv_new(uint32_t n_layers, uint32_t kv_dim, uint32_t n_tokens, uint32_t max_seqs);
+/* The same cache with Q8_0 rows (lt_kv.h, LT_KV_Q8_0): every kv_dim row is
+ * kept as kv_dim/32 groups of int8 values + one f16 scale each; kv_dim must
+ * be a multiple of 32.  Bookkeeping is unchanged; writes quantise, reads
+ * (rows, attention) use q * d. */
+okv* okv_new_q8(uint32_t n_layers, uint32_t kv_dim, uint32_t n_tokens, uint32_t max_seqs);
+
+/* One 32-value group as the engine's int8 quantiser does it
+ * (quant.rs:785-795): amax folded from 0 with f32::max (NaN ignored),
+ * d = amax / 127, id = d > 0 ? 1 / d : 0, q = round(x * id) half away from
+ * zero, cast to int8 saturating (NaN -> 0).  Returns d (f32); the cache
+ * keeps okv_f32_to_f16(d). */
+float okv_q8_group(const float* x, int8_t* q);
 void okv_delete(okv* kv);
 
 uint32_t okv_capacity(const okv* kv);            /* kv.rs:50 */
@@ -74,8 +86,15 @@ uint32_t okv_free_list(const okv* kv, int32_t* out, uint32_t cap);
 /* Pool in reference layout [layer][block][slot][kv_dim] (f16 bits). */
 const uint16_t* okv_pool_k(const okv* kv);
 const uint16_t* okv_pool_v(const okv* kv);
+/* Q8_0 pool: int8 [layer][block][slot][kv_dim] and f16 scales
+ * [layer][block][slot][kv_dim/32]; NULL for an f16 cache. */
+const int8_t* okv_pool_kq(const okv* kv);
+const int8_t* okv_pool_vq(const okv* kv);
+const uint16_t* okv_pool_kd(const okv* kv);
+const uint16_t* okv_pool_vd(const okv* kv);
 
-/* Rows 0..n of seq (KvCache::rows, kv.rs:135-150) copied out as f16 bits. */
+/* Rows 0..n of seq (KvCache::rows, kv.rs:135-150) copied out as f16 bits
+ * (Q8_0: q * d rounded to f16). */
 void okv_rows(const okv* kv, uint32_t layer, uint32_t seq, uint32_t n, uint16_t* k_out, uint16_t* v_out);
 
 /* Attention closure of Model::forward (model.rs:431-476) for n tokens:

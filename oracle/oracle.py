@@ -62,6 +62,13 @@ def lib():
         u32, i32, u64, p = C.c_uint32, C.c_int32, C.c_uint64, C.c_void_p
         L.okv_new.restype = p
         L.okv_new.argtypes = [u32, u32, u32, u32]
+        L.okv_new_q8.restype = p
+        L.okv_new_q8.argtypes = [u32, u32, u32, u32]
+        L.okv_q8_group.restype = C.c_float
+        L.okv_q8_group.argtypes = [p, p]
+        for name in ("okv_pool_kq", "okv_pool_vq", "okv_pool_kd", "okv_pool_vd"):
+            getattr(L, name).restype = p
+            getattr(L, name).argtypes = [p]
         L.okv_delete.argtypes = [p]
         for name in ("okv_capacity", "okv_free_blocks", "okv_n_blocks"):
             getattr(L, name).restype = u32
@@ -118,13 +125,28 @@ class OracleError(RuntimeError):
         self.code = code
 
 
-class OracleKv:
-    """KvCache (kv.rs:15-188) restated: same method names and error behaviour."""
+def q8_group(x) -> tuple[np.ndarray, float]:
+    """One 32-value group through the engine's int8 quantiser (quant.rs:785-795):
+    (int8 values, f32 scale d)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    assert x.size == 32
+    q = np.zeros(32, np.int8)
+    d = lib().okv_q8_group(_ptr(x), _ptr(q))
+    return q, float(np.float32(d))
 
-    def __init__(self, n_layers: int, kv_dim: int, n_tokens: int, max_seqs: int = 1024):
-        self._h = lib().okv_new(n_layers, kv_dim, n_tokens, max_seqs)
+
+class OracleKv:
+    """KvCache (kv.rs:15-188) restated: same method names and error behaviour.
+    kv_format "q8_0" keeps rows as Q8_0 groups (lt_kv.h LT_KV_Q8_0)."""
+
+    def __init__(self, n_layers: int, kv_dim: int, n_tokens: int, max_seqs: int = 1024,
+                 kv_format: str = "f16"):
+        assert kv_format in ("f16", "q8_0")
+        make = lib().okv_new_q8 if kv_format == "q8_0" else lib().okv_new
+        self._h = make(n_layers, kv_dim, n_tokens, max_seqs)
         if not self._h:
             raise MemoryError("okv_new failed")
+        self.kv_format = kv_format
         self.n_layers, self.kv_dim, self.max_seqs = n_layers, kv_dim, max_seqs
         self.n_blocks = lib().okv_n_blocks(self._h)
 
@@ -226,6 +248,19 @@ class OracleKv:
         k = np.ctypeslib.as_array(kp, shape=(n,)).reshape(shape)
         v = np.ctypeslib.as_array(vp, shape=(n,)).reshape(shape)
         return k, v
+
+    def pool_q8(self):
+        """Q8_0 cache: (Kq, Vq) int8 [layer][block][slot][kv_dim] and (Kd, Vd) f16 bits
+        [layer][block][slot][kv_dim/32]."""
+        assert self.kv_format == "q8_0"
+        shape = (self.n_layers, self.n_blocks, BLOCK, self.kv_dim)
+        dshape = shape[:3] + (self.kv_dim // 32,)
+        out = []
+        for name, ct, shp in (("okv_pool_kq", C.c_int8, shape), ("okv_pool_vq", C.c_int8, shape),
+                              ("okv_pool_kd", C.c_uint16, dshape), ("okv_pool_vd", C.c_uint16, dshape)):
+            ptr = C.cast(getattr(lib(), name)(self._h), C.POINTER(ct))
+            out.append(np.ctypeslib.as_array(ptr, shape=(int(np.prod(shp)),)).reshape(shp))
+        return tuple(out)
 
     def rows(self, layer: int, seq: int, n: int):
         k = np.zeros((n, self.kv_dim), np.uint16)

@@ -26,12 +26,14 @@ class Twin:
     """The GPU cache and the oracle, driven with identical calls."""
 
     def __init__(self, oracle_mod, n_layers, n_kv_heads, head_dim, n_tokens, n_heads=None, max_seqs=16,
-                 max_batch=4096):
+                 max_batch=4096, kv_format="f16"):
         from langtrain_studio_b200.kv import KvCache
 
         self.kv = KvCache(n_layers, n_kv_heads, head_dim, n_tokens, n_heads=n_heads or n_kv_heads,
-                          max_seqs=max_seqs, max_batch=max_batch, device=0)
-        self.ok = oracle_mod.OracleKv(n_layers, n_kv_heads * head_dim, n_tokens, max_seqs=max_seqs)
+                          max_seqs=max_seqs, max_batch=max_batch, device=0, kv_format=kv_format)
+        self.ok = oracle_mod.OracleKv(n_layers, n_kv_heads * head_dim, n_tokens, max_seqs=max_seqs,
+                                      kv_format=kv_format)
+        self.kv_format = kv_format
         self.om = oracle_mod
         self.L, self.hkv, self.d = n_layers, n_kv_heads, head_dim
         self.hq = n_heads or n_kv_heads
@@ -75,6 +77,13 @@ class Twin:
 
     def check_pool(self):
         torch.cuda.synchronize()
+        if self.kv_format == "q8_0":
+            ref = self.ok.pool_q8()
+            for layer in range(self.L):
+                got = self.kv.pool_reference_layout(layer)
+                for name, a, r in zip(("Kq", "Vq", "Kd", "Vd"), got, ref):
+                    assert np.array_equal(a, r[layer]), f"{name} pool differs in layer {layer}"
+            return
         ko, vo = self.ok.pool()
         for layer in range(self.L):
             k, v = self.kv.pool_reference_layout(layer)
