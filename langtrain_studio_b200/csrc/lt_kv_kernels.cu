@@ -901,10 +901,14 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
     const long long NW = p.n_warps;
     const int nb = dc.pos / kBlock + 1 - dc.skip;
     const int w_last = (int)(((dc.ps + nb) * NW - 1) / T);  // warp holding its last tile
+    // Lane j waits for neighbour gw+1+j (32 at a time), so the flags' round
+    // trips overlap instead of following one another.
     int ready = 1;
-    if (lane == 0)
-        for (int w = gw + 1; w <= w_last && ready; ++w) ready = wait_flag_bounded(p.flags + w, p.epoch);
-    ready = __shfl_sync(kFull, ready, 0);
+    for (int w0 = gw + 1; w0 <= w_last && ready; w0 += 32) {
+        int ok = 1;
+        if (w0 + lane <= w_last) ok = wait_flag_bounded(p.flags + w0 + lane, p.epoch);
+        ready = __all_sync(kFull, ok);
+    }
     __syncwarp();
     if (!ready) {
         if (lane == 0) atomicExch(p.err, 1);
@@ -915,8 +919,18 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
     l += __shfl_xor_sync(kFull, l, 2);
     if (g < G) {
         const size_t GD = (size_t)G * D;
+        // Loads are issued U partials at a time (indices past w_last clamp to
+        // it and get weight 0), so a merge of many pieces pays one L2 round
+        // trip per U partials; partials still combine in warp order.
+        constexpr int U = D == 64 ? 4 : 2;
         float M = m_run;
-        for (int w = gw + 1; w <= w_last; ++w) M = fmaxf(M, __ldcg(p.part_ml + ((size_t)w * G + g) * 2));
+        for (int w = gw + 1; w <= w_last; w += 4) {
+            float mm[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) mm[u] = __ldcg(p.part_ml + ((size_t)min(w + u, w_last) * G + g) * 2);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) M = fmaxf(M, mm[u]);
+        }
         const float own = ex2(m_run - M);
         float L = l * own;
         float acc[NT][2];
@@ -925,15 +939,27 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
             acc[nt][0] = (o[nt][0] + o[nt][2]) * own;
             acc[nt][1] = (o[nt][1] + o[nt][3]) * own;
         }
-        for (int w = gw + 1; w <= w_last; ++w) {
-            const float sw = ex2(__ldcg(p.part_ml + ((size_t)w * G + g) * 2) - M);
-            L += __ldcg(p.part_ml + ((size_t)w * G + g) * 2 + 1) * sw;
-            const float* po = p.part_o + (size_t)w * GD + (size_t)g * D + 2 * t4;
+        for (int w = gw + 1; w <= w_last; w += U) {
+            float pm[U], pl[U];
+            float2 v2[U][NT];
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const float2 v2 = __ldcg(reinterpret_cast<const float2*>(po + nt * 8));
-                acc[nt][0] += v2.x * sw;
-                acc[nt][1] += v2.y * sw;
+            for (int u = 0; u < U; ++u) {
+                const size_t ww = (size_t)min(w + u, w_last);
+                pm[u] = __ldcg(p.part_ml + (ww * G + g) * 2);
+                pl[u] = __ldcg(p.part_ml + (ww * G + g) * 2 + 1);
+                const float* po = p.part_o + ww * GD + (size_t)g * D + 2 * t4;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) v2[u][nt] = __ldcg(reinterpret_cast<const float2*>(po + nt * 8));
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const float sw = w + u <= w_last ? ex2(pm[u] - M) : 0.f;
+                L += pl[u] * sw;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    acc[nt][0] += v2[u][nt].x * sw;
+                    acc[nt][1] += v2[u][nt].y * sw;
+                }
             }
         }
         if (dc.skip > 0) fold_prefix<D>(p, dc.tok, dc.h, g, t4, M, L, acc);

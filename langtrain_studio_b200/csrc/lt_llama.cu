@@ -390,8 +390,8 @@ cudaError_t launch_argmax(const float* x, int n, int cols, int32_t* idx, cudaStr
 // ---------------------------------------------------------------------------
 // Decode matmul: q8_gemv_kernel, for n <= 8 tokens and cols % 256 == 0.
 //
-// One CTA owns 16 weight rows.  Thread 0 bulk-copies the rows and their f16
-// scales into shared memory (cp.async.bulk, one mbarrier) before the CTA
+// One CTA owns 16 weight rows.  Lanes 0-15 bulk-copy one row each and its
+// f16 scales into shared memory (cp.async.bulk, one mbarrier) before the CTA
 // waits for the kernel that produced its activations (programmatic
 // dependent launch: griddepcontrol), so the weight stream of this matmul
 // overlaps the tail of the previous kernel.  The activation prologue is fused:
@@ -559,19 +559,21 @@ __global__ void __launch_bounds__(kGvThreads) q8_gemv_kernel(const __grid_consta
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
                      "r"((uint32_t)(16 * (a.cols + nb * 2)))
                      : "memory");
-        for (int r = 0; r < 16; r++) {
-            const int rr = min(r0 + r, a.rows - 1);
-            asm volatile(
-                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                    smem_u32(sm + L.off_w + (size_t)r * L.pitch)),
-                "l"(a.wq + (size_t)rr * a.cols), "r"((uint32_t)a.cols), "r"(bar)
-                : "memory");
-            asm volatile(
-                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                    smem_u32(sm + L.off_ws + (size_t)r * L.ws_pitch)),
-                "l"(a.ws + (size_t)rr * nb), "r"((uint32_t)(nb * 2)), "r"(bar)
-                : "memory");
-        }
+    }
+    __syncwarp();
+    if (tid < 16) {  // one lane per weight row: the 32 copies are issued side by side
+        const int r = tid;
+        const int rr = min(r0 + r, a.rows - 1);
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                smem_u32(sm + L.off_w + (size_t)r * L.pitch)),
+            "l"(a.wq + (size_t)rr * a.cols), "r"((uint32_t)a.cols), "r"(bar)
+            : "memory");
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                smem_u32(sm + L.off_ws + (size_t)r * L.ws_pitch)),
+            "l"(a.ws + (size_t)rr * nb), "r"((uint32_t)(nb * 2)), "r"(bar)
+            : "memory");
     }
     pdl_trigger_and_wait();  // activations come from the previous kernel
     int8_t* xq_s = reinterpret_cast<int8_t*>(sm + L.off_xq);
