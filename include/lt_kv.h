@@ -52,8 +52,10 @@ typedef enum lt_status {
     LT_E_NCCL = 5,        /* an NCCL call failed                                */
     LT_E_TIMEOUT = 6,     /* a bounded device wait gave up (kernel error flag)  */
     LT_E_UNSUPPORTED = 7, /* shape outside what the kernels implement           */
-    LT_E_SCRATCH = 8      /* request too large for lt_paged_attend_noalloc's
+    LT_E_SCRATCH = 8,     /* request too large for lt_paged_attend_noalloc's
                              fixed scratch (see LT_NOALLOC_*)                   */
+    LT_E_BOUNDS = 9       /* a device block table named a block outside the
+                             pool (only LT_FEATURE_BOUNDS_CHECK builds test)    */
 } lt_status;
 
 typedef enum lt_dtype {
@@ -189,8 +191,31 @@ lt_status lt_kv_rows(lt_kv* kv, uint32_t layer, uint32_t seq, uint32_t n, void* 
                      void* stream);
 
 /* Reads (and clears) the device error flag set by bounded waits in the
- * kernels; synchronises `stream`.  LT_OK or LT_E_TIMEOUT / LT_E_CUDA. */
+ * kernels; synchronises `stream`.  LT_OK or LT_E_TIMEOUT / LT_E_CUDA, or
+ * LT_E_BOUNDS from a bounds-checked build. */
 lt_status lt_kv_check(lt_kv* kv, void* stream);
+
+/* ---- failure paths and debug builds ---------------------------------------
+ * No counterpart in the reference, whose path has no device code.  Every
+ * device wait in these kernels (pipeline barriers, the stream-K merge's
+ * neighbour flags) is bounded: when its limit runs out the kernel raises the
+ * handle's error flag and returns instead of hanging, and lt_kv_check reports
+ * LT_E_TIMEOUT. */
+
+/* Failure-path self-test: one warp waits, through the same bounded flag
+ * wait as the attention merge, for a device word that nothing ever sets,
+ * with a limit of limit_us microseconds (1 .. 2,000,000).  When the limit
+ * runs out the error flag is raised; the next lt_kv_check returns
+ * LT_E_TIMEOUT and clears it, and the handle stays usable.  Asynchronous on
+ * `stream`. */
+lt_status lt_kv_selftest_wait(lt_kv* kv, uint32_t limit_us, void* stream);
+
+/* Build features of the loaded library.  LT_FEATURE_BOUNDS_CHECK: compiled
+ * with -DLT_BOUNDS_CHECK (liblt_kv_checked.so): every block id the kernels
+ * read from a device table is tested against the pool; a bad one raises
+ * LT_E_BOUNDS at the next lt_kv_check and block 0 is read in its place. */
+#define LT_FEATURE_BOUNDS_CHECK 1u
+uint32_t lt_kv_build_features(void);
 
 /* ---- introspection (parity checks, debugging) ---------------------------- */
 

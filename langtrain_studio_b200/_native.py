@@ -3,15 +3,20 @@
 This is the same binding a Python host of the reference would write; the
 Rust host binds the same symbols through `extern "C"`.
 There is no fallback: if the library cannot be loaded or built, import fails.
+LT_KV_VARIANT=checked|asan loads a debug build of the same sources instead
+(see build.py).
 """
 from __future__ import annotations
 
 import ctypes as C
+import os
 import threading
 
 from . import build as _build
 
-LT_OK, LT_E_FULL, LT_E_NONCONTIG, LT_E_ARG, LT_E_CUDA, LT_E_NCCL, LT_E_TIMEOUT, LT_E_UNSUPPORTED, LT_E_SCRATCH = range(9)
+(LT_OK, LT_E_FULL, LT_E_NONCONTIG, LT_E_ARG, LT_E_CUDA, LT_E_NCCL, LT_E_TIMEOUT, LT_E_UNSUPPORTED, LT_E_SCRATCH,
+ LT_E_BOUNDS) = range(10)
+LT_FEATURE_BOUNDS_CHECK = 1
 LT_NOALLOC_SCRATCH_BYTES = 8 << 20
 LT_NOALLOC_MAX_TOKENS = 1024
 LT_F32, LT_F16 = 0, 1
@@ -26,7 +31,7 @@ EXPORTS = (
     "lt_kv_seq_blocks", "lt_kv_refs", "lt_kv_free_list", "lt_kv_n_blocks", "lt_kv_device_pool",
     "lt_kv_device_tables", "lt_kv_read_pool", "lt_kv_launch_count", "lt_kv_profile", "lt_kv_profile_read",
     "lt_kv_nccl_unique_id", "lt_kv_nccl_init", "lt_kv_nccl_destroy", "lt_kv_gather_heads",
-    "lt_paged_attend_noalloc", "lt_kv_set_min_tiles_per_warp", "lt_kv_set_cascade", "lt_kv_cascade_launches",
+    "lt_paged_attend_noalloc", "lt_kv_selftest_wait", "lt_kv_build_features", "lt_kv_set_min_tiles_per_warp", "lt_kv_set_cascade", "lt_kv_cascade_launches",
     "lt_llama_create", "lt_llama_destroy", "lt_llama_last_error", "lt_llama_set_tensor", "lt_llama_forward",
     "lt_llama_step_greedy", "lt_llama_launch_count", "lt_llama_profile", "lt_llama_profile_read", "lt_q8_quantize", "lt_q8_matmul", "lt_rms_norm_q8",
     "lt_silu_q8", "lt_argmax_f32", "lt_q8_project", "lt_q8_check",
@@ -110,6 +115,8 @@ def _declare(L):
         "lt_kv_flush": (st, [p, p]),
         "lt_kv_rows": (st, [p, u32, u32, u32, p, p, p]),
         "lt_kv_check": (st, [p, p]),
+        "lt_kv_selftest_wait": (st, [p, u32, p]),
+        "lt_kv_build_features": (u32, []),
         "lt_kv_seq_blocks": (u32, [p, u32, p, u32]),
         "lt_kv_refs": (u32, [p, p, u32]),
         "lt_kv_free_list": (u32, [p, p, u32]),
@@ -157,12 +164,17 @@ def _declare(L):
         f.argtypes = args
 
 
+def variant() -> str:
+    """The library variant this process loads (LT_KV_VARIANT, default release)."""
+    return os.environ.get("LT_KV_VARIANT", "release") or "release"
+
+
 def lib():
     """Load liblt_kv.so (building it with nvcc first if it is missing or stale)."""
     global _lib
     with _lock:
         if _lib is None:
-            path = _build.build()
+            path = _build.build(variant=variant())
             L = C.CDLL(str(path))
             _declare(L)
             _lib = L
@@ -170,4 +182,4 @@ def lib():
 
 
 def library_path() -> str:
-    return str(_build.LIB)
+    return str(_build.library(variant()))

@@ -3,6 +3,16 @@
 The library is the product: C++ host bookkeeping + sm_100a CUDA kernels
 behind the C ABI declared in include/lt_kv.h.  It is built into
 langtrain_studio_b200/lib/ so it travels with the source tree.
+
+Two debug variants of the same sources sit beside it:
+  checked  liblt_kv_checked.so  -DLT_BOUNDS_CHECK: the kernels test every
+           block id they read from a device table against the pool and
+           report a bad one (LT_E_BOUNDS) instead of reading outside it;
+  asan     liblt_kv_asan.so     host code under AddressSanitizer and
+           UndefinedBehaviorSanitizer (the C++ bookkeeping, scheduler and
+           ABI glue); load it into a process started with libasan preloaded.
+The environment variable LT_KV_VARIANT (release | checked | asan) picks the
+one langtrain_studio_b200._native loads.
 """
 from __future__ import annotations
 
@@ -17,6 +27,13 @@ CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "liblt_kv.so"
+VARIANTS = {
+    "release": (LIB, []),
+    "checked": (LIB_DIR / "liblt_kv_checked.so", ["-DLT_BOUNDS_CHECK"]),
+    "asan": (LIB_DIR / "liblt_kv_asan.so",
+             ["-Xcompiler", "-fsanitize=address,-fsanitize=undefined,-fno-omit-frame-pointer,-fno-sanitize-recover=all",
+              "-lasan", "-lubsan"]),
+}
 
 SOURCES = [CSRC / "lt_kv_kernels.cu", CSRC / "lt_kv.cpp", CSRC / "lt_kv_nccl.cpp", CSRC / "lt_kv_noalloc.cu",
            CSRC / "lt_llama.cu", CSRC / "lt_sched.cpp"]
@@ -34,27 +51,38 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found: the CUDA toolkit is required to build liblt_kv.so")
 
 
-def stale() -> bool:
-    if not LIB.exists():
+def library(variant: str = "release") -> Path:
+    if variant not in VARIANTS:
+        raise ValueError(f"unknown library variant {variant!r} (one of {sorted(VARIANTS)})")
+    return VARIANTS[variant][0]
+
+
+def stale(variant: str = "release") -> bool:
+    lib = library(variant)
+    if not lib.exists():
         return True
-    t = LIB.stat().st_mtime
+    t = lib.stat().st_mtime
     return any(p.stat().st_mtime > t for p in SOURCES + HEADERS + [Path(__file__)])
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile liblt_kv.so if it is missing or older than its sources."""
-    if not force and not stale():
-        return LIB
+def build(force: bool = False, verbose: bool = False, variant: str = "release") -> Path:
+    """Compile the library variant if it is missing or older than its sources."""
+    lib = library(variant)
+    if not force and not stale(variant):
+        return lib
     LIB_DIR.mkdir(exist_ok=True)
-    tmp = LIB.with_suffix(".so.tmp%d" % os.getpid())
-    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-o", str(tmp),
+    tmp = lib.with_suffix(".so.tmp%d" % os.getpid())
+    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *VARIANTS[variant][1], "-I", str(INCLUDE), "-I", str(CSRC), "-o", str(tmp),
            *map(str, SOURCES)]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force=True, verbose=True))
+    import sys
+
+    for v in sys.argv[1:] or ["release"]:
+        print(build(force=True, verbose=True, variant=v))

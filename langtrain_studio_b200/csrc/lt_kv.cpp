@@ -229,7 +229,8 @@ lt_status run_plan(lt_kv* kv, const std::vector<int2>& copies, const std::vector
         LT_CUDA(kv, cudaMemcpyAsync(kv->slots[s].dev, h, (nc + nt) * sizeof(int2), cudaMemcpyHostToDevice, st));
         const int2* d = static_cast<const int2*>(kv->slots[s].dev);
         LT_CUDA(kv, ltkv::launch_apply_plan(kv->d_pool, kv->layer_elems, kv->block_elems, (int)kv->cfg.n_layers, d,
-                                            (int)nc, kv->d_tables, d + nc, (int)nt, st));
+                                            (int)nc, kv->d_tables, d + nc, (int)nt, (int)kv->n_blocks,
+                                            (long long)kv->cfg.max_seqs * kv->max_blocks, kv->d_err, st));
         kv->launches++;
         lt_status rc = mark_slot_use(kv, s, st);
         if (rc) return rc;
@@ -533,6 +534,7 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     p.pool_layer_w = kv->d_pool + (size_t)layer * kv->layer_elems;
     p.tables = kv->d_tables;
     p.max_blocks = (int32_t)kv->max_blocks;
+    p.n_blocks = (int32_t)kv->n_blocks;
     p.n_tok = (int32_t)n;
     p.tiles_per_head = (int32_t)tiles;
     // At least min_tiles_per_warp tiles a warp: a small step (few tokens, short
@@ -593,6 +595,7 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
         pp.pool_layer = p.pool_layer;
         pp.tables = kv->d_tables;
         pp.max_blocks = (int32_t)kv->max_blocks;
+        pp.n_blocks = (int32_t)kv->n_blocks;
         pp.items = static_cast<const ltkv::PrefixItem*>(d_casc);
         pp.tok_list = static_cast<const int32_t*>(d_casc) + (size_t)n_items * (sizeof(ltkv::PrefixItem) / 4);
         pp.n_kv_heads = (int32_t)kv->cfg.n_kv_heads;
@@ -752,6 +755,7 @@ uint32_t lt_kv_n_blocks(const lt_kv* kv) { return kv->n_blocks; }
 
 lt_status lt_kv_append(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n, int32_t* block_out,
                        int32_t* slot_out, uint32_t* n_done, void* stream) {
+    ltkv::NvtxRange nv("lt_kv_append");
     if (!kv) return LT_E_ARG;
     DeviceGuard g(kv->dev ? kv->cfg.device : -1);
     uint32_t i = 0;
@@ -766,6 +770,7 @@ lt_status lt_kv_append(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint
 
 lt_status lt_kv_write(lt_kv* kv, uint32_t layer, const int32_t* block, const int32_t* slot, uint32_t n,
                       const void* k, const void* v, lt_dtype dtype, void* stream) {
+    ltkv::NvtxRange nv("lt_kv_write");
     if (!kv) return LT_E_ARG;
     lt_status rc = require_device(kv);
     if (rc) return rc;
@@ -789,6 +794,7 @@ lt_status lt_kv_write(lt_kv* kv, uint32_t layer, const int32_t* block, const int
 
 lt_status lt_kv_attend(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype, const uint32_t* seq,
                        const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale, void* stream) {
+    ltkv::NvtxRange nv("lt_kv_attend");
     if (!kv) return LT_E_ARG;
     lt_status rc = require_device(kv);
     if (rc) return rc;
@@ -803,6 +809,7 @@ lt_status lt_kv_write_attend(lt_kv* kv, uint32_t layer, const int32_t* block, co
                              const void* v, lt_dtype kv_dtype, const void* q, lt_dtype q_dtype, const uint32_t* seq,
                              const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale,
                              void* stream) {
+    ltkv::NvtxRange nv("lt_kv_write_attend");
     if (!kv) return LT_E_ARG;
     lt_status rc = require_device(kv);
     if (rc) return rc;
@@ -855,6 +862,7 @@ void lt_kv_share(lt_kv* kv, uint32_t src, uint32_t dst, uint32_t len) {  // kv.r
 }
 
 lt_status lt_kv_compact(lt_kv* kv, uint32_t* n_moved, void* stream) {
+    ltkv::NvtxRange nv("lt_kv_compact");
     if (!kv) return LT_E_ARG;
     DeviceGuard g(kv->dev ? kv->cfg.device : -1);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -922,7 +930,7 @@ lt_status lt_kv_rows(lt_kv* kv, uint32_t layer, uint32_t seq, uint32_t n, void* 
     LT_CUDA(kv, ltkv::launch_rows(kv->d_pool + (size_t)layer * kv->layer_elems,
                                   kv->d_tables + (size_t)seq * kv->max_blocks, (int)n, (int)kv->cfg.n_kv_heads,
                                   (int)kv->cfg.head_dim, static_cast<uint16_t*>(k_out), static_cast<uint16_t*>(v_out),
-                                  kv->q8, st));
+                                  kv->q8, (int)kv->n_blocks, kv->d_err, st));
     kv->launches++;
     return LT_OK;
 }
@@ -935,13 +943,29 @@ lt_status lt_kv_check(lt_kv* kv, void* stream) {
     int32_t flag = 0;
     LT_CUDA(kv, cudaMemcpy(&flag, kv->d_err, sizeof flag, cudaMemcpyDeviceToHost));
     if (flag) {
-        // A timed-out work item leaves its (token, head) counter behind.
         LT_CUDA(kv, cudaMemset(kv->d_err, 0, sizeof(int32_t)));
         LT_CUDA(kv, cudaDeviceSynchronize());
+        if (flag & ltkv::kErrBounds)
+            return fail(kv, LT_E_BOUNDS, "a device block table named a block outside the pool (access redirected "
+                                         "to block 0); the affected outputs are invalid");
         return fail(kv, LT_E_TIMEOUT, "a bounded device wait timed out; the affected outputs are invalid");
     }
     return LT_OK;
 }
+
+lt_status lt_kv_selftest_wait(lt_kv* kv, uint32_t limit_us, void* stream) {
+    if (!kv) return LT_E_ARG;
+    lt_status rc = require_device(kv);
+    if (rc) return rc;
+    if (limit_us == 0 || limit_us > 2000000u)
+        return fail(kv, LT_E_ARG, "selftest_wait: limit %u us outside [1, 2000000]", limit_us);
+    DeviceGuard g(kv->cfg.device);
+    LT_CUDA(kv, ltkv::launch_wait_selftest((uint64_t)limit_us * 1000u, kv->d_err, static_cast<cudaStream_t>(stream)));
+    kv->launches++;
+    return LT_OK;
+}
+
+uint32_t lt_kv_build_features(void) { return ltkv::bounds_checked_build() ? LT_FEATURE_BOUNDS_CHECK : 0u; }
 
 uint32_t lt_kv_seq_blocks(const lt_kv* kv, uint32_t seq, int32_t* out, uint32_t cap) {
     if (!kv || seq >= kv->cfg.max_seqs) return 0;

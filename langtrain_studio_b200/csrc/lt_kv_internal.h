@@ -2,12 +2,18 @@
 // kernels (lt_kv_kernels.cu).  Not part of the C ABI.
 #pragma once
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 
 namespace ltkv {
 
 constexpr int kBlock = 16;           // tokens per block (kv.rs:13)
 constexpr int kMaxGroup = 8;         // q heads per KV head the attention kernel handles
+
+// Bits of the device error word (lt_kv_check turns them into statuses).
+constexpr int32_t kErrTimeout = 1;   // a bounded wait gave up -> LT_E_TIMEOUT
+constexpr int32_t kErrBounds = 2;    // a table entry named no block of the pool -> LT_E_BOUNDS
+                                     // (only builds with LT_BOUNDS_CHECK test for it)
 
 // Per-token input of one attention launch: the token's sequence, its
 // position (it attends over blocks [0, pos/16]), the physical id of its last
@@ -25,6 +31,7 @@ struct AttnParams {
     uint16_t* pool_layer_w;      // same, for the fused append
     int32_t* tables;             // [max_seqs][max_blocks]; each token's last entry is (re)written
     int32_t max_blocks;
+    int32_t n_blocks;            // blocks in the pool, for LT_BOUNDS_CHECK builds (0: not checked)
     const TokenDesc* toks;       // n_tok entries in global memory, or null: use inl
     int32_t n_tok;
     int32_t tiles_per_head;      // prefix of n_tok (total blocks over the tokens)
@@ -71,6 +78,7 @@ struct PrefixParams {
     const uint16_t* pool_layer;
     const int32_t* tables;
     int32_t max_blocks;
+    int32_t n_blocks;  // blocks in the pool, for LT_BOUNDS_CHECK builds (0: not checked)
     const PrefixItem* items;
     const int32_t* tok_list;  // token indices of the call (into q, pre_o, pre_ml)
     int32_t n_kv_heads, group;
@@ -101,13 +109,23 @@ cudaError_t launch_write(uint16_t* pool_layer, const int2* cells, int n, int n_k
                          const void* k, const void* v, int in_f32, int q8, cudaStream_t s);
 
 // Block copies (copy-on-write and compaction moves) and table scatter.
-// copies: (src, dst) pairs; tw: (flat table index, value) pairs.
+// copies: (src, dst) pairs; tw: (flat table index, value) pairs.  n_blocks
+// and n_entries (pool blocks, table entries) bound the indices in
+// LT_BOUNDS_CHECK builds, which report a bad one through err.
 cudaError_t launch_apply_plan(uint16_t* pool, size_t layer_stride_elems, size_t block_elems, int n_layers,
                               const int2* copies, int n_copies, int32_t* tables, const int2* tw, int n_tw,
-                              cudaStream_t s);
+                              int n_blocks, long long n_entries, int32_t* err, cudaStream_t s);
 
 cudaError_t launch_rows(const uint16_t* pool_layer, const int32_t* table_row, int n, int n_kv_heads,
-                        int head_dim, uint16_t* k_out, uint16_t* v_out, int q8, cudaStream_t s);
+                        int head_dim, uint16_t* k_out, uint16_t* v_out, int q8, int n_blocks, int32_t* err,
+                        cudaStream_t s);
+
+// One warp waits, through the kernels' bounded flag wait with a limit of
+// limit_ns, for a device word that nothing sets, then raises kErrTimeout in
+// err: the failure path of every bounded wait, made to run out on purpose.
+cudaError_t launch_wait_selftest(uint64_t limit_ns, int32_t* err, cudaStream_t s);
+// Whether this build checks table entries on the device (LT_BOUNDS_CHECK).
+bool bounds_checked_build();
 
 }  // namespace ltkv
 
@@ -119,4 +137,16 @@ size_t local_out_row_bytes(const lt_kv* kv, int dtype);  // n_heads*head_dim*ele
 int handle_device(const lt_kv* kv);
 const lt_kv_config* handle_config(const lt_kv* kv);
 void count_launch(lt_kv* kv);
+}  // namespace ltkv
+
+namespace ltkv {
+// NVTX range over one C ABI call, named after it, so a timeline from a
+// profiler shows the host bookkeeping and launches of each call.  With no
+// profiler attached the push/pop cost one test of a null pointer each.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
 }  // namespace ltkv

@@ -104,15 +104,33 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     return v;
 }
 
-// Wait until *flag == epoch, giving up after kWaitLimitNs.
-__device__ __forceinline__ int wait_flag_bounded(const uint32_t* flag, uint32_t epoch) {
+// Wait until *flag == epoch, giving up after limit_ns.
+__device__ __forceinline__ int wait_flag_bounded(const uint32_t* flag, uint32_t epoch,
+                                                 uint64_t limit_ns = kWaitLimitNs) {
     if (ld_acquire_gpu(flag) == epoch) return 1;
     const uint64_t t0 = global_ns();
     for (;;) {
         __nanosleep(64);
         if (ld_acquire_gpu(flag) == epoch) return 1;
-        if (global_ns() - t0 > kWaitLimitNs) return 0;
+        if (global_ns() - t0 > limit_ns) return 0;
     }
+}
+
+// A block id read from a block table.  Builds with LT_BOUNDS_CHECK test it
+// against the pool (n_blocks > 0): a bad id raises kErrBounds and block 0
+// stands in for it, so the access stays inside the pool and only the
+// output is wrong (and reported).  Other builds trust the host bookkeeping.
+__device__ __forceinline__ int checked_block(int b, int n_blocks, int32_t* err) {
+#ifdef LT_BOUNDS_CHECK
+    if (n_blocks > 0 && (unsigned)b >= (unsigned)n_blocks) {
+        atomicOr(err, kErrBounds);
+        return 0;
+    }
+#else
+    (void)n_blocks;
+    (void)err;
+#endif
+    return b;
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -654,7 +672,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
         const int bb = b + lane;
         if (bb >= r.b1) return 0;
         if (bb == r.b1 - 1 && r.last_block >= 0) return r.last_block;
-        return __ldg(p.tables + (size_t)r.seq * p.max_blocks + r.skip + bb);
+        return checked_block(__ldg(p.tables + (size_t)r.seq * p.max_blocks + r.skip + bb), p.n_blocks, p.err);
     };
 
     // ---- issuer state ----
@@ -890,7 +908,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
     if (!ok) {
         // bounded drain of the copies still in flight, then report
         for (int jj = consumed + 1; jj < issued; ++jj) mbar_wait_bounded(bar0 + 8u * (jj % S), (jj / S) & 1);
-        if (lane == 0) atomicExch(p.err, 1);
+        if (lane == 0) atomicOr(p.err, kErrTimeout);
     }
     // Publish: every partial this warp wrote is visible before its flag.
     __syncwarp();
@@ -911,7 +929,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
     }
     __syncwarp();
     if (!ready) {
-        if (lane == 0) atomicExch(p.err, 1);
+        if (lane == 0) atomicOr(p.err, kErrTimeout);
         return;
     }
     float l = l_run;
@@ -1155,7 +1173,7 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
         const int nblk = step_blocks(j);
 #pragma unroll
         for (int bb = 0; bb < kPreStepBlocks; ++bb)
-            ids[bb] = bb < nblk ? __ldg(trow + j * kPreStepBlocks + bb) : 0;
+            ids[bb] = bb < nblk ? checked_block(__ldg(trow + j * kPreStepBlocks + bb), p.n_blocks, p.err) : 0;
     };
     auto issue_step = [&](int j, const int (&ids)[kPreStepBlocks]) {
         const int st = j % kPreStages;
@@ -1245,7 +1263,7 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
                 // bounded drain of the copies still in flight, then report
                 for (int jj = 0; jj < issued; ++jj)
                     mbar_wait_bounded(kv_full + 8u * (jj % kPreStages), (jj / kPreStages) & 1);
-                atomicExch(p.err, 1);
+                atomicOr(p.err, kErrTimeout);
             }
         }
     } else if (warp == 4) {
@@ -1299,7 +1317,7 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
                 issue_pv(j);
                 if (j + 2 < n_steps && !(ok = issue_s(j + 2))) { j_fail = j; break; }
             }
-            if (!ok) atomicExch(p.err, 1);
+            if (!ok) atomicOr(p.err, kErrTimeout);
         }
     } else {
         // ===== softmax warps: thread r owns query row r (TMEM lane r) =====
@@ -1410,7 +1428,7 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
                 p.pre_ml[row * 2 + 1] = l_run;
             }
         } else if (lane == 0) {
-            atomicExch(p.err, 1);
+            atomicOr(p.err, kErrTimeout);
         }
     }
     tc_fence_before();
@@ -1428,11 +1446,17 @@ __global__ void __launch_bounds__(256) apply_plan_kernel(uint16_t* __restrict__ 
                                                          size_t block_elems, int n_layers,
                                                          const int2* __restrict__ copies, int n_copies,
                                                          int32_t* __restrict__ tables, const int2* __restrict__ tw,
-                                                         int n_tw) {
+                                                         int n_tw, int n_blocks, long long n_entries, int32_t* err) {
     const int n_copy_ctas = n_copies * n_layers;
     if ((int)blockIdx.x < n_copy_ctas) {
         const int ci = blockIdx.x / n_layers, l = blockIdx.x % n_layers;
         const int2 cp = copies[ci];
+#ifdef LT_BOUNDS_CHECK
+        if ((unsigned)cp.x >= (unsigned)n_blocks || (unsigned)cp.y >= (unsigned)n_blocks) {
+            if (threadIdx.x == 0) atomicOr(err, kErrBounds);
+            return;
+        }
+#endif
         const uint4* src = reinterpret_cast<const uint4*>(pool + (size_t)l * layer_stride + (size_t)cp.x * block_elems);
         uint4* dst = reinterpret_cast<uint4*>(pool + (size_t)l * layer_stride + (size_t)cp.y * block_elems);
         // 8 independent 16-byte loads in flight per thread before their stores
@@ -1451,9 +1475,27 @@ __global__ void __launch_bounds__(256) apply_plan_kernel(uint16_t* __restrict__ 
         const int i = (blockIdx.x - n_copy_ctas) * blockDim.x + threadIdx.x;
         if (i < n_tw) {
             const int2 w = tw[i];
+#ifdef LT_BOUNDS_CHECK
+            if (w.x < 0 || w.x >= n_entries || w.y >= n_blocks) {
+                atomicOr(err, kErrBounds);
+                return;
+            }
+#endif
             tables[w.x] = w.y;
         }
     }
+}
+
+// ---------------------------------------------------------- selftest ----
+// A word that no code ever sets: the failure-path self-test waits on it.
+__device__ uint32_t g_never_set;
+
+// Lane 0 waits for g_never_set == 1 through the same bounded flag wait the
+// attention merge uses, with the caller's limit; when the limit runs out it
+// raises kErrTimeout and the kernel returns, leaving the context usable.
+__global__ void wait_selftest_kernel(uint64_t limit_ns, int32_t* err) {
+    if (threadIdx.x != 0) return;
+    if (!wait_flag_bounded(&g_never_set, 1u, limit_ns)) atomicOr(err, kErrTimeout);
 }
 
 // ---------------------------------------------------------- gather ----
@@ -1472,7 +1514,8 @@ __global__ void __launch_bounds__(256) gather_permute_kernel(const uint4* __rest
 template <int D>
 __global__ void __launch_bounds__(256) rows_kernel(const uint16_t* __restrict__ pool_layer,
                                                    const int32_t* __restrict__ trow, int n, int n_kv_heads,
-                                                   uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out) {
+                                                   uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out,
+                                                   int n_blocks, int32_t* err) {
     constexpr int CH = D / 8;
     const int gid = blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= n * n_kv_heads * 2 * CH) return;
@@ -1482,7 +1525,7 @@ __global__ void __launch_bounds__(256) rows_kernel(const uint16_t* __restrict__ 
     r >>= 1;
     const int h = r % n_kv_heads;
     const int pos = r / n_kv_heads;
-    const int b = trow[pos / kBlock], slot = pos % kBlock;
+    const int b = checked_block(trow[pos / kBlock], n_blocks, err), slot = pos % kBlock;
     const uint16_t* src = pool_layer + (((size_t)b * n_kv_heads + h) * 2 + kvsel) * (kBlock * D) + chunk_off(c, slot);
     uint16_t* dst = (kvsel ? v_out : k_out) + (size_t)pos * n_kv_heads * D + (size_t)h * D + (size_t)c * 8;
     *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
@@ -1492,7 +1535,8 @@ __global__ void __launch_bounds__(256) rows_kernel(const uint16_t* __restrict__ 
 template <int D>
 __global__ void __launch_bounds__(256) rows_q8_kernel(const uint8_t* __restrict__ pool_layer,
                                                       const int32_t* __restrict__ trow, int n, int n_kv_heads,
-                                                      uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out) {
+                                                      uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out,
+                                                      int n_blocks, int32_t* err) {
     constexpr int CH = D / 8;
     const int gid = blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= n * n_kv_heads * 2 * CH) return;
@@ -1502,7 +1546,7 @@ __global__ void __launch_bounds__(256) rows_q8_kernel(const uint8_t* __restrict_
     r >>= 1;
     const int h = r % n_kv_heads;
     const int pos = r / n_kv_heads;
-    const int b = trow[pos / kBlock], slot = pos % kBlock;
+    const int b = checked_block(trow[pos / kBlock], n_blocks, err), slot = pos % kBlock;
     const uint8_t* tile = pool_layer + ((size_t)b * n_kv_heads + h) * q8_tile_bytes(D);
     const float d = __half2float(__ushort_as_half(
         *reinterpret_cast<const uint16_t*>(tile + (kvsel ? 33 : 32) * D + ((c >> 2) * 16 + q8_pos(slot)) * 2)));
@@ -1648,29 +1692,42 @@ cudaError_t launch_write(uint16_t* pool_layer, const int2* cells, int n, int n_k
 
 cudaError_t launch_apply_plan(uint16_t* pool, size_t layer_stride_elems, size_t block_elems, int n_layers,
                               const int2* copies, int n_copies, int32_t* tables, const int2* tw, int n_tw,
-                              cudaStream_t s) {
+                              int n_blocks, long long n_entries, int32_t* err, cudaStream_t s) {
     const int ctas = n_copies * n_layers + (n_tw + 255) / 256;
     if (ctas == 0) return cudaSuccess;
     apply_plan_kernel<<<ctas, 256, 0, s>>>(pool, layer_stride_elems, block_elems, n_layers, copies, n_copies, tables,
-                                           tw, n_tw);
+                                           tw, n_tw, n_blocks, n_entries, err);
     return cudaGetLastError();
 }
 
 cudaError_t launch_rows(const uint16_t* pool_layer, const int32_t* table_row, int n, int n_kv_heads, int head_dim,
-                        uint16_t* k_out, uint16_t* v_out, int q8, cudaStream_t s) {
+                        uint16_t* k_out, uint16_t* v_out, int q8, int n_blocks, int32_t* err, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
     const int threads = n * n_kv_heads * 2 * (head_dim / 8);
     const int blocks = (threads + 255) / 256;
     const uint8_t* pool_bytes = reinterpret_cast<const uint8_t*>(pool_layer);
     if (q8 && head_dim == 64)
-        rows_q8_kernel<64><<<blocks, 256, 0, s>>>(pool_bytes, table_row, n, n_kv_heads, k_out, v_out);
+        rows_q8_kernel<64><<<blocks, 256, 0, s>>>(pool_bytes, table_row, n, n_kv_heads, k_out, v_out, n_blocks, err);
     else if (q8)
-        rows_q8_kernel<128><<<blocks, 256, 0, s>>>(pool_bytes, table_row, n, n_kv_heads, k_out, v_out);
+        rows_q8_kernel<128><<<blocks, 256, 0, s>>>(pool_bytes, table_row, n, n_kv_heads, k_out, v_out, n_blocks, err);
     else if (head_dim == 64)
-        rows_kernel<64><<<blocks, 256, 0, s>>>(pool_layer, table_row, n, n_kv_heads, k_out, v_out);
+        rows_kernel<64><<<blocks, 256, 0, s>>>(pool_layer, table_row, n, n_kv_heads, k_out, v_out, n_blocks, err);
     else
-        rows_kernel<128><<<blocks, 256, 0, s>>>(pool_layer, table_row, n, n_kv_heads, k_out, v_out);
+        rows_kernel<128><<<blocks, 256, 0, s>>>(pool_layer, table_row, n, n_kv_heads, k_out, v_out, n_blocks, err);
     return cudaGetLastError();
+}
+
+cudaError_t launch_wait_selftest(uint64_t limit_ns, int32_t* err, cudaStream_t s) {
+    wait_selftest_kernel<<<1, 32, 0, s>>>(limit_ns, err);
+    return cudaGetLastError();
+}
+
+bool bounds_checked_build() {
+#ifdef LT_BOUNDS_CHECK
+    return true;
+#else
+    return false;
+#endif
 }
 
 }  // namespace ltkv

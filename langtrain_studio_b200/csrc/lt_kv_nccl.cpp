@@ -85,6 +85,7 @@ void lt_kv_nccl_destroy(void* comm) {
 
 lt_status lt_kv_gather_heads(lt_kv* kv, const void* local, void* gathered, void* out, uint32_t n, lt_dtype dtype,
                              void* comm, int nranks, void* stream) {
+    ltkv::NvtxRange nv("lt_kv_gather_heads");
     if (!kv || !local || !gathered || !out || !comm || nranks < 1) return LT_E_ARG;
     NcclApi& api = nccl();
     if (!api.ok) return LT_E_NCCL;

@@ -1030,6 +1030,7 @@ lt_status lt_llama_set_tensor(lt_llama* m, lt_tensor which, uint32_t layer, cons
 
 lt_status lt_llama_forward(lt_llama* m, lt_kv* kv, const int32_t* tokens, const uint32_t* seqs, const uint32_t* pos,
                            uint32_t n, const uint32_t* want, uint32_t n_want, float* logits, void* stream) {
+    ltkv::NvtxRange nv("lt_llama_forward");
     if (!m || !kv) return LT_E_ARG;
     const lt_llama_config& c = m->cfg;
     if (n == 0) return LT_OK;

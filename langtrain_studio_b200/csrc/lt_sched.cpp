@@ -195,6 +195,7 @@ lt_status lt_sched_get_stats(const lt_sched* s, lt_sched_stats* out) {
 
 lt_status lt_sched_step(lt_sched* s, const void* kv_src, uint32_t src_rows, const void* q_src, void* out,
                         uint32_t* n_decode, void* stream) {
+    ltkv::NvtxRange nv("lt_sched_step");
     if (!s) return LT_E_ARG;
     if (s->cfg.data && (!kv_src || !q_src || !out || src_rows == 0))
         return fail(s, LT_E_ARG, "data mode needs kv_src, q_src and out");

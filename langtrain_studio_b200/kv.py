@@ -233,6 +233,11 @@ class KvCache:
         st = _stream(stream) if self.device >= 0 else C.c_void_p(0)
         self._check(self._lib.lt_kv_check(self._h, st))
 
+    def selftest_wait(self, limit_us: int, stream=None):
+        """Make one bounded device wait run out (a flag nothing sets, limit
+        `limit_us`); the next check() raises KvError(LT_E_TIMEOUT)."""
+        self._check(self._lib.lt_kv_selftest_wait(self._h, int(limit_us), _stream(stream)))
+
     def rows(self, layer: int, seq: int, n: int, stream=None):
         """K and V rows 0..n of seq (kv.rs:135-150) as f16 CUDA [n, kv_dim]."""
         import torch
