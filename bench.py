@@ -208,7 +208,7 @@ def build_cache(kv_mod, torch, device: int, lens: np.ndarray, seed: int, kv_form
 class Stepper:
     """One decode step through the public API: append + fused write/attend."""
 
-    def __init__(self, kv, lens, k, v, q, out):
+    def __init__(self, kv, lens, k, v, q, out, gather: bool = False):
         import ctypes
 
         import torch
@@ -218,11 +218,13 @@ class Stepper:
         self.k, self.v, self.q, self.out = k, v, q, out
         self.phase = 0
         self.stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        # head-sharded: the NVLink gather fused into the attention call
+        self.attend = kv.write_attend_gather if gather else kv.write_attend
 
     def step(self):
         pos = (self.lens + self.phase).astype(np.uint32)
         b, s = self.kv.append_batch(self.seqs, pos, stream=self.stream)
-        self.kv.write_attend(0, b, s, self.k, self.v, self.q, self.seqs, pos, out=self.out, stream=self.stream)
+        self.attend(0, b, s, self.k, self.v, self.q, self.seqs, pos, out=self.out, stream=self.stream)
         lens_now = self.lens + self.phase + 1
         self.phase += 1
         if self.phase == CYCLE:
@@ -511,7 +513,9 @@ def run_c4(args, rank, world, local, mode):
     heads, 8 KV heads, head_dim 128): 16 sequences of 32768 tokens.
       batch: sequences sharded across ranks (16/N each), no collective;
       head:  KV heads sharded across ranks (8/N each), bookkeeping replicated,
-             one NCCL all-gather of the per-head attention outputs per step."""
+             the per-head attention outputs gathered every step: by default
+             inside the attention call (NVLink peer stores, lt_kv_*_gather),
+             with --gather nccl by a separate NCCL all-gather + permute."""
     import datetime
 
     import torch
@@ -549,13 +553,17 @@ def run_c4(args, rank, world, local, mode):
     q = torch.randn((n_seq, my_hq * d), generator=g, device=dev, dtype=torch.float16)
     out = torch.empty_like(q)
     comm = None
-    if mode == "head" and world > 1:
+    peer = mode == "head" and world > 1 and args.gather == "peer"
+    if mode == "head" and world > 1 and not peer:
         uid = [kv_mod.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         comm = kv_mod.NcclComm(world, uid[0], rank, local)
         gathered = torch.empty((world, n_seq, my_hq * d), device=dev, dtype=torch.float16)
         full = torch.empty((n_seq, world * my_hq * d), device=dev, dtype=torch.float16)
-    st = Stepper(kv, lens, k, v, q, out)
+    if peer:
+        kv_mod.setup_peer_gather(kv, rank, world, max_tokens=n_seq)
+        out = torch.empty((n_seq, world * my_hq * d), device=dev, dtype=torch.float16)
+    st = Stepper(kv, lens, k, v, q, out, gather=peer)
 
     def step():
         lens_now = st.step()
@@ -596,16 +604,20 @@ def run_c4(args, rank, world, local, mode):
                         f"{mode}-sharded x{world}, one layer",
             "n_heads": hq, "n_kv_heads": hkv, "head_dim": d, "block_tokens": BLOCK, "kv_format": args.kv_format,
             "per_rank": {"seqs": n_seq, "kv_heads": my_hkv, "q_heads": my_hq},
-            "collective": "lt_kv_gather_heads: NCCL all-gather of [seqs, q_heads*D] f16 per step + permute"
+            "collective": ("lt_kv_write_attend_gather: outputs stored to every rank over NVLink by the attention "
+                           "kernel, flag wait + copy" if peer else
+                           "lt_kv_gather_heads: NCCL all-gather of [seqs, q_heads*D] f16 per step + permute")
             if mode == "head" and world > 1 else "none"})
         res["scaling"] = "strong" if mode == "head" else "weak"
         res["hbm_gbs_per_gpu"] = byts / args.steps / (ms / args.steps * 1e-3) / 1e9
-        res["roofline"] = {"bound": "hbm", "kernel": "paged_attn_kernel<128> + kv_combine_kernel (rank 0)",
+        res["roofline"] = {"bound": "hbm", "kernel": "paged_attn_kernel<128> (rank 0)",
                            "achieved": achieved, "peak": peak, "peak_kind": kind, "unit": "GB/s",
                            "frac": achieved / peak, "traffic": None,
                            "algorithmic_bytes_per_launch": int(byts / args.steps), "avg_launch_ms": attn_ms / attn_n}
         res["gpu_launches"] = kv.launch_count() - l0
     if world > 1:
+        if peer:
+            kv.peer_close()  # every rank unmaps the others' buffers before any is freed
         dist.barrier()
         if comm is not None:
             comm.close()
@@ -1032,6 +1044,9 @@ def main():
                     help="c2: configs[1] (default, the headline); c1: configs[0]; c3: configs[2]; "
                          "c4-*: configs[3]; c5: configs[4]")
     ap.add_argument("--c5-rate", type=float, default=32.0, help="c5: mean arrivals per step over the whole job")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="c4-head: gather the sharded heads inside the attention call over NVLink (peer) or with "
+                         "a separate NCCL all-gather (nccl)")
     ap.add_argument("--kv-format", choices=["f16", "q8_0"], default="f16",
                     help="c2 / c4-*: cached K/V format (f16: the reference's; q8_0: int8 + f16 scale per 32)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,

@@ -309,6 +309,40 @@ void lt_kv_nccl_destroy(void* comm);
 lt_status lt_kv_gather_heads(lt_kv* kv, const void* local, void* gathered, void* out, uint32_t n, lt_dtype dtype,
                              void* comm, int nranks, void* stream);
 
+/* ---- KV-head sharding with the gather fused into attention (NVLink) ------
+ * The same head-sharded decode without a collective launch: each rank's
+ * attention kernel stores every output row straight into every rank's
+ * gather buffer over NVLink (peer memory, CUDA IPC), and the launch's last
+ * warp raises this rank's flag on every rank; one small kernel per rank then
+ * waits (bounded) for all ranks' flags and copies the gathered rows to
+ * `out`.  Replaces lt_kv_attend + lt_kv_gather_heads; no counterpart in the
+ * reference (one process).  Set-up, on every rank:
+ *   1. lt_kv_peer_export: allocate this rank's gather buffer (max_tokens
+ *      tokens a call) and write its 64-byte CUDA IPC handle;
+ *   2. exchange the handles between ranks (any host transport);
+ *   3. lt_kv_peer_import with all nranks handles in rank order.
+ * Every rank then makes the same sequence of *_gather calls (the gather
+ * buffer alternates halves between calls, so a rank may run one call ahead).
+ * A rank that misses a call leaves the others' waits to run out:
+ * lt_kv_check then reports LT_E_TIMEOUT.  Tear-down: lt_kv_peer_close on
+ * every rank, a host barrier, then lt_kv_destroy (which frees the buffer the
+ * peers had mapped). */
+#define LT_IPC_HANDLE_BYTES 64
+lt_status lt_kv_peer_export(lt_kv* kv, int rank, int nranks, uint32_t max_tokens, void* ipc_handle_out);
+lt_status lt_kv_peer_import(lt_kv* kv, const void* ipc_handles /* nranks * LT_IPC_HANDLE_BYTES */);
+lt_status lt_kv_peer_close(lt_kv* kv);
+/* lt_kv_attend / lt_kv_write_attend of this rank's KV heads with the gather
+ * fused in: `out` receives [n][nranks * n_heads * head_dim], the layout of
+ * the unsharded attention (rank r's heads at [r * n_heads, (r+1) * n_heads)),
+ * as lt_kv_gather_heads produces it.  n <= max_tokens. */
+lt_status lt_kv_attend_gather(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype, const uint32_t* seq,
+                              const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale,
+                              void* stream);
+lt_status lt_kv_write_attend_gather(lt_kv* kv, uint32_t layer, const int32_t* block, const int32_t* slot,
+                                    const void* k, const void* v, lt_dtype kv_dtype, const void* q, lt_dtype q_dtype,
+                                    const uint32_t* seq, const uint32_t* pos, uint32_t n, void* out,
+                                    lt_dtype out_dtype, float scale, void* stream);
+
 /* ---- allocation-free attention ------------------------------------------- */
 
 /* No counterpart in the reference.  The same paged decode attention as

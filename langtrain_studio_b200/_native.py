@@ -17,6 +17,7 @@ from . import build as _build
 (LT_OK, LT_E_FULL, LT_E_NONCONTIG, LT_E_ARG, LT_E_CUDA, LT_E_NCCL, LT_E_TIMEOUT, LT_E_UNSUPPORTED, LT_E_SCRATCH,
  LT_E_BOUNDS) = range(10)
 LT_FEATURE_BOUNDS_CHECK = 1
+LT_IPC_HANDLE_BYTES = 64
 LT_NOALLOC_SCRATCH_BYTES = 8 << 20
 LT_NOALLOC_MAX_TOKENS = 1024
 LT_F32, LT_F16 = 0, 1
@@ -31,7 +32,8 @@ EXPORTS = (
     "lt_kv_seq_blocks", "lt_kv_refs", "lt_kv_free_list", "lt_kv_n_blocks", "lt_kv_device_pool",
     "lt_kv_device_tables", "lt_kv_read_pool", "lt_kv_launch_count", "lt_kv_profile", "lt_kv_profile_read",
     "lt_kv_nccl_unique_id", "lt_kv_nccl_init", "lt_kv_nccl_destroy", "lt_kv_gather_heads",
-    "lt_paged_attend_noalloc", "lt_kv_selftest_wait", "lt_kv_build_features", "lt_kv_set_min_tiles_per_warp", "lt_kv_set_cascade", "lt_kv_cascade_launches",
+    "lt_paged_attend_noalloc", "lt_kv_peer_export", "lt_kv_peer_import", "lt_kv_peer_close",
+    "lt_kv_attend_gather", "lt_kv_write_attend_gather", "lt_kv_selftest_wait", "lt_kv_build_features", "lt_kv_set_min_tiles_per_warp", "lt_kv_set_cascade", "lt_kv_cascade_launches",
     "lt_llama_create", "lt_llama_destroy", "lt_llama_last_error", "lt_llama_set_tensor", "lt_llama_forward",
     "lt_llama_step_greedy", "lt_llama_launch_count", "lt_llama_profile", "lt_llama_profile_read", "lt_q8_quantize", "lt_q8_matmul", "lt_rms_norm_q8",
     "lt_silu_q8", "lt_argmax_f32", "lt_q8_project", "lt_q8_check",
@@ -116,6 +118,12 @@ def _declare(L):
         "lt_kv_rows": (st, [p, u32, u32, u32, p, p, p]),
         "lt_kv_check": (st, [p, p]),
         "lt_kv_selftest_wait": (st, [p, u32, p]),
+        "lt_kv_peer_export": (st, [p, C.c_int, C.c_int, u32, p]),
+        "lt_kv_peer_import": (st, [p, p]),
+        "lt_kv_peer_close": (st, [p]),
+        "lt_kv_attend_gather": (st, [p, u32, p, C.c_int, p, p, u32, p, C.c_int, C.c_float, p]),
+        "lt_kv_write_attend_gather": (st, [p, u32, p, p, p, p, C.c_int, p, C.c_int, p, p, u32, p, C.c_int,
+                                           C.c_float, p]),
         "lt_kv_build_features": (u32, []),
         "lt_kv_seq_blocks": (u32, [p, u32, p, u32]),
         "lt_kv_refs": (u32, [p, p, u32]),

@@ -64,8 +64,28 @@ struct DeviceGuard {
 
 }  // namespace
 
+// Head-sharded gather over NVLink (lt_kv_peer_*): this rank's exported
+// buffer is [flags: u32 per rank][done counter][half 0][half 1], each half
+// [max_tokens][nranks * n_heads][head_dim] of f32 (f16 rows use half of it),
+// of which this rank writes its own heads; calls alternate halves (epoch
+// parity).  Peers' buffers are IPC mappings, read after their flags.
+struct PeerGather {
+    int rank = -1, nranks = 0;
+    uint32_t max_tokens = 0;
+    size_t half_bytes = 0;
+    unsigned char* d_buf = nullptr;                 // own allocation (exported)
+    unsigned char* base[ltkv::kMaxPeers] = {};      // every rank's buffer in this process (own: d_buf)
+    bool mapped[ltkv::kMaxPeers] = {};              // opened with cudaIpcOpenMemHandle
+    uint32_t epoch = 0;                             // gather calls so far (same on every rank)
+    bool ready = false;
+};
+constexpr size_t kPeerFlagsBytes = 256, kPeerHeaderBytes = 512;
+static_assert(sizeof(cudaIpcMemHandle_t) == LT_IPC_HANDLE_BYTES, "IPC handle size");
+static_assert(ltkv::kMaxPeers * sizeof(uint32_t) <= kPeerFlagsBytes, "peer flags");
+
 struct lt_kv {
     lt_kv_config cfg{};
+    PeerGather peer;
     uint32_t min_tiles_per_warp = 8;  // attention launch sizing (lt_kv_set_min_tiles_per_warp)
     // shared-prefix (cascade) pass: groups of >= cascade_min_tokens tokens
     // whose sequences share >= kCascadeMinBlocks leading blocks (0: off)
@@ -150,7 +170,20 @@ lt_status fail(lt_kv* kv, lt_status s, const char* fmt, ...) {
         if (e_ != cudaSuccess) return fail((kv), LT_E_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
     } while (0)
 
+void peer_unmap(lt_kv* kv) {
+    PeerGather& pg = kv->peer;
+    for (int r = 0; r < ltkv::kMaxPeers; ++r) {
+        if (pg.mapped[r]) cudaIpcCloseMemHandle(pg.base[r]);
+        pg.mapped[r] = false;
+        pg.base[r] = nullptr;
+    }
+    pg.ready = false;
+}
+
 void free_device(lt_kv* kv) {
+    peer_unmap(kv);
+    cudaFree(kv->peer.d_buf);
+    kv->peer = PeerGather{};
     cudaFree(kv->d_pool);
     cudaFree(kv->d_tables);
     cudaFree(kv->d_part_o);
@@ -471,10 +504,16 @@ int plan_cascade(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n
 
 lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype, const uint32_t* seq,
                       const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale, const void* k,
-                      const void* v, lt_dtype kv_dtype, bool fused, cudaStream_t st) {
+                      const void* v, lt_dtype kv_dtype, bool fused, cudaStream_t st, bool gather = false) {
     if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
         (k && (reinterpret_cast<uintptr_t>(k) & 15)) || (v && (reinterpret_cast<uintptr_t>(v) & 15)))
         return fail(kv, LT_E_ARG, "q, out, k and v must be 16-byte aligned device pointers");
+    if (gather) {
+        if (!kv->peer.ready) return fail(kv, LT_E_ARG, "attend_gather before lt_kv_peer_import");
+        if (n > kv->peer.max_tokens)
+            return fail(kv, LT_E_ARG, "attend_gather of %u tokens exceeds the exported max_tokens %u", n,
+                        kv->peer.max_tokens);
+    }
     if (n == 0) return flush(kv, st);
     // Per-token descriptors; the kernel derives its stream-K partition from them.
     const int q_f32 = q_dtype == LT_F32;
@@ -553,6 +592,9 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     p.part_o = kv->d_part_o;
     p.part_ml = kv->d_part_ml;
     p.flags = kv->d_flags;
+    p.part2_o = kv->d_part_o + kv->ws_slots * kv->group * kv->cfg.head_dim;
+    p.part2_ml = kv->d_part_ml + kv->ws_slots * kv->group * 2;
+    p.flags2 = kv->d_flags + kv->ws_slots;
     if (++kv->attn_epoch == 0) kv->attn_epoch = 1;  // 0 is the flags' initial value
     p.epoch = kv->attn_epoch;
     p.err = kv->d_err;
@@ -577,6 +619,20 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     p.pre_splits = n_items > 0 ? kv->casc_splits : 0;
     p.q8 = kv->q8;
     p.pre_split_rows = (int64_t)kv->pre_cap * kv->cfg.n_heads;
+    p.n_peers = 0;
+    uint32_t g_epoch = 0;
+    if (gather) {
+        PeerGather& pg = kv->peer;
+        if (++pg.epoch == 0) pg.epoch = 1;  // flags start at 0
+        g_epoch = pg.epoch;
+        p.n_peers = pg.nranks;
+        p.peer_rank = pg.rank;
+        p.peer_epoch = g_epoch;
+        p.done_count = reinterpret_cast<uint32_t*>(pg.d_buf + kPeerFlagsBytes);
+        p.gather_out = pg.d_buf + kPeerHeaderBytes + (g_epoch & 1) * pg.half_bytes;
+        for (int r = 0; r < pg.nranks; ++r) p.peer_flag[r] = reinterpret_cast<uint32_t*>(pg.base[r]) + pg.rank;
+        p.out = nullptr;
+    }
     cudaEvent_t ev_end = nullptr;
     if (kv->profiling) {
         lt_status prc = prof_begin(kv, st, &ev_end);
@@ -622,6 +678,15 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     }
     kv->launches += ltkv::attend_launches(p);
     if (ev_end) LT_CUDA(kv, cudaEventRecord(ev_end, st));
+    if (gather) {
+        const PeerGather& pg = kv->peer;
+        const size_t slice = (size_t)kv->cfg.n_heads * kv->cfg.head_dim * (out_dtype == LT_F32 ? 4 : 2);
+        void* srcs[ltkv::kMaxPeers] = {};
+        for (int r = 0; r < pg.nranks; ++r) srcs[r] = pg.base[r] + kPeerHeaderBytes + (g_epoch & 1) * pg.half_bytes;
+        LT_CUDA(kv, ltkv::launch_gather_wait_copy(reinterpret_cast<const uint32_t*>(pg.d_buf), pg.nranks, g_epoch,
+                                                  srcs, out, n, slice, kv->d_err, st));
+        kv->launches++;
+    }
     if (s_casc >= 0 && (rc = mark_slot_use(kv, s_casc, st)) != LT_OK) return rc;
     return s_plan >= 0 ? mark_slot_use(kv, s_plan, st) : LT_OK;
 }
@@ -700,11 +765,12 @@ lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
         const size_t tbytes = (size_t)c.max_seqs * kv->max_blocks * 4;
         if (rc == LT_OK) ck(cudaMalloc(&kv->d_tables, tbytes), "cudaMalloc(tables)");
         if (rc == LT_OK) ck(cudaMemset(kv->d_tables, 0, tbytes), "cudaMemset(tables)");
-        if (rc == LT_OK) ck(cudaMalloc(&kv->d_part_o, kv->ws_slots * gd * sizeof(float)), "cudaMalloc(partials)");
+        // Two sets: the warps' partials and the group partials of the two-level merge.
+        if (rc == LT_OK) ck(cudaMalloc(&kv->d_part_o, 2 * kv->ws_slots * gd * sizeof(float)), "cudaMalloc(partials)");
         if (rc == LT_OK)
-            ck(cudaMalloc(&kv->d_part_ml, kv->ws_slots * kv->group * 2 * sizeof(float)), "cudaMalloc(partials)");
-        if (rc == LT_OK) ck(cudaMalloc(&kv->d_flags, kv->ws_slots * sizeof(uint32_t) + 4), "cudaMalloc(flags)");
-        if (rc == LT_OK) ck(cudaMemset(kv->d_flags, 0, kv->ws_slots * sizeof(uint32_t) + 4), "cudaMemset(flags)");
+            ck(cudaMalloc(&kv->d_part_ml, 2 * kv->ws_slots * kv->group * 2 * sizeof(float)), "cudaMalloc(partials)");
+        if (rc == LT_OK) ck(cudaMalloc(&kv->d_flags, 2 * kv->ws_slots * sizeof(uint32_t) + 4), "cudaMalloc(flags)");
+        if (rc == LT_OK) ck(cudaMemset(kv->d_flags, 0, 2 * kv->ws_slots * sizeof(uint32_t) + 4), "cudaMemset(flags)");
         kv->pre_cap = std::min<uint32_t>(c.max_batch, kCascadeMaxTokens);
         const size_t pre_rows = (size_t)kv->pre_cap * c.n_heads * ltkv::kPreMaxSplits;
         if (rc == LT_OK) ck(cudaDeviceGetAttribute(&kv->sm_count, cudaDevAttrMultiProcessorCount, c.device),
@@ -792,9 +858,13 @@ lt_status lt_kv_write(lt_kv* kv, uint32_t layer, const int32_t* block, const int
     return mark_slot_use(kv, s, st);
 }
 
-lt_status lt_kv_attend(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype, const uint32_t* seq,
-                       const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale, void* stream) {
-    ltkv::NvtxRange nv("lt_kv_attend");
+}  // extern "C"
+
+namespace {
+
+lt_status attend_entry(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype, const uint32_t* seq,
+                       const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale, void* stream,
+                       bool gather) {
     if (!kv) return LT_E_ARG;
     lt_status rc = require_device(kv);
     if (rc) return rc;
@@ -802,14 +872,13 @@ lt_status lt_kv_attend(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtyp
     if ((rc = check_tokens(kv, seq, pos, n))) return rc;
     DeviceGuard g(kv->cfg.device);
     return attend_impl(kv, layer, q, q_dtype, seq, pos, n, out, out_dtype, scale, nullptr, nullptr, LT_F32, false,
-                       static_cast<cudaStream_t>(stream));
+                       static_cast<cudaStream_t>(stream), gather);
 }
 
-lt_status lt_kv_write_attend(lt_kv* kv, uint32_t layer, const int32_t* block, const int32_t* slot, const void* k,
+lt_status write_attend_entry(lt_kv* kv, uint32_t layer, const int32_t* block, const int32_t* slot, const void* k,
                              const void* v, lt_dtype kv_dtype, const void* q, lt_dtype q_dtype, const uint32_t* seq,
                              const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale,
-                             void* stream) {
-    ltkv::NvtxRange nv("lt_kv_write_attend");
+                             void* stream, bool gather) {
     if (!kv) return LT_E_ARG;
     lt_status rc = require_device(kv);
     if (rc) return rc;
@@ -834,11 +903,111 @@ lt_status lt_kv_write_attend(lt_kv* kv, uint32_t layer, const int32_t* block, co
     }
     if (!fusable) {
         if ((rc = lt_kv_write(kv, layer, block, slot, n, k, v, kv_dtype, stream))) return rc;
-        return lt_kv_attend(kv, layer, q, q_dtype, seq, pos, n, out, out_dtype, scale, stream);
+        return attend_entry(kv, layer, q, q_dtype, seq, pos, n, out, out_dtype, scale, stream, gather);
     }
     DeviceGuard g(kv->cfg.device);
     return attend_impl(kv, layer, q, q_dtype, seq, pos, n, out, out_dtype, scale, k, v, kv_dtype, true,
-                       static_cast<cudaStream_t>(stream));
+                       static_cast<cudaStream_t>(stream), gather);
+}
+
+}  // namespace
+
+extern "C" {
+
+lt_status lt_kv_attend(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype, const uint32_t* seq,
+                       const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale, void* stream) {
+    ltkv::NvtxRange nv("lt_kv_attend");
+    return attend_entry(kv, layer, q, q_dtype, seq, pos, n, out, out_dtype, scale, stream, false);
+}
+
+lt_status lt_kv_write_attend(lt_kv* kv, uint32_t layer, const int32_t* block, const int32_t* slot, const void* k,
+                             const void* v, lt_dtype kv_dtype, const void* q, lt_dtype q_dtype, const uint32_t* seq,
+                             const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale,
+                             void* stream) {
+    ltkv::NvtxRange nv("lt_kv_write_attend");
+    return write_attend_entry(kv, layer, block, slot, k, v, kv_dtype, q, q_dtype, seq, pos, n, out, out_dtype, scale,
+                              stream, false);
+}
+
+lt_status lt_kv_attend_gather(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype, const uint32_t* seq,
+                              const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale,
+                              void* stream) {
+    ltkv::NvtxRange nv("lt_kv_attend_gather");
+    return attend_entry(kv, layer, q, q_dtype, seq, pos, n, out, out_dtype, scale, stream, true);
+}
+
+lt_status lt_kv_write_attend_gather(lt_kv* kv, uint32_t layer, const int32_t* block, const int32_t* slot,
+                                    const void* k, const void* v, lt_dtype kv_dtype, const void* q, lt_dtype q_dtype,
+                                    const uint32_t* seq, const uint32_t* pos, uint32_t n, void* out,
+                                    lt_dtype out_dtype, float scale, void* stream) {
+    ltkv::NvtxRange nv("lt_kv_write_attend_gather");
+    return write_attend_entry(kv, layer, block, slot, k, v, kv_dtype, q, q_dtype, seq, pos, n, out, out_dtype, scale,
+                              stream, true);
+}
+
+lt_status lt_kv_peer_export(lt_kv* kv, int rank, int nranks, uint32_t max_tokens, void* ipc_handle_out) {
+    if (!kv || !ipc_handle_out) return LT_E_ARG;
+    lt_status rc = require_device(kv);
+    if (rc) return rc;
+    if (nranks < 1 || nranks > ltkv::kMaxPeers || rank < 0 || rank >= nranks || max_tokens == 0)
+        return fail(kv, LT_E_ARG, "peer_export: rank %d of %d (at most %d ranks), max_tokens %u", rank, nranks,
+                    ltkv::kMaxPeers, max_tokens);
+    DeviceGuard g(kv->cfg.device);
+    PeerGather& pg = kv->peer;
+    peer_unmap(kv);
+    LT_CUDA(kv, cudaDeviceSynchronize());
+    cudaFree(pg.d_buf);
+    pg = PeerGather{};
+    const size_t half = ((size_t)max_tokens * nranks * kv->cfg.n_heads * kv->cfg.head_dim * 4 + 255) & ~(size_t)255;
+    LT_CUDA(kv, cudaMalloc(&pg.d_buf, kPeerHeaderBytes + 2 * half));
+    // Flags and the done counter start at zero before any peer can see the buffer.
+    LT_CUDA(kv, cudaMemset(pg.d_buf, 0, kPeerHeaderBytes));
+    LT_CUDA(kv, cudaDeviceSynchronize());
+    cudaIpcMemHandle_t h;
+    LT_CUDA(kv, cudaIpcGetMemHandle(&h, pg.d_buf));
+    std::memcpy(ipc_handle_out, &h, sizeof h);
+    pg.rank = rank;
+    pg.nranks = nranks;
+    pg.max_tokens = max_tokens;
+    pg.half_bytes = half;
+    return LT_OK;
+}
+
+lt_status lt_kv_peer_import(lt_kv* kv, const void* ipc_handles) {
+    if (!kv || !ipc_handles) return LT_E_ARG;
+    PeerGather& pg = kv->peer;
+    if (!pg.d_buf) return fail(kv, LT_E_ARG, "peer_import before peer_export");
+    DeviceGuard g(kv->cfg.device);
+    peer_unmap(kv);
+    const unsigned char* hs = static_cast<const unsigned char*>(ipc_handles);
+    for (int r = 0; r < pg.nranks; ++r) {
+        if (r == pg.rank) {
+            pg.base[r] = pg.d_buf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hs + (size_t)r * LT_IPC_HANDLE_BYTES, sizeof h);
+        void* ptr = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            peer_unmap(kv);
+            return fail(kv, LT_E_CUDA, "cudaIpcOpenMemHandle(rank %d): %s", r, cudaGetErrorString(e));
+        }
+        pg.base[r] = static_cast<unsigned char*>(ptr);
+        pg.mapped[r] = true;
+    }
+    pg.epoch = 0;
+    pg.ready = true;
+    return LT_OK;
+}
+
+lt_status lt_kv_peer_close(lt_kv* kv) {
+    if (!kv) return LT_E_ARG;
+    if (!kv->dev) return LT_OK;
+    DeviceGuard g(kv->cfg.device);
+    LT_CUDA(kv, cudaDeviceSynchronize());
+    peer_unmap(kv);
+    return LT_OK;
 }
 
 void lt_kv_truncate(lt_kv* kv, uint32_t seq, uint32_t from) {

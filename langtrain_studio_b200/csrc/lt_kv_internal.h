@@ -25,6 +25,8 @@ struct TokenDesc {
 };
 
 constexpr int kInlineTokens = 512;  // tokens passed inside the kernel parameters
+constexpr int kMaxPeers = 8;        // ranks of a head-sharded peer gather
+constexpr int kMergeGroup = 8;      // partials a group leader combines (two-level merge)
 
 struct AttnParams {
     const uint16_t* pool_layer;  // pool + layer offset
@@ -46,6 +48,14 @@ struct AttnParams {
     float* part_o;               // [n_warps][group][D]: partial of warp w's first piece
     float* part_ml;              // [n_warps][group][2]
     uint32_t* flags;             // [n_warps]: warp w stores `epoch` once its range is done
+    // Two-level merge of (token, head)s cut into more than kMergeGroup + 1
+    // pieces: the helper warps' partials are first combined in groups of
+    // kMergeGroup by each group's first warp (into slot w of part2_*, flag
+    // flags2[w]); the merging warp then reads one partial per group.  Null:
+    // one level (the merging warp reads every helper's partial).
+    float* part2_o;
+    float* part2_ml;
+    uint32_t* flags2;
     uint32_t epoch;              // distinct per launch on a flags array
     int32_t* err;                // device error flag
     const void* k_new;           // fused append: new K/V rows [n][n_kv_heads*D], or null
@@ -56,6 +66,18 @@ struct AttnParams {
     int32_t pre_splits;          // partials per row (the prefix blocks split over that many CTAs)
     int64_t pre_split_rows;      // rows between split slabs
     int32_t q8;                  // pool tiles are Q8_0 (lt_kv.h LT_KV_Q8_0); no prefix partials then
+    // Head-sharded gather over NVLink (lt_kv_attend_gather).  With n_peers > 0
+    // every output row goes, instead of to `out`, to this rank's gather half
+    // gather_out at row tok*(n_peers*n_heads) + peer_rank*n_heads + head, and
+    // the (token, head) that completes the count publishes peer_epoch into
+    // every rank's flag for this rank (peer_flag[r]); the ranks then read
+    // each other's rows (launch_gather_wait_copy).
+    int32_t n_peers;
+    int32_t peer_rank;
+    uint32_t peer_epoch;
+    uint32_t* done_count;        // this rank's count of stored (token, head)s (zero between launches)
+    void* gather_out;
+    uint32_t* peer_flag[kMaxPeers];
     TokenDesc inl[kInlineTokens];
 };
 
@@ -126,6 +148,14 @@ cudaError_t launch_rows(const uint16_t* pool_layer, const int32_t* table_row, in
 cudaError_t launch_wait_selftest(uint64_t limit_ns, int32_t* err, cudaStream_t s);
 // Whether this build checks table entries on the device (LT_BOUNDS_CHECK).
 bool bounds_checked_build();
+
+// Peer gather, receiving side: wait (bounded, system-scope acquire) until
+// every rank's flag in `flags` has reached `epoch`, then assemble `out`
+// [n][nranks][slice_bytes]: slice r of every token comes from rank r's
+// gather half srcs[r] (the same layout; over NVLink for the other ranks).
+// A wait that gives up raises kErrTimeout and copies nothing.
+cudaError_t launch_gather_wait_copy(const uint32_t* flags, int nranks, uint32_t epoch, void* const* srcs, void* out,
+                                    uint32_t n, size_t slice_bytes, int32_t* err, cudaStream_t s);
 
 }  // namespace ltkv
 

@@ -104,6 +104,24 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     return v;
 }
 
+// System scope (another GPU over NVLink reads or writes the word).
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+
 // Wait until *flag == epoch, giving up after limit_ns.
 __device__ __forceinline__ int wait_flag_bounded(const uint32_t* flag, uint32_t epoch,
                                                  uint64_t limit_ns = kWaitLimitNs) {
@@ -406,6 +424,121 @@ __device__ __forceinline__ void fold_prefix(const AttnParams& p, int tok, int h,
     }
 }
 
+// Final output row (tok, h, g) of a lane: acc * inv at columns nt*8 + 2*t4.
+// Plain calls store to p.out [n][n_heads][D]; a peer gather stores the row
+// to this rank's gather half, at its place among all ranks' heads.
+template <int D>
+__device__ __forceinline__ void store_out(const AttnParams& p, int tok, int h, int g, int t4,
+                                          const float (&acc)[D / 8][2], float inv) {
+    constexpr int NT = D / 8;
+    const int hl = p.n_kv_heads * p.group;  // this rank's q heads
+    if (p.n_peers == 0) {
+        const size_t ob = ((size_t)tok * hl + (size_t)h * p.group + g) * D + 2 * t4;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const float v0 = acc[nt][0] * inv, v1 = acc[nt][1] * inv;
+            if (p.out_f32)
+                *reinterpret_cast<float2*>(static_cast<float*>(p.out) + ob + nt * 8) = make_float2(v0, v1);
+            else
+                *reinterpret_cast<__half2*>(static_cast<__half*>(p.out) + ob + nt * 8) = __floats2half2_rn(v0, v1);
+        }
+        return;
+    }
+    const size_t row = (size_t)tok * p.n_peers * hl + (size_t)p.peer_rank * hl + (size_t)h * p.group + g;
+    const size_t ob = row * D + 2 * t4;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const float v0 = acc[nt][0] * inv, v1 = acc[nt][1] * inv;
+        if (p.out_f32)
+            *reinterpret_cast<float2*>(static_cast<float*>(p.gather_out) + ob + nt * 8) = make_float2(v0, v1);
+        else
+            *reinterpret_cast<__half2*>(static_cast<__half*>(p.gather_out) + ob + nt * 8) = __floats2half2_rn(v0, v1);
+    }
+}
+
+// Peer gather: a warp is done and stored the output rows of `items`
+// (token, head) items into this rank's gather half (local memory).  Only
+// such warps take part: after the warp barrier, lane 0 adds the items to
+// this launch's count with an acq_rel RMW on this GPU, so the warp that
+// completes the count (n_tok * n_kv_heads items) has every row ordered
+// before it, in this GPU's memory.  It publishes this launch's epoch into
+// every rank's flag for this rank with system-scope release stores; a rank
+// that acquires the flag then reads the rows from here over NVLink.
+__device__ __forceinline__ void peer_done(const AttnParams& p, int lane, int items) {
+    if (p.n_peers == 0 || items == 0) return;
+    __syncwarp();
+    const uint32_t total = (uint32_t)p.n_tok * (uint32_t)p.n_kv_heads;
+    if (lane == 0 && atom_add_acq_rel_gpu(p.done_count, (uint32_t)items) + (uint32_t)items == total) {
+        *p.done_count = 0u;  // ready for the next launch (which starts after this one ends)
+        for (int r = 0; r < p.n_peers; ++r) st_release_sys(p.peer_flag[r], p.peer_epoch);
+    }
+}
+
+// Wait (bounded) until flags[w] == epoch for w = first, first + stride, ...
+// <= last; lane j polls every 32nd of them, so the round trips overlap.
+// Warp-uniform result.
+__device__ __forceinline__ bool wait_flags(const uint32_t* flags, uint32_t epoch, int first, int last, int stride,
+                                           int lane) {
+    int ready = 1;
+    for (int w0 = first; w0 <= last && ready; w0 += 32 * stride) {
+        int ok = 1;
+        const int w = w0 + lane * stride;
+        if (w <= last) ok = wait_flag_bounded(flags + w, epoch);
+        ready = __all_sync(kFull, ok);
+    }
+    return ready != 0;
+}
+
+// Fold the (m, l, O) partials in slots first, first + stride, ... <= last of
+// (po, pml) into the running (M, L, acc) of row g (log2 units; acc is the
+// unnormalised sum at maximum M), in one pass: each batch of U partials is
+// loaded together (one L2 round trip; indices past the set clamp to its last
+// member and get weight 0), the running maximum moves to the batch's, and
+// the partials are added in slot order.
+template <int D>
+__device__ __forceinline__ void merge_slots(const float* po, const float* pml, int G, int g, int t4, int first,
+                                            int last, int stride, float& M, float& L, float (&acc)[D / 8][2]) {
+    constexpr int NT = D / 8;
+    constexpr int U = D == 64 ? 8 : 4;
+    const size_t GD = (size_t)G * D;
+    const int lastv = first + ((last - first) / stride) * stride;  // last member of the set
+    for (int w = first; w <= lastv; w += U * stride) {
+        float pm[U], pl[U];
+        float2 v2[U][NT];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const size_t ww = (size_t)min(w + u * stride, lastv);
+            pm[u] = __ldcg(pml + (ww * G + g) * 2);
+            pl[u] = __ldcg(pml + (ww * G + g) * 2 + 1);
+            const float* src = po + ww * GD + (size_t)g * D + 2 * t4;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) v2[u][nt] = __ldcg(reinterpret_cast<const float2*>(src + nt * 8));
+        }
+        float Mn = M;
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (w + u * stride <= lastv) Mn = fmaxf(Mn, pm[u]);
+        const float own = M == -INFINITY ? 0.f : ex2(M - Mn);
+        M = Mn;
+        L *= own;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            acc[nt][0] *= own;
+            acc[nt][1] *= own;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const float sw = w + u * stride <= lastv ? ex2(pm[u] - M) : 0.f;
+            L += pl[u] * sw;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                acc[nt][0] += v2[u][nt].x * sw;
+                acc[nt][1] += v2[u][nt].y * sw;
+            }
+        }
+    }
+}
+
 // S = Q K^T, online softmax and O += P V for one staged (block, head) tile.
 template <int D>
 __device__ __forceinline__ void attend_tile(const uint8_t* tile, int valid, const uint32_t (&qa)[D / 16][4],
@@ -606,6 +739,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
     constexpr int S = Q8 ? kStagesQ8 : kStages;
     extern __shared__ __align__(1024) uint8_t smem[];
 
+    // A kernel launched after this one as a programmatic dependent (the
+    // decode matmul that consumes the output, the peer-gather wait) may start
+    // as this launch's CTAs retire; it still waits for this grid's completion
+    // (griddepcontrol.wait) before it reads what this grid wrote.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gw = blockIdx.x * kWarps + warp;
     const int Hkv = p.n_kv_heads, G = p.group;
@@ -678,6 +816,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
     // ---- issuer state ----
     PieceRegs di{}, dn{};
     gen_piece(di);
+    // The range's first piece: a warp whose first piece continues a cut
+    // (token, head) may lead a group of its helpers in the two-level merge.
+    const long long f_ps = di.ps;
+    const int f_nb = di.pos / kBlock + 1 - di.skip, f_kind = di.kind;
     bool dn_valid = gt < t1;
     if (dn_valid) gen_piece(dn);
     int ii = 0;  // issuer piece ordinal
@@ -754,6 +896,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
     for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    int items_out = 0;   // (token, head) outputs this warp stored
     for (;;) {
         const int s = consumed % S;
         if (!mbar_wait_bounded(bar0 + 8u * s, (consumed / S) & 1)) {
@@ -859,9 +1002,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
             l += __shfl_xor_sync(kFull, l, 1);
             l += __shfl_xor_sync(kFull, l, 2);
             const size_t GD = (size_t)G * D;
+            if (dc.kind == 0) ++items_out;
             if (g < G) {
                 if (dc.kind == 0) {
-                    const size_t ob = ((size_t)dc.tok * Hkv + dc.h) * GD + (size_t)g * D + 2 * t4;
                     float acc[NT][2];
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
@@ -869,16 +1012,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
                         acc[nt][1] = o[nt][1] + o[nt][3];
                     }
                     if (dc.skip > 0) fold_prefix<D>(p, dc.tok, dc.h, g, t4, m_run, l, acc);
-                    const float inv = 1.f / l;
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        const float v0 = acc[nt][0] * inv, v1 = acc[nt][1] * inv;
-                        if (p.out_f32)
-                            *reinterpret_cast<float2*>(static_cast<float*>(p.out) + ob + nt * 8) = make_float2(v0, v1);
-                        else
-                            *reinterpret_cast<__half2*>(static_cast<__half*>(p.out) + ob + nt * 8) =
-                                __floats2half2_rn(v0, v1);
-                    }
+                    store_out<D>(p, dc.tok, dc.h, g, t4, acc, 1.f / l);
                 } else {
                     const size_t sl = (size_t)gw;  // partial slot of this warp (its first piece)
 #pragma unroll
@@ -913,86 +1047,72 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
     // Publish: every partial this warp wrote is visible before its flag.
     __syncwarp();
     if (lane == 0) st_release_gpu(p.flags + gw, p.epoch);
-    if (!ok || dc.kind != 2 || ct != dc.b1 - dc.b0) return;
+    const long long NW = p.n_warps;
+
+    // ---- two-level merge: lead a group of helpers of a long cut (token, head) ----
+    // Helpers of a (token, head) are the warps after the one holding its first
+    // tile; with more than kMergeGroup of them, every kMergeGroup-th helper
+    // combines its own partial and its next kMergeGroup-1 neighbours' into a
+    // group partial, so the merging warp reads one partial per group.
+    if (ok && f_kind == 1 && p.part2_o) {
+        const int ws = (int)(((f_ps + 1) * NW - 1) / T), we = (int)(((f_ps + f_nb) * NW - 1) / T);
+        if (we - ws > kMergeGroup && (gw - ws - 1) % kMergeGroup == 0) {
+            const int last = min(gw + kMergeGroup - 1, we);
+            const bool rd = wait_flags(p.flags, p.epoch, gw + 1, last, 1, lane);
+            __syncwarp();
+            if (rd && g < G) {
+                float M = -INFINITY, L = 0.f, acc[NT][2];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
+                merge_slots<D>(p.part_o, p.part_ml, G, g, t4, gw, last, 1, M, L, acc);
+                const size_t GD = (size_t)G * D;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                    *reinterpret_cast<float2*>(p.part2_o + (size_t)gw * GD + (size_t)g * D + nt * 8 + 2 * t4) =
+                        make_float2(acc[nt][0], acc[nt][1]);
+                if (t4 == 0) {
+                    p.part2_ml[((size_t)gw * G + g) * 2] = M;
+                    p.part2_ml[((size_t)gw * G + g) * 2 + 1] = L;
+                }
+            }
+            if (!rd && lane == 0) atomicOr(p.err, kErrTimeout);
+            __syncwarp();
+            if (lane == 0) st_release_gpu(p.flags2 + gw, p.epoch);  // published either way: no second wait
+        }
+    }
+    if (!ok || dc.kind != 2 || ct != dc.b1 - dc.b0) {
+        peer_done(p, lane, items_out);
+        return;
+    }
 
     // ---- merge the cut (token, head) this range ends with ----
-    const long long NW = p.n_warps;
     const int nb = dc.pos / kBlock + 1 - dc.skip;
     const int w_last = (int)(((dc.ps + nb) * NW - 1) / T);  // warp holding its last tile
-    // Lane j waits for neighbour gw+1+j (32 at a time), so the flags' round
-    // trips overlap instead of following one another.
-    int ready = 1;
-    for (int w0 = gw + 1; w0 <= w_last && ready; w0 += 32) {
-        int ok = 1;
-        if (w0 + lane <= w_last) ok = wait_flag_bounded(p.flags + w0 + lane, p.epoch);
-        ready = __all_sync(kFull, ok);
-    }
+    const bool grouped = p.part2_o && w_last - gw > kMergeGroup;
+    const int stride = grouped ? kMergeGroup : 1;
+    const bool ready = wait_flags(grouped ? p.flags2 : p.flags, p.epoch, gw + 1, w_last, stride, lane);
     __syncwarp();
     if (!ready) {
         if (lane == 0) atomicOr(p.err, kErrTimeout);
+        peer_done(p, lane, items_out + 1);  // its item stays unwritten; the error flag says so
         return;
     }
     float l = l_run;
     l += __shfl_xor_sync(kFull, l, 1);
     l += __shfl_xor_sync(kFull, l, 2);
     if (g < G) {
-        const size_t GD = (size_t)G * D;
-        // Loads are issued U partials at a time (indices past w_last clamp to
-        // it and get weight 0), so a merge of many pieces pays one L2 round
-        // trip per U partials; partials still combine in warp order.
-        constexpr int U = D == 64 ? 4 : 2;
-        float M = m_run;
-        for (int w = gw + 1; w <= w_last; w += 4) {
-            float mm[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) mm[u] = __ldcg(p.part_ml + ((size_t)min(w + u, w_last) * G + g) * 2);
-#pragma unroll
-            for (int u = 0; u < 4; ++u) M = fmaxf(M, mm[u]);
-        }
-        const float own = ex2(m_run - M);
-        float L = l * own;
-        float acc[NT][2];
+        float M = m_run, L = l, acc[NT][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            acc[nt][0] = (o[nt][0] + o[nt][2]) * own;
-            acc[nt][1] = (o[nt][1] + o[nt][3]) * own;
+            acc[nt][0] = o[nt][0] + o[nt][2];
+            acc[nt][1] = o[nt][1] + o[nt][3];
         }
-        for (int w = gw + 1; w <= w_last; w += U) {
-            float pm[U], pl[U];
-            float2 v2[U][NT];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const size_t ww = (size_t)min(w + u, w_last);
-                pm[u] = __ldcg(p.part_ml + (ww * G + g) * 2);
-                pl[u] = __ldcg(p.part_ml + (ww * G + g) * 2 + 1);
-                const float* po = p.part_o + ww * GD + (size_t)g * D + 2 * t4;
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) v2[u][nt] = __ldcg(reinterpret_cast<const float2*>(po + nt * 8));
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const float sw = w + u <= w_last ? ex2(pm[u] - M) : 0.f;
-                L += pl[u] * sw;
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    acc[nt][0] += v2[u][nt].x * sw;
-                    acc[nt][1] += v2[u][nt].y * sw;
-                }
-            }
-        }
+        merge_slots<D>(grouped ? p.part2_o : p.part_o, grouped ? p.part2_ml : p.part_ml, G, g, t4, gw + 1, w_last,
+                       stride, M, L, acc);
         if (dc.skip > 0) fold_prefix<D>(p, dc.tok, dc.h, g, t4, M, L, acc);
-        const float inv = 1.f / L;
-        const size_t ob = ((size_t)dc.tok * Hkv + dc.h) * GD + (size_t)g * D + 2 * t4;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            if (p.out_f32)
-                *reinterpret_cast<float2*>(static_cast<float*>(p.out) + ob + nt * 8) =
-                    make_float2(acc[nt][0] * inv, acc[nt][1] * inv);
-            else
-                *reinterpret_cast<__half2*>(static_cast<__half*>(p.out) + ob + nt * 8) =
-                    __floats2half2_rn(acc[nt][0] * inv, acc[nt][1] * inv);
-        }
+        store_out<D>(p, dc.tok, dc.h, g, t4, acc, 1.f / L);
     }
+    peer_done(p, lane, items_out + 1);
 }
 
 // ------------------------------------------------------------ prefix ----
@@ -1498,6 +1618,50 @@ __global__ void wait_selftest_kernel(uint64_t limit_ns, int32_t* err) {
     if (!wait_flag_bounded(&g_never_set, 1u, limit_ns)) atomicOr(err, kErrTimeout);
 }
 
+// ------------------------------------------------------ peer gather ----
+struct GatherSrcs {
+    const uint4* r[kMaxPeers];  // each rank's gather half (this process's mapping)
+};
+
+// Thread 0 of every CTA waits (bounded, system-scope acquire) for each
+// rank's flag to reach `epoch` (wrap-safe comparison: a rank may already be
+// one call ahead); the CTA then copies its share of out [n][nranks][slice],
+// slice r of each token from rank r's gather half (NVLink loads for the
+// other ranks; the acquire orders them after that rank's stores).  Launched
+// as a programmatic dependent of the attention launch, so it starts polling
+// while that launch's last CTAs retire; griddepcontrol.wait before it exits
+// keeps "this kernel done" meaning "the attention launch done" for the work
+// after it.
+__global__ void __launch_bounds__(256) gather_wait_copy_kernel(const uint32_t* flags, int nranks, uint32_t epoch,
+                                                               const __grid_constant__ GatherSrcs srcs, uint4* dst,
+                                                               uint32_t n, uint32_t slice16, int32_t* err) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        int good = 1;
+        const uint64_t t0 = global_ns();
+        for (int r = 0; r < nranks && good; ++r) {
+            while ((int32_t)(ld_acquire_sys(flags + r) - epoch) < 0) {
+                if (global_ns() - t0 > kWaitLimitNs) {
+                    good = 0;
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+        if (!good) atomicOr(err, kErrTimeout);
+        ok = good;
+    }
+    __syncthreads();
+    if (ok) {
+        const size_t row16 = (size_t)nranks * slice16, total = (size_t)n * row16;
+        for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+            const int r = (int)((i % row16) / slice16);
+            dst[i] = __ldcg(srcs.r[r] + i);
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------- gather ----
 // out[t][r] = gathered[r][t] for 16-byte chunks of one token's local heads.
 __global__ void __launch_bounds__(256) gather_permute_kernel(const uint4* __restrict__ gathered, uint4* __restrict__ out,
@@ -1715,6 +1879,28 @@ cudaError_t launch_rows(const uint16_t* pool_layer, const int32_t* table_row, in
     else
         rows_kernel<128><<<blocks, 256, 0, s>>>(pool_layer, table_row, n, n_kv_heads, k_out, v_out, n_blocks, err);
     return cudaGetLastError();
+}
+
+cudaError_t launch_gather_wait_copy(const uint32_t* flags, int nranks, uint32_t epoch, void* const* srcs, void* out,
+                                    uint32_t n, size_t slice_bytes, int32_t* err, cudaStream_t s) {
+    if (nranks < 1 || nranks > kMaxPeers) return cudaErrorInvalidValue;
+    GatherSrcs gs{};
+    for (int r = 0; r < nranks; ++r) gs.r[r] = static_cast<const uint4*>(srcs[r]);
+    const uint32_t slice16 = (uint32_t)(slice_bytes / 16);
+    const size_t n16 = (size_t)n * nranks * slice16;
+    const unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((n16 + 255) / 256, 148));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gather_wait_copy_kernel, flags, nranks, epoch, gs, static_cast<uint4*>(out), n,
+                              slice16, err);
 }
 
 cudaError_t launch_wait_selftest(uint64_t limit_ns, int32_t* err, cudaStream_t s) {

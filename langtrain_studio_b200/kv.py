@@ -211,6 +211,60 @@ class KvCache:
             _ptr(seqs), _ptr(positions), n, _dptr(out), _dtype_code(out), scale, _stream(stream)))
         return out
 
+    # ------------------------------------------- head-sharded peer gather
+    def peer_export(self, rank: int, nranks: int, max_tokens: int) -> bytes:
+        """Allocate this rank's gather buffer; returns its 64-byte IPC handle."""
+        buf = C.create_string_buffer(N.LT_IPC_HANDLE_BYTES)
+        self._check(self._lib.lt_kv_peer_export(self._h, rank, nranks, max_tokens, buf))
+        self.peer_ranks = nranks
+        return buf.raw
+
+    def peer_import(self, handles):
+        """Map every rank's gather buffer (handles in rank order)."""
+        blob = b"".join(bytes(h) for h in handles)
+        assert len(blob) == N.LT_IPC_HANDLE_BYTES * self.peer_ranks
+        self._check(self._lib.lt_kv_peer_import(self._h, C.create_string_buffer(blob, len(blob))))
+
+    def peer_close(self):
+        self._check(self._lib.lt_kv_peer_close(self._h))
+
+    def attend_gather(self, layer: int, q, seqs, positions, out=None, out_dtype=None, scale: float | None = None,
+                      stream=None):
+        """attend() of this rank's heads, gathered over NVLink into
+        [n, nranks * n_heads * head_dim] (lt_kv_attend_gather)."""
+        import torch
+
+        seqs, positions = _u32(seqs), _u32(positions)
+        n = seqs.size
+        assert q.is_cuda and q.is_contiguous() and q.numel() == n * self.n_heads * self.head_dim
+        if out is None:
+            out = torch.empty((n, self.peer_ranks * self.n_heads * self.head_dim), dtype=out_dtype or torch.float32,
+                              device=q.device)
+        if scale is None:
+            scale = float(np.float32(1.0) / np.float32(math.sqrt(self.head_dim)))
+        self._check(self._lib.lt_kv_attend_gather(self._h, layer, _dptr(q), _dtype_code(q), _ptr(seqs),
+                                                  _ptr(positions), n, _dptr(out), _dtype_code(out), scale,
+                                                  _stream(stream)))
+        return out
+
+    def write_attend_gather(self, layer: int, blocks, slots, k, v, q, seqs, positions, out=None, out_dtype=None,
+                            scale: float | None = None, stream=None):
+        """write_attend() with the gather fused in (lt_kv_write_attend_gather)."""
+        import torch
+
+        blocks, slots = _i32(blocks), _i32(slots)
+        seqs, positions = _u32(seqs), _u32(positions)
+        n = seqs.size
+        if out is None:
+            out = torch.empty((n, self.peer_ranks * self.n_heads * self.head_dim), dtype=out_dtype or torch.float32,
+                              device=q.device)
+        if scale is None:
+            scale = float(np.float32(1.0) / np.float32(math.sqrt(self.head_dim)))
+        self._check(self._lib.lt_kv_write_attend_gather(
+            self._h, layer, _ptr(blocks), _ptr(slots), _dptr(k), _dptr(v), _dtype_code(k), _dptr(q), _dtype_code(q),
+            _ptr(seqs), _ptr(positions), n, _dptr(out), _dtype_code(out), scale, _stream(stream)))
+        return out
+
     def truncate(self, seq: int, start: int):
         """Drop positions start.. of seq (kv.rs:153-169; Backend::kv_remove)."""
         self._lib.lt_kv_truncate(self._h, seq, start)
@@ -334,6 +388,17 @@ def nccl_unique_id() -> bytes:
     if rc != N.LT_OK:
         raise KvError(rc, "NCCL is not available (libnccl.so.2)")
     return buf.raw
+
+
+def setup_peer_gather(kv: "KvCache", rank: int, nranks: int, max_tokens: int):
+    """Export this rank's gather buffer, exchange IPC handles over the
+    default torch.distributed group, and map every rank's buffer."""
+    import torch.distributed as dist
+
+    mine = kv.peer_export(rank, nranks, max_tokens)
+    handles = [None] * nranks
+    dist.all_gather_object(handles, mine)
+    kv.peer_import(handles)
 
 
 def gather_heads(kv: "KvCache", local, comm: NcclComm, out=None, gathered=None, stream=None):

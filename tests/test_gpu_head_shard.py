@@ -77,3 +77,116 @@ def test_head_sharded_attention_matches_unsharded(tmp_path):
     for r in range(2):
         err = float(np.load(tmp_path / f"err{r}.npy")[0])
         assert err < 2e-5, err  # f32 outputs; the north-star bar is 2e-3
+
+
+# ---- the gather fused into attention: NVLink peer stores, no collective ----
+
+def _peer_rank(rank, world, port, out_dir, skip_rank):
+    import datetime
+    import sys
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from langtrain_studio_b200 import _native as N
+    from langtrain_studio_b200 import kv as kvm
+    from oracle import oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    torch.cuda.set_device(rank)
+    hkv, hq, d = 4, 16, 128
+    hl, ql = hkv // world, hq // world
+    lens = [100, 333, 1000, 17]
+    n = len(lens)
+    rng = np.random.default_rng(0)  # the same full K/V and q on every rank
+    K = [rng.standard_normal((L, hkv * d)).astype(np.float32) for L in lens]
+    V = [rng.standard_normal((L, hkv * d)).astype(np.float32) for L in lens]
+    steps = 3
+    q = rng.standard_normal((steps + 2, n, hq * d)).astype(np.float32)
+    Kn = rng.standard_normal((steps, n, hkv * d)).astype(np.float32)
+    Vn = rng.standard_normal((steps, n, hkv * d)).astype(np.float32)
+    nb = sum((L + steps + 16) // 16 for L in lens) + 8
+    kv = kvm.KvCache(1, hl, d, nb * 16, n_heads=ql, max_seqs=n, max_batch=4096, device=rank)
+    ok = oracle.OracleKv(1, hkv * d, nb * 16, max_seqs=n)
+    cols = slice(rank * hl * d, (rank + 1) * hl * d)
+    qcols = slice(rank * ql * d, (rank + 1) * ql * d)
+    for s, L in enumerate(lens):
+        b, sl = kv.append_batch(np.full(L, s), np.arange(L))
+        kv.write(0, b, sl, torch.from_numpy(np.ascontiguousarray(K[s][:, cols])).cuda(),
+                 torch.from_numpy(np.ascontiguousarray(V[s][:, cols])).cuda())
+        rc, _, bo, so = ok.append_batch(np.full(L, s), np.arange(L))
+        ok.write_batch(0, bo, so, K[s], V[s])
+    kvm.setup_peer_gather(kv, rank, world, max_tokens=16)
+    seqs = np.arange(n)
+    errs = []
+
+    def local_q(i):
+        return torch.from_numpy(np.ascontiguousarray(q[i][:, qcols])).cuda()
+
+    if skip_rank is None:
+        # attend only: f32 out, then f16 out (the other half of the gather buffer)
+        pos = np.array(lens) - 1
+        ref = ok.attend(0, q[0], seqs, pos, hq, hkv, d)
+        full = kv.attend_gather(0, local_q(0), seqs, pos, out_dtype=torch.float32)
+        kv.check()
+        errs.append(float(np.abs(full.cpu().numpy() - ref).max()))
+        ref = ok.attend(0, q[1], seqs, pos, hq, hkv, d)
+        full = kv.attend_gather(0, local_q(1).half(), seqs, pos, out_dtype=torch.float16)
+        kv.check()
+        np.testing.assert_allclose(full.float().cpu().numpy(), ref, rtol=1e-3, atol=2e-3)
+        # decode steps: append + fused K/V write + attention + gather, one call each
+        for t in range(steps):
+            pos = np.array(lens) + t
+            b, sl = kv.append_batch(seqs, pos)
+            rc, _, bo, so = ok.append_batch(seqs, pos)
+            full = kv.write_attend_gather(0, b, sl, torch.from_numpy(np.ascontiguousarray(Kn[t][:, cols])).cuda(),
+                                          torch.from_numpy(np.ascontiguousarray(Vn[t][:, cols])).cuda(),
+                                          local_q(t + 2), seqs, pos, out_dtype=torch.float32)
+            kv.check()
+            ok.write_batch(0, bo, so, Kn[t], Vn[t])
+            ref = ok.attend(0, q[t + 2], seqs, pos, hq, hkv, d)
+            errs.append(float(np.abs(full.cpu().numpy() - ref).max()))
+        np.save(os.path.join(out_dir, f"err{rank}.npy"), np.array(errs))
+    else:
+        # One rank misses a call: the others' bounded wait runs out and the
+        # handle reports LT_E_TIMEOUT; nothing hangs.  The missing rank stays
+        # alive (its buffer mapped) until they are done.
+        pos = np.array(lens) - 1
+        status = "skipped"
+        if rank != skip_rank:
+            kv.attend_gather(0, local_q(0), seqs, pos, out_dtype=torch.float32)
+            try:
+                kv.check()
+                status = "no error"
+            except kvm.KvError as e:
+                status = "timeout" if e.code == N.LT_E_TIMEOUT else f"code {e.code}"
+        np.save(os.path.join(out_dir, f"status{rank}.npy"), np.array([status]))
+    torch.cuda.synchronize()
+    kv.peer_close()
+    dist.barrier()
+    kv.close()
+    dist.destroy_process_group()
+
+
+def test_peer_gather_matches_unsharded(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_peer_rank, args=(2, _port(), str(tmp_path), None), nprocs=2, join=True,
+                       start_method="spawn")
+    for r in range(2):
+        errs = np.load(tmp_path / f"err{r}.npy")
+        assert errs.size == 4 and float(errs.max()) < 2e-5, errs  # f32 outputs
+
+
+def test_peer_gather_rank_missing_a_call_times_out(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_peer_rank, args=(2, _port(), str(tmp_path), 1), nprocs=2, join=True, start_method="spawn")
+    assert str(np.load(tmp_path / "status0.npy")[0]) == "timeout"
+    assert str(np.load(tmp_path / "status1.npy")[0]) == "skipped"

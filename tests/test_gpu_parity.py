@@ -194,6 +194,7 @@ ATT_CASES = [
     (128, 64, 8, [513, 1100]),          # G=8, multi-chunk split-K
     (64, 32, 4, [31, 192, 64]),         # config-1 shape
     (128, 8, 2, [2049]),
+    (128, 16, 2, [131, 149, 160]),      # with min_tiles 1: 8, 9, 10 helper warps (two-level merge from 9)
 ]
 
 
