@@ -656,11 +656,17 @@ __device__ __forceinline__ void attend_tile_q8(const uint8_t* tile, int valid, c
     }
 #pragma unroll
     for (int e = 0; e < 4; ++e) sc[e] *= scale_log2;
-    const bool ok0 = 2 * t < valid, ok1 = 2 * t + 1 < valid, ok2 = 2 * t + 8 < valid, ok3 = 2 * t + 9 < valid;
-    if (!ok0) sc[0] = -INFINITY;
-    if (!ok1) sc[1] = -INFINITY;
-    if (!ok2) sc[2] = -INFINITY;
-    if (!ok3) sc[3] = -INFINITY;
+    // Slots past `valid` (only in a sequence's last block) are masked out of
+    // S and weigh exactly 0 in O, whatever their stale bytes and scales.
+    const bool part = valid < kBlock;  // warp-uniform
+    const bool ok0 = !part || 2 * t < valid, ok1 = !part || 2 * t + 1 < valid, ok2 = !part || 2 * t + 8 < valid,
+               ok3 = !part || 2 * t + 9 < valid;
+    if (part) {
+        if (!ok0) sc[0] = -INFINITY;
+        if (!ok1) sc[1] = -INFINITY;
+        if (!ok2) sc[2] = -INFINITY;
+        if (!ok3) sc[3] = -INFINITY;
+    }
     float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
     mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
@@ -686,8 +692,13 @@ __device__ __forceinline__ void attend_tile_q8(const uint8_t* tile, int valid, c
         const uint2 vd = *reinterpret_cast<const uint2*>(tile + 33 * D + (c * 16 + 4 * t) * 2);
         const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&vd.x));
         const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&vd.y));
-        const float p0 = ok0 ? pr[0] * d01.x : 0.f, p1 = ok1 ? pr[1] * d01.y : 0.f;
-        const float p2 = ok2 ? pr[2] * d23.x : 0.f, p3 = ok3 ? pr[3] * d23.y : 0.f;
+        float p0 = pr[0] * d01.x, p1 = pr[1] * d01.y, p2 = pr[2] * d23.x, p3 = pr[3] * d23.y;
+        if (part) {
+            p0 = ok0 ? p0 : 0.f;
+            p1 = ok1 ? p1 : 0.f;
+            p2 = ok2 ? p2 : 0.f;
+            p3 = ok3 ? p3 : 0.f;
+        }
         uint32_t pa[4];
         {
             const __half2 h01 = __floats2half2_rn(p0, p1), h23 = __floats2half2_rn(p2, p3);
@@ -840,6 +851,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
     table_write(di);
 
     int issued = 0, consumed = 0;
+    int istage = 0;              // ring stage of the next copy (issued % S)
+    int cstage = 0, cphase = 0;  // ring stage and barrier phase of the next tile consumed
     auto issue_one = [&]() {
         if (it - wb >= 32) {
             win = win_n;
@@ -848,7 +861,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
         }
         const int b = __shfl_sync(kFull, win, it - wb);
         if (lane == 0) {
-            const int s = issued % S;
+            const int s = istage;
             const uint32_t bar = bar0 + 8u * s;
             mbar_arrive_expect_tx(bar, TILE + (it == 0 ? qbytes : 0u));
             bulk_g2s(smem_u32(stages + (size_t)s * TILE), p.pool_layer + ((size_t)b * Hkv + di.h) * tile_elems, TILE,
@@ -860,6 +873,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
         }
         ++it;
         ++issued;
+        istage = istage + 1 == S ? 0 : istage + 1;
     };
     auto issuer_advance = [&]() {  // piece di is fully issued; move to dn
         ++ii;
@@ -898,8 +912,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
     bool ok = true;
     int items_out = 0;   // (token, head) outputs this warp stored
     for (;;) {
-        const int s = consumed % S;
-        if (!mbar_wait_bounded(bar0 + 8u * s, (consumed / S) & 1)) {
+        const int s = cstage;
+        if (!mbar_wait_bounded(bar0 + 8u * s, (uint32_t)cphase)) {
             ok = false;
             break;
         }
@@ -989,6 +1003,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
         else
             attend_tile<D>(tile, valid, qa, o, m_run, l_run, p.scale_log2, lane);
         ++consumed;
+        if (++cstage == S) {
+            cstage = 0;
+            cphase ^= 1;
+        }
         ++ct;
         // Generic-proxy writes into this stage must be ordered before the
         // async-proxy copy that may refill it.
