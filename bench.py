@@ -747,6 +747,20 @@ def run_c5(args, rank, world, local):
             "compaction_gb_moved_per_s": moved_bytes / (ms * 1e-3) / 1e9,
             "gpu_launches": kv.launch_count() - l0,
         })
+        # Rank 0's decode attention launches: K+V rows of every attended
+        # position, q and out rows, and the fused append (source read + row write).
+        kvd = hkv * d
+        attn_bytes = (delta["attended_positions"] * kvd * 2 * 2 + delta["decode_tokens"] * hq * d * 2 * 2
+                      + delta["decode_tokens"] * kvd * 2 * 2 * 2)
+        if attn_n:
+            per_launch = attn_bytes / attn_n
+            achieved = per_launch / (attn_ms / attn_n * 1e-3) / 1e9
+            peak, kind = measured_peak()
+            res["roofline"] = {"bound": "hbm", "kernel": "paged_attn_kernel<128> (fused append + decode attention, "
+                                                          "rank 0)",
+                               "achieved": achieved, "peak": peak, "peak_kind": kind, "unit": "GB/s",
+                               "frac": achieved / peak, "traffic": None,
+                               "algorithmic_bytes_per_launch": int(per_launch), "avg_launch_ms": attn_ms / attn_n}
     sched.close()
     if world > 1:
         dist.barrier()

@@ -51,6 +51,7 @@ typedef struct lt_sched_stats {
     uint64_t steps, admitted, finished, evicted, preempted;
     uint64_t decode_tokens, prefill_tokens, moved_blocks;
     uint32_t running, queued;
+    uint64_t attended_positions;  /* sum over decode tokens of pos + 1: cached rows the attention reads */
 } lt_sched_stats;
 
 lt_status lt_sched_create(lt_kv* kv, const lt_sched_config* cfg, lt_sched** out);

@@ -88,7 +88,7 @@ class lt_sched_config(C.Structure):
 class lt_sched_stats(C.Structure):
     _fields_ = [(name, C.c_uint64) for name in ("steps", "admitted", "finished", "evicted", "preempted",
                                                  "decode_tokens", "prefill_tokens", "moved_blocks")] + \
-               [("running", C.c_uint32), ("queued", C.c_uint32)]
+               [("running", C.c_uint32), ("queued", C.c_uint32), ("attended_positions", C.c_uint64)]
 
 
 _lock = threading.Lock()

@@ -105,8 +105,10 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
 }
 
 // System scope (another GPU over NVLink reads or writes the word).
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
@@ -462,15 +464,18 @@ __device__ __forceinline__ void store_out(const AttnParams& p, int tok, int h, i
 // this launch's count with an acq_rel RMW on this GPU, so the warp that
 // completes the count (n_tok * n_kv_heads items) has every row ordered
 // before it, in this GPU's memory.  It publishes this launch's epoch into
-// every rank's flag for this rank with system-scope release stores; a rank
-// that acquires the flag then reads the rows from here over NVLink.
+// every rank's flag for this rank: one system-scope fence, then relaxed
+// system-scope stores (fence + store is a release; a release store per rank
+// would pay the fence once per rank).  A rank that acquires the flag then
+// reads the rows from here over NVLink.
 __device__ __forceinline__ void peer_done(const AttnParams& p, int lane, int items) {
     if (p.n_peers == 0 || items == 0) return;
     __syncwarp();
     const uint32_t total = (uint32_t)p.n_tok * (uint32_t)p.n_kv_heads;
     if (lane == 0 && atom_add_acq_rel_gpu(p.done_count, (uint32_t)items) + (uint32_t)items == total) {
         *p.done_count = 0u;  // ready for the next launch (which starts after this one ends)
-        for (int r = 0; r < p.n_peers; ++r) st_release_sys(p.peer_flag[r], p.peer_epoch);
+        fence_acq_rel_sys();
+        for (int r = 0; r < p.n_peers; ++r) st_relaxed_sys(p.peer_flag[r], p.peer_epoch);
     }
 }
 
@@ -1663,7 +1668,7 @@ __global__ void __launch_bounds__(256) gather_wait_copy_kernel(const uint32_t* f
                     good = 0;
                     break;
                 }
-                __nanosleep(32);
+                __nanosleep(200);  // gentle: this polls while the attention launch still streams
             }
         }
         if (!good) atomicOr(err, kErrTimeout);

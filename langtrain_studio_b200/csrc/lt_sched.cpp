@@ -260,6 +260,7 @@ lt_status lt_sched_step(lt_sched* s, const void* kv_src, uint32_t src_rows, cons
             if (rc != LT_OK) return fail(s, rc, "decode attention: %s", lt_kv_last_error(s->kv));
         }
         s->st.decode_tokens += nd;
+        for (uint32_t i = 0; i < nd; ++i) s->st.attended_positions += (uint64_t)s->pos[i] + 1;
     }
     if (n_decode) *n_decode = nd;
     // advance, retire (scheduler.rs:452-473)
