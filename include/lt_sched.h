@@ -15,8 +15,29 @@
  *     then preempt the youngest running sequence (it ends with Length);
  *   - a finished sequence keeps its KV in its now idle slot for prefix reuse;
  *   - optionally lt_kv_compact after every step (no reference counterpart).
- * Requests carry lengths only: the prompts are random ids, so no prefix is
- * ever reused and the driver never calls kv_copy.
+ * Length-only requests (lt_sched_submit) stand for random prompts: no prefix
+ * is ever reused and the driver never calls kv_copy.
+ *
+ * Requests that carry token ids (lt_sched_submit_tokens) go through the
+ * reference's token-level admission instead (a driver takes one kind or the
+ * other):
+ *   - placement by the slot-level prefix cache (lt_prefix.h, prefix.rs:58-92):
+ *     the free slot with the longest common prefix keeps it
+ *     (kv_remove(slot, reuse)); when another slot matches at least 16 tokens
+ *     more, its KV is copied (kv_remove(slot, 0) + kv_copy = lt_kv_share);
+ *   - admission while the prompt suffix plus min(output, decode_headroom)
+ *     fits, evicting idle prefixes LRU, re-planning after eviction
+ *     (scheduler.rs:252-317);
+ *   - one batch per step: decode tokens, then prompt chunks, in the order of
+ *     the active list (scheduler.rs:356-407); its blocks include one
+ *     copy-on-write block per first write into a shared partial block;
+ *   - a step that does not fit evicts idle prefixes, else marks the
+ *     youngest sequence finished and skips the step (scheduler.rs:321-334,
+ *     409-411);
+ *   - retire keeps exactly the tokens in KV in the idle slot for reuse
+ *     (prefix.rs:105-112, scheduler.rs:452-473; Vec::swap_remove order).
+ * Generated tokens get negative ids, which no prompt uses.  Adapter ids only
+ * separate prefixes; adapter-group scheduling is not restated.
  *
  * The step's K/V rows and q rows are cut from caller-provided device arrays
  * (synthetic inputs of the benchmark): prompt tokens are appended and their
@@ -52,6 +73,9 @@ typedef struct lt_sched_stats {
     uint64_t decode_tokens, prefill_tokens, moved_blocks;
     uint32_t running, queued;
     uint64_t attended_positions;  /* sum over decode tokens of pos + 1: cached rows the attention reads */
+    /* token requests: prefix copies (kv_copy), prompt tokens admitted, and
+     * those already in KV at admission (the reference's cached_tokens) */
+    uint64_t copies, prompt_tokens, cached_tokens;
 } lt_sched_stats;
 
 lt_status lt_sched_create(lt_kv* kv, const lt_sched_config* cfg, lt_sched** out);
@@ -60,6 +84,10 @@ const char* lt_sched_last_error(const lt_sched* s);
 
 /* Queue a request of prompt_len prompt tokens and out_len output tokens. */
 lt_status lt_sched_submit(lt_sched* s, uint32_t prompt_len, uint32_t out_len);
+/* Queue a request with its prompt token ids (ids >= 0), out_len output
+ * tokens and an adapter id (LT_NO_ADAPTER for none); see the header
+ * comment.  LT_E_ARG when the driver already took length-only requests. */
+lt_status lt_sched_submit_tokens(lt_sched* s, const int32_t* tokens, uint32_t n, uint32_t out_len, int32_t adapter);
 
 /* One scheduler step (see the header comment).  kv_src: device f16
  * [src_rows][n_kv_heads*head_dim] rows for the appended tokens (a contiguous

@@ -38,7 +38,10 @@ EXPORTS = (
     "lt_llama_step_greedy", "lt_llama_launch_count", "lt_llama_profile", "lt_llama_profile_read", "lt_q8_quantize", "lt_q8_matmul", "lt_rms_norm_q8",
     "lt_silu_q8", "lt_argmax_f32", "lt_q8_project", "lt_q8_check",
     "lt_sched_create", "lt_sched_destroy", "lt_sched_last_error", "lt_sched_submit", "lt_sched_step",
-    "lt_sched_get_stats",
+    "lt_sched_get_stats", "lt_sched_submit_tokens",
+    "lt_slot_cache_create", "lt_slot_cache_destroy", "lt_slot_cache_place", "lt_slot_cache_acquire",
+    "lt_slot_cache_release", "lt_slot_cache_evict_lru", "lt_slot_cache_idle_cells", "lt_slot_cache_has_free",
+    "lt_slot_cache_tokens", "lt_slot_cache_slot_state", "lt_slot_cache_set_slot",
 )
 
 
@@ -85,10 +88,15 @@ class lt_sched_config(C.Structure):
     ]
 
 
+class lt_placement(C.Structure):
+    _fields_ = [("slot", C.c_uint32), ("reuse", C.c_uint32), ("copy_src", C.c_int32), ("copy_len", C.c_uint32)]
+
+
 class lt_sched_stats(C.Structure):
     _fields_ = [(name, C.c_uint64) for name in ("steps", "admitted", "finished", "evicted", "preempted",
                                                  "decode_tokens", "prefill_tokens", "moved_blocks")] + \
-               [("running", C.c_uint32), ("queued", C.c_uint32), ("attended_positions", C.c_uint64)]
+               [("running", C.c_uint32), ("queued", C.c_uint32), ("attended_positions", C.c_uint64),
+                ("copies", C.c_uint64), ("prompt_tokens", C.c_uint64), ("cached_tokens", C.c_uint64)]
 
 
 _lock = threading.Lock()
@@ -165,6 +173,18 @@ def _declare(L):
         "lt_sched_submit": (st, [p, u32, u32]),
         "lt_sched_step": (st, [p, p, u32, p, p, C.POINTER(u32), p]),
         "lt_sched_get_stats": (st, [p, C.POINTER(lt_sched_stats)]),
+        "lt_sched_submit_tokens": (st, [p, p, u32, u32, i32]),
+        "lt_slot_cache_create": (st, [u32, C.POINTER(p)]),
+        "lt_slot_cache_destroy": (None, [p]),
+        "lt_slot_cache_place": (st, [p, p, u32, i32, C.POINTER(lt_placement)]),
+        "lt_slot_cache_acquire": (st, [p, C.POINTER(lt_placement), p, u32, i32]),
+        "lt_slot_cache_release": (st, [p, u32, p, u32]),
+        "lt_slot_cache_evict_lru": (i32, [p]),
+        "lt_slot_cache_idle_cells": (u64, [p]),
+        "lt_slot_cache_has_free": (C.c_int, [p]),
+        "lt_slot_cache_tokens": (u32, [p, u32, p, u32]),
+        "lt_slot_cache_slot_state": (st, [p, u32, C.POINTER(i32), C.POINTER(i32), C.POINTER(u64)]),
+        "lt_slot_cache_set_slot": (st, [p, u32, p, u32, i32]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

@@ -700,6 +700,8 @@ size_t local_out_row_bytes(const lt_kv* kv, int dtype) {
 int handle_device(const lt_kv* kv) { return kv->cfg.device; }
 const lt_kv_config* handle_config(const lt_kv* kv) { return &kv->cfg; }
 void count_launch(lt_kv* kv) { kv->launches++; }
+int32_t seq_block_at(const lt_kv* kv, uint32_t seq, uint32_t idx) { return kv->blocks[seq][idx]; }
+uint32_t block_refs(const lt_kv* kv, int32_t block) { return kv->refs[(size_t)block]; }
 }  // namespace ltkv
 
 // ============================================================== C ABI ====

@@ -167,6 +167,10 @@ size_t local_out_row_bytes(const lt_kv* kv, int dtype);  // n_heads*head_dim*ele
 int handle_device(const lt_kv* kv);
 const lt_kv_config* handle_config(const lt_kv* kv);
 void count_launch(lt_kv* kv);
+// Host bookkeeping reads for the scheduler driver: entry idx of seq's block
+// list, and a block's refcount.
+int32_t seq_block_at(const lt_kv* kv, uint32_t seq, uint32_t idx);
+uint32_t block_refs(const lt_kv* kv, int32_t block);
 }  // namespace ltkv
 
 namespace ltkv {

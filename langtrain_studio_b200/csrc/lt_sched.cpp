@@ -23,6 +23,7 @@
 
 #include "lt_kv.h"
 #include "lt_kv_internal.h"
+#include "lt_prefix.h"
 #include "lt_sched.h"
 
 namespace {
@@ -31,8 +32,28 @@ constexpr uint32_t kBlock = LT_KV_BLOCK;
 uint32_t blocks_for(uint32_t tokens) { return (tokens + kBlock - 1) / kBlock; }
 }  // namespace
 
+// Token requests (lt_sched_submit_tokens).
+struct TokReq {
+    std::vector<int32_t> toks;
+    uint32_t out;
+    int32_t adapter;
+};
+struct TokSeq {  // scheduler.rs Seq, the KV side
+    uint32_t slot;
+    std::vector<int32_t> tokens;  // prompt, then sampled tokens
+    uint32_t n_prompt, n_past, max_total;
+    uint64_t admit;  // admission order (youngest = largest)
+    bool finished;
+};
+
 struct lt_sched {
     lt_kv* kv = nullptr;
+    int mode = 0;  // 0: no request yet, 1: length-only requests, 2: token requests
+    lt_slot_cache* sc = nullptr;
+    std::deque<TokReq> tqueue;
+    std::vector<TokSeq> tactive;  // the reference's active list (swap_remove on retire)
+    uint64_t admit_seq = 0;
+    int32_t gen_id = -2;          // next sampled token id (prompt ids are >= 0)
     lt_sched_config cfg{};
     std::string err;
     std::vector<uint8_t> busy;
@@ -152,6 +173,98 @@ void ensure_room(lt_sched* s) {
     }
 }
 
+// ---- token requests: the reference's admission with prefix reuse ----
+
+bool tok_evict(lt_sched* s) {  // prefix.rs:115-125 + Backend::kv_remove(i, 0)
+    const int32_t i = lt_slot_cache_evict_lru(s->sc);
+    if (i < 0) return false;
+    lt_kv_truncate(s->kv, (uint32_t)i, 0);
+    s->st.evicted++;
+    return true;
+}
+
+// scheduler.rs:252-317, KV room in blocks.
+void tok_admit(lt_sched* s) {
+    while (!s->tqueue.empty()) {
+        const TokReq& r = s->tqueue.front();
+        const uint32_t n = (uint32_t)r.toks.size();
+        lt_placement pl{};
+        if (lt_slot_cache_place(s->sc, r.toks.data(), n, r.adapter, &pl) != LT_OK) break;  // every slot busy
+        const int64_t need = (int64_t)blocks_for(n + std::min(r.out, s->cfg.decode_headroom)) - pl.reuse / kBlock;
+        while ((int64_t)lt_kv_free_blocks(s->kv) < need && tok_evict(s)) {
+        }
+        if ((int64_t)lt_kv_free_blocks(s->kv) < need && !s->tactive.empty()) break;
+        TokReq req = std::move(s->tqueue.front());
+        s->tqueue.pop_front();
+        lt_slot_cache_place(s->sc, req.toks.data(), n, req.adapter, &pl);  // eviction may have cleared the prefix
+        if (pl.copy_src >= 0) {
+            lt_kv_truncate(s->kv, pl.slot, 0);
+            lt_kv_share(s->kv, (uint32_t)pl.copy_src, pl.slot, pl.copy_len);  // Backend::kv_copy
+            s->st.copies++;
+        } else {
+            lt_kv_truncate(s->kv, pl.slot, pl.reuse);
+        }
+        lt_slot_cache_acquire(s->sc, &pl, req.toks.data(), n, req.adapter);
+        TokSeq q;
+        q.slot = pl.slot;
+        q.n_prompt = n;
+        q.n_past = pl.reuse;
+        q.max_total = n + req.out;
+        q.admit = ++s->admit_seq;
+        q.finished = false;
+        q.tokens = std::move(req.toks);
+        s->tactive.push_back(std::move(q));
+        s->st.admitted++;
+        s->st.prompt_tokens += n;
+        s->st.cached_tokens += pl.reuse;
+    }
+}
+
+// Blocks a work item (p0, cnt) of the slot takes: the blocks its tokens open,
+// plus a copy-on-write block when it first writes into a shared partial
+// block (kv.rs:99-110).
+uint32_t tok_item_blocks(const lt_sched* s, uint32_t slot, uint32_t p0, uint32_t cnt) {
+    uint32_t b = blocks_for(p0 + cnt) - blocks_for(p0);
+    if (p0 % kBlock && ltkv::block_refs(s->kv, ltkv::seq_block_at(s->kv, slot, p0 / kBlock)) > 1) b += 1;
+    return b;
+}
+
+// scheduler.rs:321-334: evict idle prefixes; else the youngest live sequence
+// finishes (Length) and the step is skipped.
+bool tok_ensure_room(lt_sched* s, uint64_t need) {
+    while (lt_kv_free_blocks(s->kv) < need) {
+        if (tok_evict(s)) continue;
+        TokSeq* y = nullptr;
+        for (TokSeq& q : s->tactive)
+            if (!q.finished && (!y || q.admit > y->admit)) y = &q;
+        if (y) {
+            y->finished = true;
+            s->st.preempted++;
+        }
+        return false;
+    }
+    return true;
+}
+
+// scheduler.rs:452-473: the slot keeps exactly the tokens in KV.
+void tok_retire(lt_sched* s) {
+    for (size_t i = 0; i < s->tactive.size();) {
+        if (!s->tactive[i].finished) {
+            ++i;
+            continue;
+        }
+        TokSeq q = std::move(s->tactive[i]);
+        if (i + 1 != s->tactive.size()) s->tactive[i] = std::move(s->tactive.back());  // Vec::swap_remove
+        s->tactive.pop_back();
+        lt_slot_cache_release(s->sc, q.slot, q.tokens.data(), q.n_past);
+        if (q.n_past < q.tokens.size()) lt_kv_truncate(s->kv, q.slot, q.n_past);
+        s->st.finished++;
+    }
+}
+
+lt_status tok_step(lt_sched* s, const void* kv_src, uint32_t src_rows, const void* q_src, void* out,
+                   uint32_t* n_decode, void* stream);
+
 }  // namespace
 
 extern "C" {
@@ -175,21 +288,40 @@ lt_status lt_sched_create(lt_kv* kv, const lt_sched_config* cfg, lt_sched** out)
     return LT_OK;
 }
 
-void lt_sched_destroy(lt_sched* s) { delete s; }
+void lt_sched_destroy(lt_sched* s) {
+    if (s) lt_slot_cache_destroy(s->sc);
+    delete s;
+}
 
 const char* lt_sched_last_error(const lt_sched* s) { return s ? s->err.c_str() : "null handle"; }
 
 lt_status lt_sched_submit(lt_sched* s, uint32_t prompt_len, uint32_t out_len) {
     if (!s || prompt_len == 0) return LT_E_ARG;
+    if (s->mode == 2) return fail(s, LT_E_ARG, "this driver takes token requests (lt_sched_submit_tokens)");
+    s->mode = 1;
     s->queue.emplace_back(prompt_len, out_len);
+    return LT_OK;
+}
+
+lt_status lt_sched_submit_tokens(lt_sched* s, const int32_t* tokens, uint32_t n, uint32_t out_len, int32_t adapter) {
+    if (!s || !tokens || n == 0) return LT_E_ARG;
+    if (s->mode == 1) return fail(s, LT_E_ARG, "this driver takes length-only requests (lt_sched_submit)");
+    for (uint32_t i = 0; i < n; ++i)
+        if (tokens[i] < 0) return fail(s, LT_E_ARG, "prompt token ids must be >= 0");
+    if (!s->sc) {
+        lt_status rc = lt_slot_cache_create(s->cfg.n_slots, &s->sc);
+        if (rc != LT_OK) return fail(s, rc, "slot cache");
+    }
+    s->mode = 2;
+    s->tqueue.push_back(TokReq{std::vector<int32_t>(tokens, tokens + n), out_len, adapter});
     return LT_OK;
 }
 
 lt_status lt_sched_get_stats(const lt_sched* s, lt_sched_stats* out) {
     if (!s || !out) return LT_E_ARG;
     *out = s->st;
-    out->running = (uint32_t)s->order.size();
-    out->queued = (uint32_t)s->queue.size();
+    out->running = (uint32_t)(s->mode == 2 ? s->tactive.size() : s->order.size());
+    out->queued = (uint32_t)(s->mode == 2 ? s->tqueue.size() : s->queue.size());
     return LT_OK;
 }
 
@@ -199,6 +331,7 @@ lt_status lt_sched_step(lt_sched* s, const void* kv_src, uint32_t src_rows, cons
     if (!s) return LT_E_ARG;
     if (s->cfg.data && (!kv_src || !q_src || !out || src_rows == 0))
         return fail(s, LT_E_ARG, "data mode needs kv_src, q_src and out");
+    if (s->mode == 2) return tok_step(s, kv_src, src_rows, q_src, out, n_decode, stream);
     s->step_no++;
     s->st.steps++;
     admit(s);
@@ -284,3 +417,105 @@ lt_status lt_sched_step(lt_sched* s, const void* kv_src, uint32_t src_rows, cons
 }
 
 }  // extern "C"
+
+namespace {
+
+// One engine iteration for token requests: admit, one batch (decode tokens,
+// then prompt chunks, in active order), sampling's bookkeeping, retire.
+lt_status tok_step(lt_sched* s, const void* kv_src, uint32_t src_rows, const void* q_src, void* out,
+                   uint32_t* n_decode, void* stream) {
+    s->step_no++;
+    s->st.steps++;
+    tok_admit(s);
+    uint32_t nd = 0;
+    if (!s->tactive.empty()) {
+        std::vector<uint32_t>& dec = s->dec;  // indices into tactive
+        std::vector<uint32_t>& pre = s->pre;
+        dec.clear();
+        pre.clear();
+        uint64_t need = 0;
+        for (uint32_t i = 0; i < s->tactive.size(); ++i) {
+            const TokSeq& q = s->tactive[i];
+            if (q.finished) continue;
+            if (q.n_past >= q.n_prompt) {
+                dec.push_back(i);
+                need += tok_item_blocks(s, q.slot, q.n_past, 1);
+            }
+        }
+        for (uint32_t i = 0; i < s->tactive.size(); ++i) {
+            const TokSeq& q = s->tactive[i];
+            if (q.finished || q.n_past >= q.n_prompt) continue;
+            pre.push_back(i);
+            need += tok_item_blocks(s, q.slot, q.n_past, std::min(q.n_prompt - q.n_past, s->cfg.prefill_chunk));
+        }
+        if ((!dec.empty() || !pre.empty()) && tok_ensure_room(s, need)) {
+            s->seqs.clear();
+            s->pos.clear();
+            for (uint32_t i : dec) {
+                s->seqs.push_back(s->tactive[i].slot);
+                s->pos.push_back(s->tactive[i].n_past);
+            }
+            nd = (uint32_t)dec.size();
+            for (uint32_t i : pre) {
+                const TokSeq& q = s->tactive[i];
+                const uint32_t cnt = std::min(q.n_prompt - q.n_past, s->cfg.prefill_chunk);
+                for (uint32_t k = 0; k < cnt; ++k) {
+                    s->seqs.push_back(q.slot);
+                    s->pos.push_back(q.n_past + k);
+                }
+            }
+            const uint32_t n = (uint32_t)s->seqs.size();
+            s->blocks.resize(n);
+            s->slots.resize(n);
+            uint32_t done = 0;
+            lt_status rc = lt_kv_append(s->kv, s->seqs.data(), s->pos.data(), n, s->blocks.data(), s->slots.data(),
+                                        &done, stream);
+            if (rc != LT_OK) return fail(s, rc, "batch claim: %s", lt_kv_last_error(s->kv));
+            if (s->cfg.data) {
+                const lt_kv_config* kc = ltkv::handle_config(s->kv);
+                const size_t kv_row = (size_t)kc->n_kv_heads * kc->head_dim * 2;  // f16 bytes
+                if (n > src_rows || nd > s->cfg.n_slots) return fail(s, LT_E_ARG, "source arrays too small");
+                const char* k = static_cast<const char*>(kv_src) +
+                                (src_rows > n ? (s->step_no * 2654435761ull) % (src_rows - n + 1) : 0) * kv_row;
+                if (n > nd) {
+                    rc = lt_kv_write(s->kv, 0, s->blocks.data() + nd, s->slots.data() + nd, n - nd, k + nd * kv_row,
+                                     k + nd * kv_row, LT_F16, stream);
+                    if (rc != LT_OK) return fail(s, rc, "prefill write: %s", lt_kv_last_error(s->kv));
+                }
+                if (nd) {
+                    const float scale = 1.0f / std::sqrt((float)kc->head_dim);
+                    rc = lt_kv_write_attend(s->kv, 0, s->blocks.data(), s->slots.data(), k, k, LT_F16, q_src, LT_F16,
+                                            s->seqs.data(), s->pos.data(), nd, out, LT_F16, scale, stream);
+                    if (rc != LT_OK) return fail(s, rc, "decode attention: %s", lt_kv_last_error(s->kv));
+                }
+            }
+            s->st.decode_tokens += nd;
+            s->st.prefill_tokens += n - nd;
+            for (uint32_t j = 0; j < nd; ++j) s->st.attended_positions += (uint64_t)s->pos[j] + 1;
+            for (uint32_t i : pre) {
+                TokSeq& q = s->tactive[i];
+                q.n_past += std::min(q.n_prompt - q.n_past, s->cfg.prefill_chunk);
+            }
+            // sample_at order: the decode tokens, then the prompts whose last chunk ran
+            auto sample = [&](TokSeq& q) {
+                if (q.n_past >= q.n_prompt && q.n_past < q.tokens.size()) q.n_past += 1;  // pending token now in KV
+                q.tokens.push_back(s->gen_id--);
+                if (q.tokens.size() >= q.max_total) q.finished = true;
+            };
+            for (uint32_t i : dec) sample(s->tactive[i]);
+            for (uint32_t i : pre)
+                if (s->tactive[i].n_past == s->tactive[i].n_prompt) sample(s->tactive[i]);
+        }
+    }
+    if (n_decode) *n_decode = nd;
+    tok_retire(s);
+    if (s->cfg.compact) {
+        uint32_t moved = 0;
+        lt_status rc = lt_kv_compact(s->kv, &moved, stream);
+        if (rc != LT_OK) return fail(s, rc, "compaction: %s", lt_kv_last_error(s->kv));
+        s->st.moved_blocks += moved;
+    }
+    return LT_OK;
+}
+
+}  // namespace

@@ -47,6 +47,14 @@ class Scheduler:
     def submit(self, prompt_len: int, out_len: int):
         self._check(self._lib.lt_sched_submit(self._h, prompt_len, out_len))
 
+    def submit_tokens(self, tokens, out_len: int, adapter: int = -1):
+        """A request with its prompt token ids: admitted with prefix reuse
+        (lt_sched_submit_tokens)."""
+        import numpy as np
+
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        self._check(self._lib.lt_sched_submit_tokens(self._h, t.ctypes.data, t.size, out_len, adapter))
+
     def step(self, kv_src=None, q_src=None, out=None, stream=None) -> int:
         """One scheduler step; returns the number of decode tokens."""
         nd = C.c_uint32()

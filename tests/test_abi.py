@@ -37,7 +37,7 @@ def test_header_declares_and_library_exports_everything(native):
 
 
 def test_header_compiles_as_c():
-    src = ('#include "lt_kv.h"\n#include "lt_llama.h"\n'
+    src = ('#include "lt_kv.h"\n#include "lt_llama.h"\n#include "lt_sched.h"\n#include "lt_prefix.h"\n'
            'int main(void){ lt_kv_config c = {0}; lt_llama_config m = {0}; (void)c; (void)m; return LT_OK; }\n')
     subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", str(ROOT / "include"), "-x", "c", "-", "-o",
                     "/dev/null"], input=src, text=True, check=True)

@@ -123,6 +123,15 @@ class _OracleData:
     def compact(self):
         return len(self.ok.compact())
 
+    def share(self, src, dst, n):
+        self.ok.share(src, dst, n)
+
+    def seq_blocks(self, s):
+        return self.ok.seq_blocks(s)
+
+    def refs(self):
+        return self.ok.refs()
+
 
 def test_native_scheduler_on_gpu_matches_oracle(oracle_mod):
     import bench
@@ -162,6 +171,62 @@ def test_native_scheduler_on_gpu_matches_oracle(oracle_mod):
             worst = max(worst, float(np.abs(got - facade.last_attn).max()))
     st = sched.stats
     assert st["evicted"] > 0 and st["moved_blocks"] > 0 and st["decode_tokens"] > 0 and st["prefill_tokens"] > 0
+    torch.cuda.synchronize()
+    kref, vref = ok.pool()
+    kd, vd = kv.pool_reference_layout(0)
+    assert np.array_equal(kd, kref[0]) and np.array_equal(vd, vref[0])
+    kv.check()
+    sched.close()
+    kv.close()
+
+
+def test_token_requests_with_prefix_reuse_on_gpu(oracle_mod):
+    """Token requests (lt_sched_submit_tokens): shared system prompts are
+    placed on or copied from the slots that hold them (kv_copy, then
+    copy-on-write of the shared partial block on the GPU), only the suffix is
+    written, decode tokens run the fused append + attention.  The Python
+    restatement (oracle/prefix.py) drives the oracle with the same rows."""
+    from langtrain_studio_b200.kv import KvCache
+    from langtrain_studio_b200.sched import Scheduler
+    from oracle import prefix as pref
+
+    hq, hkv, d = 8, 2, 128
+    n_slots, pool = 8, 160
+    kv = KvCache(1, hkv, d, pool * 16, n_heads=hq, max_seqs=n_slots, max_batch=8192, max_blocks_per_seq=pool,
+                 device=0)
+    sched = Scheduler(kv, n_slots)
+    ok = oracle_mod.OracleKv(1, hkv * d, pool * 16, max_seqs=n_slots)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(9)
+    kv_src = torch.randn((4096, hkv * d), generator=g, device="cuda", dtype=torch.float16)
+    q_src = torch.randn((n_slots, hq * d), generator=g, device="cuda", dtype=torch.float16)
+    out = torch.empty((n_slots, hq * d), device="cuda", dtype=torch.float16)
+    facade = _OracleData(ok, hq, hkv, d)
+    drv = pref.PrefixDriver(facade, n_slots, kv_src=kv_src.cpu().numpy(), q_src=q_src.cpu().numpy())
+    rng = np.random.default_rng(4)
+    worst = 0.0
+    for step in range(90):
+        if step < 70:
+            for _ in range(int(rng.poisson(0.8))):
+                k = int(rng.integers(0, 2))
+                prompt = np.concatenate([(np.arange(40 + 37 * k) * 5 + k) % 997,
+                                         rng.integers(1000, 9000, int(rng.integers(3, 60)))]).astype(np.int32)
+                o = int(rng.integers(3, 30))
+                sched.submit_tokens(prompt, o)
+                drv.submit(prompt, o)
+        nd = sched.step(kv_src, q_src, out)
+        facade.last_attn = None
+        assert drv.step() == nd, step
+        assert np.array_equal(kv.free_list(), ok.free_list()), step
+        assert np.array_equal(kv.refs(), ok.refs()), step
+        for s in range(n_slots):
+            assert np.array_equal(kv.seq_blocks(s), ok.seq_blocks(s)), (step, s)
+        if nd:
+            got = out[:nd].float().cpu().numpy()
+            np.testing.assert_allclose(got, facade.last_attn, rtol=1e-3, atol=2e-3)
+            worst = max(worst, float(np.abs(got - facade.last_attn).max()))
+    st = sched.stats
+    assert st["copies"] > 0 and st["cached_tokens"] > 0 and st["decode_tokens"] > 0, st
     torch.cuda.synchronize()
     kref, vref = ok.pool()
     kd, vd = kv.pool_reference_layout(0)

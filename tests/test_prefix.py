@@ -1,0 +1,245 @@
+"""The slot-level prefix cache and token-level admission (include/lt_prefix.h,
+lt_sched_submit_tokens) on CPU.
+
+- The reference's own known-answer tests of SlotCache (prefix.rs:136-181),
+  ported verbatim, against the native cache and the Python restatement
+  (oracle/prefix.py).
+- Random place / acquire / release / evict sequences with shared prompt
+  prefixes: native and restatement take identical decisions.
+- The native scheduler on token requests against the restatement of the
+  reference's admission (placement, kv_copy, eviction, preemption, retire)
+  over the oracle's KvCache: identical tables, refcounts, free lists and
+  counts after every step, on a shared-system-prompt workload.
+"""
+import numpy as np
+import pytest
+
+from langtrain_studio_b200.kv import KvCache
+from langtrain_studio_b200.prefix import Placement, SlotCache
+from langtrain_studio_b200.sched import Scheduler
+from oracle import prefix as ref
+
+
+def toks(n):
+    return list(range(n))
+
+
+@pytest.fixture(params=["native", "restated"])
+def cache_kind(request):
+    return request.param
+
+
+def make(kind, n):
+    return SlotCache(n) if kind == "native" else ref.SlotCache(n)
+
+
+def place(c, prompt, adapter=-1):
+    p = c.place(prompt, adapter)
+    if p is None or isinstance(p, Placement):
+        return p
+    slot, reuse, src, n = p
+    return Placement(slot, reuse, (src, n) if src >= 0 else None)
+
+
+def acquire(c, p, prompt, adapter=-1):
+    if isinstance(c, SlotCache):
+        c.acquire(p, prompt, adapter)
+    else:
+        c.acquire((p.slot, p.reuse, p.copy_from[0] if p.copy_from else -1, p.copy_from[1] if p.copy_from else 0),
+                  prompt, adapter)
+
+
+def set_slot(c, slot, tokens, adapter=-1):
+    if isinstance(c, SlotCache):
+        c.set_slot(slot, tokens, adapter)
+    else:
+        c.tokens[slot], c.adapter[slot] = list(tokens), adapter
+
+
+# ---- prefix.rs:136-181, ported ----
+
+def test_prefers_slot_with_longest_prefix(cache_kind):
+    c = make(cache_kind, 3)
+    c.release(1, toks(50))
+    prompt = toks(50) + [999, 998]
+    assert place(c, prompt) == Placement(slot=1, reuse=50, copy_from=None)
+
+
+def test_full_match_still_evaluates_last_token(cache_kind):
+    c = make(cache_kind, 1)
+    c.release(0, toks(10))
+    assert place(c, toks(10)).reuse == 9
+
+
+def test_copies_from_busy_slot_when_worth_it(cache_kind):
+    c = make(cache_kind, 2)
+    prompt = toks(100)
+    p0 = place(c, prompt)
+    acquire(c, p0, prompt)
+    set_slot(c, p0.slot, toks(100))
+    p1 = place(c, prompt)
+    assert p1.slot != p0.slot
+    assert p1.copy_from == (p0.slot, 99)
+
+
+def test_adapters_do_not_share_kv(cache_kind):
+    ADAPTER = 7  # the reference's Some("support")
+    c = make(cache_kind, 1)
+    c.release(0, toks(40))
+    set_slot(c, 0, toks(40), ADAPTER)
+    assert place(c, toks(40)).reuse == 0
+    assert place(c, toks(40), ADAPTER).reuse == 39
+
+
+def test_evicts_least_recently_used(cache_kind):
+    c = make(cache_kind, 2)
+    c.release(0, toks(5))
+    c.release(1, toks(5))
+    assert c.evict_lru() == 0
+    assert c.idle_cells() == 5
+
+
+def test_every_slot_busy_places_nothing(cache_kind):
+    c = make(cache_kind, 2)
+    for _ in range(2):
+        p = place(c, toks(8))
+        acquire(c, p, toks(8))
+    assert place(c, toks(8)) is None and not c.has_free()
+
+
+# ---- native == restatement on random sequences ----
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_random_operations_match_restatement(seed):
+    rng = np.random.default_rng(seed)
+    n = 6
+    nat, res = SlotCache(n), ref.SlotCache(n)
+    systems = [list(rng.integers(0, 50, int(rng.integers(10, 60)))) for _ in range(3)]
+    held = {}
+    for _ in range(600):
+        op = rng.random()
+        if op < 0.45:
+            prompt = list(systems[int(rng.integers(0, 3))]) + list(rng.integers(0, 50, int(rng.integers(0, 40))))
+            prompt = prompt[:int(rng.integers(1, len(prompt) + 1))]
+            ad = int(rng.integers(-1, 2))
+            pn, pr = place(nat, prompt, ad), place(res, prompt, ad)
+            assert pn == pr, (pn, pr)
+            if pn is not None and rng.random() < 0.7:
+                acquire(nat, pn, prompt, ad)
+                acquire(res, pn, prompt, ad)
+                held[pn.slot] = prompt
+        elif op < 0.8 and held:
+            slot = int(rng.choice(list(held)))
+            kv = held.pop(slot)[:int(rng.integers(0, 80))] + list(rng.integers(100, 200, int(rng.integers(0, 5))))
+            nat.release(slot, kv)
+            res.release(slot, kv)
+        else:
+            assert nat.evict_lru() == res.evict_lru()
+        assert nat.idle_cells() == res.idle_cells()
+        for s in range(n):
+            assert nat.tokens(s) == [int(x) for x in res.tokens[s]]
+            busy, ad, lu = nat.slot_state(s)
+            assert (busy, ad, lu) == (res.busy[s], res.adapter[s], res.last_used[s])
+
+
+# ---- the scheduler's token-level admission ----
+
+class _OracleKv:
+    """KvCache facade over the oracle (bookkeeping only)."""
+
+    def __init__(self, ok):
+        self.ok = ok
+
+    def free_blocks(self):
+        return self.ok.free_blocks()
+
+    def truncate(self, s, frm):
+        self.ok.truncate(s, frm)
+
+    def share(self, src, dst, n):
+        self.ok.share(src, dst, n)
+
+    def append_batch(self, seqs, pos):
+        rc, done, b, sl = self.ok.append_batch(np.asarray(seqs), np.asarray(pos))
+        assert rc == 0, (rc, done)
+        return b, sl
+
+    def seq_blocks(self, s):
+        return self.ok.seq_blocks(s)
+
+    def refs(self):
+        return self.ok.refs()
+
+    def compact(self):
+        return len(self.ok.compact())
+
+
+KEYS = ["admitted", "finished", "evicted", "preempted", "copies", "prompt_tokens", "cached_tokens",
+        "decode_tokens", "prefill_tokens", "moved_blocks"]
+
+
+def _workload(rng, n_systems, step):
+    """Chat-like arrivals: a shared system prompt (one of n_systems), a random
+    user suffix; now and then a follow-up that repeats a whole earlier prompt."""
+    out = []
+    for _ in range(int(rng.poisson(1.2))):
+        sysp = (np.arange(48 + 40 * (k := int(rng.integers(0, n_systems)))) * 7 + k) % 1000
+        user = rng.integers(1000, 30000, int(rng.integers(4, 120)))
+        out.append((np.concatenate([sysp, user]).astype(np.int32), int(rng.integers(4, 48))))
+    return out
+
+
+@pytest.mark.parametrize("seed,pool,slots,systems,pressure", [(0, 120, 8, 2, False), (1, 60, 6, 3, True),
+                                                               (2, 200, 12, 1, False)])
+def test_token_admission_matches_restatement(oracle_mod, seed, pool, slots, systems, pressure):
+    """pressure: a pool far below the demand (preemption, eviction of every
+    idle prefix); otherwise the shared system prompts are reused."""
+    kv = KvCache(1, 2, 64, pool * 16, n_heads=4, max_seqs=slots, max_batch=1 << 14, max_blocks_per_seq=pool,
+                 device=-1)
+    sched = Scheduler(kv, slots, data=False)
+    ok = oracle_mod.OracleKv(1, 2 * 64, pool * 16, max_seqs=slots)
+    drv = ref.PrefixDriver(_OracleKv(ok), slots)
+    rng = np.random.default_rng(seed)
+    for step in range(250):
+        if step < 200:
+            for prompt, out in _workload(rng, systems, step):
+                sched.submit_tokens(prompt, out)
+                drv.submit(prompt, out)
+        sched.step()
+        drv.step()
+        st = sched.stats
+        for k in KEYS:
+            assert drv.stats[k] == st[k], (step, k, drv.stats[k], st[k])
+        assert st["running"] == len(drv.active) and st["queued"] == len(drv.queue)
+        assert np.array_equal(kv.free_list(), ok.free_list()), step
+        assert np.array_equal(kv.refs(), ok.refs()), step
+        for s in range(slots):
+            assert np.array_equal(kv.seq_blocks(s), ok.seq_blocks(s)), (step, s)
+    st = sched.stats
+    reuse = st["cached_tokens"] / st["prompt_tokens"]
+    print(f"prefix reuse {reuse:.1%} of {st['prompt_tokens']} prompt tokens; copies {st['copies']}, "
+          f"evictions {st['evicted']}, preemptions {st['preempted']}")
+    assert st["finished"] > 50, st
+    if pressure:
+        assert st["preempted"] > 0 and st["evicted"] > 0, st
+    else:
+        assert reuse > 0.2 and st["cached_tokens"] > 0, st
+    sched.close()
+
+
+def test_one_kind_of_request_per_driver():
+    from langtrain_studio_b200.kv import KvError
+
+    kv = KvCache(1, 2, 64, 64 * 16, n_heads=4, max_seqs=4, max_batch=1 << 12, device=-1)
+    s1 = Scheduler(kv, 4, data=False)
+    s1.submit(10, 5)
+    with pytest.raises(KvError):
+        s1.submit_tokens([1, 2, 3], 5)
+    s1.close()
+    s2 = Scheduler(kv, 4, data=False)
+    s2.submit_tokens([1, 2, 3], 5)
+    with pytest.raises(KvError):
+        s2.submit(10, 5)
+    with pytest.raises(KvError):
+        s2.submit_tokens([1, -5], 5)
+    s2.close()
