@@ -243,3 +243,32 @@ def test_one_kind_of_request_per_driver():
     with pytest.raises(KvError):
         s2.submit_tokens([1, -5], 5)
     s2.close()
+
+
+def test_shared_system_prompt_reuse():
+    """The reference's one published number for this path: 93-97 % of prompt
+    tokens reused on a shared system prompt (engine/README.md:100).  A
+    480-token system prompt with 10-40-token user turns: the first request on
+    each slot prefills it, every later one reuses it from its slot."""
+    pool, slots = 400, 8
+    kv = KvCache(1, 2, 64, pool * 16, n_heads=4, max_seqs=slots, max_batch=1 << 14, max_blocks_per_seq=pool,
+                 device=-1)
+    s = Scheduler(kv, slots, data=False)
+    rng = np.random.default_rng(0)
+    system = (np.arange(480) * 13) % 997
+    first = None
+    for step in range(300):
+        for _ in range(int(rng.poisson(0.5))):
+            s.submit_tokens(np.concatenate([system, rng.integers(1000, 30000, int(rng.integers(10, 40)))]),
+                            int(rng.integers(8, 64)))
+        s.step()
+        st = s.stats
+        if first is None and st["admitted"] >= slots:
+            first = (st["prompt_tokens"], st["cached_tokens"])
+    st = s.stats
+    overall = st["cached_tokens"] / st["prompt_tokens"]
+    steady = (st["cached_tokens"] - first[1]) / (st["prompt_tokens"] - first[0])
+    print(f"reuse {overall:.1%} overall, {steady:.1%} after every slot has served once")
+    assert 0.93 <= steady <= 0.97, steady
+    assert overall > 0.8, overall
+    s.close()
