@@ -108,6 +108,15 @@ struct lt_kv {
     std::vector<uint32_t> lens;
     std::vector<uint32_t> refs;
     std::vector<int32_t> free_list;  // stack: back() is popped first
+    // free_list[0, free_run) is the run nb-1, nb-2, ..., nb-free_run (ids no
+    // one touched since the last compaction): compaction only sorts the rest.
+    size_t free_run = 0;
+    // The sequence and table index that took a block (alloc, copy-on-write,
+    // compaction move), and whether it was ever shared (then a move falls back
+    // to scanning every table).
+    std::vector<int32_t> owner_seq, owner_idx;
+    std::vector<uint8_t> ever_shared;
+    std::vector<int32_t> cmp_low;  // compaction scratch
 
     std::string err;
     bool dev = false;
@@ -328,8 +337,12 @@ lt_status append_one(lt_kv* kv, uint32_t seq, uint32_t pos, int32_t* block_out, 
         if (kv->free_list.empty()) return fail(kv, LT_E_FULL, "KV cache full");
         const int32_t b = kv->free_list.back();  // kv.rs:67-74
         kv->free_list.pop_back();
+        kv->free_run = std::min(kv->free_run, kv->free_list.size());
         kv->refs[b] = 1;
         bl.push_back(b);
+        kv->owner_seq[b] = (int32_t)seq;
+        kv->owner_idx[b] = (int32_t)bl.size() - 1;
+        kv->ever_shared[b] = 0;
         mark_dirty(kv, seq, (uint32_t)bl.size() - 1);
     } else {
         const int32_t last = bl.back();
@@ -347,9 +360,13 @@ lt_status append_one(lt_kv* kv, uint32_t seq, uint32_t pos, int32_t* block_out, 
                 kv->mark_dst[nb] = kv->epoch;
             }
             kv->free_list.pop_back();
+            kv->free_run = std::min(kv->free_run, kv->free_list.size());
             kv->refs[nb] = 1;
             release_block(kv, last);
             bl.back() = nb;
+            kv->owner_seq[nb] = (int32_t)seq;
+            kv->owner_idx[nb] = (int32_t)bl.size() - 1;
+            kv->ever_shared[nb] = 0;
             mark_dirty(kv, seq, (uint32_t)bl.size() - 1);
         }
     }
@@ -740,6 +757,10 @@ lt_status lt_kv_create(const lt_kv_config* cfg, lt_kv** out) {
     kv->refs.assign(kv->n_blocks, 0);
     kv->free_list.resize(kv->n_blocks);
     for (uint32_t i = 0; i < kv->n_blocks; ++i) kv->free_list[i] = (int32_t)(kv->n_blocks - 1 - i);  // kv.rs:45
+    kv->free_run = kv->n_blocks;
+    kv->owner_seq.assign(kv->n_blocks, -1);
+    kv->owner_idx.assign(kv->n_blocks, -1);
+    kv->ever_shared.assign(kv->n_blocks, 0);
     kv->dirty_from.assign(c.max_seqs, kClean);
     kv->fold_mark.assign(c.max_seqs, 0);
     kv->fold_pos.assign(c.max_seqs, 0);
@@ -1024,7 +1045,10 @@ void lt_kv_share(lt_kv* kv, uint32_t src, uint32_t dst, uint32_t len) {  // kv.r
     if (slen == 0) return;  // unknown source (share(x, x, _) lands here as well)
     len = std::min(len, slen);
     const size_t nb = (len + kBlock - 1) / kBlock;
-    for (size_t i = 0; i < nb; ++i) kv->refs[kv->blocks[src][i]] += 1;
+    for (size_t i = 0; i < nb; ++i) {
+        kv->refs[kv->blocks[src][i]] += 1;
+        kv->ever_shared[kv->blocks[src][i]] = 1;
+    }
     if (len > 0) {
         kv->blocks[dst].assign(kv->blocks[src].begin(), kv->blocks[src].begin() + nb);
         kv->lens[dst] = len;
@@ -1039,42 +1063,68 @@ lt_status lt_kv_compact(lt_kv* kv, uint32_t* n_moved, void* stream) {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     lt_status rc = flush(kv, st);
     if (rc) return rc;
+    // The rule: the j-th lowest free block receives the j-th highest live
+    // block while it is lower (so live blocks end up as [0, n_live)).  Free
+    // ids at or above W = nb - free_run were untouched since the last
+    // compaction; only the free ids below W (released since) need sorting,
+    // and the live ids are found by walking down from W - 1.
     const uint32_t nb = kv->n_blocks;
-    std::vector<int32_t> fr, lv, remap(nb);
-    for (uint32_t b = 0; b < nb; ++b) {
-        remap[b] = (int32_t)b;
-        if (kv->refs[b] == 0) fr.push_back((int32_t)b);
-    }
-    for (uint32_t b = nb; b-- > 0;)
-        if (kv->refs[b] != 0) lv.push_back((int32_t)b);
+    const size_t r = std::min(kv->free_run, kv->free_list.size());
+    const int32_t W = (int32_t)(nb - r);
+    std::vector<int32_t>& low = kv->cmp_low;
+    low.assign(kv->free_list.begin() + (std::ptrdiff_t)r, kv->free_list.end());
+    std::sort(low.begin(), low.end());
     std::vector<int2> moves;
-    for (size_t j = 0; j < fr.size() && j < lv.size() && fr[j] < lv[j]; ++j) {
-        const int32_t src = lv[j], dst = fr[j];
-        moves.push_back(make_int2(src, dst));
-        kv->refs[dst] = kv->refs[src];
-        kv->refs[src] = 0;
-        remap[src] = dst;
-    }
-    std::vector<int2> tw;
-    if (!moves.empty()) {
-        for (uint32_t s = 0; s < kv->cfg.max_seqs; ++s) {
-            auto& bl = kv->blocks[s];
-            for (size_t i = 0; i < bl.size(); ++i) {
-                const int32_t nbk = remap[bl[i]];
-                if (nbk != bl[i]) {
-                    bl[i] = nbk;
-                    const size_t idx = (size_t)s * kv->max_blocks + i;
-                    if (kv->dev && kv->dev_shadow[idx] != nbk) {
-                        kv->dev_shadow[idx] = nbk;
-                        tw.push_back(make_int2((int)idx, nbk));
-                    }
-                }
+    {
+        int32_t cand = W - 1;     // next live candidate from the top
+        size_t top = low.size();  // low[top - 1] is the highest free id not yet passed by cand
+        for (size_t j = 0; j < low.size(); ++j) {
+            while (cand >= 0 && top > 0 && low[top - 1] == cand) {
+                --cand;
+                --top;
             }
+            if (cand < 0 || low[j] >= cand) break;
+            const int32_t src = cand--, dst = low[j];
+            moves.push_back(make_int2(src, dst));
+            kv->refs[dst] = kv->refs[src];
+            kv->refs[src] = 0;
+            kv->owner_seq[dst] = kv->owner_seq[src];
+            kv->owner_idx[dst] = kv->owner_idx[src];
+            kv->ever_shared[dst] = kv->ever_shared[src];
         }
     }
-    kv->free_list.clear();
-    for (uint32_t b = nb; b-- > 0;)
-        if (kv->refs[b] == 0) kv->free_list.push_back((int32_t)b);
+    std::vector<int2> tw;
+    auto remap_entry = [&](uint32_t s, size_t i, int32_t nbk) {
+        kv->blocks[s][i] = nbk;
+        const size_t idx = (size_t)s * kv->max_blocks + i;
+        if (kv->dev && kv->dev_shadow[idx] != nbk) {
+            kv->dev_shadow[idx] = nbk;
+            tw.push_back(make_int2((int)idx, nbk));
+        }
+    };
+    bool shared = false;
+    for (const int2& m : moves) shared |= kv->ever_shared[m.y] != 0;
+    if (!shared) {
+        // each moved block sits in exactly one table entry: the one that took it
+        for (const int2& m : moves) {
+            const int32_t s = kv->owner_seq[m.y], i = kv->owner_idx[m.y];
+            remap_entry((uint32_t)s, (size_t)i, m.y);
+        }
+    } else if (!moves.empty()) {
+        std::vector<int32_t> remap(nb);
+        for (uint32_t b = 0; b < nb; ++b) remap[b] = (int32_t)b;
+        for (const int2& m : moves) remap[m.x] = m.y;
+        for (uint32_t s = 0; s < kv->cfg.max_seqs; ++s) {
+            auto& bl = kv->blocks[s];
+            for (size_t i = 0; i < bl.size(); ++i)
+                if (remap[bl[i]] != bl[i]) remap_entry(s, i, remap[bl[i]]);
+        }
+    }
+    // Free blocks are now exactly [n_live, nb): the list nb-1, ..., n_live,
+    // whose first r entries are already in place.
+    const size_t F = kv->free_list.size();
+    for (size_t i = r; i < F; ++i) kv->free_list[i] = (int32_t)(nb - 1 - i);
+    kv->free_run = F;
     if (n_moved) *n_moved = (uint32_t)moves.size();
     if (kv->dev && (!moves.empty() || !tw.empty())) {
         rc = run_plan(kv, moves, tw, st);

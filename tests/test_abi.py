@@ -181,3 +181,42 @@ def test_compaction_bookkeeping_matches_oracle(oracle_mod):
     compare_state(kv, ok, max_seqs)
     live = np.nonzero(kv.refs())[0]
     assert list(live) == list(range(live.size))
+
+
+@pytest.mark.parametrize("share_rate", [0.0, 0.03])
+def test_compaction_paths_match_oracle(oracle_mod, share_rate):
+    """Compaction after every few operations, over a larger pool: with no
+    sharing every moved block is rewritten through its owner entry; with
+    occasional kv_copy some moves fall back to scanning every table.  The
+    moves, tables, refcounts and free list must equal the oracle's full scan."""
+    from langtrain_studio_b200.kv import KvError
+
+    max_seqs, pool = 24, 16 * 300
+    kv = host_kv(1, 1, 64, pool, max_seqs=max_seqs)
+    ok = oracle_mod.OracleKv(1, 64, pool, max_seqs=max_seqs)
+    rng = np.random.default_rng(int(share_rate * 1000) + 5)
+    for step in range(1500):
+        r = rng.random()
+        if r < 0.6:
+            s = int(rng.integers(0, max_seqs))
+            n = int(rng.integers(1, 40))
+            seqs, pos = np.full(n, s), np.arange(kv.len(s), kv.len(s) + n)
+            rc, done, bo, so = ok.append_batch(seqs, pos)
+            try:
+                b, sl = kv.append_batch(seqs, pos)
+                assert rc == 0 and np.array_equal(b, bo) and np.array_equal(sl, so)
+            except KvError as e:
+                assert e.code == rc and e.n_done == done
+        elif r < 0.8:
+            s = int(rng.integers(0, max_seqs))
+            frm = int(rng.integers(0, kv.len(s) + 1))
+            kv.truncate(s, frm)
+            ok.truncate(s, frm)
+        elif r < 0.8 + share_rate:
+            src, dst = (int(x) for x in rng.integers(0, max_seqs, 2))
+            n = int(rng.integers(0, kv.len(src) + 1))
+            kv.share(src, dst, n)
+            ok.share(src, dst, n)
+        else:
+            assert kv.compact() == len(ok.compact()), step
+        compare_state(kv, ok, max_seqs)
