@@ -1102,8 +1102,14 @@ lt_status lt_kv_compact(lt_kv* kv, uint32_t* n_moved, void* stream) {
             tw.push_back(make_int2((int)idx, nbk));
         }
     };
+    // The owner entry is used only when it still holds the moved block (it
+    // always does for a block never shared; checked anyway).
     bool shared = false;
-    for (const int2& m : moves) shared |= kv->ever_shared[m.y] != 0;
+    for (const int2& m : moves) {
+        const int32_t s = kv->owner_seq[m.y], i = kv->owner_idx[m.y];
+        shared |= kv->ever_shared[m.y] != 0 || s < 0 || (uint32_t)s >= kv->cfg.max_seqs || i < 0 ||
+                  (size_t)i >= kv->blocks[(size_t)s].size() || kv->blocks[(size_t)s][(size_t)i] != m.x;
+    }
     if (!shared) {
         // each moved block sits in exactly one table entry: the one that took it
         for (const int2& m : moves) {
