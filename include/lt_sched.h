@@ -86,7 +86,9 @@ const char* lt_sched_last_error(const lt_sched* s);
 lt_status lt_sched_submit(lt_sched* s, uint32_t prompt_len, uint32_t out_len);
 /* Queue a request with its prompt token ids (ids >= 0), out_len output
  * tokens and an adapter id (LT_NO_ADAPTER for none); see the header
- * comment.  LT_E_ARG when the driver already took length-only requests. */
+ * comment.  LT_E_ARG when the driver already took length-only requests, or
+ * when the prompt plus one token exceeds the context window (the pool, or
+ * max_blocks_per_seq blocks; scheduler.rs:234-237). */
 lt_status lt_sched_submit_tokens(lt_sched* s, const int32_t* tokens, uint32_t n, uint32_t out_len, int32_t adapter);
 
 /* One scheduler step (see the header comment).  kv_src: device f16

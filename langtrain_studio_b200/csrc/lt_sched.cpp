@@ -308,6 +308,15 @@ lt_status lt_sched_submit_tokens(lt_sched* s, const int32_t* tokens, uint32_t n,
     if (s->mode == 1) return fail(s, LT_E_ARG, "this driver takes length-only requests (lt_sched_submit)");
     for (uint32_t i = 0; i < n; ++i)
         if (tokens[i] < 0) return fail(s, LT_E_ARG, "prompt token ids must be >= 0");
+    // scheduler.rs:234-237 (enqueue): the prompt and one generated token must fit
+    const lt_kv_config* kc = ltkv::handle_config(s->kv);
+    const uint64_t n_ctx = std::min<uint64_t>(lt_kv_capacity(s->kv),
+                                              (uint64_t)(kc->max_blocks_per_seq ? std::min(kc->max_blocks_per_seq,
+                                                                                           lt_kv_n_blocks(s->kv))
+                                                                                : lt_kv_n_blocks(s->kv)) *
+                                                  kBlock);
+    if ((uint64_t)n + 1 > n_ctx)
+        return fail(s, LT_E_ARG, "prompt has %u tokens; context window is %llu", n, (unsigned long long)n_ctx);
     if (!s->sc) {
         lt_status rc = lt_slot_cache_create(s->cfg.n_slots, &s->sc);
         if (rc != LT_OK) return fail(s, rc, "slot cache");
