@@ -36,8 +36,15 @@ class KvNonContiguous(KvError):
     pass
 
 
-def _ptr(a: np.ndarray):
-    return a.ctypes.data_as(C.c_void_p)
+def _ptr(a: np.ndarray) -> int:
+    """Address of a C-contiguous numpy array for a c_void_p parameter (the
+    array must outlive the call).  ctypes.from_buffer is ~3x cheaper than
+    ndarray.ctypes, which matters on the per-step call path; read-only and
+    empty arrays take the general route."""
+    try:
+        return C.addressof(C.c_char.from_buffer(a))
+    except (TypeError, ValueError, BufferError):
+        return a.ctypes.data
 
 
 def _dptr(t) -> C.c_void_p:
@@ -107,6 +114,8 @@ class KvCache:
             raise KvError(rc, f"lt_kv_create failed with status {rc}")
         self._h = h
         self.n_layers, self.n_kv_heads, self.head_dim = n_layers, n_kv_heads, head_dim
+        # model.rs:402: 1 / sqrt(head_dim) in f32
+        self.default_scale = float(np.float32(1.0) / np.float32(math.sqrt(head_dim)))
         self.n_heads = cfg.n_heads
         self.kv_dim = n_kv_heads * head_dim
         self.max_seqs, self.max_batch, self.device = max_seqs, max_batch, device
@@ -189,7 +198,7 @@ class KvCache:
         if out is None:
             out = torch.empty((n, self.n_heads * self.head_dim), dtype=out_dtype or torch.float32, device=q.device)
         if scale is None:
-            scale = float(np.float32(1.0) / np.float32(math.sqrt(self.head_dim)))
+            scale = self.default_scale
         self._check(self._lib.lt_kv_attend(self._h, layer, _dptr(q), _dtype_code(q), _ptr(seqs), _ptr(positions), n,
                                            _dptr(out), _dtype_code(out), scale, _stream(stream)))
         return out
@@ -205,7 +214,7 @@ class KvCache:
         if out is None:
             out = torch.empty((n, self.n_heads * self.head_dim), dtype=out_dtype or torch.float32, device=q.device)
         if scale is None:
-            scale = float(np.float32(1.0) / np.float32(math.sqrt(self.head_dim)))
+            scale = self.default_scale
         self._check(self._lib.lt_kv_write_attend(
             self._h, layer, _ptr(blocks), _ptr(slots), _dptr(k), _dptr(v), _dtype_code(k), _dptr(q), _dtype_code(q),
             _ptr(seqs), _ptr(positions), n, _dptr(out), _dtype_code(out), scale, _stream(stream)))
@@ -241,7 +250,7 @@ class KvCache:
             out = torch.empty((n, self.peer_ranks * self.n_heads * self.head_dim), dtype=out_dtype or torch.float32,
                               device=q.device)
         if scale is None:
-            scale = float(np.float32(1.0) / np.float32(math.sqrt(self.head_dim)))
+            scale = self.default_scale
         self._check(self._lib.lt_kv_attend_gather(self._h, layer, _dptr(q), _dtype_code(q), _ptr(seqs),
                                                   _ptr(positions), n, _dptr(out), _dtype_code(out), scale,
                                                   _stream(stream)))
@@ -259,7 +268,7 @@ class KvCache:
             out = torch.empty((n, self.peer_ranks * self.n_heads * self.head_dim), dtype=out_dtype or torch.float32,
                               device=q.device)
         if scale is None:
-            scale = float(np.float32(1.0) / np.float32(math.sqrt(self.head_dim)))
+            scale = self.default_scale
         self._check(self._lib.lt_kv_write_attend_gather(
             self._h, layer, _ptr(blocks), _ptr(slots), _dptr(k), _dptr(v), _dtype_code(k), _dptr(q), _dtype_code(q),
             _ptr(seqs), _ptr(positions), n, _dptr(out), _dtype_code(out), scale, _stream(stream)))
