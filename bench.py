@@ -509,6 +509,86 @@ def run_c3(args, rank, world, local):
     return res
 
 
+def run_prefill(args, rank, world, local):
+    """Chunked prefill attention (the reference's prefill chunks,
+    scheduler.rs:388-407): 4 sequences with 2048 cached tokens each take a
+    256-token prompt chunk per step -- append, K/V write, and causal attention
+    of all 1024 chunk tokens in one call (token at position p attends [0, p]).
+    The tokens of a sequence share its first 128 blocks, which the tensor-core
+    prefix pass attends once per group; the stream-K launch covers each
+    token's own blocks.  Each step ends with kv_remove back to 2048 tokens, so
+    every step does the same work.  Llama-3-8B attention shape, one layer."""
+    import torch
+
+    from langtrain_studio_b200 import kv as kv_mod
+
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    n_seq, ctx, chunk = 4, 2048, 256
+    hq, hkv, d = 32, 8, 128
+    kvd = hkv * d
+    n_blocks = n_seq * ((ctx + chunk + BLOCK - 1) // BLOCK) + 8
+    kv = kv_mod.KvCache(1, hkv, d, n_blocks * BLOCK, n_heads=hq, max_seqs=n_seq, max_batch=8192, device=local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(shard_seed(rank))
+    rnd = lambda n, w=kvd: torch.randn((n, w), generator=g, device=dev, dtype=torch.float16)
+    for sq in range(n_seq):
+        b, s = kv.append_batch(np.full(ctx, sq), np.arange(ctx))
+        kv.write(0, b, s, rnd(ctx), rnd(ctx))
+    seqs = np.repeat(np.arange(n_seq, dtype=np.uint32), chunk)
+    pos = np.tile(np.arange(ctx, ctx + chunk, dtype=np.uint32), n_seq)
+    n = seqs.size
+    k, v, q = rnd(n), rnd(n), rnd(n, hq * d)
+    out = torch.empty_like(q)
+
+    def step():
+        b, s = kv.append_batch(seqs, pos)
+        kv.write(0, b, s, k, v)
+        kv.attend(0, q, seqs, pos, out=out)
+        for sq in range(n_seq):
+            kv.truncate(sq, ctx)  # Backend::kv_remove back to the cached context
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    casc0 = kv.cascade_launches()
+    kv.profile(True)
+    l0 = kv.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    attn_ms, attn_n = kv.profile_read()
+    kv.check()
+    flops = float(((pos.astype(np.int64) + 1) * hq * d * 4).sum())  # S = QK^T and O = PV, 2 flop per MAC
+    uniq = n_seq * (ctx + chunk) * kvd * 2 * 2 + n * (hq * d * 2 * 2 + kvd * 2 * 2)  # K/V once, q, out, new rows
+    tf = flops / (attn_ms / attn_n * 1e-3) / 1e12
+    with open(ROOT / "MEASURED_PEAKS.json") as f:
+        peaks = json.load(f)
+    peak_tf = float(peaks.get("bf16_tflops", 1590.0))
+    res = _json_common(args, world, n * args.steps / (ms * 1e-3), "tokens/s", ms / args.steps, {
+        "workload": "chunked prefill (SURVEY 8(f)2): 4 seqs x 2048 cached tokens, a 256-token chunk each per step, "
+                    "causal attention of the 1024 chunk tokens in one call, Llama-3-8B attention shape, one layer",
+        "n_heads": hq, "n_kv_heads": hkv, "head_dim": d, "block_tokens": BLOCK})
+    res.update({
+        "roofline": {"bound": "tensor", "kernel": "prefix_attn_kernel<128> (tcgen05) + paged_attn_kernel<128>",
+                     "achieved": tf, "peak": peak_tf, "peak_kind": "measured (cuBLAS bf16 GEMM, burst)",
+                     "unit": "TFLOP/s", "frac": tf / peak_tf, "traffic": None,
+                     "algorithmic_flops_per_launch": flops,
+                     "note": "q and P enter the tensor cores as f16 value + f16 residual, so the MMAs carry "
+                             "2x these FLOPs",
+                     "avg_launch_ms": attn_ms / attn_n},
+        "hbm_gbs_unique": uniq / (attn_ms / attn_n * 1e-3) / 1e9,
+        "cascade_launches_per_step": (kv.cascade_launches() - casc0) / max(args.steps, 1),
+        "gpu_launches": kv.launch_count() - l0,
+    })
+    kv.close()
+    return res
+
+
 def run_c4(args, rank, world, local, mode):
     """configs[3], long-context decode at the Llama-3-70B attention shape (64 q
     heads, 8 KV heads, head_dim 128): 16 sequences of 32768 tokens.
@@ -1055,9 +1135,9 @@ def main():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4-batch", "c4-head", "c5"], default="c2",
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4-batch", "c4-head", "c5", "prefill"], default="c2",
                     help="c2: configs[1] (default, the headline); c1: configs[0]; c3: configs[2]; "
-                         "c4-*: configs[3]; c5: configs[4]")
+                         "c4-*: configs[3]; c5: configs[4]; prefill: chunked prefill attention (8(f)2)")
     ap.add_argument("--c5-rate", type=float, default=32.0, help="c5: mean arrivals per step over the whole job")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="c4-head: gather the sharded heads inside the attention call over NVLink (peer) or with "
@@ -1089,6 +1169,11 @@ def main():
         return
     if args.config == "c3":
         res = run_c3(args, rank, world, local)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
+    if args.config == "prefill":
+        res = run_prefill(args, rank, world, local)
         if rank == 0:
             print(json.dumps(res), flush=True)
         return
