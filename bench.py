@@ -25,6 +25,7 @@ import math
 import os
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -137,7 +138,7 @@ class Clocks:
 
     def __init__(self, device_id: str):
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+        self.path = Path(tempfile.gettempdir()) / f"lt_bench_clocks_{os.getpid()}.csv"
         try:
             self.path.parent.mkdir(exist_ok=True)
             self.f = open(self.path, "w")
@@ -510,7 +511,7 @@ def run_c3(args, rank, world, local):
 
 
 def run_prefill(args, rank, world, local):
-    """Chunked prefill attention (SURVEY 8(f)2; the reference's prefill chunks,
+    """Chunked prefill attention (the reference's prefill chunks,
     scheduler.rs:388-407): 4 sequences with 2048 cached tokens each take a
     256-token prompt chunk per step -- append, K/V write, and causal attention
     of all 1024 chunk tokens in one call (token at position p attends [0, p]).
@@ -570,7 +571,7 @@ def run_prefill(args, rank, world, local):
         peaks = json.load(f)
     peak_tf = float(peaks.get("bf16_tflops", 1590.0))
     res = _json_common(args, world, n * args.steps / (ms * 1e-3), "tokens/s", ms / args.steps, {
-        "workload": "chunked prefill (SURVEY 8(f)2): 4 seqs x 2048 cached tokens, a 256-token chunk each per step, "
+        "workload": "chunked prefill: 4 seqs x 2048 cached tokens, a 256-token chunk each per step, "
                     "causal attention of the 1024 chunk tokens in one call, Llama-3-8B attention shape, one layer",
         "n_heads": hq, "n_kv_heads": hkv, "head_dim": d, "block_tokens": BLOCK})
     res.update({
@@ -1137,7 +1138,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["c1", "c2", "c3", "c4-batch", "c4-head", "c5", "prefill"], default="c2",
                     help="c2: configs[1] (default, the headline); c1: configs[0]; c3: configs[2]; "
-                         "c4-*: configs[3]; c5: configs[4]; prefill: chunked prefill attention (8(f)2)")
+                         "c4-*: configs[3]; c5: configs[4]; prefill: chunked prefill attention")
     ap.add_argument("--c5-rate", type=float, default=32.0, help="c5: mean arrivals per step over the whole job")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="c4-head: gather the sharded heads inside the attention call over NVLink (peer) or with "

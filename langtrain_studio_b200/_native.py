@@ -1,7 +1,7 @@
 """ctypes binding of the C ABI in include/lt_kv.h (liblt_kv.so).
 
 This is the same binding a Python host of the reference would write; the
-Rust host binds the same symbols through `extern "C"`.
+Rust host binds the same symbols through an `extern "C"` block.
 There is no fallback: if the library cannot be loaded or built, import fails.
 LT_KV_VARIANT=checked|asan loads a debug build of the same sources instead
 (see build.py).
