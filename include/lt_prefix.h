@@ -23,7 +23,9 @@
  * reference compares Option<String>.
  *
  * Host-only bookkeeping: no device memory, no CUDA calls.  A cache belongs to
- * one thread.
+ * one thread.  place() scans every slot and compares prompts token by token,
+ * O(slots x prompt), as the reference does: sized for the engine's parallel
+ * slots (hardware.rs picks 2-16), not for thousands of slots.
  */
 #ifndef LT_PREFIX_H
 #define LT_PREFIX_H
