@@ -145,7 +145,8 @@ int lt_slot_cache_has_free(const lt_slot_cache* c) {
 uint32_t lt_slot_cache_tokens(const lt_slot_cache* c, uint32_t slot, int32_t* out, uint32_t cap) {
     if (!c || slot >= c->slots.size()) return 0;
     const auto& t = c->slots[slot].tokens;
-    if (out) std::memcpy(out, t.data(), std::min<size_t>(t.size(), cap) * sizeof(int32_t));
+    const size_t k = std::min<size_t>(t.size(), cap);
+    if (out && k) std::memcpy(out, t.data(), k * sizeof(int32_t));  // an empty vector's data() may be null
     return (uint32_t)t.size();
 }
 

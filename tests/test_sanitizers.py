@@ -6,8 +6,9 @@ are argued in comments, `pool.rs:36-39`).  Here the C++ bookkeeping, the
 scheduler driver and the ABI glue are rebuilt with -fsanitize=address,undefined
 (liblt_kv_asan.so, `build.py` variant "asan") and the CPU bookkeeping suites
 -- the reference's known-answer tests, error paths, random operation
-sequences against the oracle, and the scheduler driver against its Python
-restatement -- run against it in a child process with libasan preloaded.
+sequences against the oracle, the scheduler driver against its Python
+restatement, and the prefix cache with token-level admission -- run against
+it in a child process with libasan preloaded.
 Any report aborts the child (halt_on_error), which fails this test.
 """
 from __future__ import annotations
@@ -32,7 +33,8 @@ _native.lib()
 maps = open("/proc/self/maps").read()
 assert "liblt_kv_asan.so" in maps, "the sanitized library is not the one loaded"
 assert "libasan" in maps and "libubsan" in maps, "sanitizer runtimes not loaded"
-sys.exit(pytest.main(["-q", "-m", "not gpu", "-p", "no:cacheprovider", "tests/test_abi.py", "tests/test_sched.py"]))
+sys.exit(pytest.main(["-q", "-m", "not gpu", "-p", "no:cacheprovider", "tests/test_abi.py", "tests/test_sched.py",
+                      "tests/test_prefix.py"]))
 """
 
 
