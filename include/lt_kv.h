@@ -326,7 +326,10 @@ lt_status lt_kv_gather_heads(lt_kv* kv, const void* local, void* gathered, void*
  * A rank that misses a call leaves the others' waits to run out:
  * lt_kv_check then reports LT_E_TIMEOUT.  Tear-down: lt_kv_peer_close on
  * every rank, a host barrier, then lt_kv_destroy (which frees the buffer the
- * peers had mapped). */
+ * peers had mapped).  Each import follows a new export (LT_E_ARG otherwise):
+ * the buffers keep the flags of earlier calls.  After LT_E_TIMEOUT the ranks'
+ * call counts may differ; recover with lt_kv_peer_close on every rank, a
+ * host barrier, and set-up steps 1-3 again. */
 #define LT_IPC_HANDLE_BYTES 64
 lt_status lt_kv_peer_export(lt_kv* kv, int rank, int nranks, uint32_t max_tokens, void* ipc_handle_out);
 lt_status lt_kv_peer_import(lt_kv* kv, const void* ipc_handles /* nranks * LT_IPC_HANDLE_BYTES */);

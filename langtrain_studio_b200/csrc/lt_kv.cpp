@@ -78,6 +78,10 @@ struct PeerGather {
     bool mapped[ltkv::kMaxPeers] = {};              // opened with cudaIpcOpenMemHandle
     uint32_t epoch = 0;                             // gather calls so far (same on every rank)
     bool ready = false;
+    // Set by export, cleared by import: the flags in a buffer hold the epochs
+    // of every call made through it, so a second import of the same buffers
+    // (epoch back at 0) would see stale flags as raised.
+    bool fresh = false;
 };
 constexpr size_t kPeerFlagsBytes = 256, kPeerHeaderBytes = 512;
 static_assert(sizeof(cudaIpcMemHandle_t) == LT_IPC_HANDLE_BYTES, "IPC handle size");
@@ -993,6 +997,7 @@ lt_status lt_kv_peer_export(lt_kv* kv, int rank, int nranks, uint32_t max_tokens
     pg.nranks = nranks;
     pg.max_tokens = max_tokens;
     pg.half_bytes = half;
+    pg.fresh = true;
     return LT_OK;
 }
 
@@ -1000,6 +1005,9 @@ lt_status lt_kv_peer_import(lt_kv* kv, const void* ipc_handles) {
     if (!kv || !ipc_handles) return LT_E_ARG;
     PeerGather& pg = kv->peer;
     if (!pg.d_buf) return fail(kv, LT_E_ARG, "peer_import before peer_export");
+    if (!pg.fresh)
+        return fail(kv, LT_E_ARG, "peer_import needs a new peer_export on every rank (the buffers hold the flags of "
+                                  "earlier calls)");
     DeviceGuard g(kv->cfg.device);
     peer_unmap(kv);
     const unsigned char* hs = static_cast<const unsigned char*>(ipc_handles);
@@ -1019,8 +1027,9 @@ lt_status lt_kv_peer_import(lt_kv* kv, const void* ipc_handles) {
         pg.base[r] = static_cast<unsigned char*>(ptr);
         pg.mapped[r] = true;
     }
-    pg.epoch = 0;
+    pg.epoch = 0;  // export zeroed every rank's flags
     pg.ready = true;
+    pg.fresh = false;
     return LT_OK;
 }
 

@@ -1,7 +1,9 @@
 """KV-head sharding across 2 GPUs: each rank holds half the KV heads of every
 sequence (identical bookkeeping calls on both ranks), attends with its own
 q heads, and lt_kv_gather_heads (NCCL all-gather + permute) must reproduce
-the unsharded attention of the oracle within the north-star tolerance."""
+the unsharded attention of the oracle within the north-star tolerance.  The
+gather fused into attention (lt_kv_*_gather) is checked the same way on 2
+GPUs, and its set-up rules on one GPU (nranks = 1)."""
 import os
 import socket
 
@@ -190,3 +192,48 @@ def test_peer_gather_rank_missing_a_call_times_out(tmp_path):
     mp.start_processes(_peer_rank, args=(2, _port(), str(tmp_path), 1), nprocs=2, join=True, start_method="spawn")
     assert str(np.load(tmp_path / "status0.npy")[0]) == "timeout"
     assert str(np.load(tmp_path / "status1.npy")[0]) == "skipped"
+
+
+def test_peer_gather_single_rank_and_reimport():
+    """One rank (nranks = 1): the fused gather returns attend()'s rows through
+    its own buffer and flag, on both halves.  A second import of the same
+    buffers is refused (their flags hold the epochs of the calls made so far);
+    close + a new export + import make the gather usable again."""
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from langtrain_studio_b200 import _native as N
+    from langtrain_studio_b200 import kv as kvm
+
+    hkv, hq, d = 2, 8, 128
+    lens = [40, 300, 17]
+    n = len(lens)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    nb = sum((L + 15) // 16 for L in lens) + 4
+    kv = kvm.KvCache(1, hkv, d, nb * 16, n_heads=hq, max_seqs=n, max_batch=512, device=0)
+    try:
+        for s, L in enumerate(lens):
+            b, sl = kv.append_batch(np.full(L, s), np.arange(L))
+            kv.write(0, b, sl, torch.randn(L, hkv * d, device="cuda", generator=g),
+                     torch.randn(L, hkv * d, device="cuda", generator=g))
+        seqs, pos = np.arange(n), np.array(lens) - 1
+        q = torch.randn(n, hq * d, device="cuda", generator=g)
+        ref = kv.attend(0, q, seqs, pos, out_dtype=torch.float32)
+        h = kv.peer_export(0, 1, max_tokens=8)
+        kv.peer_import([h])
+        for _ in range(3):  # halves 1, 0, 1
+            out = kv.attend_gather(0, q, seqs, pos, out_dtype=torch.float32)
+            kv.check()
+            torch.testing.assert_close(out, ref, rtol=0, atol=1e-6)
+        with pytest.raises(kvm.KvError) as e:
+            kv.peer_import([h])
+        assert e.value.code == N.LT_E_ARG
+        kv.peer_close()
+        h = kv.peer_export(0, 1, max_tokens=8)
+        kv.peer_import([h])
+        out = kv.attend_gather(0, q, seqs, pos, out_dtype=torch.float32)
+        kv.check()
+        torch.testing.assert_close(out, ref, rtol=0, atol=1e-6)
+        kv.peer_close()
+    finally:
+        kv.close()
