@@ -14,7 +14,6 @@ from __future__ import annotations
 
 import ctypes as C
 import re
-import subprocess
 import sys
 import types
 from pathlib import Path
@@ -23,10 +22,12 @@ import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
 sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+import _headers as H  # noqa: E402
 
 from langtrain_studio_b200 import _native as N  # noqa: E402
 
-HEADERS = ("lt_kv.h", "lt_llama.h", "lt_sched.h", "lt_prefix.h")
 STRUCTS = (N.lt_kv_config, N.lt_llama_config, N.lt_sched_config, N.lt_placement, N.lt_sched_stats)
 OPAQUE = {"lt_kv", "lt_llama", "lt_sched", "lt_slot_cache"}
 ENUMS = {"lt_status", "lt_dtype", "lt_kv_format", "lt_tensor"}
@@ -37,33 +38,12 @@ SCALARS = {
 }
 POINTERS = (C.c_void_p, C.c_char_p)
 
-
-def _gcc():
-    try:
-        subprocess.run(["gcc", "--version"], capture_output=True, check=True)
-    except (OSError, subprocess.CalledProcessError):
-        pytest.skip("gcc is not installed")
+pytestmark = pytest.mark.skipif(not H.have_gcc(), reason="gcc is not installed")
 
 
 @pytest.fixture(scope="module")
-def prototypes(tmp_path_factory):
-    _gcc()
-    d = tmp_path_factory.mktemp("aux")
-    src = d / "hdr.c"
-    src.write_text("".join(f'#include "{h}"\n' for h in HEADERS))
-    aux = d / "aux.txt"
-    subprocess.run(["gcc", "-I", str(ROOT / "include"), "-aux-info", str(aux), "-fsyntax-only", str(src)],
-                   check=True, capture_output=True, text=True)
-    protos = {}
-    pat = re.compile(r"^/\* (\S+?):\d+:\w+ \*/ extern (.+?)\s*\b(lt_\w+) \((.*)\);$")
-    for line in aux.read_text().splitlines():
-        m = pat.match(line)
-        if not m or Path(m.group(1)).name not in HEADERS:
-            continue
-        ret, name, args = m.group(2).strip(), m.group(3), m.group(4).strip()
-        protos[name] = (ret, [] if args in ("", "void") else [a.strip() for a in args.split(",")])
-    assert len(protos) > 50, "no prototypes parsed from gcc -aux-info"
-    return protos
+def prototypes():
+    return H.prototypes()
 
 
 def _declared():
@@ -140,46 +120,21 @@ def test_binding_signatures_match_the_prototypes(prototypes):
             _check(a, b, f"{name} argument {i} ({a})")
 
 
-def test_struct_layouts_match_the_compiler(tmp_path):
-    _gcc()
-    lines = [f'#include "{h}"' for h in HEADERS] + ["#include <stddef.h>", "#include <stdio.h>", "int main(void) {"]
-    for s in STRUCTS:
-        lines.append(f'    printf("{s.__name__} sizeof %zu\\n", sizeof({s.__name__}));')
-        for f, _ in s._fields_:
-            lines.append(f'    printf("{s.__name__} {f} %zu %zu\\n", offsetof({s.__name__}, {f}), '
-                         f'sizeof((({s.__name__}*)0)->{f}));')
-    lines += ["    return 0;", "}"]
-    src = tmp_path / "layout.c"
-    src.write_text("\n".join(lines) + "\n")
-    exe = tmp_path / "layout"
-    r = subprocess.run(["gcc", "-I", str(ROOT / "include"), "-o", str(exe), str(src)], capture_output=True, text=True)
-    assert r.returncode == 0, r.stderr  # a field the binding names that C lacks fails here
-    got = {}
-    for line in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.splitlines():
-        parts = line.split()
-        got[tuple(parts[:-2]) if len(parts) == 4 else tuple(parts[:2])] = tuple(int(x) for x in parts[2:])
-    for s in STRUCTS:
-        assert got[(s.__name__, "sizeof")] == (C.sizeof(s),), f"{s.__name__}: sizeof differs"
-        for f, ft in s._fields_:
-            off, size = got[(s.__name__, f)]
-            assert getattr(s, f).offset == off, f"{s.__name__}.{f}: offset {getattr(s, f).offset} vs C {off}"
-            assert C.sizeof(ft) == size, f"{s.__name__}.{f}: {C.sizeof(ft)} bytes vs C {size}"
+def test_struct_layouts_match_the_compiler():
+    got = H.layouts({st.__name__: [f for f, _ in st._fields_] for st in STRUCTS})
+    for st in STRUCTS:
+        lay = got[st.__name__]
+        assert lay["sizeof"] == C.sizeof(st), f"{st.__name__}: sizeof differs"
+        for f, ft in st._fields_:
+            off, size = lay[f]
+            assert getattr(st, f).offset == off, f"{st.__name__}.{f}: offset {getattr(st, f).offset} vs C {off}"
+            assert C.sizeof(ft) == size, f"{st.__name__}.{f}: {C.sizeof(ft)} bytes vs C {size}"
 
 
-def test_binding_constants_match_the_headers(tmp_path):
-    _gcc()
+def test_binding_constants_match_the_headers():
     names = ["LT_OK", "LT_E_FULL", "LT_E_NONCONTIG", "LT_E_ARG", "LT_E_CUDA", "LT_E_NCCL", "LT_E_TIMEOUT",
              "LT_E_UNSUPPORTED", "LT_E_SCRATCH", "LT_E_BOUNDS", "LT_F32", "LT_F16", "LT_KV_F16", "LT_KV_Q8_0",
              "LT_FEATURE_BOUNDS_CHECK", "LT_IPC_HANDLE_BYTES", "LT_NOALLOC_SCRATCH_BYTES", "LT_NOALLOC_MAX_TOKENS"]
-    lines = [f'#include "{h}"' for h in HEADERS] + ["#include <stdio.h>", "int main(void) {"]
-    lines += [f'    printf("{n} %lld\\n", (long long)({n}));' for n in names]
-    lines += ["    return 0;", "}"]
-    src = tmp_path / "consts.c"
-    src.write_text("\n".join(lines) + "\n")
-    exe = tmp_path / "consts"
-    r = subprocess.run(["gcc", "-I", str(ROOT / "include"), "-o", str(exe), str(src)], capture_output=True, text=True)
-    assert r.returncode == 0, r.stderr
-    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
-    got = dict(zip(out[0::2], (int(x) for x in out[1::2])))
+    got = H.constants(names)
     for n in names:
         assert getattr(N, n) == got[n], f"{n}: binding {getattr(N, n)} vs header {got[n]}"
