@@ -364,8 +364,9 @@ lt_status lt_kv_write_attend_gather(lt_kv* kv, uint32_t layer, const int32_t* bl
  *   - The first call on a device looks up the array's address with that
  *     device current; make that first call before any stream capture.
  *   - All calls share the array and it keeps the last call's contents; each
- *     call clears its error word and rewrites what it reads.  Calls that
- *     overlap on the GPU race: issue them in order on one stream.
+ *     call clears its error word, tags its flags with a fresh epoch and
+ *     rewrites the rest of what it reads.  Calls that overlap on the GPU
+ *     race: issue them in order on one stream.
  *   - The call does not synchronise; a bounded device wait that gives up
  *     leaves that call's outputs invalid without a status. */
 #define LT_NOALLOC_SCRATCH_BYTES (8u << 20)

@@ -616,8 +616,21 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     p.part2_o = kv->d_part_o + kv->ws_slots * kv->group * kv->cfg.head_dim;
     p.part2_ml = kv->d_part_ml + kv->ws_slots * kv->group * 2;
     p.flags2 = kv->d_flags + kv->ws_slots;
-    if (++kv->attn_epoch == 0) kv->attn_epoch = 1;  // 0 is the flags' initial value
-    p.epoch = kv->attn_epoch;
+    // A waiter tests flag == epoch.  When the count wraps, a warp slot that
+    // only large launches reach may still hold any earlier epoch, so the
+    // flags restart from zero (0 is never an epoch).  On failure the count is
+    // left as it was and the next launch tries again.
+    uint32_t epoch = kv->attn_epoch + 1;
+    if (epoch == 0) {
+        const cudaError_t e = cudaMemsetAsync(kv->d_flags, 0, 2 * kv->ws_slots * sizeof(uint32_t) + 4, st);
+        if (e != cudaSuccess) {
+            rollback();
+            return fail(kv, LT_E_CUDA, "cudaMemsetAsync(flags): %s", cudaGetErrorString(e));
+        }
+        epoch = 1;
+    }
+    kv->attn_epoch = epoch;
+    p.epoch = epoch;
     p.err = kv->d_err;
     p.k_new = k;
     p.v_new = v;

@@ -17,10 +17,11 @@
 // call on a device looks up the array's device address with that device
 // current (cudaGetSymbolAddress) and caches it; make that first call before
 // any stream capture.  Every call shares the array and it keeps the last
-// call's contents, so each call clears its error word before its launch and
-// overwrites everything else it reads; calls that overlap on the GPU
-// (different streams, no ordering) race on it -- issue them in order on one
-// stream.
+// call's contents, so each call clears its error word before its launch,
+// keeps its range-done flags at a fixed place where they only ever hold
+// epochs (a fresh one per call), and overwrites everything else it reads;
+// calls that overlap on the GPU (different streams, no ordering) race on it
+// -- issue them in order on one stream.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -35,6 +36,13 @@ namespace {
 
 constexpr size_t kScratchBytes = LT_NOALLOC_SCRATCH_BYTES;
 constexpr int kMaxDevices = 64;
+// The range-done flags sit at a fixed place and only ever hold epochs: the
+// descriptors and partials after them move with the call's size, and a flag
+// placed over an earlier call's descriptor word (a small integer) could
+// already equal the new epoch.
+constexpr size_t kFlagsOffset = 256;
+constexpr size_t kMaxFlagWarps = 16384;
+constexpr size_t kFlagsBytes = kMaxFlagWarps * sizeof(uint32_t);
 
 static __device__ __align__(256) unsigned char lt_noalloc_scratch[kScratchBytes];
 
@@ -94,17 +102,16 @@ extern "C" lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_
     if (n_warps <= 0) return LT_E_CUDA;
     n_warps = (int)std::min<long long>(n_warps, tiles * n_kv_heads);
 
-    // Scratch layout: [error word][descriptors beyond the inline ones]
-    // [range-done flags][partial (m, l)][partial O], 256-byte aligned; one
-    // flag and one partial slot per warp.  Fewer warps are used when the
+    // Scratch layout: [error word][range-done flags, fixed][descriptors
+    // beyond the inline ones][partial (m, l)][partial O], 256-byte aligned;
+    // one flag and one partial slot per warp.  Fewer warps are used when the
     // partials would not fit.
     const size_t gd = (size_t)group * head_dim;
-    const size_t o_toks = 256;
-    const size_t o_flags = o_toks + round256(n > (uint32_t)ltkv::kInlineTokens ? n * sizeof(ltkv::TokenDesc) : 0);
-    const size_t per_warp = sizeof(uint32_t) + group * 2 * sizeof(float) + gd * sizeof(float);
-    if (o_flags + 1024 + per_warp > kScratchBytes) return LT_E_SCRATCH;
-    n_warps = (int)std::min<size_t>((size_t)n_warps, (kScratchBytes - o_flags - 1024) / per_warp);
-    const size_t o_ml = o_flags + round256((size_t)n_warps * sizeof(uint32_t));
+    const size_t o_toks = kFlagsOffset + kFlagsBytes;
+    const size_t o_ml = o_toks + round256(n > (uint32_t)ltkv::kInlineTokens ? n * sizeof(ltkv::TokenDesc) : 0);
+    const size_t per_warp = group * 2 * sizeof(float) + gd * sizeof(float);
+    if (o_ml + 512 + per_warp > kScratchBytes) return LT_E_SCRATCH;
+    n_warps = (int)std::min<size_t>({(size_t)n_warps, kMaxFlagWarps, (kScratchBytes - o_ml - 512) / per_warp});
     const size_t o_o = o_ml + round256((size_t)n_warps * group * 2 * sizeof(float));
 
     void* base = nullptr;
@@ -151,11 +158,17 @@ extern "C" lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_
     p.scale_log2 = scale * 1.4426950408889634f;
     p.part_ml = reinterpret_cast<float*>(b + o_ml);
     p.part_o = reinterpret_cast<float*>(b + o_o);
-    // The flags keep the last call's epochs: a fresh epoch per call on this
-    // device (the array starts zeroed, and 0 is never used).
-    p.flags = reinterpret_cast<uint32_t*>(b + o_flags);
-    if (++g_epoch[dev] == 0) g_epoch[dev] = 1;
-    p.epoch = g_epoch[dev];
+    // The flags keep earlier calls' epochs: a fresh epoch per call on this
+    // device (the array starts zeroed, and 0 is never used).  When the count
+    // wraps, any earlier epoch may still be there, so the flags are cleared.
+    p.flags = reinterpret_cast<uint32_t*>(b + kFlagsOffset);
+    uint32_t epoch = g_epoch[dev] + 1;
+    if (epoch == 0) {
+        if (cudaMemsetAsync(b + kFlagsOffset, 0, kFlagsBytes, st) != cudaSuccess) return LT_E_CUDA;
+        epoch = 1;
+    }
+    g_epoch[dev] = epoch;
+    p.epoch = epoch;
     // A bounded wait that gives up sets the error word (first int32 of the
     // array) and leaves this call's outputs invalid; nothing synchronises
     // here to report it, and the next call clears it.

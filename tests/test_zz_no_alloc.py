@@ -8,8 +8,9 @@ and keeps the kernel's scratch in a fixed static device array.  This file is
 named so that pytest collects it last.
 
 Checks, through the C ABI: two calls in a row each match lt_kv_attend on the
-same cache within the suite's attention tolerance, and oversized requests
-are refused with LT_E_SCRATCH before any work.
+same cache within the suite's attention tolerance; so do calls of alternating
+sizes, whose work plans sit at different places in the shared array; and
+oversized requests are refused with LT_E_SCRATCH before any work.
 """
 import ctypes as C
 
@@ -74,6 +75,45 @@ def test_noalloc_matches_attend_two_calls(q_dtype):
             assert rc == N.LT_OK, rc
             torch.cuda.synchronize()
             np.testing.assert_allclose(out.cpu().numpy(), ref.cpu().numpy(), rtol=RTOL, atol=ATOL)
+    kv.close()
+
+
+def test_noalloc_alternating_call_sizes():
+    """600 tokens (more than the launch parameters carry, so the work plan goes
+    through the array), then 8, then 600 again: each call must match
+    lt_kv_attend although the previous call left its plan and partials where
+    this call's layout differs."""
+    if not torch.cuda.is_available():
+        pytest.fail("CUDA device required for -m gpu tests")
+    from langtrain_studio_b200 import _native as N
+    from langtrain_studio_b200.kv import KvCache
+
+    lib = N.lib()
+    hq, hkv, d = 16, 4, 128
+    lens = [900, 75, 1300, 260, 640, 33, 1024, 512]
+    nblk = sum((L + 16) // 16 for L in lens) + 8
+    kv = KvCache(1, hkv, d, 16 * nblk, n_heads=hq, max_seqs=len(lens), max_batch=4096, device=0)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    for s, L in enumerate(lens):
+        b, sl = kv.append_batch(np.full(L, s), np.arange(L))
+        kv.write(0, b, sl, torch.randn((L, hkv * d), generator=g, device="cuda"),
+                 torch.randn((L, hkv * d), generator=g, device="cuda"))
+    kv.flush()
+    rng = np.random.default_rng(11)
+    big_seqs = np.repeat(np.arange(len(lens)), 75)  # 600 tokens
+    big_pos = np.array([rng.integers(0, lens[s]) for s in big_seqs])
+    small_seqs = np.arange(len(lens))
+    small_pos = np.array(lens) - 1
+    scale = float(np.float32(1.0) / np.float32(np.sqrt(d)))
+    for seqs, pos in ((big_seqs, big_pos), (small_seqs, small_pos), (big_seqs, big_pos)):
+        q = torch.randn((seqs.size, hq * d), generator=g, device="cuda")
+        ref = kv.attend(0, q, seqs, pos, out_dtype=torch.float32, scale=scale)
+        out = torch.full((seqs.size, hq * d), float("nan"), device="cuda")
+        rc = _noalloc(lib, kv, 0, q, out, seqs, pos, scale)
+        assert rc == N.LT_OK, rc
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(out.cpu().numpy(), ref.cpu().numpy(), rtol=RTOL, atol=ATOL)
     kv.close()
 
 
