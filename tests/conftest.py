@@ -1,4 +1,3 @@
-import os
 import sys
 from pathlib import Path
 
@@ -11,12 +10,6 @@ if str(ROOT) not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200); run with -m gpu")
-
-
-def pytest_collection_modifyitems(config, items):
-    # GPU tests fail loudly when no device is present; they are selected with
-    # -m gpu on the GPU box and deselected with -m "not gpu" here.
-    pass
 
 
 @pytest.fixture(scope="session")

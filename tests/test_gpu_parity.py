@@ -4,7 +4,6 @@ Bar (north star): bit-exact for append (pool bytes), block tables, copy-on-
 write and compaction; attention within max-abs 2e-3 / rel 1e-3 of the
 oracle's f32 result (ATOL / RTOL below).
 """
-import math
 
 import numpy as np
 import pytest

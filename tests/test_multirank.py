@@ -11,7 +11,6 @@ import os
 import socket
 
 import numpy as np
-import pytest
 import torch.multiprocessing as mp
 
 
@@ -29,7 +28,6 @@ def _rank_main(rank, world, port, out_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     import datetime
 
-    import torch
     import torch.distributed as dist
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
