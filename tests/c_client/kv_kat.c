@@ -2,14 +2,19 @@
  * A plain C client of the library, linked the way the engine's Rust FFI would
  * link it (no Python, no CUDA headers).  On a bookkeeping-only handle
  * (device = -1) it runs the reference's own KvCache known-answer tests,
- * engine/crates/native/src/kv.rs:202-217 and :219-229 (bookkeeping half), and
- * the SlotCache placement test prefix.rs:136-144.  Exit status 0 on success.
+ * engine/crates/native/src/kv.rs:202-217 and :219-229 (bookkeeping half),
+ * the SlotCache placement test prefix.rs:136-144, and the reference
+ * scheduler's tests of KV behaviour (scheduler.rs:584-592, 615-621, 623-636,
+ * 675-682) through the native driver (lt_sched.h) with token requests on
+ * byte-level tokens, as the reference's MockBackend tests use.  Exit status 0
+ * on success.
  */
 #include <stdio.h>
 #include <string.h>
 
 #include "lt_kv.h"
 #include "lt_prefix.h"
+#include "lt_sched.h"
 
 #define CHECK(cond)                                                          \
     do {                                                                     \
@@ -88,8 +93,138 @@ static int prefers_slot_with_longest_prefix(void) { /* prefix.rs:136-144 */
     return 0;
 }
 
+/* ---- scheduler.rs tests of KV behaviour, through lt_sched ---- */
+
+static lt_kv* make_engine_kv(uint32_t n_ctx, uint32_t n_seq) {
+    lt_kv_config c;
+    memset(&c, 0, sizeof c);
+    c.n_layers = 1;
+    c.n_kv_heads = 2;
+    c.head_dim = 64;
+    c.n_heads = 4;
+    c.n_tokens = n_ctx;
+    c.max_seqs = n_seq;
+    c.max_batch = 1u << 14;
+    c.device = -1;
+    lt_kv* kv = NULL;
+    return lt_kv_create(&c, &kv) == LT_OK ? kv : NULL;
+}
+
+static lt_sched* make_sched(lt_kv* kv, uint32_t n_seq, uint32_t chunk) {
+    lt_sched_config c;
+    memset(&c, 0, sizeof c);
+    c.n_slots = n_seq;
+    c.decode_headroom = 256;
+    c.prefill_chunk = chunk;
+    c.compact = 1;
+    c.data = 0; /* bookkeeping only */
+    lt_sched* s = NULL;
+    return lt_sched_create(kv, &c, &s) == LT_OK ? s : NULL;
+}
+
+/* A chat prompt as byte-level token ids: a shared system prompt, the
+ * question, role tags. */
+static uint32_t chat(const char* question, int32_t* out, uint32_t cap) {
+    char text[512];
+    strcpy(text, "<|system|>");
+    for (int i = 0; i < 8; ++i) strcat(text, "You are helpful. ");
+    strcat(text, "<|user|>");
+    strcat(text, question);
+    strcat(text, "<|assistant|>");
+    uint32_t n = (uint32_t)strlen(text);
+    if (n > cap) n = cap;
+    for (uint32_t i = 0; i < n; ++i) out[i] = (int32_t)(unsigned char)text[i];
+    return n;
+}
+
+/* Step until n_requests have finished (bounded). */
+static int drive(lt_sched* s, uint64_t n_requests, lt_sched_stats* st) {
+    for (int i = 0; i < 10000; ++i) {
+        if (lt_sched_step(s, NULL, 0, NULL, NULL, NULL, NULL) != LT_OK) return 1;
+        if (lt_sched_get_stats(s, st) != LT_OK) return 1;
+        if (st->finished >= n_requests) return 0;
+    }
+    return 1;
+}
+
+static int second_request_reuses_prefix(void) { /* scheduler.rs:584-592 */
+    lt_kv* kv = make_engine_kv(4096, 2);
+    CHECK(kv);
+    lt_sched* s = make_sched(kv, 2, 32);
+    CHECK(s);
+    int32_t t[256];
+    lt_sched_stats st;
+    uint32_t n = chat("first question", t, 256);
+    CHECK(lt_sched_submit_tokens(s, t, n, 20, LT_NO_ADAPTER) == LT_OK);
+    CHECK(drive(s, 1, &st) == 0);
+    CHECK(st.cached_tokens == 0);
+    n = chat("second question", t, 256);
+    CHECK(lt_sched_submit_tokens(s, t, n, 20, LT_NO_ADAPTER) == LT_OK);
+    CHECK(drive(s, 2, &st) == 0);
+    CHECK(st.cached_tokens > 100); /* the system prompt and role tags come from the cache */
+    lt_sched_destroy(s);
+    lt_kv_destroy(kv);
+    return 0;
+}
+
+static int long_prompt_is_chunked(void) { /* scheduler.rs:615-621 */
+    lt_kv* kv = make_engine_kv(4096, 2);
+    CHECK(kv);
+    lt_sched* s = make_sched(kv, 2, 32);
+    CHECK(s);
+    int32_t t[1000];
+    for (int i = 0; i < 1000; ++i) t[i] = 'x';
+    lt_sched_stats st;
+    CHECK(lt_sched_submit_tokens(s, t, 1000, 20, LT_NO_ADAPTER) == LT_OK);
+    CHECK(lt_sched_step(s, NULL, 0, NULL, NULL, NULL, NULL) == LT_OK);
+    CHECK(lt_sched_get_stats(s, &st) == LT_OK);
+    CHECK(st.prefill_tokens == 32); /* one chunk per step */
+    CHECK(drive(s, 1, &st) == 0);
+    CHECK(st.prompt_tokens == 1000 && st.prefill_tokens == 1000 && st.finished == 1);
+    lt_sched_destroy(s);
+    lt_kv_destroy(kv);
+    return 0;
+}
+
+static int context_pressure_ends_youngest_gracefully(void) { /* scheduler.rs:623-636 */
+    lt_kv* kv = make_engine_kv(600, 3); /* three prompts fit, not their replies too */
+    CHECK(kv);
+    lt_sched* s = make_sched(kv, 3, 32);
+    CHECK(s);
+    int32_t t[256];
+    char q[8];
+    for (int i = 0; i < 3; ++i) {
+        snprintf(q, sizeof q, "q%d", i);
+        const uint32_t n = chat(q, t, 256);
+        CHECK(lt_sched_submit_tokens(s, t, n, 200, LT_NO_ADAPTER) == LT_OK);
+    }
+    lt_sched_stats st;
+    CHECK(drive(s, 3, &st) == 0); /* every request ends (Stop or Length), no error */
+    CHECK(st.finished == 3 && st.admitted == 3);
+    lt_sched_destroy(s);
+    lt_kv_destroy(kv);
+    return 0;
+}
+
+static int rejects_prompt_larger_than_context(void) { /* scheduler.rs:675-682 */
+    lt_kv* kv = make_engine_kv(64, 1);
+    CHECK(kv);
+    lt_sched* s = make_sched(kv, 1, 32);
+    CHECK(s);
+    int32_t t[100];
+    for (int i = 0; i < 100; ++i) t[i] = 'y';
+    CHECK(lt_sched_submit_tokens(s, t, 100, 10, LT_NO_ADAPTER) == LT_E_ARG);
+    CHECK(strstr(lt_sched_last_error(s), "context window") != NULL);
+    lt_sched_destroy(s);
+    lt_kv_destroy(kv);
+    return 0;
+}
+
 int main(void) {
     if (share_then_diverge() || truncate_frees_blocks() || prefers_slot_with_longest_prefix()) return 1;
-    printf("C client: kv.rs and prefix.rs known-answer tests passed\n");
+    if (second_request_reuses_prefix() || long_prompt_is_chunked() || context_pressure_ends_youngest_gracefully() ||
+        rejects_prompt_larger_than_context())
+        return 1;
+    printf("C client: kv.rs, prefix.rs and scheduler.rs known-answer tests passed\n");
     return 0;
 }

@@ -1,7 +1,8 @@
 """The C ABI from a plain C program: tests/c_client/kv_kat.c is compiled with
 gcc against include/*.h, linked to liblt_kv.so as the engine's FFI would link
-it, and runs the reference's KvCache and SlotCache known-answer tests on a
-bookkeeping-only handle (no GPU)."""
+it, and runs the reference's KvCache and SlotCache known-answer tests and its
+scheduler's tests of KV behaviour (through lt_sched) on a bookkeeping-only
+handle (no GPU)."""
 import subprocess
 from pathlib import Path
 
