@@ -6,7 +6,7 @@ are argued in comments, `pool.rs:36-39`).  Here the C++ bookkeeping, the
 scheduler driver and the ABI glue are rebuilt with -fsanitize=address,undefined
 (liblt_kv_asan.so, `build.py` variant "asan") and the CPU bookkeeping suites
 -- the reference's known-answer tests, error paths, random operation
-sequences against the oracle, the scheduler driver against its Python
+sequences against the oracle (fixed seeds and a hypothesis state machine), the scheduler driver against its Python
 restatement, the prefix cache with token-level admission, and the plain C
 client of the ABI -- run against it in a child process with libasan
 preloaded (the C client inherits the preload).
@@ -35,7 +35,7 @@ maps = open("/proc/self/maps").read()
 assert "liblt_kv_asan.so" in maps, "the sanitized library is not the one loaded"
 assert "libasan" in maps and "libubsan" in maps, "sanitizer runtimes not loaded"
 sys.exit(pytest.main(["-q", "-m", "not gpu", "-p", "no:cacheprovider", "tests/test_abi.py", "tests/test_sched.py",
-                      "tests/test_prefix.py", "tests/test_c_client.py"]))
+                      "tests/test_prefix.py", "tests/test_c_client.py", "tests/test_abi_stateful.py"]))
 """
 
 
