@@ -336,3 +336,55 @@ def test_rejects_prompt_larger_than_context():  # scheduler.rs:675-682
         s.submit_tokens(np.full(100, ord("y"), np.int32), 10)
     assert "context window" in str(e.value)
     s.close()
+
+
+def test_first_write_into_copied_partial_block_counts_its_copy(oracle_mod):
+    """Room for a step counts one block for the copy-on-write of a shared
+    partial block (kv.rs:99-110).  Request A leaves a 40-token system prompt
+    in its slot; C reuses it there; B, placed while C runs, copies C's 40
+    tokens into the other slot (kv_copy: 2.5 blocks, the third one shared),
+    so B's first prompt chunk copies that block on write.  On a 5-block pool
+    that copy decides whether the step fits.  The native driver must match
+    the restatement step by step, and a restatement that leaves the copy out
+    of the count must not (so the scenario really turns on it)."""
+
+    class NoCowNeed(ref.PrefixDriver):  # a mistake planted in the checker
+        def _need(self, items):
+            return sum(ref._blocks(p0 + cnt) - ref._blocks(p0) for _, p0, cnt in items)
+
+    system = ((np.arange(40) * 7) % 1000).astype(np.int32)
+    a = np.concatenate([system, np.full(8, 5000, np.int32)])
+    c = np.concatenate([system, np.array([7000], np.int32)])
+    b = np.concatenate([system, np.arange(6000, 6009, dtype=np.int32)])
+    pool, slots = 5, 2
+
+    def trace(driver_cls=None):
+        if driver_cls is None:
+            kv = KvCache(1, 2, 64, pool * 16, n_heads=4, max_seqs=slots, max_batch=1 << 14, max_blocks_per_seq=pool,
+                         device=-1)
+            d = Scheduler(kv, slots, data=False)
+            submit, step, stats, free = d.submit_tokens, d.step, (lambda: d.stats), kv.free_list
+        else:
+            ok = oracle_mod.OracleKv(1, 2 * 64, pool * 16, max_seqs=slots)
+            d = driver_cls(_OracleKv(ok), slots)
+            submit, step, stats, free = d.submit, d.step, (lambda: d.stats), ok.free_list
+        out = []
+        submit(a, 2)
+        for t in range(40):
+            if t == 3:
+                submit(c, 4)
+                submit(b, 1)
+            try:
+                step()
+            except AssertionError:  # the planted mistake runs the oracle out of blocks
+                out.append("out of blocks")
+                break
+            out.append((tuple(int(x) for x in free()), tuple(stats()[k] for k in KEYS)))
+        if driver_cls is None:
+            d.close()
+        return out
+
+    native = trace()
+    assert native == trace(ref.PrefixDriver)
+    assert native[-1][1][KEYS.index("copies")] == 1 and native[-1][1][KEYS.index("finished")] == 3
+    assert trace(NoCowNeed) != native
