@@ -36,7 +36,8 @@ assert "liblt_kv_asan.so" in maps, "the sanitized library is not the one loaded"
 assert "libasan" in maps and "libubsan" in maps, "sanitizer runtimes not loaded"
 sys.exit(pytest.main(["-q", "-m", "not gpu", "-p", "no:cacheprovider", "tests/test_abi.py", "tests/test_sched.py",
                       "tests/test_prefix.py", "tests/test_c_client.py", "tests/test_abi_stateful.py",
-                      "tests/test_prefix_stateful.py", "tests/test_sched_stateful.py"]))
+                      "tests/test_prefix_stateful.py", "tests/test_sched_stateful.py",
+                      "tests/test_sched_length_stateful.py"]))
 """
 
 
