@@ -16,6 +16,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <string>
 #include <vector>
 
@@ -388,6 +389,19 @@ void truncate_impl(lt_kv* kv, uint32_t seq, uint32_t from) {  // kv.rs:153-169
     for (size_t i = keep; i < bl.size(); ++i) release_block(kv, bl[i]);  // ascending order
     bl.resize(keep);
     kv->lens[seq] = from;
+}
+
+// lt_dtype arguments must name one of the enum's values: anything else is
+// refused rather than read as f16.  Checked at the extern "C" entry, through
+// the arguments' addresses, before any copy of them.
+lt_status check_dtypes(lt_kv* kv, std::initializer_list<const lt_dtype*> ds) {
+    for (const lt_dtype* d : ds)
+        if (!ltkv::dtype_valid(*d)) {
+            int32_t v;
+            std::memcpy(&v, d, sizeof v);
+            return fail(kv, LT_E_ARG, "dtype %d is neither LT_F32 nor LT_F16", (int)v);
+        }
+    return LT_OK;
 }
 
 lt_status require_device(lt_kv* kv) {
@@ -878,8 +892,8 @@ lt_status lt_kv_write(lt_kv* kv, uint32_t layer, const int32_t* block, const int
                       const void* k, const void* v, lt_dtype dtype, void* stream) {
     ltkv::NvtxRange nv("lt_kv_write");
     if (!kv) return LT_E_ARG;
-    lt_status rc = require_device(kv);
-    if (rc) return rc;
+    lt_status rc = check_dtypes(kv, {&dtype});
+    if (rc || (rc = require_device(kv))) return rc;
     if (layer >= kv->cfg.n_layers) return fail(kv, LT_E_ARG, "layer %u out of range", layer);
     if ((rc = check_cells(kv, block, slot, n))) return rc;
     DeviceGuard g(kv->cfg.device);
@@ -957,6 +971,8 @@ extern "C" {
 lt_status lt_kv_attend(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype, const uint32_t* seq,
                        const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale, void* stream) {
     ltkv::NvtxRange nv("lt_kv_attend");
+    if (!kv) return LT_E_ARG;
+    if (lt_status rc = check_dtypes(kv, {&q_dtype, &out_dtype})) return rc;
     return attend_entry(kv, layer, q, q_dtype, seq, pos, n, out, out_dtype, scale, stream, false);
 }
 
@@ -965,6 +981,8 @@ lt_status lt_kv_write_attend(lt_kv* kv, uint32_t layer, const int32_t* block, co
                              const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale,
                              void* stream) {
     ltkv::NvtxRange nv("lt_kv_write_attend");
+    if (!kv) return LT_E_ARG;
+    if (lt_status rc = check_dtypes(kv, {&kv_dtype, &q_dtype, &out_dtype})) return rc;
     return write_attend_entry(kv, layer, block, slot, k, v, kv_dtype, q, q_dtype, seq, pos, n, out, out_dtype, scale,
                               stream, false);
 }
@@ -973,6 +991,8 @@ lt_status lt_kv_attend_gather(lt_kv* kv, uint32_t layer, const void* q, lt_dtype
                               const uint32_t* pos, uint32_t n, void* out, lt_dtype out_dtype, float scale,
                               void* stream) {
     ltkv::NvtxRange nv("lt_kv_attend_gather");
+    if (!kv) return LT_E_ARG;
+    if (lt_status rc = check_dtypes(kv, {&q_dtype, &out_dtype})) return rc;
     return attend_entry(kv, layer, q, q_dtype, seq, pos, n, out, out_dtype, scale, stream, true);
 }
 
@@ -981,6 +1001,8 @@ lt_status lt_kv_write_attend_gather(lt_kv* kv, uint32_t layer, const int32_t* bl
                                     const uint32_t* seq, const uint32_t* pos, uint32_t n, void* out,
                                     lt_dtype out_dtype, float scale, void* stream) {
     ltkv::NvtxRange nv("lt_kv_write_attend_gather");
+    if (!kv) return LT_E_ARG;
+    if (lt_status rc = check_dtypes(kv, {&kv_dtype, &q_dtype, &out_dtype})) return rc;
     return write_attend_entry(kv, layer, block, slot, k, v, kv_dtype, q, q_dtype, seq, pos, n, out, out_dtype, scale,
                               stream, true);
 }

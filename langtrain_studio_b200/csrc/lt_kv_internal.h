@@ -4,8 +4,21 @@
 #include <cuda_runtime.h>
 #include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
+#include <string.h>
+
+#include "lt_kv.h"
 
 namespace ltkv {
+
+// Whether an lt_dtype argument names LT_F32 or LT_F16.  A C caller may pass
+// any 32-bit value; reading an out-of-range value through the C++ enum type
+// is undefined, so the argument's bytes are read instead.
+static_assert(sizeof(lt_dtype) == sizeof(int32_t), "lt_dtype is passed as a 32-bit int");
+inline bool dtype_valid(const lt_dtype& d) {
+    int32_t v;
+    memcpy(&v, &d, sizeof v);
+    return v == (int32_t)LT_F32 || v == (int32_t)LT_F16;
+}
 
 constexpr int kBlock = 16;           // tokens per block (kv.rs:13)
 constexpr int kMaxGroup = 8;         // q heads per KV head the attention kernel handles

@@ -87,6 +87,7 @@ lt_status lt_kv_gather_heads(lt_kv* kv, const void* local, void* gathered, void*
                              void* comm, int nranks, void* stream) {
     ltkv::NvtxRange nv("lt_kv_gather_heads");
     if (!kv || !local || !gathered || !out || !comm || nranks < 1) return LT_E_ARG;
+    if (!ltkv::dtype_valid(dtype)) return LT_E_ARG;
     NcclApi& api = nccl();
     if (!api.ok) return LT_E_NCCL;
     const size_t row = ltkv::local_out_row_bytes(kv, dtype);  // one token's local heads

@@ -81,6 +81,7 @@ extern "C" lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_
                                              lt_dtype q_dtype, void* out, lt_dtype out_dtype, float scale,
                                              void* stream) {
     if (!pool_layer || !tables || !q || !out || (n && (!seq || !pos))) return LT_E_ARG;
+    if (!ltkv::dtype_valid(q_dtype) || !ltkv::dtype_valid(out_dtype)) return LT_E_ARG;
     if (n_kv_heads == 0 || n_heads == 0 || n_heads % n_kv_heads) return LT_E_ARG;
     if (head_dim != 64 && head_dim != 128) return LT_E_UNSUPPORTED;
     const uint32_t group = n_heads / n_kv_heads;

@@ -220,3 +220,41 @@ def test_compaction_paths_match_oracle(oracle_mod, share_rate):
         else:
             assert kv.compact() == len(ok.compact()), step
         compare_state(kv, ok, max_seqs)
+
+
+def test_dtype_arguments_outside_the_enum_are_refused(native):
+    """A dtype that is neither LT_F32 nor LT_F16 is refused (LT_E_ARG) before
+    any other check or device work, on every entry point that takes one;
+    nothing is dereferenced (the pointers here are placeholders)."""
+    import ctypes as C
+
+    from langtrain_studio_b200 import _native as N
+
+    lib = native
+    kv = host_kv(1, 1, 64, 64)
+    h = kv._h
+    p = C.c_void_p(256)  # 16-byte aligned placeholder, never dereferenced
+    one = np.zeros(1, np.uint32)
+    cell = np.zeros(1, np.int32)
+    addr = lambda a: C.c_void_p(a.ctypes.data)  # noqa: E731
+    bad, f32, f16 = 7, N.LT_F32, N.LT_F16
+    calls = {
+        "lt_kv_write": lambda d: lib.lt_kv_write(h, 0, addr(cell), addr(cell), 1, p, p, d, None),
+        "lt_kv_attend q": lambda d: lib.lt_kv_attend(h, 0, p, d, addr(one), addr(one), 1, p, f32, 0.125, None),
+        "lt_kv_attend out": lambda d: lib.lt_kv_attend(h, 0, p, f16, addr(one), addr(one), 1, p, d, 0.125, None),
+        "lt_kv_write_attend": lambda d: lib.lt_kv_write_attend(h, 0, addr(cell), addr(cell), p, p, d, p, f16,
+                                                               addr(one), addr(one), 1, p, f32, 0.125, None),
+        "lt_kv_attend_gather": lambda d: lib.lt_kv_attend_gather(h, 0, p, f16, addr(one), addr(one), 1, p, d, 0.125,
+                                                                 None),
+    }
+    for name, call in calls.items():
+        assert call(bad) == N.LT_E_ARG, name
+        assert "neither LT_F32 nor LT_F16" in lib.lt_kv_last_error(h).decode(), name
+        assert call(f32 if "out" not in name else f16) == N.LT_E_ARG  # valid dtype: refused for having no device
+        assert "without a device" in lib.lt_kv_last_error(h).decode(), name
+    assert lib.lt_kv_gather_heads(h, p, p, p, 1, bad, p, 2, None) == N.LT_E_ARG
+    assert lib.lt_paged_attend_noalloc(p, 1, 64, 1, p, 4, addr(one), addr(one), 1, p, bad, p, f32, C.c_float(0.125),
+                                       None) == N.LT_E_ARG
+    assert lib.lt_paged_attend_noalloc(p, 1, 64, 1, p, 4, addr(one), addr(one), 1, p, f32, p, bad, C.c_float(0.125),
+                                       None) == N.LT_E_ARG
+    kv.close()
