@@ -58,6 +58,8 @@ typedef enum lt_status {
                              pool (only LT_FEATURE_BOUNDS_CHECK builds test)    */
 } lt_status;
 
+/* Element type of a device array argument.  Any other value is refused with
+ * LT_E_ARG before the call does anything. */
 typedef enum lt_dtype {
     LT_F32 = 0,
     LT_F16 = 1
