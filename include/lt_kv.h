@@ -111,6 +111,7 @@ void lt_kv_destroy(lt_kv* kv);
 /* Message of the last failed call on this handle ("" if none). */
 const char* lt_kv_last_error(const lt_kv* kv);
 
+/* The accessors below return 0 for a null handle. */
 /* KvCache::capacity (kv.rs:50-52): n_blocks * 16 tokens. Backend::n_ctx. */
 uint32_t lt_kv_capacity(const lt_kv* kv);
 /* KvCache::bytes (kv.rs:54-56): K + V pool bytes (LT_KV_Q8_0: values and
@@ -354,30 +355,53 @@ lt_status lt_kv_write_attend_gather(lt_kv* kv, uint32_t layer, const int32_t* bl
  * lt_kv_attend, for callers that cannot call cudaMalloc: hosts whose device
  * memory is wholly owned by their own allocator or fixed budget, and hosts
  * that cannot pay for cudaMalloc's possible device-wide synchronisation on
- * their step path.  The caller passes everything: the pool of one layer
- * (lt_kv_device_pool layout, i.e. lt_kv_device_pool(kv) + layer *
- * n_blocks * n_kv_heads * 2 * 16 * head_dim halves), the device block tables
- * ([seq][max_blocks_per_seq] int32), host seq/pos arrays, device q and out.
- * Nothing is allocated: the kernel's scratch (split-K partials and the work
- * plan) lives in one static device array of LT_NOALLOC_SCRATCH_BYTES
- * that every GPU loading this library holds until the process exits.
- *   - At most LT_NOALLOC_MAX_TOKENS tokens per call, and the partials must
- *     fit the array; larger requests return LT_E_SCRATCH before any work.
+ * their step path.  The caller passes everything:
+ *   - pool_layer: the K/V tiles of one layer in the lt_kv_device_pool layout
+ *     (lt_kv_device_pool(kv) + layer * n_blocks * n_kv_heads * 2 * 16 *
+ *     head_dim halves), 16-byte aligned, holding n_blocks blocks;
+ *     kv_format states its format and must be LT_KV_F16 (LT_KV_Q8_0 pools
+ *     are refused with LT_E_UNSUPPORTED);
+ *   - tables: device block tables, int32 [n_table_rows][max_blocks_per_seq],
+ *     4-byte aligned;
+ *   - host seq/pos arrays, device q and out (16-byte aligned).
+ * Every seq must be below n_table_rows and every pos below
+ * 16 * max_blocks_per_seq (and below 2^31 - 16): anything else is refused
+ * with LT_E_ARG before any work.  The block ids in entries [0, pos/16] of
+ * each token's row are read on the device and tested against n_blocks; an
+ * id outside the pool reads block 0 instead (that token's output is then
+ * wrong) and raises LT_E_BOUNDS, reported by lt_paged_attend_noalloc_check.
+ *
+ * Nothing is allocated: the kernel's scratch (split-K partials and
+ * range-done flags) lives in one static device array of
+ * LT_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until
+ * the process exits.
+ *   - At most LT_NOALLOC_MAX_TOKENS tokens per call; larger requests return
+ *     LT_E_SCRATCH before any work.  Calls of more than 512 tokens run as
+ *     consecutive launches on `stream`.
  *   - The first call on a device looks up the array's address with that
  *     device current; make that first call before any stream capture.
  *   - All calls share the array and it keeps the last call's contents; each
- *     call clears its error word, tags its flags with a fresh epoch and
- *     rewrites the rest of what it reads.  Calls that overlap on the GPU
- *     race: issue them in order on one stream.
- *   - The call does not synchronise; a bounded device wait that gives up
- *     leaves that call's outputs invalid without a status. */
+ *     launch tags its flags with a fresh epoch and rewrites the partials it
+ *     reads.  Calls that overlap on the GPU race: issue them in order on
+ *     one stream.
+ *   - The call does not synchronise.  Device-side failures of every call on
+ *     the current device (a bounded wait that gave up, a block id past the
+ *     pool) accumulate in the array's error word until
+ *     lt_paged_attend_noalloc_check reads it. */
 #define LT_NOALLOC_SCRATCH_BYTES (8u << 20)
 #define LT_NOALLOC_MAX_TOKENS 1024u
-lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_kv_heads, uint32_t head_dim,
-                                  uint32_t n_heads, const int32_t* tables, uint32_t max_blocks_per_seq,
+lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t kv_format, uint32_t n_blocks,
+                                  uint32_t n_kv_heads, uint32_t head_dim, uint32_t n_heads,
+                                  const int32_t* tables, uint32_t n_table_rows, uint32_t max_blocks_per_seq,
                                   const uint32_t* seq_host, const uint32_t* pos_host, uint32_t n,
                                   const void* q, lt_dtype q_dtype, void* out, lt_dtype out_dtype,
                                   float scale, void* stream);
+/* No counterpart in the reference.  Synchronises `stream`, then reads and
+ * clears the error word of lt_paged_attend_noalloc on the current device:
+ * LT_OK when no call since the last check failed on the device,
+ * LT_E_TIMEOUT when a bounded wait gave up (those calls' outputs are
+ * invalid), else LT_E_BOUNDS (a table named a block outside the pool). */
+lt_status lt_paged_attend_noalloc_check(void* stream);
 
 #ifdef __cplusplus
 }

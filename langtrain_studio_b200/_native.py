@@ -32,7 +32,7 @@ EXPORTS = (
     "lt_kv_seq_blocks", "lt_kv_refs", "lt_kv_free_list", "lt_kv_n_blocks", "lt_kv_device_pool",
     "lt_kv_device_tables", "lt_kv_read_pool", "lt_kv_launch_count", "lt_kv_profile", "lt_kv_profile_read",
     "lt_kv_nccl_unique_id", "lt_kv_nccl_init", "lt_kv_nccl_destroy", "lt_kv_gather_heads",
-    "lt_paged_attend_noalloc", "lt_kv_peer_export", "lt_kv_peer_import", "lt_kv_peer_close",
+    "lt_paged_attend_noalloc", "lt_paged_attend_noalloc_check", "lt_kv_peer_export", "lt_kv_peer_import", "lt_kv_peer_close",
     "lt_kv_attend_gather", "lt_kv_write_attend_gather", "lt_kv_selftest_wait", "lt_kv_build_features", "lt_kv_set_min_tiles_per_warp", "lt_kv_set_cascade", "lt_kv_cascade_launches",
     "lt_llama_create", "lt_llama_destroy", "lt_llama_last_error", "lt_llama_set_tensor", "lt_llama_forward",
     "lt_llama_step_greedy", "lt_llama_launch_count", "lt_llama_profile", "lt_llama_profile_read", "lt_q8_quantize", "lt_q8_matmul", "lt_rms_norm_q8",
@@ -149,8 +149,9 @@ def _declare(L):
         "lt_kv_nccl_init": (st, [C.POINTER(p), C.c_int, p, C.c_int, C.c_int]),
         "lt_kv_nccl_destroy": (None, [p]),
         "lt_kv_gather_heads": (st, [p, p, p, p, u32, C.c_int, p, C.c_int, p]),
-        "lt_paged_attend_noalloc": (st, [p, u32, u32, u32, p, u32, p, p, u32, p, C.c_int, p, C.c_int,
-                                         C.c_float, p]),
+        "lt_paged_attend_noalloc": (st, [p, u32, u32, u32, u32, u32, p, u32, u32, p, p, u32, p, C.c_int, p,
+                                         C.c_int, C.c_float, p]),
+        "lt_paged_attend_noalloc_check": (st, [p]),
         "lt_llama_create": (st, [C.POINTER(lt_llama_config), C.POINTER(p)]),
         "lt_llama_destroy": (None, [p]),
         "lt_llama_last_error": (C.c_char_p, [p]),

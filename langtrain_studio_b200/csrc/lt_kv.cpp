@@ -609,6 +609,7 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     p.tables = kv->d_tables;
     p.max_blocks = (int32_t)kv->max_blocks;
     p.n_blocks = (int32_t)kv->n_blocks;
+    p.check_ids = 0;  // this handle's bookkeeping wrote the tables
     p.n_tok = (int32_t)n;
     p.tiles_per_head = (int32_t)tiles;
     // At least min_tiles_per_warp tiles a warp: a small step (few tokens, short
@@ -863,15 +864,15 @@ void lt_kv_destroy(lt_kv* kv) {
 
 const char* lt_kv_last_error(const lt_kv* kv) { return kv ? kv->err.c_str() : "null handle"; }
 
-uint32_t lt_kv_capacity(const lt_kv* kv) { return kv->n_blocks * kBlock; }
+uint32_t lt_kv_capacity(const lt_kv* kv) { return kv ? kv->n_blocks * kBlock : 0; }
 
-uint64_t lt_kv_bytes(const lt_kv* kv) { return (uint64_t)kv->cfg.n_layers * kv->layer_elems * 2; }
+uint64_t lt_kv_bytes(const lt_kv* kv) { return kv ? (uint64_t)kv->cfg.n_layers * kv->layer_elems * 2 : 0; }
 
-uint32_t lt_kv_len(const lt_kv* kv, uint32_t seq) { return seq < kv->cfg.max_seqs ? kv->lens[seq] : 0; }
+uint32_t lt_kv_len(const lt_kv* kv, uint32_t seq) { return kv && seq < kv->cfg.max_seqs ? kv->lens[seq] : 0; }
 
-uint32_t lt_kv_free_blocks(const lt_kv* kv) { return (uint32_t)kv->free_list.size(); }
+uint32_t lt_kv_free_blocks(const lt_kv* kv) { return kv ? (uint32_t)kv->free_list.size() : 0; }
 
-uint32_t lt_kv_n_blocks(const lt_kv* kv) { return kv->n_blocks; }
+uint32_t lt_kv_n_blocks(const lt_kv* kv) { return kv ? kv->n_blocks : 0; }
 
 lt_status lt_kv_append(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n, int32_t* block_out,
                        int32_t* slot_out, uint32_t* n_done, void* stream) {
@@ -1246,11 +1247,13 @@ uint32_t lt_kv_seq_blocks(const lt_kv* kv, uint32_t seq, int32_t* out, uint32_t 
 }
 
 uint32_t lt_kv_refs(const lt_kv* kv, uint32_t* out, uint32_t cap) {
+    if (!kv) return 0;
     for (uint32_t b = 0; b < kv->n_blocks && b < cap; ++b) out[b] = kv->refs[b];
     return kv->n_blocks;
 }
 
 uint32_t lt_kv_free_list(const lt_kv* kv, int32_t* out, uint32_t cap) {
+    if (!kv) return 0;
     for (size_t i = 0; i < kv->free_list.size() && i < cap; ++i) out[i] = kv->free_list[i];
     return (uint32_t)kv->free_list.size();
 }

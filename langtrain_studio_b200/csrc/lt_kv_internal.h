@@ -26,7 +26,8 @@ constexpr int kMaxGroup = 8;         // q heads per KV head the attention kernel
 // Bits of the device error word (lt_kv_check turns them into statuses).
 constexpr int32_t kErrTimeout = 1;   // a bounded wait gave up -> LT_E_TIMEOUT
 constexpr int32_t kErrBounds = 2;    // a table entry named no block of the pool -> LT_E_BOUNDS
-                                     // (only builds with LT_BOUNDS_CHECK test for it)
+                                     // (tested by LT_BOUNDS_CHECK builds, and by every build
+                                     // for tables the caller owns)
 
 // Per-token input of one attention launch: the token's sequence, its
 // position (it attends over blocks [0, pos/16]), the physical id of its last
@@ -47,6 +48,8 @@ struct AttnParams {
     int32_t* tables;             // [max_seqs][max_blocks]; each token's last entry is (re)written
     int32_t max_blocks;
     int32_t n_blocks;            // blocks in the pool, for LT_BOUNDS_CHECK builds (0: not checked)
+    int32_t check_ids;           // test every block id read from `tables` against n_blocks in every
+                                 // build (caller-owned tables, lt_paged_attend_noalloc)
     const TokenDesc* toks;       // n_tok entries in global memory, or null: use inl
     int32_t n_tok;
     int32_t tiles_per_head;      // prefix of n_tok (total blocks over the tokens)

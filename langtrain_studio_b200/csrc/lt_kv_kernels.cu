@@ -137,19 +137,19 @@ __device__ __forceinline__ int wait_flag_bounded(const uint32_t* flag, uint32_t 
 }
 
 // A block id read from a block table.  Builds with LT_BOUNDS_CHECK test it
-// against the pool (n_blocks > 0): a bad id raises kErrBounds and block 0
+// against the pool (n_blocks > 0), and so does every build when `check` is
+// set (tables the caller owns): a bad id raises kErrBounds and block 0
 // stands in for it, so the access stays inside the pool and only the
-// output is wrong (and reported).  Other builds trust the host bookkeeping.
-__device__ __forceinline__ int checked_block(int b, int n_blocks, int32_t* err) {
+// output is wrong (and reported).  Otherwise the host bookkeeping that
+// wrote the table is trusted.
+__device__ __forceinline__ int checked_block(int b, int n_blocks, int32_t* err, bool check = false) {
 #ifdef LT_BOUNDS_CHECK
-    if (n_blocks > 0 && (unsigned)b >= (unsigned)n_blocks) {
+    check = true;
+#endif
+    if (check && n_blocks > 0 && (unsigned)b >= (unsigned)n_blocks) {
         atomicOr(err, kErrBounds);
         return 0;
     }
-#else
-    (void)n_blocks;
-    (void)err;
-#endif
     return b;
 }
 
@@ -826,7 +826,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) paged_attn_kernel(const __grid
         const int bb = b + lane;
         if (bb >= r.b1) return 0;
         if (bb == r.b1 - 1 && r.last_block >= 0) return r.last_block;
-        return checked_block(__ldg(p.tables + (size_t)r.seq * p.max_blocks + r.skip + bb), p.n_blocks, p.err);
+        return checked_block(__ldg(p.tables + (size_t)r.seq * p.max_blocks + r.skip + bb), p.n_blocks, p.err,
+                             p.check_ids != 0);
     };
 
     // ---- issuer state ----

@@ -9,7 +9,7 @@
 // caller has the block pool and block tables already (in the layout of
 // lt_kv_device_pool / lt_kv_device_tables) and only needs the attention
 // kernel.  That kernel needs scratch beyond its inputs and outputs (split-K
-// partials and the work plan), so this entry point keeps it in one fixed,
+// partials and range-done flags), so this entry point keeps it in one fixed,
 // file-scope device array instead of allocating.
 //
 // The array is LT_NOALLOC_SCRATCH_BYTES (8 MiB).  Every GPU on which the
@@ -17,11 +17,23 @@
 // call on a device looks up the array's device address with that device
 // current (cudaGetSymbolAddress) and caches it; make that first call before
 // any stream capture.  Every call shares the array and it keeps the last
-// call's contents, so each call clears its error word before its launch,
-// keeps its range-done flags at a fixed place where they only ever hold
-// epochs (a fresh one per call), and overwrites everything else it reads;
-// calls that overlap on the GPU (different streams, no ordering) race on it
-// -- issue them in order on one stream.
+// call's contents: the range-done flags sit at a fixed place where they only
+// ever hold epochs (a fresh one per launch), each launch overwrites the
+// partials it reads, and the error word collects the failures of every call
+// until lt_paged_attend_noalloc_check reads and clears it.  Calls that
+// overlap on the GPU (different streams, no ordering) race on the array --
+// issue them in order on one stream.
+//
+// The tables and block ids come from the caller, not from this library's
+// bookkeeping, so everything the kernel would index with is checked: on the
+// host, before any work, every sequence id against the table rows and every
+// position against the row length; on the device, every block id read from
+// the tables against the caller's pool size (an id past it reads block 0
+// instead and raises LT_E_BOUNDS in the error word).
+//
+// The per-token work descriptors travel inside the kernel parameters, up to
+// 512 tokens a launch; a call with more tokens is issued as consecutive
+// launches on the caller's stream, so no host buffer is ever copied.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -36,29 +48,25 @@ namespace {
 
 constexpr size_t kScratchBytes = LT_NOALLOC_SCRATCH_BYTES;
 constexpr int kMaxDevices = 64;
-// The range-done flags sit at a fixed place and only ever hold epochs: the
-// descriptors and partials after them move with the call's size, and a flag
-// placed over an earlier call's descriptor word (a small integer) could
-// already equal the new epoch.
+// Scratch layout: [error word][range-done flags][partial (m, l)][partial O],
+// 256-byte aligned.  The flags sit at a fixed place and only ever hold
+// epochs, so a later launch never finds a stale word equal to its epoch.
 constexpr size_t kFlagsOffset = 256;
 constexpr size_t kMaxFlagWarps = 16384;
 constexpr size_t kFlagsBytes = kMaxFlagWarps * sizeof(uint32_t);
+constexpr size_t kPartialsOffset = kFlagsOffset + kFlagsBytes;
 
 static __device__ __align__(256) unsigned char lt_noalloc_scratch[kScratchBytes];
 
 std::atomic<void*> g_scratch[kMaxDevices];
-// Host-side descriptors of one call (file scope, guarded by a mutex): the
-// launch parameters carry up to kInlineTokens of them, the rest go through
-// the scratch array.
-std::mutex g_mu;
-uint32_t g_epoch[kMaxDevices];  // per-device launch epoch for the range-done flags
-ltkv::AttnParams g_params;
-ltkv::TokenDesc g_toks[LT_NOALLOC_MAX_TOKENS];
+std::mutex g_mu;                  // guards g_epoch and g_params
+uint32_t g_epoch[kMaxDevices];    // per-device launch epoch for the range-done flags
+ltkv::AttnParams g_params;        // one launch's parameters (large: kept off the stack)
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Device address of the scratch array on the current device (set up once).
-cudaError_t scratch_ptr(void** out) {
+cudaError_t scratch_ptr(int* dev_out, void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -69,119 +77,142 @@ cudaError_t scratch_ptr(void** out) {
         if (e != cudaSuccess) return e;
         g_scratch[dev].store(p, std::memory_order_release);
     }
+    *dev_out = dev;
     *out = p;
     return cudaSuccess;
 }
 
+bool misaligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
+
 }  // namespace
 
-extern "C" lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t n_kv_heads, uint32_t head_dim,
-                                             uint32_t n_heads, const int32_t* tables, uint32_t max_blocks_per_seq,
-                                             const uint32_t* seq, const uint32_t* pos, uint32_t n, const void* q,
-                                             lt_dtype q_dtype, void* out, lt_dtype out_dtype, float scale,
-                                             void* stream) {
+extern "C" lt_status lt_paged_attend_noalloc(const void* pool_layer, uint32_t kv_format, uint32_t n_blocks,
+                                             uint32_t n_kv_heads, uint32_t head_dim, uint32_t n_heads,
+                                             const int32_t* tables, uint32_t n_table_rows,
+                                             uint32_t max_blocks_per_seq, const uint32_t* seq, const uint32_t* pos,
+                                             uint32_t n, const void* q, lt_dtype q_dtype, void* out,
+                                             lt_dtype out_dtype, float scale, void* stream) {
+    // ---- every argument, before any device work ----
     if (!pool_layer || !tables || !q || !out || (n && (!seq || !pos))) return LT_E_ARG;
     if (!ltkv::dtype_valid(q_dtype) || !ltkv::dtype_valid(out_dtype)) return LT_E_ARG;
+    if (kv_format == LT_KV_Q8_0) return LT_E_UNSUPPORTED;  // the kernel below reads f16 tiles only
+    if (kv_format != LT_KV_F16) return LT_E_ARG;
+    if (n_blocks == 0 || n_blocks > 0x7FFFFFFFu) return LT_E_ARG;
+    if (n_table_rows == 0 || max_blocks_per_seq == 0 || max_blocks_per_seq > 0x7FFFFFFFu) return LT_E_ARG;
     if (n_kv_heads == 0 || n_heads == 0 || n_heads % n_kv_heads) return LT_E_ARG;
     if (head_dim != 64 && head_dim != 128) return LT_E_UNSUPPORTED;
     const uint32_t group = n_heads / n_kv_heads;
     if (group > (uint32_t)ltkv::kMaxGroup) return LT_E_UNSUPPORTED;
-    if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) return LT_E_ARG;
+    // Bulk copies read pool tiles and q rows from 16-byte boundaries.
+    if (misaligned(pool_layer, 16) || misaligned(q, 16) || misaligned(out, 16) || misaligned(tables, 4))
+        return LT_E_ARG;
     if (n == 0) return LT_OK;
     if (n > LT_NOALLOC_MAX_TOKENS) return LT_E_SCRATCH;
-    long long tiles = 0;
     for (uint32_t i = 0; i < n; ++i) {
-        if ((pos[i] + ltkv::kBlock) / ltkv::kBlock > max_blocks_per_seq) return LT_E_ARG;
-        tiles += pos[i] / ltkv::kBlock + 1;
+        if (seq[i] >= n_table_rows) return LT_E_ARG;
+        // pos is carried as int32 and attends over table entries [0, pos/16].
+        if (pos[i] > 0x7FFFFFFFu - ltkv::kBlock || pos[i] / ltkv::kBlock >= max_blocks_per_seq) return LT_E_ARG;
     }
-    if (tiles > 0x7FFFFFFFll / n_kv_heads) return LT_E_SCRATCH;
-
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return LT_E_CUDA;
-    const int q_f32 = q_dtype == LT_F32;
-    int n_warps = ltkv::attend_warps(dev, (int)group, (int)head_dim, q_f32, 0);
-    if (n_warps <= 0) return LT_E_CUDA;
-    n_warps = (int)std::min<long long>(n_warps, tiles * n_kv_heads);
-
-    // Scratch layout: [error word][range-done flags, fixed][descriptors
-    // beyond the inline ones][partial (m, l)][partial O], 256-byte aligned;
-    // one flag and one partial slot per warp.  Fewer warps are used when the
-    // partials would not fit.
+    const uint32_t kInline = (uint32_t)ltkv::kInlineTokens;
+    for (uint32_t c0 = 0; c0 < n; c0 += kInline) {
+        long long tiles = 0;
+        for (uint32_t i = c0; i < std::min(n, c0 + kInline); ++i) tiles += pos[i] / ltkv::kBlock + 1;
+        if (tiles > 0x7FFFFFFFll / n_kv_heads) return LT_E_SCRATCH;
+    }
     const size_t gd = (size_t)group * head_dim;
-    const size_t o_toks = kFlagsOffset + kFlagsBytes;
-    const size_t o_ml = o_toks + round256(n > (uint32_t)ltkv::kInlineTokens ? n * sizeof(ltkv::TokenDesc) : 0);
     const size_t per_warp = group * 2 * sizeof(float) + gd * sizeof(float);
-    if (o_ml + 512 + per_warp > kScratchBytes) return LT_E_SCRATCH;
-    n_warps = (int)std::min<size_t>({(size_t)n_warps, kMaxFlagWarps, (kScratchBytes - o_ml - 512) / per_warp});
-    const size_t o_o = o_ml + round256((size_t)n_warps * group * 2 * sizeof(float));
 
+    // ---- set-up (first call on this device: look up the array's address) ----
+    int dev = 0;
     void* base = nullptr;
-    if (scratch_ptr(&base) != cudaSuccess) return LT_E_CUDA;
+    if (scratch_ptr(&dev, &base) != cudaSuccess) return LT_E_CUDA;
     unsigned char* b = static_cast<unsigned char*>(base);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int q_f32 = q_dtype == LT_F32;
+    const int max_warps = ltkv::attend_warps(dev, (int)group, (int)head_dim, q_f32, 0);
+    if (max_warps <= 0) return LT_E_CUDA;
+    const size_t warp_cap =
+        std::min<size_t>({(size_t)max_warps, kMaxFlagWarps, (kScratchBytes - kPartialsOffset - 256) / per_warp});
+    const size_t q_row = (size_t)n_heads * head_dim * (q_f32 ? 4 : 2);
+    const size_t out_row = (size_t)n_heads * head_dim * (out_dtype == LT_F32 ? 4 : 2);
 
     std::lock_guard<std::mutex> lock(g_mu);
     ltkv::AttnParams& p = g_params;
-    long long prefix = 0;
-    ltkv::TokenDesc* td = n <= (uint32_t)ltkv::kInlineTokens ? p.inl : g_toks;
-    for (uint32_t i = 0; i < n; ++i) {
-        td[i].seq = (int32_t)seq[i];
-        td[i].pos = (int32_t)pos[i];
-        td[i].last_block = -1;  // unknown here: the kernel reads every block id from the tables
-        td[i].prefix = (int32_t)prefix;
-        td[i].skip = 0;
-        prefix += pos[i] / ltkv::kBlock + 1;
+    for (uint32_t c0 = 0; c0 < n; c0 += kInline) {
+        const uint32_t cn = std::min(n - c0, kInline);
+        long long prefix = 0;
+        for (uint32_t i = 0; i < cn; ++i) {
+            ltkv::TokenDesc& td = p.inl[i];
+            td.seq = (int32_t)seq[c0 + i];
+            td.pos = (int32_t)pos[c0 + i];
+            td.last_block = -1;  // every block id is read (and checked) from the caller's tables
+            td.prefix = (int32_t)prefix;
+            td.skip = 0;
+            prefix += pos[c0 + i] / ltkv::kBlock + 1;
+        }
+        const int n_warps = (int)std::min<long long>((long long)warp_cap, prefix * n_kv_heads);
+        p.toks = nullptr;  // descriptors travel in the kernel parameters
+        p.pool_layer = static_cast<const uint16_t*>(pool_layer);
+        p.pool_layer_w = nullptr;                 // no fused append on this entry point
+        p.tables = const_cast<int32_t*>(tables);  // not written: no descriptor carries a last block id
+        p.max_blocks = (int32_t)max_blocks_per_seq;
+        p.n_blocks = (int32_t)n_blocks;
+        p.check_ids = 1;
+        p.n_tok = (int32_t)cn;
+        p.tiles_per_head = (int32_t)prefix;
+        p.n_warps = n_warps;
+        p.n_kv_heads = (int32_t)n_kv_heads;
+        p.group = (int32_t)group;
+        p.q = static_cast<const uint8_t*>(q) + (size_t)c0 * q_row;
+        p.q_f32 = q_f32;
+        p.out = static_cast<uint8_t*>(out) + (size_t)c0 * out_row;
+        p.out_f32 = out_dtype == LT_F32;
+        p.scale_log2 = scale * 1.4426950408889634f;
+        p.part_ml = reinterpret_cast<float*>(b + kPartialsOffset);
+        p.part_o = reinterpret_cast<float*>(b + kPartialsOffset + round256((size_t)n_warps * group * 2 * sizeof(float)));
+        p.part2_o = nullptr;  // one-level merge
+        p.part2_ml = nullptr;
+        p.flags2 = nullptr;
+        // The flags keep earlier launches' epochs: a fresh epoch per launch on
+        // this device (the array starts zeroed, and 0 is never used).  When the
+        // count wraps, any earlier epoch may still be there, so the flags are
+        // cleared.
+        p.flags = reinterpret_cast<uint32_t*>(b + kFlagsOffset);
+        uint32_t epoch = g_epoch[dev] + 1;
+        if (epoch == 0) {
+            if (cudaMemsetAsync(b + kFlagsOffset, 0, kFlagsBytes, st) != cudaSuccess) return LT_E_CUDA;
+            epoch = 1;
+        }
+        g_epoch[dev] = epoch;
+        p.epoch = epoch;
+        // Failures (a bounded wait that gave up, a block id past the pool) are
+        // OR-ed into the array's first word and stay there until
+        // lt_paged_attend_noalloc_check reads and clears it.
+        p.err = reinterpret_cast<int32_t*>(b);
+        p.k_new = nullptr;
+        p.v_new = nullptr;
+        p.kv_f32 = 0;
+        p.pre_o = nullptr;
+        p.pre_ml = nullptr;
+        p.pre_splits = 0;
+        p.pre_split_rows = 0;
+        p.q8 = 0;
+        p.n_peers = 0;
+        if (ltkv::launch_attend(p, (int)head_dim, st) != cudaSuccess) return LT_E_CUDA;
     }
-    // The error word must start at zero; the array keeps the previous call's bytes.
-    if (cudaMemsetAsync(b, 0, sizeof(int32_t), st) != cudaSuccess) return LT_E_CUDA;
-    if (td == g_toks) {
-        // Pageable source: the call returns once the bytes are staged.
-        if (cudaMemcpyAsync(b + o_toks, g_toks, n * sizeof(ltkv::TokenDesc), cudaMemcpyHostToDevice, st) !=
-            cudaSuccess)
-            return LT_E_CUDA;
-        p.toks = reinterpret_cast<const ltkv::TokenDesc*>(b + o_toks);
-    } else {
-        p.toks = nullptr;
-    }
-    p.pool_layer = static_cast<const uint16_t*>(pool_layer);
-    p.pool_layer_w = nullptr;  // no fused append on this entry point
-    p.tables = const_cast<int32_t*>(tables);  // not written: no descriptor carries a last block id
-    p.max_blocks = (int32_t)max_blocks_per_seq;
-    p.n_tok = (int32_t)n;
-    p.tiles_per_head = (int32_t)tiles;
-    p.n_warps = n_warps;
-    p.n_kv_heads = (int32_t)n_kv_heads;
-    p.group = (int32_t)group;
-    p.q = q;
-    p.q_f32 = q_f32;
-    p.out = out;
-    p.out_f32 = out_dtype == LT_F32;
-    p.scale_log2 = scale * 1.4426950408889634f;
-    p.part_ml = reinterpret_cast<float*>(b + o_ml);
-    p.part_o = reinterpret_cast<float*>(b + o_o);
-    // The flags keep earlier calls' epochs: a fresh epoch per call on this
-    // device (the array starts zeroed, and 0 is never used).  When the count
-    // wraps, any earlier epoch may still be there, so the flags are cleared.
-    p.flags = reinterpret_cast<uint32_t*>(b + kFlagsOffset);
-    uint32_t epoch = g_epoch[dev] + 1;
-    if (epoch == 0) {
-        if (cudaMemsetAsync(b + kFlagsOffset, 0, kFlagsBytes, st) != cudaSuccess) return LT_E_CUDA;
-        epoch = 1;
-    }
-    g_epoch[dev] = epoch;
-    p.epoch = epoch;
-    // A bounded wait that gives up sets the error word (first int32 of the
-    // array) and leaves this call's outputs invalid; nothing synchronises
-    // here to report it, and the next call clears it.
-    p.err = reinterpret_cast<int32_t*>(b);
-    p.k_new = nullptr;
-    p.v_new = nullptr;
-    p.kv_f32 = 0;
-    p.pre_o = nullptr;
-    p.pre_ml = nullptr;
-    p.pre_splits = 0;
-    p.pre_split_rows = 0;
-    p.q8 = 0;  // f16 pool layout only
-    if (ltkv::launch_attend(p, (int)head_dim, st) != cudaSuccess) return LT_E_CUDA;
     return LT_OK;
+}
+
+extern "C" lt_status lt_paged_attend_noalloc_check(void* stream) {
+    int dev = 0;
+    void* base = nullptr;
+    if (scratch_ptr(&dev, &base) != cudaSuccess) return LT_E_CUDA;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int32_t word = 0;
+    if (cudaMemcpyAsync(&word, base, sizeof word, cudaMemcpyDeviceToHost, st) != cudaSuccess) return LT_E_CUDA;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return LT_E_CUDA;
+    if (word == 0) return LT_OK;
+    if (cudaMemsetAsync(base, 0, sizeof word, st) != cudaSuccess) return LT_E_CUDA;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return LT_E_CUDA;
+    return (word & ltkv::kErrTimeout) ? LT_E_TIMEOUT : LT_E_BOUNDS;
 }

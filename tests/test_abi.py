@@ -253,8 +253,67 @@ def test_dtype_arguments_outside_the_enum_are_refused(native):
         assert call(f32 if "out" not in name else f16) == N.LT_E_ARG  # valid dtype: refused for having no device
         assert "without a device" in lib.lt_kv_last_error(h).decode(), name
     assert lib.lt_kv_gather_heads(h, p, p, p, 1, bad, p, 2, None) == N.LT_E_ARG
-    assert lib.lt_paged_attend_noalloc(p, 1, 64, 1, p, 4, addr(one), addr(one), 1, p, bad, p, f32, C.c_float(0.125),
-                                       None) == N.LT_E_ARG
-    assert lib.lt_paged_attend_noalloc(p, 1, 64, 1, p, 4, addr(one), addr(one), 1, p, f32, p, bad, C.c_float(0.125),
-                                       None) == N.LT_E_ARG
+    assert lib.lt_paged_attend_noalloc(p, N.LT_KV_F16, 4, 1, 64, 1, p, 1, 4, addr(one), addr(one), 1, p, bad, p,
+                                       f32, C.c_float(0.125), None) == N.LT_E_ARG
+    assert lib.lt_paged_attend_noalloc(p, N.LT_KV_F16, 4, 1, 64, 1, p, 1, 4, addr(one), addr(one), 1, p, f32, p,
+                                       bad, C.c_float(0.125), None) == N.LT_E_ARG
     kv.close()
+
+
+def test_noalloc_refuses_what_would_index_outside_the_callers_buffers(native):
+    """lt_paged_attend_noalloc takes its pool and tables from the caller, so
+    every argument the kernel would index with is checked on the host before
+    any device work; these calls return before touching a GPU (the pointers
+    are placeholders, never dereferenced)."""
+    import ctypes as C
+
+    from langtrain_studio_b200 import _native as N
+
+    lib = native
+    p = C.c_void_p(256)  # 16-byte aligned placeholder
+    f32 = N.LT_F32
+
+    def call(pos=0, seq=0, pool=p, tables=p, kv_format=N.LT_KV_F16, n_blocks=4, rows=2, max_blocks=4,
+             n=1, q=p, out=p):
+        s = np.full(max(n, 1), seq, np.uint32)
+        ps = np.full(max(n, 1), pos, np.uint32)
+        return lib.lt_paged_attend_noalloc(pool, kv_format, n_blocks, 1, 64, 1, tables, rows, max_blocks,
+                                           C.c_void_p(s.ctypes.data), C.c_void_p(ps.ctypes.data), n, q, f32, out,
+                                           f32, C.c_float(0.125), None)
+
+    # positions: past the row, and the uint32 values whose (pos + 16) / 16 wraps to 0
+    assert call(pos=4 * 16) == N.LT_E_ARG
+    for pos in (0xFFFFFFF0, 0xFFFFFFFF, 0x7FFFFFFF, 0x80000000):
+        assert call(pos=pos, max_blocks=0x7FFFFFFF) == N.LT_E_ARG, hex(pos)
+    # sequence ids past the caller's table rows
+    assert call(seq=2) == N.LT_E_ARG
+    assert call(seq=0xFFFFFFFF) == N.LT_E_ARG
+    # sizes the kernel carries as int32, and empty pools or tables
+    assert call(max_blocks=0x80000000) == N.LT_E_ARG
+    assert call(n_blocks=0x80000000) == N.LT_E_ARG
+    assert call(n_blocks=0) == N.LT_E_ARG
+    assert call(rows=0) == N.LT_E_ARG
+    assert call(max_blocks=0) == N.LT_E_ARG
+    # bulk copies start at 16-byte boundaries; table entries are int32
+    assert call(pool=C.c_void_p(256 + 8)) == N.LT_E_ARG
+    assert call(tables=C.c_void_p(256 + 2)) == N.LT_E_ARG
+    assert call(q=C.c_void_p(256 + 4)) == N.LT_E_ARG
+    assert call(out=C.c_void_p(256 + 4)) == N.LT_E_ARG
+    # the pool's format: f16 only
+    assert call(kv_format=N.LT_KV_Q8_0) == N.LT_E_UNSUPPORTED
+    assert call(kv_format=7) == N.LT_E_ARG
+    # too many tokens for the fixed scratch
+    assert call(n=N.LT_NOALLOC_MAX_TOKENS + 1) == N.LT_E_SCRATCH
+    assert call(n=0) == N.LT_OK  # nothing to do, nothing touched
+
+
+def test_accessors_of_a_null_handle_return_zero(native):
+    lib = native
+    assert lib.lt_kv_capacity(None) == 0
+    assert lib.lt_kv_bytes(None) == 0
+    assert lib.lt_kv_len(None, 0) == 0
+    assert lib.lt_kv_free_blocks(None) == 0
+    assert lib.lt_kv_n_blocks(None) == 0
+    assert lib.lt_kv_refs(None, None, 0) == 0
+    assert lib.lt_kv_free_list(None, None, 0) == 0
+    assert lib.lt_kv_seq_blocks(None, 0, None, 0) == 0

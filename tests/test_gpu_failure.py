@@ -11,8 +11,9 @@ kernels add two device-side paths, both tested here:
   (LT_E_TIMEOUT), that it clears, and that the handle keeps working.
 - Bounds checks (debug build liblt_kv_checked.so, -DLT_BOUNDS_CHECK).  Run
   in a child process: the parity suite against the checked build, then a
-  block-table entry overwritten with an id past the pool, which the checked
-  kernel redirects to block 0 and reports as LT_E_BOUNDS.  The child first
+  block-table entry overwritten with an id past the layer's blocks (inside
+  the two-layer allocation), which the checked kernel redirects to block 0
+  and reports as LT_E_BOUNDS.  The child first
   asserts that the checked library is the one loaded.
 """
 from __future__ import annotations
@@ -40,11 +41,12 @@ def _need_cuda():
         pytest.fail("CUDA device required for -m gpu tests")
 
 
-def _filled(oracle_mod, lens, hq=32, hkv=8, d=128, seed=0):
+def _filled(oracle_mod, lens, hq=32, hkv=8, d=128, seed=0, n_layers=1):
+    """A cache with `lens` tokens per sequence, rows written in layer 0."""
     from langtrain_studio_b200.kv import KvCache
 
-    kv = KvCache(1, hkv, d, 16 * 64, n_heads=hq, max_seqs=len(lens), max_batch=1024, device=0)
-    ok = oracle_mod.OracleKv(1, hkv * d, 16 * 64, max_seqs=len(lens))
+    kv = KvCache(n_layers, hkv, d, 16 * 64, n_heads=hq, max_seqs=len(lens), max_batch=1024, device=0)
+    ok = oracle_mod.OracleKv(n_layers, hkv * d, 16 * 64, max_seqs=len(lens))
     rng = np.random.default_rng(seed)
     for s, n in enumerate(lens):
         seqs, pos = np.full(n, s), np.arange(n)
@@ -117,7 +119,10 @@ if rc != 0:
 from cuda.bindings import runtime as rt
 oracle.build()
 lens = [40, 21]
-kv, ok, rng = T._filled(oracle, lens)
+# Two layers: an id just past layer 0's blocks is outside the pool the kernel
+# is told about but still inside the allocation (it names layer 1's block 0),
+# so even a regressed check could not read past the allocation.
+kv, ok, rng = T._filled(oracle, lens, n_layers=2)
 T._attend_matches(kv, ok, rng, lens)
 import ctypes as C
 mb = C.c_uint32(0)
@@ -129,7 +134,7 @@ def put(val):
     a = np.array([val], np.int32)
     err, = rt.cudaMemcpy(tables, a.ctypes.data, 4, rt.cudaMemcpyKind.cudaMemcpyHostToDevice)
     assert err == rt.cudaError_t.cudaSuccess, err
-put(n_blocks + 7)  # seq 0, entry 0 (not the last block: the kernel reads it from the table)
+put(n_blocks)  # seq 0, entry 0 (not the last block: the kernel reads it from the table)
 q = torch.from_numpy(rng.standard_normal((2, 32 * 128)).astype(np.float32)).cuda()
 kv.attend(0, q, np.arange(2), np.array(lens) - 1, out_dtype=torch.float32)
 try:

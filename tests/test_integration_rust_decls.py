@@ -1,12 +1,13 @@
-"""The Rust declarations in INTEGRATION.md against the C headers.
+"""The Rust binding include/lt_kv_sys.rs against the C headers.
 
-Those `extern "C"` blocks are what the reference's engine would add to bind
+Its `extern "C"` blocks are what the reference's engine would add to bind
 liblt_kv.so (its native crate is Rust).  No Rust toolchain is installed here,
 so the declarations cannot be compiled; instead every one is compared with
 the prototype gcc reports for include/*.h: argument count, integer width and
 signedness, f32/f64, pointer depth, const-ness and pointee.  `#[repr(C)]`
 structs are laid out by the repr(C) rule and compared with offsetof/sizeof of
 the C struct, field names included, and `pub const` values with the header's.
+Every Rust excerpt that INTEGRATION.md quotes must appear in the file verbatim.
 """
 from __future__ import annotations
 
@@ -38,11 +39,23 @@ def _snake(camel: str) -> str:
     return re.sub(r"(?<!^)([A-Z])", r"_\1", camel).lower()
 
 
+RUST_FILE = ROOT / "include" / "lt_kv_sys.rs"
+
+
 def _rust_blocks() -> str:
-    text = (ROOT / "INTEGRATION.md").read_text()
-    code = "\n".join(re.findall(r"```rust\n(.*?)```", text, flags=re.S))
+    code = RUST_FILE.read_text()
     code = re.sub(r"/\*.*?\*/", "", code, flags=re.S)
     return re.sub(r"//[^\n]*", "", code)
+
+
+def test_integration_doc_quotes_the_binding_verbatim():
+    text = (ROOT / "INTEGRATION.md").read_text()
+    quotes = re.findall(r"```rust\n(.*?)```", text, flags=re.S)
+    assert quotes, "INTEGRATION.md quotes no Rust"
+    src = RUST_FILE.read_text()
+    for q in quotes:
+        for line in q.strip("\n").split("\n"):
+            assert line.strip() in src, f"INTEGRATION.md quotes a line that lt_kv_sys.rs lacks: {line!r}"
 
 
 def _extern_fns(code: str) -> dict[str, tuple[list[tuple[str, str]], str]]:
@@ -134,7 +147,7 @@ ENGINE_FACING = {
     "lt_kv_share", "lt_kv_compact", "lt_kv_flush", "lt_kv_check", "lt_kv_selftest_wait", "lt_kv_build_features",
     "lt_kv_set_cascade", "lt_kv_set_min_tiles_per_warp", "lt_kv_nccl_unique_id", "lt_kv_nccl_init",
     "lt_kv_nccl_destroy", "lt_kv_gather_heads", "lt_kv_peer_export", "lt_kv_peer_import", "lt_kv_peer_close",
-    "lt_kv_attend_gather", "lt_kv_write_attend_gather", "lt_paged_attend_noalloc",
+    "lt_kv_attend_gather", "lt_kv_write_attend_gather", "lt_paged_attend_noalloc", "lt_paged_attend_noalloc_check",
     "lt_llama_create", "lt_llama_destroy", "lt_llama_last_error", "lt_llama_set_tensor", "lt_llama_forward",
     "lt_llama_step_greedy",
     "lt_sched_create", "lt_sched_destroy", "lt_sched_last_error", "lt_sched_submit", "lt_sched_submit_tokens",
