@@ -351,25 +351,28 @@ class KvCache:
     def launch_count(self) -> int:
         return self._lib.lt_kv_launch_count(self._h)
 
-    def read_pool(self, layer: int) -> np.ndarray:
-        """Raw device pool of one layer: f16 caches give uint16
-        [block][kv_head][2][16][head_dim] with the chunk swizzle of
-        include/lt_kv.h still applied; Q8_0 caches give the uint8 tiles
-        [block][kv_head][34 * head_dim]."""
+    def read_pool(self, layer: int, block0: int = 0, count: int | None = None) -> np.ndarray:
+        """Raw device pool of blocks [block0, block0 + count) of one layer
+        (default: all): f16 caches give uint16 [block][kv_head][2][16][head_dim]
+        with the chunk swizzle of include/lt_kv.h still applied; Q8_0 caches
+        give the uint8 tiles [block][kv_head][34 * head_dim]."""
+        if count is None:
+            count = self.n_blocks - block0
         if self.kv_format == "q8_0":
-            out = np.zeros((self.n_blocks, self.n_kv_heads, 34 * self.head_dim), np.uint8)
+            out = np.zeros((count, self.n_kv_heads, 34 * self.head_dim), np.uint8)
         else:
-            out = np.zeros((self.n_blocks, self.n_kv_heads, 2, BLOCK, self.head_dim), np.uint16)
-        self._check(self._lib.lt_kv_read_pool(self._h, layer, 0, self.n_blocks, _ptr(out)))
+            out = np.zeros((count, self.n_kv_heads, 2, BLOCK, self.head_dim), np.uint16)
+        self._check(self._lib.lt_kv_read_pool(self._h, layer, block0, count, _ptr(out)))
         return out
 
-    def pool_reference_layout(self, layer: int):
-        """This layer's pool as the reference lays it out (kv.rs:20):
-        (K, V) uint16 [block][slot][kv_dim]; for Q8_0 (Kq, Vq) int8
-        [block][slot][kv_dim] and (Kd, Vd) f16 bits [block][slot][kv_dim/32]."""
+    def pool_reference_layout(self, layer: int, block0: int = 0, count: int | None = None):
+        """Blocks [block0, block0 + count) of this layer's pool as the
+        reference lays it out (kv.rs:20): (K, V) uint16 [block][slot][kv_dim];
+        for Q8_0 (Kq, Vq) int8 [block][slot][kv_dim] and (Kd, Vd) f16 bits
+        [block][slot][kv_dim/32]."""
         if self.kv_format == "q8_0":
-            return unswizzle_pool_q8(self.read_pool(layer), self.head_dim)
-        return unswizzle_pool(self.read_pool(layer))
+            return unswizzle_pool_q8(self.read_pool(layer, block0, count), self.head_dim)
+        return unswizzle_pool(self.read_pool(layer, block0, count))
 
 
 class NcclComm:
