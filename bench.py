@@ -51,6 +51,32 @@ def shard_seed(rank: int) -> int:
     return 1234 + rank
 
 
+def ensure_pg(world: int, local: int):
+    """One NCCL process group for the whole run (every configuration of the
+    default line runs in it), with a short timeout so ranks that wait for one
+    another end with an error instead of hanging."""
+    if world <= 1:
+        return
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+
+
+def finish_pg(world: int):
+    if world <= 1:
+        return
+    import torch.distributed as dist
+
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def reduce_max(x: float, device, world: int) -> float:
     """Max over ranks of a per-rank device time (whole-job time of a step)."""
     if world <= 1:
@@ -92,18 +118,31 @@ def kv_row_bytes(kv_dim: int, kv_format: str = "f16") -> float:
     return kv_dim * 2 if kv_format == "f16" else kv_dim * 34 / 32
 
 
-def step_bytes(lens_now: np.ndarray, kv_format: str = "f16") -> dict:
+IO_BYTES = 4  # q, new K/V rows and outputs cross the ABI as f32, the model runner's types (model.rs:393-400)
+
+
+def step_bytes(lens_now: np.ndarray, kv_format: str = "f16", io_bytes: int = IO_BYTES) -> dict:
     """Algorithmic bytes of one step (one layer) at current lengths `lens_now`
     (after the step's append): K and V of every cached position once, q, out,
-    block-table entries, and the appended rows (f16 in, cached format out)."""
+    block-table entries, and the appended rows (read in the call's type,
+    written in the cached format)."""
+    batch = len(lens_now)
     kv_row = kv_row_bytes(N_KV_HEADS * HEAD_DIM, kv_format)  # bytes of one cached K (or V) row
     attn = int(int(lens_now.sum()) * kv_row * 2)
-    q = BATCH * N_HEADS * HEAD_DIM * 2
-    out = BATCH * N_HEADS * HEAD_DIM * 2
+    q = batch * N_HEADS * HEAD_DIM * io_bytes
+    out = batch * N_HEADS * HEAD_DIM * io_bytes
     tables = int(((lens_now + BLOCK - 1) // BLOCK).sum()) * 4
-    append = int(BATCH * 2 * (N_KV_HEADS * HEAD_DIM * 2 + kv_row))  # read f16 input + write the cell, K and V
+    append = int(batch * 2 * (N_KV_HEADS * HEAD_DIM * io_bytes + kv_row))  # read the input row, write the cell
     return {"attn": attn, "q": q, "out": out, "tables": tables, "append": append,
             "total": attn + q + out + tables + append}
+
+
+def rank_lens(rank: int) -> np.ndarray:
+    """Context lengths of a rank's 64 sequences: every rank serves the same
+    multiset (configs[1]'s draw), in its own order, so the max over ranks
+    measures the system rather than one rank's longer draw."""
+    lens = workload(1234)
+    return lens if rank == 0 else np.random.default_rng(4321 + rank).permutation(lens)
 
 
 def measured_peak():
@@ -221,10 +260,15 @@ class Stepper:
         # head-sharded: the NVLink gather fused into the attention call
         self.attend = kv.write_attend_gather if gather else kv.write_attend
 
-    def step(self):
+    def step(self, bufs=None, stream=None):
+        """bufs: (k, v, q, out) for this step (default: those given at
+        construction); stream: a ctypes stream handle (default: the current
+        stream at construction)."""
+        k, v, q, out = bufs if bufs is not None else (self.k, self.v, self.q, self.out)
+        stream = stream if stream is not None else self.stream
         pos = (self.lens + self.phase).astype(np.uint32)
-        b, s = self.kv.append_batch(self.seqs, pos, stream=self.stream)
-        self.attend(0, b, s, self.k, self.v, self.q, self.seqs, pos, out=self.out, stream=self.stream)
+        b, s = self.kv.append_batch(self.seqs, pos, stream=stream)
+        self.attend(0, b, s, k, v, q, self.seqs, pos, out=out, stream=stream)
         lens_now = self.lens + self.phase + 1
         self.phase += 1
         if self.phase == CYCLE:
@@ -234,7 +278,28 @@ class Stepper:
         return lens_now
 
 
+def c2_config(world: int, kv_format: str = "f16") -> dict:
+    """The `config` of the configs[1] line; both arms print the same dict."""
+    lens = workload(1234)
+    b = step_bytes(lens + 1, kv_format)
+    return {
+        "workload": "configs[1]: isolated paged decode microbench, Llama-3-8B attention shape, one layer",
+        "batch_per_gpu": BATCH, "ctx": f"U[{CTX_LO},{CTX_HI}]", "n_heads": N_HEADS,
+        "n_kv_heads": N_KV_HEADS, "head_dim": HEAD_DIM, "block_tokens": BLOCK,
+        "kv_format": kv_format,
+        "step": "append 1 token/seq + fused K/V write + decode attention (f32 softmax/accumulate); q, new K/V rows "
+                "and outputs in f32, the model runner's types (model.rs:393-400)"
+                + ("; K/V cached as Q8_0 (int8 + f16 scale per 32 values)" if kv_format == "q8_0" else ""),
+        "kv_bytes_per_step": b["attn"],
+        "l2": "inputs larger than L2: ~%.1f GB of K/V read per step vs 126 MB L2" % (b["attn"] / 1e9),
+        "parallelism": f"seq-sharded x{world} (independent pools, no collective); every rank serves the same "
+                       "multiset of context lengths",
+    }
+
+
 def run_ours(args, rank, world, local):
+    import ctypes
+
     import torch
     import torch.distributed as dist
 
@@ -242,25 +307,28 @@ def run_ours(args, rank, world, local):
 
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    ensure_pg(world, local)
     seed = shard_seed(rank)
-    lens = workload(seed)
+    lens = rank_lens(rank)
     kv = build_cache(kv_mod, torch, local, lens, seed, args.kv_format)
     g = torch.Generator(device=dev)
     g.manual_seed(seed + 7)
-    # q, k and v of a step live in one buffer, so the end-to-end path moves
-    # them with one host->device copy
+    # A step's q, new K and new V rows live in one f32 buffer (the model
+    # runner's types), so the end-to-end path moves them with one
+    # host->device copy; two such buffers (and two outputs) for the
+    # pipelined end-to-end loop.
     kvd, qd = N_KV_HEADS * HEAD_DIM, N_HEADS * HEAD_DIM
-    packed = torch.randn((BATCH, 2 * kvd + qd), generator=g, device=dev, dtype=torch.float16)
-    flat = packed.view(-1)
-    k = flat[: BATCH * kvd].view(BATCH, kvd)
-    v = flat[BATCH * kvd: 2 * BATCH * kvd].view(BATCH, kvd)
-    q = flat[2 * BATCH * kvd:].view(BATCH, qd)
-    out = torch.empty((BATCH, N_HEADS * HEAD_DIM), device=dev, dtype=torch.float16)
-    st = Stepper(kv, lens, k, v, q, out)
+    width = 2 * kvd + qd
+    packed = [torch.randn((BATCH, width), generator=g, device=dev, dtype=torch.float32) for _ in range(2)]
+
+    def split(p):
+        flat = p.view(-1)
+        return (flat[: BATCH * kvd].view(BATCH, kvd), flat[BATCH * kvd: 2 * BATCH * kvd].view(BATCH, kvd),
+                flat[2 * BATCH * kvd:].view(BATCH, qd))
+
+    outs = [torch.empty((BATCH, qd), device=dev, dtype=torch.float32) for _ in range(2)]
+    bufs = [split(packed[i]) + (outs[i],) for i in range(2)]
+    st = Stepper(kv, lens, *bufs[0])
 
     def barrier():
         if world > 1:
@@ -273,25 +341,17 @@ def run_ours(args, rank, world, local):
     # align to a cycle boundary so every run sees the same phases
     while st.phase != 0:
         st.step()
-    try:
-        uuid = str(torch.cuda.get_device_properties(local).uuid)
-        dev_id = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
-    except Exception:
-        dev_id = str(local)
-    clocks = Clocks(dev_id)
+    clocks = Clocks(device_uuid(torch, local))
     time.sleep(0.3)
     kv.profile(True)
     launches0 = kv.launch_count()
     total_bytes = 0
-    attn_bytes = 0
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
         lens_now = st.step()
-        b = step_bytes(lens_now, args.kv_format)
-        total_bytes += b["total"]
-        attn_bytes += b["total"]
+        total_bytes += step_bytes(lens_now, args.kv_format)["total"]
     e1.record()
     barrier()
     ms = e0.elapsed_time(e1)
@@ -301,43 +361,76 @@ def run_ours(args, rank, world, local):
     clk = clocks.stop()
     kv.check()
     ms_max = reduce_max(ms, dev, world)
+
     # ---------------- end-to-end through the public API ----------------
-    hpacked = torch.empty_like(packed, device="cpu").pin_memory()
-    hout = torch.empty_like(out, device="cpu").pin_memory()
-    hout_np = hout.numpy()  # the same pinned bytes, read without a torch call
-    hpacked.copy_(packed)
-    stream = torch.cuda.current_stream()
-    e2e_steps = args.steps
+    # Every step copies its inputs from pinned host memory and reads its
+    # result back on the host.  The copies run on their own streams against
+    # double buffers: step t+1's inputs land while step t computes, and the
+    # host reads step t's result while step t+1 computes.
+    hin = torch.empty((BATCH, width), dtype=torch.float32).pin_memory()
+    hin.copy_(packed[0].cpu())
+    hout = [torch.empty((BATCH, qd), dtype=torch.float32).pin_memory() for _ in range(2)]
+    hout_np = [h.numpy() for h in hout]  # the same pinned bytes, read without a torch call
+    s_comp, s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    comp_ptr = ctypes.c_void_p(s_comp.cuda_stream)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        packed.copy_(hpacked, non_blocking=True)  # this step's q, k, v
-        st.step()
-        hout.copy_(out, non_blocking=True)
-        stream.synchronize()  # the host reads this step's result
-        return float(hout_np[0, 0])
+    def e2e_run(n):
+        """n pipelined steps, from host inputs to host results; returns the
+        last result the host read."""
+        with torch.cuda.stream(s_in):
+            s_in.wait_stream(s_comp)
+            packed[0].copy_(hin, non_blocking=True)
+            ev_in[0].record(s_in)
+        last = 0.0
+        for t in range(n):
+            i = t & 1
+            s_comp.wait_event(ev_in[i])  # this step's inputs have landed
+            if t >= 2:
+                s_comp.wait_event(ev_out[i])  # step t-2's result has left this output buffer
+            st.step(bufs[i], comp_ptr)
+            ev_comp[i].record(s_comp)
+            if t + 1 < n:  # step t+1's inputs, once step t-1 has consumed that buffer
+                with torch.cuda.stream(s_in):
+                    if t >= 1:
+                        s_in.wait_event(ev_comp[i ^ 1])
+                    packed[i ^ 1].copy_(hin, non_blocking=True)
+                    ev_in[i ^ 1].record(s_in)
+            with torch.cuda.stream(s_out):  # step t's result to the host
+                s_out.wait_event(ev_comp[i])
+                hout[i].copy_(outs[i], non_blocking=True)
+                ev_out[i].record(s_out)
+            if t >= 1:  # the host reads step t-1's result
+                ev_out[i ^ 1].synchronize()
+                last = float(hout_np[i ^ 1][0, 0])
+        ev_out[(n - 1) & 1].synchronize()
+        last = float(hout_np[(n - 1) & 1][0, 0])
+        s_comp.wait_stream(s_out)
+        return last
 
-    for _ in range(max(args.warmup, 1)):
-        e2e_step()
+    e2e_run(max(args.warmup, 2))
     while st.phase != 0:
-        e2e_step()
+        st.step(bufs[0], comp_ptr)
     barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    f1.record()
+    f0.record(s_comp)
+    e2e_run(args.steps)
+    f1.record(s_comp)
+    f1.synchronize()
     barrier()
-    e2e_ms = f0.elapsed_time(f1)
-    e2e_ms = reduce_max(e2e_ms, dev, world)
-    h2d = packed.numel() * 2
-    d2h = out.numel() * 2
+    e2e_ms = reduce_max(f0.elapsed_time(f1), dev, world)
+    h2d = hin.numel() * 4
+    d2h = outs[0].numel() * 4
+    kv.check()
 
     result = None
     if rank == 0:
         q8 = args.kv_format == "q8_0"
         peak, peak_kind = measured_peak()
         avg_attn_ms = attn_ms / max(attn_n, 1)
-        per_launch_bytes = attn_bytes / max(args.steps, 1)
+        per_launch_bytes = total_bytes / max(args.steps, 1)
         achieved = per_launch_bytes / (avg_attn_ms * 1e-3) / 1e9
         tokens = BATCH * args.steps * world
         result = {
@@ -352,20 +445,9 @@ def run_ours(args, rank, world, local):
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "f16",
-            "data": "synthetic: f16 K/V and q ~ N(0,1), seeded; lengths U[512,4096] seeded",
-            "config": {
-                "workload": "configs[1]: isolated paged decode microbench, Llama-3-8B attention shape, one layer",
-                "batch_per_gpu": BATCH, "ctx": f"U[{CTX_LO},{CTX_HI}]", "n_heads": N_HEADS,
-                "n_kv_heads": N_KV_HEADS, "head_dim": HEAD_DIM, "block_tokens": BLOCK,
-                "kv_format": args.kv_format,
-                "step": "append 1 token/seq + fused K/V write + decode attention (f32 softmax/accumulate)"
-                        + ("; K/V cached as Q8_0 (int8 + f16 scale per 32 values)" if q8 else ""),
-                "kv_bytes_per_step": int(attn_bytes / max(args.steps, 1)),
-                "l2": "inputs larger than L2: ~%.1f GB of K/V read per step vs 126 MB L2"
-                      % (attn_bytes / max(args.steps, 1) / 1e9),
-                "parallelism": f"seq-sharded x{world} (independent pools, no collective)",
-            },
-            "hbm_gbs": total_bytes / (ms_max * 1e-3) / 1e9 / 1.0 * world,
+            "data": "synthetic: f16 K/V ~ N(0,1), f32 q and new rows ~ N(0,1), seeded; lengths U[512,4096] seeded",
+            "config": c2_config(world, args.kv_format),
+            "hbm_gbs": total_bytes / (ms_max * 1e-3) / 1e9 * world,
             "roofline": {
                 "bound": "hbm",
                 "kernel": "paged_attn_kernel<128, %s> (fused append + attention)" % ("q8" if q8 else "f16"),
@@ -374,18 +456,24 @@ def run_ours(args, rank, world, local):
                 "traffic": ncu_traffic("paged_attn_q8_c2.md" if q8 else "paged_attn_c2.md"),
                 "algorithmic_bytes_per_launch": int(per_launch_bytes), "avg_launch_ms": avg_attn_ms,
             },
-            "e2e": {"value": tokens / (e2e_ms * 1e-3) if world == 1 else BATCH * e2e_steps * world / (e2e_ms * 1e-3),
-                    "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "how": "KvCache.append_batch + KvCache.write_attend per step; inputs copied from pinned host "
+                           "memory and results read back on the host every step, double-buffered on copy "
+                           "streams"},
             "gpu_launches": int(launches),
             "clocks": clk,
         }
-    if world > 1:
-        dist.barrier()
-        kv.close()
-        dist.destroy_process_group()
-    else:
-        kv.close()
+    kv.close()
     return result
+
+
+def device_uuid(torch, local: int) -> str:
+    try:
+        uuid = str(torch.cuda.get_device_properties(local).uuid)
+        return uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+    except Exception:
+        return str(local)
 
 
 # ---------------------------------------------------------------------------
@@ -480,16 +568,17 @@ def run_c3(args, rank, world, local):
         step()
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
+    ms = reduce_max(e0.elapsed_time(e1), dev, world)
     attn_ms, attn_n = kv.profile_read()
     kv.check()
     extra = n_seq * hq * d * 2 * 2 + n_seq * 2 * kvd * 2 * 2  # q, out, appended rows
     peak, kind = measured_peak()
     per_launch_u = uniq / steps + extra
     achieved = per_launch_u / (attn_ms / attn_n * 1e-3) / 1e9
-    res = _json_common(args, world, n_seq * steps / (ms * 1e-3), "tokens/s", ms / steps, {
+    res = _json_common(args, world, n_seq * steps * world / (ms * 1e-3), "tokens/s", ms / steps, {
         "workload": "configs[2]: prefix-sharing stress, 256 seqs sharing a 2048-token prefix (share(src, s, 2047)), "
-                    "256-token distinct suffixes, decode steps, Llama-3-8B attention shape, one layer",
+                    "256-token distinct suffixes, decode steps, Llama-3-8B attention shape, one layer"
+                    + (f"; an independent replica on each of {world} GPUs" if world > 1 else ""),
         "n_heads": hq, "n_kv_heads": hkv, "head_dim": d, "block_tokens": BLOCK,
         "context_at_start": prefix + suffix})
     res.update({
@@ -560,7 +649,7 @@ def run_prefill(args, rank, world, local):
         step()
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
+    ms = reduce_max(e0.elapsed_time(e1), dev, world)
     attn_ms, attn_n = kv.profile_read()
     kv.check()
     flops = float(((pos.astype(np.int64) + 1) * hq * d * 4).sum())  # S = QK^T and O = PV, 2 flop per MAC
@@ -569,7 +658,7 @@ def run_prefill(args, rank, world, local):
     with open(ROOT / "MEASURED_PEAKS.json") as f:
         peaks = json.load(f)
     peak_tf = float(peaks.get("bf16_tflops", 1590.0))
-    res = _json_common(args, world, n * args.steps / (ms * 1e-3), "tokens/s", ms / args.steps, {
+    res = _json_common(args, world, n * args.steps * world / (ms * 1e-3), "tokens/s", ms / args.steps, {
         "workload": "chunked prefill: 4 seqs x 2048 cached tokens, a 256-token chunk each per step, "
                     "causal attention of the 1024 chunk tokens in one call, Llama-3-8B attention shape, one layer",
         "n_heads": hq, "n_kv_heads": hkv, "head_dim": d, "block_tokens": BLOCK})
@@ -606,8 +695,7 @@ def run_c4(args, rank, world, local, mode):
 
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    ensure_pg(world, local)
     B, L, hq, hkv, d = 16, 32768, 64, 8, 128
     if mode == "batch":
         assert B % world == 0
@@ -702,10 +790,7 @@ def run_c4(args, rank, world, local, mode):
         dist.barrier()
         if comm is not None:
             comm.close()
-        kv.close()
-        dist.destroy_process_group()
-    else:
-        kv.close()
+    kv.close()
     return res
 
 
@@ -745,8 +830,7 @@ def run_c5(args, rank, world, local):
 
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    ensure_pg(world, local)
     lam = args.c5_rate / world
     seed = shard_seed(rank)
     hq, hkv, d = 32, 8, 128
@@ -826,6 +910,7 @@ def run_c5(args, rank, world, local):
                       "running_at_end": s1["running"], "queued_at_end": s1["queued"],
                       "attn_ms_per_step": attn_ms / max(attn_n, 1), "host_wall_ms_per_step": wall * 1e3 / args.steps},
             "compaction_gb_moved_per_s": moved_bytes / (ms * 1e-3) / 1e9,
+            "mean_context_per_decode_token": delta["attended_positions"] / max(delta["decode_tokens"], 1),
             "gpu_launches": kv.launch_count() - l0,
         })
         # Rank 0's decode attention launches: K+V rows of every attended
@@ -845,10 +930,7 @@ def run_c5(args, rank, world, local):
     sched.close()
     if world > 1:
         dist.barrier()
-        kv.close()
-        dist.destroy_process_group()
-    else:
-        kv.close()
+    kv.close()
     return res
 
 
@@ -887,10 +969,7 @@ def run_c1(args, rank, world, local):
 
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    ensure_pg(world, local)
     seed = shard_seed(rank)
     model = LL.Llama(**C1_SHAPE, max_batch=256, device=local)
     model.load(LL.random_weights(model, seed=seed))
@@ -988,7 +1067,6 @@ def run_c1(args, rank, world, local):
         })
     if world > 1:
         dist.barrier()
-        dist.destroy_process_group()
     kv.close()
     model.close()
     return result
@@ -1075,12 +1153,249 @@ def cpu_run(lens, seed, budget_s, max_steps, threads, kv_format="f16"):
     return BATCH * steps / dt, steps, dt
 
 
+def cpu_run_c3(budget_s: float, threads: int, max_steps: int = 64):
+    """configs[2] on the restated reference path: a 2048-token source, 256
+    sequences made by share(src, s, 2047), their first appends (256
+    copy-on-write copies), 256 distinct suffix tokens each, then timed decode
+    steps (append + f32 write + attention of all 256) until `budget_s`.  The
+    reference attends every token over its whole context (model.rs:431-476),
+    shared blocks included.  Returns (tokens/s, steps, seconds)."""
+    from oracle import oracle as ok_mod
+
+    n_seq, prefix, suffix = 256, 2048, 256
+    kvd = N_KV_HEADS * HEAD_DIM
+    per_seq_blocks = 1 + (suffix + max_steps + 2 + BLOCK - 1) // BLOCK
+    n_blocks = prefix // BLOCK + n_seq * per_seq_blocks + 8
+    ok = ok_mod.OracleKv(1, kvd, n_blocks * BLOCK, max_seqs=n_seq + 1)
+    rng = np.random.default_rng(1234)
+    rows = lambda n: rng.standard_normal((n, kvd), np.float32).astype(np.float16)  # noqa: E731
+
+    def put(seqs, pos):
+        rc, done, b, sl = ok.append_batch(seqs, pos)
+        assert rc == 0
+        ok.write_batch(0, b, sl, rows(b.size), rows(b.size))
+
+    put(np.zeros(prefix, np.uint32), np.arange(prefix))
+    seqs = np.arange(1, n_seq + 1, dtype=np.uint32)
+    for i in seqs:
+        ok.share(0, int(i), prefix - 1)
+    put(seqs, np.full(n_seq, prefix - 1))
+    for i0 in range(0, n_seq, 32):
+        ss = seqs[i0:i0 + 32]
+        put(np.repeat(ss, suffix), np.tile(np.arange(prefix, prefix + suffix), ss.size))
+    lens = np.full(n_seq, prefix + suffix, np.int64)
+    kin = rng.standard_normal((n_seq, kvd), np.float32)
+    vin = rng.standard_normal((n_seq, kvd), np.float32)
+    q = rng.standard_normal((n_seq, N_HEADS * HEAD_DIM), np.float32)
+    steps = 0
+    t0 = time.perf_counter()
+    while steps < max_steps:
+        pos = lens.astype(np.uint32)
+        rc, done, b, sl = ok.append_batch(seqs, pos)
+        assert rc == 0
+        ok.write_batch(0, b, sl, kin, vin)
+        ok.attend(0, q, seqs, pos, N_HEADS, N_KV_HEADS, HEAD_DIM, n_threads=threads)
+        lens += 1
+        steps += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return n_seq * steps / dt, steps, dt
+
+
+def cpu_run_c4(budget_s: float, threads: int, max_steps: int = 64):
+    """configs[3] (16 x 32768, 64 q / 8 KV heads) on the restated reference
+    path: the cache filled in 8192-token appends (rows tiled from one
+    8192-row N(0,1) draw: the arithmetic per position is the same for any
+    values), then timed decode steps of append + f32 write + attention, with
+    kv_remove back to 32768 every 16 steps.  Returns (tokens/s, steps, s)."""
+    from oracle import oracle as ok_mod
+
+    B, L, hq, hkv, d = 16, 32768, 64, 8, 128
+    kvd = hkv * d
+    n_blocks = B * ((L + CYCLE + 1 + BLOCK - 1) // BLOCK) + 8
+    ok = ok_mod.OracleKv(1, kvd, n_blocks * BLOCK, max_seqs=B)
+    rng = np.random.default_rng(1234)
+    chunk = 8192
+    kc = rng.standard_normal((chunk, kvd), np.float32).astype(np.float16)
+    vc = rng.standard_normal((chunk, kvd), np.float32).astype(np.float16)
+    for sq in range(B):
+        for p0 in range(0, L, chunk):
+            rc, done, b, sl = ok.append_batch(np.full(chunk, sq), np.arange(p0, p0 + chunk))
+            assert rc == 0
+            ok.write_batch(0, b, sl, kc, vc)
+    kin = rng.standard_normal((B, kvd), np.float32)
+    vin = rng.standard_normal((B, kvd), np.float32)
+    q = rng.standard_normal((B, hq * d), np.float32)
+    seqs = np.arange(B, dtype=np.uint32)
+    phase = steps = 0
+    t0 = time.perf_counter()
+    while steps < max_steps:
+        pos = np.full(B, L + phase, np.uint32)
+        rc, done, b, sl = ok.append_batch(seqs, pos)
+        assert rc == 0
+        ok.write_batch(0, b, sl, kin, vin)
+        ok.attend(0, q, seqs, pos, hq, hkv, d, n_threads=threads)
+        phase += 1
+        if phase == CYCLE:
+            for sq in range(B):
+                ok.truncate(sq, L)
+            phase = 0
+        steps += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return B * steps / dt, steps, dt
+
+
+def cpu_run_prefill(budget_s: float, threads: int, max_steps: int = 16):
+    """The chunked-prefill line on the restated reference path: 4 sequences
+    of 2048 cached tokens, each step a 256-token chunk per sequence (append +
+    f32 write + causal attention of the 1024 chunk tokens), then kv_remove
+    back to 2048.  Returns (prompt tokens/s, steps, seconds)."""
+    from oracle import oracle as ok_mod
+
+    n_seq, ctx, chunk = 4, 2048, 256
+    kvd = N_KV_HEADS * HEAD_DIM
+    n_blocks = n_seq * ((ctx + chunk + BLOCK - 1) // BLOCK) + 8
+    ok = ok_mod.OracleKv(1, kvd, n_blocks * BLOCK, max_seqs=n_seq)
+    rng = np.random.default_rng(1234)
+    for sq in range(n_seq):
+        rc, done, b, sl = ok.append_batch(np.full(ctx, sq), np.arange(ctx))
+        assert rc == 0
+        ok.write_batch(0, b, sl, rng.standard_normal((ctx, kvd), np.float32).astype(np.float16),
+                       rng.standard_normal((ctx, kvd), np.float32).astype(np.float16))
+    seqs = np.repeat(np.arange(n_seq, dtype=np.uint32), chunk)
+    pos = np.tile(np.arange(ctx, ctx + chunk, dtype=np.uint32), n_seq)
+    n = seqs.size
+    kin = rng.standard_normal((n, kvd), np.float32)
+    vin = rng.standard_normal((n, kvd), np.float32)
+    q = rng.standard_normal((n, N_HEADS * HEAD_DIM), np.float32)
+    steps = 0
+    t0 = time.perf_counter()
+    while steps < max_steps:
+        rc, done, b, sl = ok.append_batch(seqs, pos)
+        assert rc == 0
+        ok.write_batch(0, b, sl, kin, vin)
+        ok.attend(0, q, seqs, pos, N_HEADS, N_KV_HEADS, HEAD_DIM, n_threads=threads)
+        for sq in range(n_seq):
+            ok.truncate(sq, ctx)
+        steps += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return n * steps / dt, steps, dt
+
+
 def cpu_desc():
     try:
         model = [l.split(":", 1)[1].strip() for l in open("/proc/cpuinfo") if l.startswith("model name")][0]
     except Exception:
         model = "unknown CPU"
     return model
+
+
+def _sub_args(args, **kw):
+    ns = argparse.Namespace(**vars(args))
+    ns.__dict__.update(kw)
+    return ns
+
+
+# The other configurations of BASELINE.json, run after the headline in the
+# same process at step counts that keep the whole line within a few minutes:
+# key -> (runner, CPU-baseline leg for rank 0 at N = 1).
+def _sub_q8(args, rank, world, local):
+    return run_ours(_sub_args(args, kv_format="q8_0"), rank, world, local)
+
+
+def _sub_c3(args, rank, world, local):
+    return run_c3(_sub_args(args, steps=32, warmup=5), rank, world, local)
+
+
+def _sub_c4(mode):
+    return lambda args, rank, world, local: run_c4(_sub_args(args, steps=32, warmup=16), rank, world, local, mode)
+
+
+def _sub_c5(args, rank, world, local):
+    return run_c5(_sub_args(args, steps=60, warmup=500 if world == 1 else 400), rank, world, local)
+
+
+def _sub_c1(args, rank, world, local):
+    return run_c1(_sub_args(args, steps=32, warmup=8), rank, world, local)
+
+
+def _sub_prefill(args, rank, world, local):
+    return run_prefill(_sub_args(args, steps=20, warmup=3), rank, world, local)
+
+
+def _cpu_leg(name, res, budget, threads):
+    """cpu_baseline of one sub-configuration: the restated reference path on
+    a bounded sample of the same workload."""
+    how = f"{threads} threads of {cpu_desc()}"
+    if name == "q8":
+        v, n, dt = cpu_run(workload(1234), 1234, budget, 10 ** 6, threads, kv_format="q8_0")
+        sample = f"{n} full steps (64 seqs, one layer, Q8_0 cache) in {dt:.1f} s on {how}"
+    elif name == "c3":
+        v, n, dt = cpu_run_c3(budget, threads)
+        sample = (f"{n} decode steps of all 256 sequences after the untimed build (prefix, 256 shares and "
+                  f"copy-on-write copies, suffixes) in {dt:.1f} s on {how}")
+    elif name == "c4_batch":
+        v, n, dt = cpu_run_c4(budget, threads)
+        sample = f"{n} decode steps of all 16 sequences (32768 tokens, 64/8 heads) in {dt:.1f} s on {how}"
+    elif name == "c5":
+        ctx = int(round(res["mean_context_per_decode_token"]))
+        lens = np.full(BATCH, max(ctx - 8, 1), np.int64)  # a 16-step cycle attends lens + 1 .. lens + 16
+        v, n, dt = cpu_run(lens, 1234, budget, 10 ** 6, threads)
+        sample = (f"{n} steps of 64 decode tokens at the GPU run's mean attended context per decode token "
+                  f"({ctx} positions; the churn's prefill chunks are not timed) in {dt:.1f} s on {how}")
+    elif name == "c1":
+        v, n, dt = cpu_run_c1(budget, threads)
+        sample = f"{n} greedy decode steps of 4 tokens after an untimed prefill, {dt:.1f} s on {how}"
+    elif name == "prefill":
+        v, n, dt = cpu_run_prefill(budget, threads)
+        sample = f"{n} steps of 4 x 256 prompt tokens over 2048 cached tokens in {dt:.1f} s on {how}"
+    else:
+        return None
+    return {"value": v, "unit": res.get("unit", "tokens/s"), "cores": threads, "kind": "port",
+            "sample": sample + "; restated reference (oracle/)"}
+
+
+SUB_RUNNERS = {"q8": _sub_q8, "c3": _sub_c3, "c4_batch": _sub_c4("batch"), "c4_head": _sub_c4("head"),
+               "c5": _sub_c5, "prefill": _sub_prefill, "c1": _sub_c1}
+
+
+def run_subconfigs(args, rank, world, local) -> dict:
+    """Every other configuration, one after the other on every rank (the same
+    collective calls in the same order), each summarised under its key.
+    c4_head is the KV-head-sharded long-context mode; on one GPU it is the
+    same launch as c4_batch and is left out."""
+    import torch
+
+    names = list(SUB_RUNNERS) if args.sub == "all" else [n for n in args.sub.split(",") if n]
+    out = {}
+    threads = os.cpu_count() or 1
+    for name in names:
+        if name not in SUB_RUNNERS or (name == "c4_head" and world == 1):
+            continue
+        t0 = time.perf_counter()
+        try:
+            res = SUB_RUNNERS[name](args, rank, world, local)
+        except Exception as e:  # recorded, and the other configurations still run
+            res = {"error": f"{type(e).__name__}: {e}"}
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        if rank != 0 or res is None:
+            continue
+        res = {k: v for k, v in res.items() if k not in ("metric", "higher_is_better", "vs_baseline")}
+        res["gpu_run_s"] = round(time.perf_counter() - t0, 2)
+        res["cpu_baseline"] = None
+        if world == 1 and args.cpu_seconds > 0 and "error" not in res:
+            try:
+                res["cpu_baseline"] = _cpu_leg(name, res, min(args.cpu_seconds, 8.0), threads)
+            except Exception as e:
+                res["cpu_baseline"] = {"error": f"{type(e).__name__}: {e}"}
+        out[name] = res
+    return out
 
 
 def run_reference(args, rank, world):
@@ -1118,12 +1433,10 @@ def run_reference(args, rank, world):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": dt * 1e3 / max(steps, 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16 storage, f32 arithmetic",
-        "data": "synthetic: f16 K/V ~ N(0,1), seeded; lengths U[512,4096] seeded",
-        "config": {"workload": "configs[1]: isolated paged decode microbench, Llama-3-8B attention shape, one layer",
-                   "batch_per_gpu": BATCH, "ctx": f"U[{CTX_LO},{CTX_HI}]", "n_heads": N_HEADS,
-                   "n_kv_heads": N_KV_HEADS, "head_dim": HEAD_DIM, "block_tokens": BLOCK,
-                   "implementation": "restated reference CPU path (oracle/lt_oracle.c); the Rust reference is "
-                                     "not buildable here"},
+        "data": "synthetic: f16 K/V ~ N(0,1), f32 q and new rows ~ N(0,1), seeded; lengths U[512,4096] seeded",
+        "config": c2_config(world, "f16"),
+        "implementation": "restated reference CPU path (oracle/lt_oracle.c); the Rust reference is not buildable "
+                          "here",
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -1138,6 +1451,9 @@ def main():
     ap.add_argument("--config", choices=["c1", "c2", "c3", "c4-batch", "c4-head", "c5", "prefill"], default="c2",
                     help="c2: configs[1] (default, the headline); c1: configs[0]; c3: configs[2]; "
                          "c4-*: configs[3]; c5: configs[4]; prefill: chunked prefill attention")
+    ap.add_argument("--sub", default="all",
+                    help="c2: the other configurations to run after the headline and report under their keys "
+                         "(comma-separated from %s; 'all' or 'none')" % ",".join(SUB_RUNNERS))
     ap.add_argument("--c5-rate", type=float, default=32.0, help="c5: mean arrivals per step over the whole job")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="c4-head: gather the sharded heads inside the attention call over NVLink (peer) or with "
@@ -1153,38 +1469,17 @@ def main():
         if res is not None:
             print(json.dumps(res), flush=True)
         return
-    if args.config == "c1":
-        res = run_c1(args, rank, world, local)
-        if rank == 0:
+    if args.config != "c2":
+        runners = {"c1": run_c1, "c3": run_c3, "prefill": run_prefill, "c5": run_c5,
+                   "c4-batch": lambda a, r, w, lo: run_c4(a, r, w, lo, "batch"),
+                   "c4-head": lambda a, r, w, lo: run_c4(a, r, w, lo, "head")}
+        res = runners[args.config](args, rank, world, local)
+        if rank == 0 and res is not None and args.config == "c1":
+            res["cpu_baseline"] = None
             if world == 1 and args.cpu_seconds > 0:
-                threads = os.cpu_count() or 1
-                value, steps, dt = cpu_run_c1(args.cpu_seconds, threads)
-                res["cpu_baseline"] = {
-                    "value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                    "sample": f"{steps} greedy decode steps of 4 tokens after an untimed prefill, {dt:.1f} s on "
-                              f"{threads} threads of {cpu_desc()}; restated reference forward (oracle/lt_model.c)"}
-            else:
-                res["cpu_baseline"] = None
-            print(json.dumps(res), flush=True)
-        return
-    if args.config == "c3":
-        res = run_c3(args, rank, world, local)
-        if rank == 0:
-            print(json.dumps(res), flush=True)
-        return
-    if args.config == "prefill":
-        res = run_prefill(args, rank, world, local)
-        if rank == 0:
-            print(json.dumps(res), flush=True)
-        return
-    if args.config == "c5":
-        res = run_c5(args, rank, world, local)
-        if rank == 0:
-            print(json.dumps(res), flush=True)
-        return
-    if args.config.startswith("c4"):
-        res = run_c4(args, rank, world, local, args.config.split("-")[1])
-        if rank == 0:
+                res["cpu_baseline"] = _cpu_leg("c1", res, args.cpu_seconds, os.cpu_count() or 1)
+        finish_pg(world)
+        if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
         return
     res = run_ours(args, rank, world, local)
@@ -1200,6 +1495,12 @@ def main():
                           f"(oracle/lt_oracle.c)"}
         else:
             res["cpu_baseline"] = None
+    if args.sub != "none":
+        subs = run_subconfigs(args, rank, world, local)
+        if rank == 0 and res is not None:
+            res["configs"] = subs
+    finish_pg(world)
+    if rank == 0 and res is not None:
         print(json.dumps(res), flush=True)
 
 
