@@ -522,6 +522,7 @@ def run_c3(args, rank, world, local):
     # divergence: 256 copy-on-write copies of the shared partial block
     c0, c1, c2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     launches0 = kv.launch_count()
+    kv.profile(True)  # times the plan launch alone (after its upload)
     c0.record()
     b, s = kv.append_batch(seqs, np.full(n_seq, prefix - 1))  # host bookkeeping: 256 allocations + plan
     c1.record()
@@ -530,16 +531,23 @@ def run_c3(args, rank, world, local):
     torch.cuda.synchronize()
     cow_ms = c0.elapsed_time(c2)
     cow_dev_ms = c1.elapsed_time(c2)
+    cow_kernel_ms, cow_kernel_n, cow_blocks, cow_entries = kv.profile_read_plan()
+    kv.profile(False)
     cow_launches = kv.launch_count() - launches0
     cow_bytes = n_seq * kvd * 2 * BLOCK * 2 * 2  # K+V block, read + write
     kv.write(0, b, s, rnd(n_seq), rnd(n_seq))
-    # distinct suffixes
+    # distinct suffixes; the K/V write kernel (append of prompt rows,
+    # kv.rs:123-131) timed alone: the table entries go first with a flush
     pos = np.arange(prefix, prefix + suffix)
+    kv.profile(True)
     for i0 in range(0, n_seq, 32):
         ss = np.repeat(seqs[i0:i0 + 32], suffix)
         pp = np.tile(pos, len(seqs[i0:i0 + 32]))
         b, s = kv.append_batch(ss, pp)
         kv.write(0, b, s, rnd(ss.size), rnd(ss.size))
+    w_ms, w_n, w_rows, w_in = kv.profile_read_write()
+    kv.profile(False)
+    w_bytes = w_in + w_rows * kvd * 2 * 2  # input rows read + f16 cells written, K and V
     lens = np.full(n_seq, prefix + suffix, np.int64)
     k, v = rnd(n_seq), rnd(n_seq)
     q = torch.randn((n_seq, hq * d), generator=g, device=dev, dtype=torch.float16)
@@ -591,7 +599,19 @@ def run_c3(args, rank, world, local):
                      "logical_bytes_per_launch": int(logical / steps + extra), "avg_launch_ms": attn_ms / attn_n},
         "cow": {"copies": n_seq, "bytes": cow_bytes, "ms": cow_ms, "gbs": cow_bytes / (cow_ms * 1e-3) / 1e9,
                 "plan_ms": cow_dev_ms, "plan_gbs": cow_bytes / (cow_dev_ms * 1e-3) / 1e9, "launches": cow_launches,
-                "note": "ms/gbs include the host bookkeeping of the 256 appends; plan_* the upload + copy launch"},
+                "kernel_ms": cow_kernel_ms, "kernel_gbs": cow_bytes / (cow_kernel_ms * 1e-3) / 1e9,
+                "kernel_launches": cow_kernel_n, "kernel_blocks_copied": cow_blocks,
+                "kernel_frac_of_peak": cow_bytes / (cow_kernel_ms * 1e-3) / 1e9 / peak,
+                "note": "ms/gbs include the host bookkeeping of the 256 appends; plan_* the upload + copy launch; "
+                        "kernel_* the apply_plan_kernel launch alone (CUDA events after the upload); bytes: a K+V "
+                        "block read and written per copy"},
+        "append": {"kernel": "kv_write_kernel<128> (f16 rows in, swizzled f16 cells out)", "rows": w_rows,
+                   "launches": w_n, "bytes": w_bytes, "kernel_ms": w_ms,
+                   "kernel_gbs": w_bytes / (w_ms * 1e-3) / 1e9,
+                   "kernel_frac_of_peak": w_bytes / (w_ms * 1e-3) / 1e9 / peak,
+                   "note": "the 256-token suffix rows of 32 sequences per lt_kv_write call (8192 rows, 32 MiB "
+                           "read + 32 MiB written), the kernel alone (CUDA events after the cells' upload); decode "
+                           "appends are fused into the attention launch"},
         "gpu_launches": kv.launch_count() - l0,
     })
     kv.close()
@@ -885,6 +905,7 @@ def run_c5(args, rank, world, local):
         dist.barrier()
     ms = reduce_max(e0.elapsed_time(e1), dev, world)
     attn_ms, attn_n = kv.profile_read()
+    plan_ms, plan_n, plan_blocks, plan_entries = kv.profile_read_plan()
     kv.check()
     s1 = sched.stats
     delta = {k: s1[k] - s0[k] for k in s1}
@@ -910,6 +931,11 @@ def run_c5(args, rank, world, local):
                       "running_at_end": s1["running"], "queued_at_end": s1["queued"],
                       "attn_ms_per_step": attn_ms / max(attn_n, 1), "host_wall_ms_per_step": wall * 1e3 / args.steps},
             "compaction_gb_moved_per_s": moved_bytes / (ms * 1e-3) / 1e9,
+            "plan_kernel": {"kernel": "apply_plan_kernel (compaction moves + block-table entries), rank 0",
+                            "launches": plan_n, "ms_per_step": plan_ms / args.steps, "blocks_copied": plan_blocks,
+                            "table_entries": plan_entries,
+                            "gbs": (plan_blocks * hkv * d * 2 * BLOCK * 2 * 2 + plan_entries * 8)
+                            / max(plan_ms * 1e-3, 1e-12) / 1e9},
             "mean_context_per_decode_token": delta["attended_positions"] / max(delta["decode_tokens"], 1),
             "gpu_launches": kv.launch_count() - l0,
         })

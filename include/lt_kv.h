@@ -259,13 +259,25 @@ const int32_t* lt_kv_device_tables(const lt_kv* kv, uint32_t* max_blocks_per_seq
  * checks of whole pools against the reference layout. */
 lt_status lt_kv_read_pool(lt_kv* kv, uint32_t layer, uint32_t block0, uint32_t count, void* out_host);
 
-/* Attention-kernel timing.  While enabled, CUDA events bracket every
- * attention launch (lt_kv_attend, lt_kv_write_attend) on its own stream;
- * enabling resets the totals. */
+/* Launch timing.  While enabled, CUDA events bracket every attention launch
+ * (lt_kv_attend, lt_kv_write_attend), every plan launch (the kernel that
+ * applies copy-on-write copies, compaction moves and block-table entries;
+ * after the plan's upload) and every K/V write launch (lt_kv_write) on its
+ * own stream; enabling resets the totals. */
 lt_status lt_kv_profile(lt_kv* kv, int enable);
 /* Total duration (ms) and count of the bracketed attention launches since
  * profiling was enabled; waits for the recorded events. */
 lt_status lt_kv_profile_read(lt_kv* kv, double* total_ms, uint64_t* launches);
+/* The same for the plan launches, with the block copies (copy-on-write and
+ * compaction; each moves one block of every layer) and table entries they
+ * applied.  New: the reference copies on the host (kv.rs:99-110). */
+lt_status lt_kv_profile_read_plan(lt_kv* kv, double* total_ms, uint64_t* launches, uint64_t* copied_blocks,
+                                  uint64_t* table_entries);
+/* The same for the K/V write launches of lt_kv_write (KvCache::write,
+ * kv.rs:123-131; the kernel alone, after the cells' upload), with the rows
+ * written and the input bytes they read. */
+lt_status lt_kv_profile_read_write(lt_kv* kv, double* total_ms, uint64_t* launches, uint64_t* rows,
+                                   uint64_t* in_bytes);
 
 /* Kernel launches made by this handle since creation (all kinds). */
 uint64_t lt_kv_launch_count(const lt_kv* kv);

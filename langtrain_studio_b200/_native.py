@@ -30,7 +30,8 @@ EXPORTS = (
     "lt_kv_free_blocks", "lt_kv_append", "lt_kv_write", "lt_kv_attend", "lt_kv_write_attend",
     "lt_kv_truncate", "lt_kv_share", "lt_kv_compact", "lt_kv_flush", "lt_kv_rows", "lt_kv_check",
     "lt_kv_seq_blocks", "lt_kv_refs", "lt_kv_free_list", "lt_kv_n_blocks", "lt_kv_device_pool",
-    "lt_kv_device_tables", "lt_kv_read_pool", "lt_kv_launch_count", "lt_kv_profile", "lt_kv_profile_read",
+    "lt_kv_device_tables", "lt_kv_read_pool", "lt_kv_launch_count", "lt_kv_profile", "lt_kv_profile_read", "lt_kv_profile_read_plan",
+    "lt_kv_profile_read_write",
     "lt_kv_nccl_unique_id", "lt_kv_nccl_init", "lt_kv_nccl_destroy", "lt_kv_gather_heads",
     "lt_paged_attend_noalloc", "lt_paged_attend_noalloc_check", "lt_kv_peer_export", "lt_kv_peer_import", "lt_kv_peer_close",
     "lt_kv_attend_gather", "lt_kv_write_attend_gather", "lt_kv_selftest_wait", "lt_kv_build_features", "lt_kv_set_min_tiles_per_warp", "lt_kv_set_cascade", "lt_kv_cascade_launches",
@@ -145,6 +146,8 @@ def _declare(L):
         "lt_kv_cascade_launches": (u64, [p]),
         "lt_kv_profile": (st, [p, C.c_int]),
         "lt_kv_profile_read": (st, [p, C.POINTER(C.c_double), C.POINTER(u64)]),
+        "lt_kv_profile_read_plan": (st, [p, C.POINTER(C.c_double), C.POINTER(u64), C.POINTER(u64), C.POINTER(u64)]),
+        "lt_kv_profile_read_write": (st, [p, C.POINTER(C.c_double), C.POINTER(u64), C.POINTER(u64), C.POINTER(u64)]),
         "lt_kv_nccl_unique_id": (st, [p]),
         "lt_kv_nccl_init": (st, [C.POINTER(p), C.c_int, p, C.c_int, C.c_int]),
         "lt_kv_nccl_destroy": (None, [p]),

@@ -88,6 +88,15 @@ constexpr size_t kPeerFlagsBytes = 256, kPeerHeaderBytes = 512;
 static_assert(sizeof(cudaIpcMemHandle_t) == LT_IPC_HANDLE_BYTES, "IPC handle size");
 static_assert(ltkv::kMaxPeers * sizeof(uint32_t) <= kPeerFlagsBytes, "peer flags");
 
+// Device timing of one kind of launch: (start, end) event pairs in a ring,
+// folded into the totals when read or when the ring is full.
+struct ProfRing {
+    std::vector<cudaEvent_t> ev;
+    size_t head = 0, pending = 0;
+    double ms = 0.0;
+    uint64_t count = 0;
+};
+
 struct lt_kv {
     lt_kv_config cfg{};
     PeerGather peer;
@@ -149,12 +158,12 @@ struct lt_kv {
 
     std::vector<int32_t> dev_shadow;  // what the device tables hold (host copy)
 
-    // attention-kernel timing (lt_kv_profile)
+    // launch timing (lt_kv_profile): attention launches, and plan launches
+    // (copy-on-write copies, compaction moves, table entries)
     bool profiling = false;
-    std::vector<cudaEvent_t> prof_ev;  // pairs (start, end), ring
-    size_t prof_head = 0, prof_pending = 0;
-    double prof_ms = 0.0;
-    uint64_t prof_count = 0;
+    ProfRing prof_attn, prof_plan, prof_write;
+    uint64_t plan_blocks = 0, plan_entries = 0;  // block copies and table entries of the timed plan launches
+    uint64_t write_rows = 0, write_in_bytes = 0;  // rows and input bytes of the timed write launches
 
     UploadCache cells_cache, items_cache, casc_cache;
     std::vector<ltkv::TokenDesc> toks_tmp;
@@ -214,8 +223,10 @@ void free_device(lt_kv* kv) {
         if (s.ev) cudaEventDestroy(s.ev);
         s = Slot{};
     }
-    for (cudaEvent_t e : kv->prof_ev) cudaEventDestroy(e);
-    kv->prof_ev.clear();
+    for (ProfRing* r : {&kv->prof_attn, &kv->prof_plan, &kv->prof_write}) {
+        for (cudaEvent_t e : r->ev) cudaEventDestroy(e);
+        r->ev.clear();
+    }
     kv->d_pool = nullptr;
     kv->d_tables = nullptr;
     kv->d_part_o = kv->d_part_ml = nullptr;
@@ -261,6 +272,8 @@ lt_status upload(lt_kv* kv, UploadCache& cache, const void* src, size_t bytes, c
     return LT_OK;
 }
 
+lt_status prof_begin(lt_kv* kv, ProfRing& r, cudaStream_t st, cudaEvent_t* end);
+
 // Launch kv_apply_plan for `copies` and table writes `tw`, split to fit the
 // staging slots.  All copies in one call are independent of each other.
 lt_status run_plan(lt_kv* kv, const std::vector<int2>& copies, const std::vector<int2>& tw, cudaStream_t st) {
@@ -275,9 +288,17 @@ lt_status run_plan(lt_kv* kv, const std::vector<int2>& copies, const std::vector
         if (nt) std::memcpy(h + nc, tw.data() + ti, nt * sizeof(int2));
         LT_CUDA(kv, cudaMemcpyAsync(kv->slots[s].dev, h, (nc + nt) * sizeof(int2), cudaMemcpyHostToDevice, st));
         const int2* d = static_cast<const int2*>(kv->slots[s].dev);
+        cudaEvent_t ev_end = nullptr;
+        if (kv->profiling) {  // the kernel alone: after the plan's upload
+            lt_status prc = prof_begin(kv, kv->prof_plan, st, &ev_end);
+            if (prc) return prc;
+            kv->plan_blocks += nc;
+            kv->plan_entries += nt;
+        }
         LT_CUDA(kv, ltkv::launch_apply_plan(kv->d_pool, kv->layer_elems, kv->block_elems, (int)kv->cfg.n_layers, d,
                                             (int)nc, kv->d_tables, d + nc, (int)nt, (int)kv->n_blocks,
                                             (long long)kv->cfg.max_seqs * kv->max_blocks, kv->d_err, st));
+        if (ev_end) LT_CUDA(kv, cudaEventRecord(ev_end, st));
         kv->launches++;
         lt_status rc = mark_slot_use(kv, s, st);
         if (rc) return rc;
@@ -431,31 +452,32 @@ lt_status check_cells(lt_kv* kv, const int32_t* block, const int32_t* slot, uint
 
 constexpr size_t kProfPairs = 512;
 
-// Fold the oldest `n` recorded (start, end) pairs into the totals.
-lt_status prof_drain(lt_kv* kv, size_t n) {
-    while (n-- && kv->prof_pending) {
-        const size_t tail = (kv->prof_head + kProfPairs - kv->prof_pending) % kProfPairs;
+// Fold the oldest `n` recorded (start, end) pairs of a ring into its totals.
+lt_status prof_drain(lt_kv* kv, ProfRing& r, size_t n) {
+    while (n-- && r.pending) {
+        const size_t tail = (r.head + kProfPairs - r.pending) % kProfPairs;
         float ms = 0.f;
-        LT_CUDA(kv, cudaEventSynchronize(kv->prof_ev[2 * tail + 1]));
-        LT_CUDA(kv, cudaEventElapsedTime(&ms, kv->prof_ev[2 * tail], kv->prof_ev[2 * tail + 1]));
-        kv->prof_ms += ms;
-        kv->prof_count++;
-        kv->prof_pending--;
+        LT_CUDA(kv, cudaEventSynchronize(r.ev[2 * tail + 1]));
+        LT_CUDA(kv, cudaEventElapsedTime(&ms, r.ev[2 * tail], r.ev[2 * tail + 1]));
+        r.ms += ms;
+        r.count++;
+        r.pending--;
     }
     return LT_OK;
 }
 
-// Record the start event of the next attention launch; *end gets its end event.
-lt_status prof_begin(lt_kv* kv, cudaStream_t st, cudaEvent_t* end) {
-    if (kv->prof_pending == kProfPairs) {
-        lt_status rc = prof_drain(kv, 1);
+// Record the start event of the next launch of a ring's kind; *end gets its
+// end event.
+lt_status prof_begin(lt_kv* kv, ProfRing& r, cudaStream_t st, cudaEvent_t* end) {
+    if (r.pending == kProfPairs) {
+        lt_status rc = prof_drain(kv, r, 1);
         if (rc) return rc;
     }
-    const size_t i = kv->prof_head;
-    kv->prof_head = (kv->prof_head + 1) % kProfPairs;
-    kv->prof_pending++;
-    LT_CUDA(kv, cudaEventRecord(kv->prof_ev[2 * i], st));
-    *end = kv->prof_ev[2 * i + 1];
+    const size_t i = r.head;
+    r.head = (r.head + 1) % kProfPairs;
+    r.pending++;
+    LT_CUDA(kv, cudaEventRecord(r.ev[2 * i], st));
+    *end = r.ev[2 * i + 1];
     return LT_OK;
 }
 
@@ -684,7 +706,7 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
     }
     cudaEvent_t ev_end = nullptr;
     if (kv->profiling) {
-        lt_status prc = prof_begin(kv, st, &ev_end);
+        lt_status prc = prof_begin(kv, kv->prof_attn, st, &ev_end);
         if (prc) return prc;
     }
     int s_casc = -1;
@@ -906,9 +928,16 @@ lt_status lt_kv_write(lt_kv* kv, uint32_t layer, const int32_t* block, const int
     const void* d_cells = nullptr;
     int s = -1;
     if ((rc = upload(kv, kv->cells_cache, kv->cells_tmp.data(), n * sizeof(int2), st, &d_cells, &s))) return rc;
+    cudaEvent_t ev_end = nullptr;
+    if (kv->profiling) {  // the kernel alone: after the cells' upload
+        if ((rc = prof_begin(kv, kv->prof_write, st, &ev_end))) return rc;
+        kv->write_rows += n;
+        kv->write_in_bytes += (uint64_t)n * 2 * kv->cfg.n_kv_heads * kv->cfg.head_dim * (dtype == LT_F32 ? 4 : 2);
+    }
     LT_CUDA(kv, ltkv::launch_write(kv->d_pool + (size_t)layer * kv->layer_elems, static_cast<const int2*>(d_cells),
                                    (int)n, (int)kv->cfg.n_kv_heads, (int)kv->cfg.head_dim, k, v, dtype == LT_F32, kv->q8,
                                    st));
+    if (ev_end) LT_CUDA(kv, cudaEventRecord(ev_end, st));
     kv->launches++;
     return mark_slot_use(kv, s, st);
 }
@@ -1284,24 +1313,54 @@ lt_status lt_kv_profile(lt_kv* kv, int enable) {
     lt_status rc = require_device(kv);
     if (rc) return rc;
     DeviceGuard g(kv->cfg.device);
-    if (kv->prof_ev.empty()) {
-        kv->prof_ev.resize(2 * kProfPairs);
-        for (auto& e : kv->prof_ev) LT_CUDA(kv, cudaEventCreate(&e));
+    for (ProfRing* r : {&kv->prof_attn, &kv->prof_plan, &kv->prof_write}) {
+        if (r->ev.empty()) {
+            r->ev.resize(2 * kProfPairs);
+            for (auto& e : r->ev) LT_CUDA(kv, cudaEventCreate(&e));
+        }
+        if ((rc = prof_drain(kv, *r, kProfPairs))) return rc;
+        r->ms = 0.0;
+        r->count = 0;
     }
-    if ((rc = prof_drain(kv, kProfPairs))) return rc;
+    kv->plan_blocks = kv->plan_entries = 0;
+    kv->write_rows = kv->write_in_bytes = 0;
     kv->profiling = enable != 0;
-    kv->prof_ms = 0.0;
-    kv->prof_count = 0;
     return LT_OK;
 }
 
 lt_status lt_kv_profile_read(lt_kv* kv, double* total_ms, uint64_t* launches) {
     if (!kv) return LT_E_ARG;
     DeviceGuard g(kv->dev ? kv->cfg.device : -1);
-    lt_status rc = prof_drain(kv, kProfPairs);
+    lt_status rc = prof_drain(kv, kv->prof_attn, kProfPairs);
     if (rc) return rc;
-    if (total_ms) *total_ms = kv->prof_ms;
-    if (launches) *launches = kv->prof_count;
+    if (total_ms) *total_ms = kv->prof_attn.ms;
+    if (launches) *launches = kv->prof_attn.count;
+    return LT_OK;
+}
+
+lt_status lt_kv_profile_read_plan(lt_kv* kv, double* total_ms, uint64_t* launches, uint64_t* copied_blocks,
+                                  uint64_t* table_entries) {
+    if (!kv) return LT_E_ARG;
+    DeviceGuard g(kv->dev ? kv->cfg.device : -1);
+    lt_status rc = prof_drain(kv, kv->prof_plan, kProfPairs);
+    if (rc) return rc;
+    if (total_ms) *total_ms = kv->prof_plan.ms;
+    if (launches) *launches = kv->prof_plan.count;
+    if (copied_blocks) *copied_blocks = kv->plan_blocks;
+    if (table_entries) *table_entries = kv->plan_entries;
+    return LT_OK;
+}
+
+lt_status lt_kv_profile_read_write(lt_kv* kv, double* total_ms, uint64_t* launches, uint64_t* rows,
+                                   uint64_t* in_bytes) {
+    if (!kv) return LT_E_ARG;
+    DeviceGuard g(kv->dev ? kv->cfg.device : -1);
+    lt_status rc = prof_drain(kv, kv->prof_write, kProfPairs);
+    if (rc) return rc;
+    if (total_ms) *total_ms = kv->prof_write.ms;
+    if (launches) *launches = kv->prof_write.count;
+    if (rows) *rows = kv->write_rows;
+    if (in_bytes) *in_bytes = kv->write_in_bytes;
     return LT_OK;
 }
 

@@ -1590,10 +1590,14 @@ __global__ void __launch_bounds__(256) apply_plan_kernel(uint16_t* __restrict__ 
                                                          size_t block_elems, int n_layers,
                                                          const int2* __restrict__ copies, int n_copies,
                                                          int32_t* __restrict__ tables, const int2* __restrict__ tw,
-                                                         int n_tw, int n_blocks, long long n_entries, int32_t* err) {
-    const int n_copy_ctas = n_copies * n_layers;
+                                                         int n_tw, int n_blocks, long long n_entries, int32_t* err,
+                                                         int parts) {
+    // One CTA per (copy, layer, part): a block's bytes are split into
+    // `parts` runs so a burst of copies keeps enough loads in flight.
+    const int n_copy_ctas = n_copies * n_layers * parts;
     if ((int)blockIdx.x < n_copy_ctas) {
-        const int ci = blockIdx.x / n_layers, l = blockIdx.x % n_layers;
+        const int part = blockIdx.x % parts;
+        const int ci = blockIdx.x / (n_layers * parts), l = (blockIdx.x / parts) % n_layers;
         const int2 cp = copies[ci];
 #ifdef LT_BOUNDS_CHECK
         if ((unsigned)cp.x >= (unsigned)n_blocks || (unsigned)cp.y >= (unsigned)n_blocks) {
@@ -1603,18 +1607,21 @@ __global__ void __launch_bounds__(256) apply_plan_kernel(uint16_t* __restrict__ 
 #endif
         const uint4* src = reinterpret_cast<const uint4*>(pool + (size_t)l * layer_stride + (size_t)cp.x * block_elems);
         uint4* dst = reinterpret_cast<uint4*>(pool + (size_t)l * layer_stride + (size_t)cp.y * block_elems);
-        // 8 independent 16-byte loads in flight per thread before their stores
+        // this part's 16-byte words, up to 4 independent loads in flight per
+        // thread before their stores
         const size_t n16 = block_elems * 2 / 16;
-        constexpr int U = 8;
-        size_t i = threadIdx.x;
-        for (; i + (U - 1) * blockDim.x < n16; i += U * blockDim.x) {
+        const size_t per = (n16 + parts - 1) / parts;
+        const size_t i0 = (size_t)part * per, i1 = min(n16, i0 + per);
+        constexpr int U = 4;
+        size_t i = i0 + threadIdx.x;
+        for (; i + (U - 1) * blockDim.x < i1; i += U * blockDim.x) {
             uint4 t[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) t[u] = __ldg(src + i + u * blockDim.x);
 #pragma unroll
             for (int u = 0; u < U; ++u) dst[i + u * blockDim.x] = t[u];
         }
-        for (; i < n16; i += blockDim.x) dst[i] = __ldg(src + i);
+        for (; i < i1; i += blockDim.x) dst[i] = __ldg(src + i);
     } else {
         const int i = (blockIdx.x - n_copy_ctas) * blockDim.x + threadIdx.x;
         if (i < n_tw) {
@@ -1881,10 +1888,13 @@ cudaError_t launch_write(uint16_t* pool_layer, const int2* cells, int n, int n_k
 cudaError_t launch_apply_plan(uint16_t* pool, size_t layer_stride_elems, size_t block_elems, int n_layers,
                               const int2* copies, int n_copies, int32_t* tables, const int2* tw, int n_tw,
                               int n_blocks, long long n_entries, int32_t* err, cudaStream_t s) {
-    const int ctas = n_copies * n_layers + (n_tw + 255) / 256;
+    // a part of 16 KiB: one round of four 16-byte loads per thread
+    const int parts = (int)std::max<size_t>(1, (block_elems * 2 + 16383) / 16384);
+    const long long ctas = (long long)n_copies * n_layers * parts + (n_tw + 255) / 256;
     if (ctas == 0) return cudaSuccess;
-    apply_plan_kernel<<<ctas, 256, 0, s>>>(pool, layer_stride_elems, block_elems, n_layers, copies, n_copies, tables,
-                                           tw, n_tw, n_blocks, n_entries, err);
+    if (ctas > 0x7FFFFFFFll) return cudaErrorInvalidValue;
+    apply_plan_kernel<<<(unsigned)ctas, 256, 0, s>>>(pool, layer_stride_elems, block_elems, n_layers, copies, n_copies,
+                                                     tables, tw, n_tw, n_blocks, n_entries, err, parts);
     return cudaGetLastError();
 }
 

@@ -337,6 +337,23 @@ class KvCache:
         self._check(self._lib.lt_kv_profile_read(self._h, C.byref(ms), C.byref(n)))
         return ms.value, n.value
 
+    def profile_read_plan(self):
+        """(total ms, launches, copied blocks, table entries) of the plan
+        launches (copy-on-write copies, compaction moves, table entries)
+        timed so far."""
+        ms, n, blocks, entries = C.c_double(), C.c_uint64(), C.c_uint64(), C.c_uint64()
+        self._check(self._lib.lt_kv_profile_read_plan(self._h, C.byref(ms), C.byref(n), C.byref(blocks),
+                                                      C.byref(entries)))
+        return ms.value, n.value, blocks.value, entries.value
+
+    def profile_read_write(self):
+        """(total ms, launches, rows, input bytes) of the K/V write launches
+        (lt_kv_write) timed so far."""
+        ms, n, rows, nbytes = C.c_double(), C.c_uint64(), C.c_uint64(), C.c_uint64()
+        self._check(self._lib.lt_kv_profile_read_write(self._h, C.byref(ms), C.byref(n), C.byref(rows),
+                                                       C.byref(nbytes)))
+        return ms.value, n.value, rows.value, nbytes.value
+
     def set_min_tiles_per_warp(self, tiles: int):
         """Attention launch sizing: at least `tiles` tiles per warp (default 8)."""
         self._check(self._lib.lt_kv_set_min_tiles_per_warp(self._h, tiles))
