@@ -717,12 +717,15 @@ def run_c4(args, rank, world, local, mode):
     dev = torch.device(f"cuda:{local}")
     ensure_pg(world, local)
     B, L, hq, hkv, d = 16, 32768, 64, 8, 128
+    # --emulate-ranks R on one GPU: the work of one rank of an R-GPU run (no
+    # collective), to time the per-rank launch that R GPUs would each run
+    split = world if world > 1 else max(1, getattr(args, "emulate_ranks", 1))
     if mode == "batch":
-        assert B % world == 0
-        n_seq, my_hkv, my_hq = B // world, hkv, hq
+        assert B % split == 0
+        n_seq, my_hkv, my_hq = B // split, hkv, hq
     else:
-        assert hkv % world == 0
-        n_seq, my_hkv, my_hq = B, hkv // world, hq // world
+        assert hkv % split == 0
+        n_seq, my_hkv, my_hq = B, hkv // split, hq // split
     kvd = my_hkv * d
     n_blocks = n_seq * ((L + CYCLE + 1 + BLOCK - 1) // BLOCK) + 8
     kv = kv_mod.KvCache(1, my_hkv, d, n_blocks * BLOCK, n_heads=my_hq, max_seqs=n_seq, max_batch=8192, device=local,
@@ -793,6 +796,7 @@ def run_c4(args, rank, world, local, mode):
                         f"{mode}-sharded x{world}, one layer",
             "n_heads": hq, "n_kv_heads": hkv, "head_dim": d, "block_tokens": BLOCK, "kv_format": args.kv_format,
             "per_rank": {"seqs": n_seq, "kv_heads": my_hkv, "q_heads": my_hq},
+            "emulated_ranks": split if world == 1 else None,
             "collective": ("lt_kv_write_attend_gather: outputs stored to every rank over NVLink by the attention "
                            "kernel, flag wait + copy" if peer else
                            "lt_kv_gather_heads: NCCL all-gather of [seqs, q_heads*D] f16 per step + permute")
@@ -1079,7 +1083,11 @@ def run_c1(args, rank, world, local):
         result.update({
             "dtype": "int8 x int8 -> int32 (Q8_0 matmuls), f32 elsewhere, f16 KV",
             "data": "synthetic: random-init Q8_0 weights (seeded), uniform-random prompt ids (seeded)",
-            "roofline": {"bound": "hbm", "kernel": "q8_matmul_kernel (all projections and the output matrix)",
+            "roofline": {"bound": "hbm",
+                         "kernel": ("decode_kernel<64> (persistent: every layer's matmuls, norms, RoPE, K/V append "
+                                    "and attention, the output matrix and the pick in one launch per step)"
+                                    if model.persistent_available() else
+                                    "q8_gemv_kernel (all projections and the output matrix)"),
                          "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None,
                          "algorithmic_bytes_per_launch": int(mm_bytes / max(mm_n, 1)),
@@ -1484,6 +1492,8 @@ def main():
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="c4-head: gather the sharded heads inside the attention call over NVLink (peer) or with "
                          "a separate NCCL all-gather (nccl)")
+    ap.add_argument("--emulate-ranks", type=int, default=1,
+                    help="c4-*: on one GPU, run the per-rank work of an R-GPU run (sequences or KV heads / R)")
     ap.add_argument("--kv-format", choices=["f16", "q8_0"], default="f16",
                     help="c2 / c4-*: cached K/V format (f16: the reference's; q8_0: int8 + f16 scale per 32)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,

@@ -103,10 +103,24 @@ lt_status lt_llama_step_greedy(lt_llama* m, lt_kv* kv, const int32_t* tokens_hos
 /* Kernel launches issued by this handle since creation. */
 uint64_t lt_llama_launch_count(const lt_llama* m);
 
+/* The persistent decode step.  A forward of up to 8 tokens, each of a
+ * different sequence, on an f16 cache runs as one cooperative launch (one
+ * CTA per SM): every layer's matmuls, norms, RoPE, K/V append and attention,
+ * then the output matrix and, for lt_llama_step_greedy, the greedy pick.  Its
+ * matmul outputs and appended K/V bytes equal the multi-launch path's bit for
+ * bit; attention is within the attention tolerance.  On by default;
+ * enable = 0 runs every forward on the multi-launch path (for comparison).
+ * lt_llama_persistent_available returns 1 when the model's shapes and the
+ * device allow the persistent step. */
+lt_status lt_llama_set_persistent(lt_llama* m, int enable);
+int lt_llama_persistent_available(const lt_llama* m);
+
 /* Profiling of the Q8_0 matmul launches of lt_llama_forward: when enabled,
- * each is bracketed by CUDA events on its stream.  profile_read waits for the
- * recorded launches, returns their summed device time, count and algorithmic
- * bytes (weights + scales, activations, outputs), and starts a new window. */
+ * each is bracketed by CUDA events on its stream (a persistent decode step
+ * counts as one launch that carries every matmul of the step).
+ * profile_read waits for the recorded launches, returns their summed device
+ * time, count and algorithmic bytes (weights + scales, activations,
+ * outputs), and starts a new window. */
 lt_status lt_llama_profile(lt_llama* m, int enable);
 lt_status lt_llama_profile_read(lt_llama* m, double* matmul_ms, uint64_t* matmul_launches, uint64_t* matmul_bytes);
 

@@ -36,7 +36,7 @@ EXPORTS = (
     "lt_paged_attend_noalloc", "lt_paged_attend_noalloc_check", "lt_kv_peer_export", "lt_kv_peer_import", "lt_kv_peer_close",
     "lt_kv_attend_gather", "lt_kv_write_attend_gather", "lt_kv_selftest_wait", "lt_kv_build_features", "lt_kv_set_min_tiles_per_warp", "lt_kv_set_cascade", "lt_kv_cascade_launches",
     "lt_llama_create", "lt_llama_destroy", "lt_llama_last_error", "lt_llama_set_tensor", "lt_llama_forward",
-    "lt_llama_step_greedy", "lt_llama_launch_count", "lt_llama_profile", "lt_llama_profile_read", "lt_q8_quantize", "lt_q8_matmul", "lt_rms_norm_q8",
+    "lt_llama_step_greedy", "lt_llama_launch_count", "lt_llama_set_persistent", "lt_llama_persistent_available", "lt_llama_profile", "lt_llama_profile_read", "lt_q8_quantize", "lt_q8_matmul", "lt_rms_norm_q8",
     "lt_silu_q8", "lt_argmax_f32", "lt_q8_project", "lt_q8_check",
     "lt_sched_create", "lt_sched_destroy", "lt_sched_last_error", "lt_sched_submit", "lt_sched_step",
     "lt_sched_get_stats", "lt_sched_submit_tokens",
@@ -164,6 +164,8 @@ def _declare(L):
         "lt_llama_launch_count": (u64, [p]),
         "lt_llama_profile": (st, [p, C.c_int]),
         "lt_llama_profile_read": (st, [p, C.POINTER(C.c_double), C.POINTER(u64), C.POINTER(u64)]),
+        "lt_llama_set_persistent": (st, [p, C.c_int]),
+        "lt_llama_persistent_available": (C.c_int, [p]),
         "lt_q8_quantize": (st, [p, u32, u32, p, p, p]),
         "lt_q8_matmul": (st, [p, p, u32, u32, p, p, u32, p, u32, C.c_int, p]),
         "lt_rms_norm_q8": (st, [p, p, p, u32, u32, C.c_float, p, p, p, p]),

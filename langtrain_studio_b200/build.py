@@ -36,9 +36,9 @@ VARIANTS = {
 }
 
 SOURCES = [CSRC / "lt_kv_kernels.cu", CSRC / "lt_kv.cpp", CSRC / "lt_kv_nccl.cpp", CSRC / "lt_kv_noalloc.cu",
-           CSRC / "lt_llama.cu", CSRC / "lt_sched.cpp", CSRC / "lt_prefix.cpp"]
-HEADERS = [CSRC / "lt_kv_internal.h", INCLUDE / "lt_kv.h", INCLUDE / "lt_llama.h", INCLUDE / "lt_sched.h",
-           INCLUDE / "lt_prefix.h"]
+           CSRC / "lt_llama.cu", CSRC / "lt_llama_decode.cu", CSRC / "lt_sched.cpp", CSRC / "lt_prefix.cpp"]
+HEADERS = [CSRC / "lt_kv_internal.h", CSRC / "lt_kv_layout.cuh", CSRC / "lt_q8_device.cuh", CSRC / "lt_llama_decode.h",
+           INCLUDE / "lt_kv.h", INCLUDE / "lt_llama.h", INCLUDE / "lt_sched.h", INCLUDE / "lt_prefix.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall", "-shared",

@@ -25,6 +25,7 @@
 #include <algorithm>
 
 #include "lt_kv_internal.h"
+#include "lt_kv_layout.cuh"
 
 namespace ltkv {
 namespace {
@@ -183,16 +184,6 @@ __device__ __forceinline__ float ex2(float x) {
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-// f32 -> f16 with the bit semantics of half 2.7.1's f16::from_f32: IEEE
-// round-to-nearest-even (the hardware cvt.rn), and NaN -> quiet NaN that
-// keeps the top 10 payload bits (the hardware returns a canonical NaN).
-__device__ __forceinline__ uint16_t f32_to_f16_ref(float x) {
-    const uint32_t u = __float_as_uint(x);
-    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu))
-        return static_cast<uint16_t>(((u >> 16) & 0x8000u) | 0x7E00u | ((u & 0x007FFFFFu) >> 13));
-    return __half_as_ushort(__float2half_rn(x));
-}
-
 // Load 8 consecutive input values (f32 or f16) and return them as 8 f16.
 __device__ __forceinline__ uint4 load8_as_f16(const void* base, size_t idx, int in_f32) {
     uint4 r;
@@ -207,15 +198,6 @@ __device__ __forceinline__ uint4 load8_as_f16(const void* base, size_t idx, int 
         r = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + idx));
     }
     return r;
-}
-
-// Element offset of 16-byte chunk c (8 f16) of slot s inside the K (or V)
-// part of a (block, head) tile: the part is head_dim/64 sub-tiles of 16 rows
-// x 128 bytes, chunk c in sub-tile c/8, at chunk position (c%8) ^ (s%8).
-// Each sub-tile is the 128-byte-swizzled row-major layout of the tensor-core
-// operand descriptors, and ldmatrix over it is bank-conflict free.
-__device__ __forceinline__ int chunk_off(int c, int slot) {
-    return (c >> 3) * (kBlock * 64) + slot * 64 + (((c & 7) ^ (slot & 7)) << 3);
 }
 
 // ---------------------------------------------------------- Q8_0 tile ----

@@ -33,10 +33,13 @@
 #include "lt_kv.h"
 #include "lt_kv_internal.h"
 #include "lt_llama.h"
+#include "lt_llama_decode.h"
+#include "lt_q8_device.cuh"
+
+using namespace ltq8;
 
 namespace {
 
-constexpr int kQK = 32;          // Q8_0 block
 constexpr int kMmWarps = 16;     // warps per matmul CTA (K blocks dealt round-robin)
 constexpr int kMmRows = 16;      // weight rows per matmul CTA (mma M)
 constexpr int kMmToks = 8;       // tokens per matmul CTA (mma N)
@@ -47,55 +50,6 @@ __device__ __forceinline__ uint2 ld_stream(const void* p) {  // weights: read on
     uint2 v;
     asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
     return v;
-}
-
-__device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                       uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%10, %10, %10, %10};"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
-}
-
-// QActs::quantize of one 32-element block held as 8 values by each of 4
-// consecutive lanes (quantize_block, quant.rs:785-795): amax folded from 0
-// with f32::max (NaN-ignoring, as fmaxf), d = amax / 127, q = round(v * (1/d))
-// half away from zero, saturated to int8 (Rust `as i8`: NaN -> 0).
-// Every lane of the warp must call it (the group shuffles); only `live`
-// lanes store.
-__device__ __forceinline__ void quant8_store(const float (&v)[8], int8_t* q_dst, float* scale_dst, bool leader,
-                                             bool live = true) {
-    float a = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 8; k++) a = fmaxf(a, fabsf(v[k]));
-    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
-    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
-    const float d = __fdiv_rn(a, 127.0f);
-    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    uint32_t w[2] = {0u, 0u};
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const float r = roundf(__fmul_rn(v[k], id));
-        int qi = 0;
-        if (!(r != r)) qi = (int)fminf(fmaxf(r, -128.0f), 127.0f);
-        w[k >> 2] |= (uint32_t)(qi & 0xff) << (8 * (k & 3));
-    }
-    if (!live) return;
-    *reinterpret_cast<uint2*>(q_dst) = make_uint2(w[0], w[1]);
-    if (leader) *scale_dst = d;
-}
-
-__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
-    const float4 a = *reinterpret_cast<const float4*>(p);
-    const float4 b = *reinterpret_cast<const float4*>(p + 4);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-
-__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
-    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
-    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
 
 // ------------------------------------------------------------ kernels -----
@@ -722,6 +676,13 @@ struct lt_llama {
     uint64_t launches = 0;
     std::vector<void*> allocs;
     bool use_gemv = true;     // fused decode matmuls for up to 8 tokens
+    // the persistent decode step (lt_llama_decode.cu) for up to 8 tokens, one per sequence
+    bool persistent = true;
+    int dec_grid = 0;                  // its CTAs (0: the shapes do not fit it)
+    lldec::Layer* d_layers = nullptr;  // device table of every layer's weights
+    uint32_t* d_sync = nullptr;        // its grid barrier, abort flag and completion counters
+    size_t sync_bytes = 0;
+    float* d_att_part = nullptr;       // its attention partials
     uint32_t* d_err = nullptr;  // device flag: a bounded wait gave up (ids[0], copied with the picks)
     // matmul profiling: an event pair around each q8_matmul launch
     bool prof = false;
@@ -923,8 +884,8 @@ lt_status lt_llama_create(const lt_llama_config* cfg, lt_llama** out) {
         m->d_err = reinterpret_cast<uint32_t*>(m->ids);
         if (cudaMemset(m->ids, 0, sizeof(int32_t)) != cudaSuccess) rc = fail(m, LT_E_CUDA, "cudaMemset failed");
     }
-    // step metadata: tokens [B] | want [B] | sincos [B][half][2]
-    m->meta_bytes = B * 4 * 2 + B * m->half * 2 * sizeof(float);
+    // step metadata: tokens [B] | want [B] | seq [B] | pos [B] | sincos [B][half][2]
+    m->meta_bytes = B * 4 * 4 + B * m->half * 2 * sizeof(float);
     if (rc == LT_OK) rc = dalloc(m, &m->meta_dev, m->meta_bytes);
     if (rc == LT_OK && (cudaMallocHost(&m->meta_host, m->meta_bytes) != cudaSuccess ||
                         cudaMallocHost(&m->ids_host, (B + 1) * sizeof(int32_t)) != cudaSuccess ||
@@ -936,6 +897,43 @@ lt_status lt_llama_create(const lt_llama_config* cfg, lt_llama** out) {
     }
     m->blocks.resize(B);
     m->slots.resize(B);
+    // The persistent decode step: a device table of the layers' weights (the
+    // matrices stay where alloc_mat put them), its synchronisation words and
+    // its attention partials.
+    const int group = (int)(c.n_heads / c.n_kv_heads);
+    if (lldec::supported((int)c.dim, (int)m->q_dim, (int)c.ffn_dim, (int)c.head_dim, group, nullptr)) {
+        std::vector<lldec::Layer> layers(c.n_layers);
+        for (uint32_t l = 0; l < c.n_layers; l++) {
+            const QMat* mats[4] = {&m->wqkv[l], &m->wo[l], &m->wgu[l], &m->wdown[l]};
+            for (int k = 0; k < 4; k++) {
+                layers[l].wq[k] = mats[k]->qs;
+                layers[l].ws[k] = mats[k]->sc;
+            }
+            layers[l].attn_norm = m->attn_norm[l];
+            layers[l].ffn_norm = m->ffn_norm[l];
+        }
+        m->sync_bytes = lldec::sync_words((int)c.ffn_dim, (int)c.n_kv_heads) * sizeof(uint32_t);
+        rc = dalloc(m, &m->d_layers, c.n_layers);
+        if (rc == LT_OK) rc = dalloc(m, &m->d_sync, m->sync_bytes / sizeof(uint32_t));
+        if (rc == LT_OK)
+            rc = dalloc(m, &m->d_att_part, lldec::att_part_floats((int)c.n_kv_heads, group, (int)c.head_dim));
+        if (rc == LT_OK && (cudaMemcpy(m->d_layers, layers.data(), c.n_layers * sizeof(lldec::Layer),
+                                       cudaMemcpyHostToDevice) != cudaSuccess ||
+                            cudaMemset(m->d_sync, 0, m->sync_bytes) != cudaSuccess))
+            rc = fail(m, LT_E_CUDA, "persistent decode set-up failed");
+        if (rc != LT_OK) {
+            lt_llama_destroy(m);
+            return rc;
+        }
+        lldec::Params probe{};
+        probe.dim = (int)c.dim;
+        probe.q_dim = (int)m->q_dim;
+        probe.ffn = (int)c.ffn_dim;
+        probe.head_dim = (int)c.head_dim;
+        probe.group = group;
+        m->dec_grid = lldec::grid_size(probe);
+        cudaGetLastError();  // a failed occupancy query leaves the step on the multi-launch path
+    }
     *out = m;
     return LT_OK;
 }
@@ -1028,9 +1026,39 @@ lt_status lt_llama_set_tensor(lt_llama* m, lt_tensor which, uint32_t layer, cons
     return LT_OK;
 }
 
-lt_status lt_llama_forward(lt_llama* m, lt_kv* kv, const int32_t* tokens, const uint32_t* seqs, const uint32_t* pos,
-                           uint32_t n, const uint32_t* want, uint32_t n_want, float* logits, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Whether a forward call can run as one persistent decode launch: up to 8
+// tokens, each of a different sequence (so each appends to its own last
+// cell), on an f16 cache, with shapes the kernel takes.
+bool decode_eligible(const lt_llama* m, const lt_kv* kv, const uint32_t* seqs, uint32_t n) {
+    if (!m->persistent || m->dec_grid <= 0 || n == 0 || n > (uint32_t)lldec::kMaxTokens) return false;
+    if (ltkv::handle_config(kv)->kv_format != LT_KV_F16) return false;
+    for (uint32_t i = 0; i < n; i++)
+        for (uint32_t j = i + 1; j < n; j++)
+            if (seqs[i] == seqs[j]) return false;
+    return true;
+}
+
+// Algorithmic bytes of one matmul as the profiling counts them: weights and
+// their f16 scales, the int8 activations and scales read, the f32 outputs
+// (read too when accumulating).
+uint64_t matmul_bytes(const QMat& w, uint32_t n, bool accumulate) {
+    const uint64_t rc = (uint64_t)w.rows * w.cols;
+    return rc + rc / kQK * 2 + (uint64_t)n * w.cols + (uint64_t)n * w.cols / kQK * 4 +
+           (uint64_t)n * w.rows * 4 * (accumulate ? 2 : 1);
+}
+
+// Model::forward (model.rs:366-518).  `greedy`: also pick the argmax of each
+// wanted row into m->ids[1..] when the persistent step runs (*picked is then
+// set); otherwise the caller launches the pick.
+lt_status forward_impl(lt_llama* m, lt_kv* kv, const int32_t* tokens, const uint32_t* seqs, const uint32_t* pos,
+                       uint32_t n, const uint32_t* want, uint32_t n_want, float* logits, void* stream, bool greedy,
+                       bool* picked) {
     ltkv::NvtxRange nv("lt_llama_forward");
+    if (picked) *picked = false;
     if (!m || !kv) return LT_E_ARG;
     const lt_llama_config& c = m->cfg;
     if (n == 0) return LT_OK;
@@ -1056,14 +1084,20 @@ lt_status lt_llama_forward(lt_llama* m, lt_kv* kv, const int32_t* tokens, const 
         if (tokens[i] < 0 || (uint32_t)tokens[i] >= c.vocab)
             return fail(m, LT_E_ARG, "token id %d out of range", tokens[i]);
 
-    // Step metadata in one copy: tokens, want, RoPE sin/cos (host libm, as model.rs:297).
+    // Step metadata in one copy: tokens, want, seq, pos, RoPE sin/cos (host libm, as model.rs:297).
     LL_CUDA(m, cudaEventSynchronize(m->meta_ev));  // the previous copy has left the staging buffer
     const size_t B = c.max_batch;
     int32_t* h_tok = reinterpret_cast<int32_t*>(m->meta_host);
     int32_t* h_want = h_tok + B;
-    float* h_sc = reinterpret_cast<float*>(h_want + B);
+    int32_t* h_seq = h_want + B;
+    int32_t* h_pos = h_seq + B;
+    float* h_sc = reinterpret_cast<float*>(h_pos + B);
     std::memcpy(h_tok, tokens, n * sizeof(int32_t));
     for (uint32_t j = 0; j < n_want; j++) h_want[j] = (int32_t)want[j];
+    for (uint32_t i = 0; i < n; i++) {
+        h_seq[i] = (int32_t)seqs[i];
+        h_pos[i] = (int32_t)pos[i];
+    }
     for (uint32_t i = 0; i < n; i++)
         for (uint32_t k = 0; k < m->half; k++) {
             const float a = (float)pos[i] * m->inv_freq[k];
@@ -1072,13 +1106,91 @@ lt_status lt_llama_forward(lt_llama* m, lt_kv* kv, const int32_t* tokens, const 
         }
     int32_t* d_tok = reinterpret_cast<int32_t*>(m->meta_dev);
     int32_t* d_want = d_tok + B;
-    float* d_sc = reinterpret_cast<float*>(d_want + B);
-    LL_CUDA(m, cudaMemcpyAsync(m->meta_dev, m->meta_host, B * 8 + (size_t)n * m->half * 2 * sizeof(float),
+    int32_t* d_seq = d_want + B;
+    int32_t* d_pos = d_seq + B;
+    float* d_sc = reinterpret_cast<float*>(d_pos + B);
+    LL_CUDA(m, cudaMemcpyAsync(m->meta_dev, m->meta_host, B * 16 + (size_t)n * m->half * 2 * sizeof(float),
                                cudaMemcpyHostToDevice, st));
     LL_CUDA(m, cudaEventRecord(m->meta_ev, st));
 
     const int dim = (int)c.dim, ffn = (int)c.ffn_dim, qd = (int)m->q_dim, kvd = (int)m->kv_dim;
     const float scale = 1.0f / sqrtf((float)c.head_dim);  // model.rs:402
+
+    if (decode_eligible(m, kv, seqs, n)) {
+        // The whole step in one launch: the cache's queued plan (new table
+        // entries, copy-on-write copies) goes first.
+        if ((rc = lt_kv_flush(kv, stream)) != LT_OK) return fail(m, rc, "%s", lt_kv_last_error(kv));
+        uint32_t max_blocks = 0;
+        const int32_t* tables = lt_kv_device_tables(kv, &max_blocks);
+        lldec::Params p{};
+        p.layers = m->d_layers;
+        p.n_layers = (int)c.n_layers;
+        p.dim = dim;
+        p.q_dim = qd;
+        p.kv_dim = kvd;
+        p.qkv_rows = (int)m->qkv_rows;
+        p.ffn = ffn;
+        p.vocab = (int)c.vocab;
+        p.head_dim = (int)c.head_dim;
+        p.group = (int)(c.n_heads / c.n_kv_heads);
+        p.n_kv_heads = (int)c.n_kv_heads;
+        p.half = (int)m->half;
+        p.neox = c.rope_neox;
+        p.eps = c.eps;
+        p.scale_log2 = scale * 1.4426950408889634f;
+        p.emb_q = m->embed.qs;
+        p.emb_s = m->embed.sc;
+        p.out_q = m->output.qs;
+        p.out_s = m->output.sc;
+        p.out_norm = m->out_norm;
+        p.n = (int)n;
+        p.n_want = (int)n_want;
+        p.tokens = d_tok;
+        p.want = d_want;
+        p.seq = d_seq;
+        p.pos = d_pos;
+        p.sincos = d_sc;
+        p.pool = static_cast<uint16_t*>(lt_kv_device_pool(kv));
+        p.layer_elems = (size_t)lt_kv_n_blocks(kv) * c.n_kv_heads * 2 * LT_KV_BLOCK * c.head_dim;
+        p.tables = tables;
+        p.max_blocks = (int)max_blocks;
+        p.x = m->x;
+        p.qkv = m->qkv;
+        p.att = m->att;
+        p.gu = m->gu;
+        p.logits = logits;
+        p.act_q = m->xq;
+        p.act_s = m->xs;
+        p.ids = m->ids;
+        p.argmax = greedy ? 1 : 0;
+        p.att_part = m->d_att_part;
+        p.sync = m->d_sync;
+        // the barrier count and abort flag start at zero (a launch that gave up may have left them set)
+        LL_CUDA(m, cudaMemsetAsync(m->d_sync, 0, lldec::kSyncHeader * sizeof(uint32_t), st));
+        if (m->prof) {
+            if (m->prof_used + 2 > m->prof_ev.size()) {
+                for (int i = 0; i < 2; i++) {
+                    cudaEvent_t e;
+                    LL_CUDA(m, cudaEventCreate(&e));
+                    m->prof_ev.push_back(e);
+                }
+            }
+            LL_CUDA(m, cudaEventRecord(m->prof_ev[m->prof_used], st));
+        }
+        LL_CUDA(m, lldec::launch(p, m->dec_grid, st));
+        m->launches++;
+        if (m->prof) {
+            LL_CUDA(m, cudaEventRecord(m->prof_ev[m->prof_used + 1], st));
+            m->prof_used += 2;
+            for (uint32_t l = 0; l < c.n_layers; l++)
+                m->prof_bytes += matmul_bytes(m->wqkv[l], n, false) + matmul_bytes(m->wo[l], n, true) +
+                                 matmul_bytes(m->wgu[l], n, false) + matmul_bytes(m->wdown[l], n, true);
+            if (n_want) m->prof_bytes += matmul_bytes(m->output, n_want, false);
+        }
+        if (picked) *picked = greedy && n_want > 0;
+        return LT_OK;
+    }
+
     embed_kernel<<<n, 256, 0, st>>>(m->embed.qs, m->embed.sc, dim, d_tok, m->x);
     LL_CUDA(m, cudaGetLastError());
     m->launches++;
@@ -1104,26 +1216,46 @@ lt_status lt_llama_forward(lt_llama* m, lt_kv* kv, const int32_t* tokens, const 
     return LT_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+lt_status lt_llama_forward(lt_llama* m, lt_kv* kv, const int32_t* tokens, const uint32_t* seqs, const uint32_t* pos,
+                           uint32_t n, const uint32_t* want, uint32_t n_want, float* logits, void* stream) {
+    return forward_impl(m, kv, tokens, seqs, pos, n, want, n_want, logits, stream, false, nullptr);
+}
+
 lt_status lt_llama_step_greedy(lt_llama* m, lt_kv* kv, const int32_t* tokens, const uint32_t* seqs,
                                const uint32_t* pos, uint32_t n, const uint32_t* want, uint32_t n_want,
                                int32_t* next_host, void* stream) {
     if (!m) return LT_E_ARG;
     if (n_want && !next_host) return fail(m, LT_E_ARG, "null next_host");
-    lt_status rc = lt_llama_forward(m, kv, tokens, seqs, pos, n, want, n_want, m->logits, stream);
+    bool picked = false;
+    lt_status rc = forward_impl(m, kv, tokens, seqs, pos, n, want, n_want, m->logits, stream, true, &picked);
     if (rc != LT_OK || n_want == 0) return rc;
     DeviceGuard dg(m->cfg.device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    LL_CUDA(m, launch_argmax(m->logits, (int)n_want, (int)m->cfg.vocab, m->ids + 1, st));
-    m->launches++;
+    if (!picked) {
+        LL_CUDA(m, launch_argmax(m->logits, (int)n_want, (int)m->cfg.vocab, m->ids + 1, st));
+        m->launches++;
+    }
     LL_CUDA(m, cudaMemcpyAsync(m->ids_host, m->ids, (n_want + 1) * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
     LL_CUDA(m, cudaStreamSynchronize(st));
     if (m->ids_host[0] != 0) {
         cudaMemsetAsync(m->ids, 0, sizeof(int32_t), st);
-        return fail(m, LT_E_TIMEOUT, "a matmul's bounded wait for its weight copies gave up");
+        return fail(m, LT_E_TIMEOUT, "a bounded device wait of the step gave up");
     }
     std::memcpy(next_host, m->ids_host + 1, n_want * sizeof(int32_t));
     return LT_OK;
 }
+
+lt_status lt_llama_set_persistent(lt_llama* m, int enable) {
+    if (!m) return LT_E_ARG;
+    m->persistent = enable != 0;
+    return LT_OK;
+}
+
+int lt_llama_persistent_available(const lt_llama* m) { return m && m->dec_grid > 0 ? 1 : 0; }
 
 // ---- op-level entry points ----
 

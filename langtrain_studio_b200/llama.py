@@ -117,6 +117,16 @@ class Llama:
             raise self._err(rc)
         return nxt[: want.size]
 
+    def set_persistent(self, enable: bool = True):
+        """Run decode forwards (up to 8 tokens, one per sequence) as one
+        persistent launch (default) or on the multi-launch path."""
+        rc = self._lib.lt_llama_set_persistent(self._h, int(enable))
+        if rc != N.LT_OK:
+            raise self._err(rc)
+
+    def persistent_available(self) -> bool:
+        return bool(self._lib.lt_llama_persistent_available(self._h))
+
     def launch_count(self) -> int:
         return self._lib.lt_llama_launch_count(self._h)
 
