@@ -680,9 +680,8 @@ struct lt_llama {
     bool persistent = true;
     int dec_grid = 0;                  // its CTAs (0: the shapes do not fit it)
     lldec::Layer* d_layers = nullptr;  // device table of every layer's weights
-    uint32_t* d_sync = nullptr;        // its grid barrier, abort flag and completion counters
+    uint32_t* d_sync = nullptr;        // its grid barrier and abort flag
     size_t sync_bytes = 0;
-    float* d_att_part = nullptr;       // its attention partials
     uint32_t* d_err = nullptr;  // device flag: a bounded wait gave up (ids[0], copied with the picks)
     // matmul profiling: an event pair around each q8_matmul launch
     bool prof = false;
@@ -912,11 +911,9 @@ lt_status lt_llama_create(const lt_llama_config* cfg, lt_llama** out) {
             layers[l].attn_norm = m->attn_norm[l];
             layers[l].ffn_norm = m->ffn_norm[l];
         }
-        m->sync_bytes = lldec::sync_words((int)c.ffn_dim, (int)c.n_kv_heads) * sizeof(uint32_t);
+        m->sync_bytes = lldec::kSyncWords * sizeof(uint32_t);
         rc = dalloc(m, &m->d_layers, c.n_layers);
         if (rc == LT_OK) rc = dalloc(m, &m->d_sync, m->sync_bytes / sizeof(uint32_t));
-        if (rc == LT_OK)
-            rc = dalloc(m, &m->d_att_part, lldec::att_part_floats((int)c.n_kv_heads, group, (int)c.head_dim));
         if (rc == LT_OK && (cudaMemcpy(m->d_layers, layers.data(), c.n_layers * sizeof(lldec::Layer),
                                        cudaMemcpyHostToDevice) != cudaSuccess ||
                             cudaMemset(m->d_sync, 0, m->sync_bytes) != cudaSuccess))
@@ -1157,16 +1154,13 @@ lt_status forward_impl(lt_llama* m, lt_kv* kv, const int32_t* tokens, const uint
         p.x = m->x;
         p.qkv = m->qkv;
         p.att = m->att;
-        p.gu = m->gu;
+        p.act = m->gu;  // the multi-launch path's gate|up buffer holds act here
         p.logits = logits;
-        p.act_q = m->xq;
-        p.act_s = m->xs;
         p.ids = m->ids;
         p.argmax = greedy ? 1 : 0;
-        p.att_part = m->d_att_part;
         p.sync = m->d_sync;
         // the barrier count and abort flag start at zero (a launch that gave up may have left them set)
-        LL_CUDA(m, cudaMemsetAsync(m->d_sync, 0, lldec::kSyncHeader * sizeof(uint32_t), st));
+        LL_CUDA(m, cudaMemsetAsync(m->d_sync, 0, lldec::kSyncWords * sizeof(uint32_t), st));
         if (m->prof) {
             if (m->prof_used + 2 > m->prof_ev.size()) {
                 for (int i = 0; i < 2; i++) {

@@ -41,31 +41,19 @@ struct Params {
     float* x;               // [n][dim] residual stream
     float* qkv;             // [n][qkv_rows]
     float* att;             // [n][q_dim]
-    float* gu;              // [n][2 * ffn]
+    float* act;             // [n][ffn]: SiLU(gate) * up
     float* logits;          // [n_want][vocab]
-    int8_t* act_q;          // [n][ffn]: SiLU(gate) * up, quantised
-    float* act_s;           // [n][ffn / 32]
     int32_t* ids;           // [0]: error word (1: a bounded wait gave up); [1 + j]: argmax of logits row j
     int argmax;             // also write the greedy picks
-    float* att_part;        // attention partials: [kMaxTokens * n_kv_heads * kMaxPieces][2 * group + group * head_dim]
     // [0] barrier arrivals (counted up through the launch; zeroed by the
-    // host before it), [1] unused, [2] abort, [3, 3 + ffn/32) SiLU group
-    // counters, then one counter per (token, KV head) for the attention pieces
+    // host before it), [1] unused, [2] abort
     uint32_t* sync;
 };
 
-// Words of `sync` before the SiLU group counters.
-constexpr int kSyncHeader = 3;
+// Words of `sync`.
+constexpr int kSyncWords = 3;
 // Tokens per step the kernel takes (one mma N tile).
 constexpr int kMaxTokens = 8;
-// Pieces a (token, KV head)'s blocks are cut into for the attention phase.
-constexpr int kMaxPieces = 32;
-// Words of `sync` for a model with these shapes.
-inline size_t sync_words(int ffn, int n_kv_heads) { return kSyncHeader + ffn / 32 + (size_t)kMaxTokens * n_kv_heads; }
-// Floats of att_part.
-inline size_t att_part_floats(int n_kv_heads, int group, int head_dim) {
-    return (size_t)kMaxTokens * n_kv_heads * kMaxPieces * (2 * group + group * head_dim);
-}
 
 // Whether the shapes fit the kernel (dims, shared memory); `smem` receives
 // the dynamic shared memory a CTA needs.

@@ -92,9 +92,10 @@ def test_decode_steps_match_multi_launch_path():
     assert np.array_equal(kp.free_list(), km.free_list())
 
 
-def test_long_context_pieces_match_multi_launch_path():
-    """Contexts of up to 700 positions: a (token, head)'s blocks are cut into
-    several pieces dealt to different warps and merged by the last one."""
+def test_long_contexts_match_multi_launch_path():
+    """Contexts of up to 700 positions: a (token, KV head)'s 44 blocks are
+    dealt over the 16 warps of one CTA (up to three each) and merged in
+    shared memory; the short ones leave warps without blocks."""
     om, ((gp, kp), (gm, km)) = _pair(TINY, seed=9, n_tokens=4096)
     rng = np.random.default_rng(10)
     lens = [700, 33, 512, 129]
