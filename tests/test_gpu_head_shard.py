@@ -237,3 +237,64 @@ def test_peer_gather_single_rank_and_reimport():
         kv.peer_close()
     finally:
         kv.close()
+
+
+# ---- the sharded data path on one GPU: every rank's handle in one process ----
+
+@pytest.mark.parametrize("world,hkv,hq", [(2, 4, 16), (8, 8, 64)])
+def test_head_shards_on_one_gpu_match_unsharded(world, hkv, hq):
+    """The KV-head-sharded mode without its collective: `world` handles, each
+    holding KV heads [r*hl, (r+1)*hl) of every sequence, all on cuda:0, get
+    the same bookkeeping calls (replicated tables), a prefill, then three
+    fused append + attention decode steps.  Every rank's block tables and free
+    list equal rank 0's, and the rank outputs laid side by side in rank order
+    (the gathered layout, [token][rank][local q heads][D]) match the
+    unsharded oracle within the f32 bar.  (8, 8, 64) is config 4's 70B
+    attention shape at its 8-GPU sharding: one KV head and 8 q heads a rank."""
+    from langtrain_studio_b200 import kv as kvm
+    from oracle import oracle
+
+    d = 128
+    hl, ql = hkv // world, hq // world
+    lens = [100, 333, 1000, 17, 2049]
+    n, steps = len(lens), 3
+    rng = np.random.default_rng(world)
+    K = [rng.standard_normal((L, hkv * d)).astype(np.float32) for L in lens]
+    V = [rng.standard_normal((L, hkv * d)).astype(np.float32) for L in lens]
+    nb = sum((L + steps + 16) // 16 for L in lens) + 8
+    kvs = [kvm.KvCache(1, hl, d, nb * 16, n_heads=ql, max_seqs=n, max_batch=4096, device=0) for _ in range(world)]
+    ok = oracle.OracleKv(1, hkv * d, nb * 16, max_seqs=n)
+    col = lambda r, h: slice(r * h * d, (r + 1) * h * d)  # noqa: E731
+    dev = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()  # noqa: E731
+    for s, L in enumerate(lens):
+        for r, kv in enumerate(kvs):
+            b, sl = kv.append_batch(np.full(L, s), np.arange(L))
+            kv.write(0, b, sl, dev(K[s][:, col(r, hl)]), dev(V[s][:, col(r, hl)]))
+        rc, _, b, sl = ok.append_batch(np.full(L, s), np.arange(L))
+        assert rc == 0
+        ok.write_batch(0, b, sl, K[s], V[s])
+    seqs = np.arange(n)
+    for step in range(steps):
+        pos = np.array(lens) + step
+        kn = rng.standard_normal((n, hkv * d)).astype(np.float32)
+        vn = rng.standard_normal((n, hkv * d)).astype(np.float32)
+        q = rng.standard_normal((n, hq * d)).astype(np.float32)
+        outs = []
+        for r, kv in enumerate(kvs):
+            b, sl = kv.append_batch(seqs, pos)
+            outs.append(kv.write_attend(0, b, sl, dev(kn[:, col(r, hl)]), dev(vn[:, col(r, hl)]), dev(q[:, col(r, ql)]),
+                                        seqs, pos).cpu().numpy())
+        rc, _, b, sl = ok.append_batch(seqs, pos)
+        assert rc == 0
+        ok.write_batch(0, b, sl, kn, vn)
+        ref = ok.attend(0, q, seqs, pos, hq, hkv, d)
+        full = np.concatenate([o.reshape(n, ql * d) for o in outs], axis=1)
+        np.testing.assert_allclose(full, ref, rtol=1e-4, atol=2e-5, err_msg=f"step {step}")
+    for kv in kvs:
+        kv.check()
+        assert np.array_equal(kv.free_list(), kvs[0].free_list())
+        for s in range(n):
+            assert np.array_equal(kv.seq_blocks(s), kvs[0].seq_blocks(s))
+            assert np.array_equal(kv.seq_blocks(s), ok.seq_blocks(s))
+    for kv in kvs:
+        kv.close()
