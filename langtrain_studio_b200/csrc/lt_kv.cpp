@@ -112,6 +112,7 @@ struct lt_kv {
     std::vector<int32_t> casc_buf;  // upload image: PrefixItems then the token list
     uint64_t cascade_launches = 0;
     int casc_splits = 1;
+    size_t casc_ntok = 0;  // tokens in the upload image's token list
     uint32_t n_blocks = 0, kv_dim = 0, group = 0, max_blocks = 0;
     bool q8 = false;          // LT_KV_Q8_0 pool
     size_t block_elems = 0;   // 16-bit units of one block in one layer (all heads, K and V)
@@ -484,9 +485,14 @@ lt_status prof_begin(lt_kv* kv, ProfRing& r, cudaStream_t st, cudaEvent_t* end) 
 // Shared-prefix groups of one attention call: tokens whose sequences start
 // with the same block, at least cascade_min_tokens of them, sharing at least
 // kCascadeMinBlocks leading blocks (all strictly before every member token's
-// own block).  Each group's tokens get skip = its shared block count; the
-// prefix pass items (KV head x chunks of the group's tokens) and the token
-// list go to casc_buf.  Returns the number of items (0: no pass).
+// own block).  Each group's tokens get skip = its shared block count.  When
+// every token of a group belongs to one sequence (a prefill chunk), each
+// token's skip is instead its own block index: the pass then covers, row by
+// row, every block before the token's own one (causally masked), and the
+// stream-K launch only the token's own block.  The prefix pass items (KV
+// head x chunks of the group's tokens, each over [0, its tokens' largest
+// skip)), the token list and the tokens' skips go to casc_buf.  Returns the
+// number of items (0: no pass).
 int plan_cascade(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n) {
     if (kv->cascade_min_tokens == 0 || n < kv->cascade_min_tokens || n > kv->pre_cap) return 0;
     auto& ord = kv->casc_order;
@@ -500,6 +506,7 @@ int plan_cascade(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n
     const uint32_t hkv = kv->cfg.n_kv_heads;
     struct Group {
         int32_t root, P, off, cnt;
+        bool one_seq;  // every token of the group is of sequence root
     };
     std::vector<Group> groups;
     std::vector<int32_t> toks;
@@ -521,22 +528,30 @@ int plan_cascade(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n
                 }
             }
             if (P >= (size_t)kCascadeMinBlocks) {
-                groups.push_back({(int32_t)root, (int32_t)P, (int32_t)toks.size(), (int32_t)(b - a)});
+                bool one_seq = true;
+                for (uint32_t k = a; k < b && one_seq; ++k) one_seq = seq[ord[k]] == root;
+                groups.push_back({(int32_t)root, (int32_t)P, (int32_t)toks.size(), (int32_t)(b - a), one_seq});
                 for (uint32_t k = a; k < b; ++k) {
                     toks.push_back((int32_t)ord[k]);
-                    kv->toks_tmp[ord[k]].skip = (int32_t)P;
+                    kv->toks_tmp[ord[k]].skip = one_seq ? (int32_t)(pos[ord[k]] / kBlock) : (int32_t)P;
                 }
             }
         }
         a = b;
     }
-    // Split every group's blocks over S CTAs so the pass fills the SMs; each
+    // Blocks each chunk of tpc tokens covers: its tokens' largest skip.
+    auto chunk_blocks = [&](const Group& g, int32_t c0) {
+        int32_t L = 0;
+        for (int32_t k = c0; k < std::min(g.cnt, c0 + tpc); ++k) L = std::max(L, kv->toks_tmp[toks[g.off + k]].skip);
+        return L;
+    };
+    // Split every chunk's blocks over S CTAs so the pass fills the SMs; each
     // split keeps at least one 4-block step.
     long long base_items = 0;
     int min_p = 1 << 30;
     for (const Group& g : groups) {
         base_items += (long long)hkv * ((g.cnt + tpc - 1) / tpc);
-        min_p = std::min(min_p, (int)g.P);
+        for (int32_t c0 = 0; c0 < g.cnt; c0 += tpc) min_p = std::min(min_p, (int)chunk_blocks(g, c0));
     }
     int S = 1;
     if (base_items > 0)
@@ -545,17 +560,22 @@ int plan_cascade(lt_kv* kv, const uint32_t* seq, const uint32_t* pos, uint32_t n
     kv->casc_splits = S;
     std::vector<ltkv::PrefixItem> items;
     for (const Group& g : groups)
-        for (uint32_t h = 0; h < hkv; ++h)
-            for (int32_t c0 = 0; c0 < g.cnt; c0 += tpc)
+        for (int32_t c0 = 0; c0 < g.cnt; c0 += tpc) {
+            const int32_t L = chunk_blocks(g, c0);
+            for (uint32_t h = 0; h < hkv; ++h)
                 for (int sp = 0; sp < S; ++sp) {
-                    const int32_t b0 = (int32_t)((long long)g.P * sp / S), b1 = (int32_t)((long long)g.P * (sp + 1) / S);
+                    const int32_t b0 = (int32_t)((long long)L * sp / S), b1 = (int32_t)((long long)L * (sp + 1) / S);
                     items.push_back({g.root, b0, b1, sp, (int32_t)h, g.off + c0, std::min(tpc, g.cnt - c0)});
                 }
-    kv->casc_buf.resize(items.size() * (sizeof(ltkv::PrefixItem) / 4) + toks.size());
+        }
+    const size_t item_words = items.size() * (sizeof(ltkv::PrefixItem) / 4);
+    kv->casc_buf.resize(item_words + 2 * toks.size());
     if (!items.empty()) std::memcpy(kv->casc_buf.data(), items.data(), items.size() * sizeof(ltkv::PrefixItem));
-    if (!toks.empty())
-        std::memcpy(kv->casc_buf.data() + items.size() * (sizeof(ltkv::PrefixItem) / 4), toks.data(),
-                    toks.size() * sizeof(int32_t));
+    for (size_t k = 0; k < toks.size(); ++k) {
+        kv->casc_buf[item_words + k] = toks[k];
+        kv->casc_buf[item_words + toks.size() + k] = kv->toks_tmp[toks[k]].skip;
+    }
+    kv->casc_ntok = toks.size();
     return (int)items.size();
 }
 
@@ -725,6 +745,7 @@ lt_status attend_impl(lt_kv* kv, uint32_t layer, const void* q, lt_dtype q_dtype
         pp.n_blocks = (int32_t)kv->n_blocks;
         pp.items = static_cast<const ltkv::PrefixItem*>(d_casc);
         pp.tok_list = static_cast<const int32_t*>(d_casc) + (size_t)n_items * (sizeof(ltkv::PrefixItem) / 4);
+        pp.tok_lim = pp.tok_list + kv->casc_ntok;
         pp.n_kv_heads = (int32_t)kv->cfg.n_kv_heads;
         pp.group = (int32_t)kv->group;
         pp.q = q;

@@ -119,6 +119,7 @@ struct PrefixParams {
     int32_t n_blocks;  // blocks in the pool, for LT_BOUNDS_CHECK builds (0: not checked)
     const PrefixItem* items;
     const int32_t* tok_list;  // token indices of the call (into q, pre_o, pre_ml)
+    const int32_t* tok_lim;   // parallel to tok_list: the token attends blocks [0, tok_lim) here
     int32_t n_kv_heads, group;
     const void* q;
     int32_t q_f32;

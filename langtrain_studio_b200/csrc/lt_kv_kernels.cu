@@ -1347,6 +1347,9 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
     const int t_item = r / G, hg = r % G;
     const bool live = r < kPreRows && t_item < item.n_tok && t_item < kPreRows / G;
     const int tok = live ? p.tok_list[item.tok_off + t_item] : 0;
+    // Row r attends positions [0, lim) of the item's blocks: the token's own
+    // skip (a prefill chunk's tokens, causally), or all of them.
+    const int lim = live ? p.tok_lim[item.tok_off + t_item] * kBlock : 0x7fffffff;
     if (r < kPreRows) {
         const int qelem = p.q_f32 ? 4 : 2;
         const uint8_t* qrow = static_cast<const uint8_t*>(p.q) + (((size_t)tok * Hkv + item.head) * G + hg) * D * qelem;
@@ -1490,9 +1493,10 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
             __syncwarp();
             if (lane == 0) mbar_arrive1(s_free + 8u * bb);  // S buffer bb may be overwritten
             float mx = -INFINITY;
+            const int pos0 = (item.blk0 + j * kPreStepBlocks) * kBlock;
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
-                sv_[i] = i < npos ? sv_[i] * scale_log2 : -INFINITY;
+                sv_[i] = i < npos && pos0 + i < lim ? sv_[i] * scale_log2 : -INFINITY;
                 mx = fmaxf(mx, sv_[i]);
             }
             float alpha = 1.f;
@@ -1523,13 +1527,16 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefix_attn_kernel(const __gri
                 }
             }
             const uint32_t pb = L.p0 + bb * PBUF;
+            // A row that has had no position yet (every one masked) keeps
+            // m = -inf; its P is 0, taken against 0 rather than -inf.
+            const float m_ref = m_use == -INFINITY ? 0.f : m_use;
             float lsum = 0.f;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 uint32_t hi[4], lo[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const float p0 = ex2(sv_[8 * c + 2 * e] - m_use), p1 = ex2(sv_[8 * c + 2 * e + 1] - m_use);
+                    const float p0 = ex2(sv_[8 * c + 2 * e] - m_ref), p1 = ex2(sv_[8 * c + 2 * e + 1] - m_ref);
                     lsum += p0 + p1;
                     const __half2 h = __floats2half2_rn(p0, p1);
                     const float2 hf = __half22float2(h);

@@ -406,6 +406,37 @@ def test_cascade_shared_prefix_matches_oracle(oracle_mod, hd, hq, hkv, n_seq, pr
     t.kv.check()
 
 
+@pytest.mark.parametrize("hd,hq,hkv,cached,chunk", [(128, 32, 8, 700, 64), (64, 32, 4, 2048, 256),
+                                                   (128, 8, 8, 333, 21), (128, 16, 2, 1000, 97)])
+def test_cascade_prefill_chunk_matches_oracle(oracle_mod, hd, hq, hkv, cached, chunk):
+    """A prefill chunk: `chunk` tokens of one sequence over `cached` cached
+    positions, written first, then attended in one call.  Every token's
+    blocks before its own go through the prefix pass with the token's causal
+    limit (the chunk's blocks included), its own block through the decode
+    launch; outputs match the oracle, and a second chunk of two sequences in
+    one call (two such groups) does too."""
+    rng = np.random.default_rng(hd + cached + chunk)
+    per = (cached + 2 * chunk + 16) // 16 + 2
+    t = Twin(oracle_mod, 1, hkv, hd, 16 * 2 * per, n_heads=hq, max_seqs=2)
+    for s in range(2):
+        t.fill(s, cached + s * 5, rng)
+    for round_ in range(2):
+        seqs, pos = [], []
+        for s in range(2 if round_ else 1):
+            start = t.kv.len(s)
+            p = np.arange(start, start + chunk)
+            t.fill(s, start + chunk, rng)  # the chunk's rows are written before the attention call
+            seqs.append(np.full(chunk, s))
+            pos.append(p)
+        seqs, pos = np.concatenate(seqs), np.concatenate(pos)
+        q = rng.standard_normal((seqs.size, hq * hd)).astype(np.float32)
+        c0 = t.kv.cascade_launches()
+        out, ref = t.attend_both(0, seqs, pos, q)
+        assert t.kv.cascade_launches() == c0 + 1, "the prefix pass did not run"
+        np.testing.assert_allclose(out, ref, rtol=1e-4, atol=2e-5, err_msg=f"round {round_}")
+    t.kv.check()
+
+
 def test_cascade_groups_mixed_with_private_sequences(oracle_mod):
     """Two prefix groups, one of them with a member that shares only part of
     the prefix (the group's shared run shortens to it), and sequences with no
